@@ -1,0 +1,195 @@
+/* lmc_cuda.h - C ABI of the B200-native LMc hot path (liblmc_b200.so).
+ *
+ * Plain C99 declarations: pointers, sizes and status codes; no CUDA, C++ or
+ * PyTorch types.  Device pointers are marked d_*, host pointers h_*; a
+ * `stream` argument is a cudaStream_t passed as void* (NULL = the legacy
+ * default stream).  Every entry point returns LMC_OK (0) or a negative
+ * LMC_ERR_* code and records a message for lmc_last_error(); none of them
+ * falls back to the CPU - without a usable sm_100 device they fail.
+ *
+ * Each entry point names the LMc interface (nile-agi/LMc, file:line) whose
+ * behaviour it replaces.  LMc reports hard errors through LMC_FATAL
+ * (src/utils.h:68-69, exit(1)); this ABI returns the status instead and the
+ * C99 drop-in layer (include/lmc_ops.h) maps a failure back to LMC_FATAL.
+ */
+#ifndef LMC_CUDA_H
+#define LMC_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define LMC_OK               0
+#define LMC_ERR_INVALID     -1   /* bad argument (null pointer, bad size/shape) */
+#define LMC_ERR_UNSUPPORTED -2   /* tensor type or shape not handled            */
+#define LMC_ERR_CUDA        -3   /* CUDA runtime error                          */
+#define LMC_ERR_OOM         -4   /* device or host allocation failed            */
+#define LMC_ERR_IO          -5   /* file missing, short read, bad GGUF          */
+#define LMC_ERR_TIMEOUT     -6   /* a bounded wait ran out                      */
+#define LMC_ERR_NCCL        -7   /* NCCL error                                  */
+
+/* GGUF tensor type IDs (src/quant.h:27-45). */
+#define LMC_TYPE_F32      0
+#define LMC_TYPE_F16      1
+#define LMC_TYPE_Q4_0     2
+#define LMC_TYPE_Q4_1     3
+#define LMC_TYPE_Q5_0     6
+#define LMC_TYPE_Q5_1     7
+#define LMC_TYPE_Q8_0     8
+#define LMC_TYPE_Q2_K    10
+#define LMC_TYPE_Q3_K    11
+#define LMC_TYPE_Q4_K    12
+#define LMC_TYPE_Q5_K    13
+#define LMC_TYPE_Q6_K    14
+#define LMC_TYPE_IQ3_XXS 18
+#define LMC_TYPE_IQ3_S   21
+#define LMC_TYPE_IQ4_XS  23
+
+/* Message for the last failing call on this host thread ("" if none). */
+const char *lmc_last_error(void);
+
+/* Select and initialise CUDA device `device` for the calling thread.
+ * Fails with LMC_ERR_CUDA when no sm_100 device is present. */
+int lmc_init(int device);
+
+/* Number of elements and bytes of one block of `type`
+ * (replaces the *_BLOCK_SIZE / *_BYTES_PER_BLOCK constants, src/quant.h:54-99). */
+int lmc_block_geometry(uint32_t type, int *block_elems, int *block_bytes);
+
+/* ---- K1: block dequantization ------------------------------------------------
+ * Replaces dequant_q4_0 ... dequant_iq4_xs (src/quant.c:178-521) and the
+ * F32/F16 cases of the loader switch (src/gguf.c:316-345).  Decodes
+ * n_elements weights from the flat block stream d_blocks into d_out (fp32),
+ * bit-exact to LMc.  n_elements must be a multiple of the block size.
+ * d_blocks must hold (n_elements / block) * block_bytes bytes, plus 2
+ * readable bytes for IQ4_XS (LMc reads 2 bytes of the next block,
+ * src/quant.c:506,515). */
+int lmc_dequant(uint32_t type, const void *d_blocks, size_t n_elements,
+                float *d_out, void *stream);
+
+/* ---- quantized tensors on the device ---------------------------------------
+ * LMc dequantizes every tensor to fp32 at load time and frees the raw bytes
+ * (LOAD_QUANT, src/gguf.c:100-111).  A qtensor keeps the raw GGUF blocks on
+ * the device instead and, for the formats with a tensor-core GEMV, a
+ * row-tiled copy of the same bytes rearranged for it.  A tensor is `rows`
+ * rows of `cols` weights stored as one flat block stream (blocks may
+ * straddle rows when cols is not a multiple of the block size, as in LMc). */
+typedef struct lmc_qtensor lmc_qtensor;
+
+int lmc_qtensor_upload(uint32_t type, int rows, int cols, const void *h_blocks,
+                       size_t bytes, lmc_qtensor **out);
+int lmc_qtensor_free(lmc_qtensor *t);
+/* Device pointer to the raw GGUF block stream (read-only view). */
+const void *lmc_qtensor_blocks(const lmc_qtensor *t);
+/* 1 when the tensor-core GEMV layout was built for this tensor. */
+int lmc_qtensor_has_tiled(const lmc_qtensor *t);
+
+/* ---- K2: quantized matrix-vector products ------------------------------------
+ * Replaces matmul_vec (src/ops.c:69-97): for each of `batch` input vectors,
+ *   y[b][m] = bias[m] + sum_k W[m][k] * x[b][k]   (fp32 accumulation)
+ * x is batch rows of ldx floats, y batch rows of ldy floats; bias may be
+ * NULL.  `epilogue` is a bit set:
+ *   LMC_EPI_GELU  apply gelu (src/ops.c:20-24) to the result,
+ *   LMC_EPI_ACCUM add the result into y instead of overwriting it (the
+ *                 residual adds of src/ops.c:198,205).
+ * lmc_matmul uses the fastest layout the qtensor carries; lmc_matmul_blocks
+ * runs the generic kernel straight on a raw block stream. */
+#define LMC_EPI_NONE  0
+#define LMC_EPI_GELU  1
+#define LMC_EPI_ACCUM 2
+int lmc_matmul(const lmc_qtensor *w, const float *d_x, int ldx, const float *d_bias,
+               float *d_y, int ldy, int batch, int epilogue, void *stream);
+int lmc_matmul_blocks(uint32_t type, const void *d_blocks, int rows, int cols,
+                      const float *d_x, int ldx, const float *d_bias, float *d_y,
+                      int ldy, int batch, int epilogue, void *stream);
+
+/* ---- small ops kept on the device --------------------------------------------
+ * Each processes `rows` independent rows. */
+/* layer_norm (src/ops.c:47-59), eps fixed at 1e-5 as in LMc. */
+int lmc_layer_norm(float *d_out, const float *d_x, const float *d_w, const float *d_b,
+                   int dim, int rows, void *stream);
+/* rms_norm (src/ops_llama.c:24-33). */
+int lmc_rms_norm(float *d_out, const float *d_x, const float *d_w, int dim, int rows,
+                 float eps, void *stream);
+/* softmax in place (src/ops.c:32-44), uniform when the exp-sum < 1e-30. */
+int lmc_softmax(float *d_x, int n, int rows, void *stream);
+/* gelu / silu in place (src/ops.c:20-29). */
+int lmc_gelu(float *d_x, size_t n, void *stream);
+int lmc_silu(float *d_x, size_t n, void *stream);
+/* d_gate[i] = silu(d_gate[i]) * d_up[i] (src/ops_llama.c:150-151). */
+int lmc_swiglu(float *d_gate, const float *d_up, size_t n, void *stream);
+/* rope_apply (src/ops_llama.c:39-48) on n_heads consecutive head vectors. */
+int lmc_rope_apply(float *d_vec, const float *d_cos_row, const float *d_sin_row,
+                   int head_dim, int n_heads, void *stream);
+/* Greedy pick (src/lmc.c:45-47): first index of the maximum of each row. */
+int lmc_argmax(const float *d_x, int n, int rows, int *d_idx, void *stream);
+
+/* ---- K4: attention over the head-major KV cache -------------------------------
+ * Replaces the cache write and per-head read of attention_forward
+ * (src/ops.c:122-178) and llama_attention_forward (src/ops_llama.c:80-134).
+ * Cache layout per layer: [Hkv][S][Dh] (src/models.h:149-162), fp32
+ * (LMC_KV_F32, LMc's layout) or fp16 (LMC_KV_F16).  For `batch` sequences
+ * the caches are batch consecutive [Hkv][S][Dh] slabs and q/k_new/v_new/out
+ * are batch rows of H*Dh (q, out) and Hkv*Dh (k_new, v_new) floats.
+ * d_pos[b] is the position written this step; positions 0..d_pos[b] are
+ * attended.  Query head h reads kv head h / (H / Hkv) (src/ops_llama.c:95).
+ * Like LMc's caller-supplied scores_buf, the scratch for the split-context
+ * partial results is supplied by the caller: d_workspace must hold
+ * lmc_attention_workspace_bytes(batch, H, Dh, S) bytes (0 = none needed). */
+#define LMC_KV_F32 0
+#define LMC_KV_F16 1
+size_t lmc_attention_workspace_bytes(int batch, int H, int Dh, int S);
+int lmc_attention_decode(float *d_out, const float *d_q, const float *d_k_new,
+                         const float *d_v_new, void *d_k_cache, void *d_v_cache,
+                         int kv_dtype, const int *d_pos, int batch, int H, int Hkv,
+                         int Dh, int S, void *d_workspace, size_t workspace_bytes,
+                         void *stream);
+
+/* ---- whole model: load_model + model_forward on the device -------------------
+ * lmc_model_load parses a GGUF v1-3 file the way load_model does
+ * (src/gguf.c:114-353, src/models.c:52-164) but uploads the raw blocks
+ * instead of dequantizing them, allocates the KV cache and activations on
+ * the device, and precomputes the RoPE table with LMc's formula
+ * (src/models.c:101-117).  max_batch sequences can be decoded together. */
+typedef struct lmc_model lmc_model;
+typedef struct {
+    int arch;        /* 1 = GPT-2, 2 = LLaMA (src/models.h:28-32) */
+    int vocab_size, seq_len, n_layers, n_heads, n_kv_heads, embed_dim, ffn_dim, head_dim;
+    float rope_theta, norm_eps;
+} lmc_model_config;
+
+int lmc_model_load(const char *gguf_path, int max_batch, int kv_dtype, lmc_model **out);
+int lmc_model_get_config(const lmc_model *m, lmc_model_config *cfg);
+int lmc_model_free(lmc_model *m);
+/* model_forward (src/ops.c:212-237, src/ops_llama.c:157-192) for `batch`
+ * sequences at once: h_tokens[b] at position h_pos[b].  Writes the next
+ * greedy id of each sequence to h_next (may be NULL) and, when h_logits is
+ * not NULL, the batch x vocab logits. */
+int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int batch,
+                      float *h_logits, int *h_next);
+/* The generate() loop of src/lmc.c:108-132 without tokenizer or EOS, run
+ * entirely on the device: the n_prompt prompt tokens of each sequence are
+ * fed one position at a time, then n_new greedy steps; h_out_ids receives
+ * batch x n_new ids.  With use_graph = 1 every step is one CUDA-graph
+ * launch and the host does not wait between steps. */
+int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int batch,
+                       int n_new, int use_graph, int *h_out_ids);
+/* Replays the step graph captured by the last lmc_model_generate(use_graph=1)
+ * `n` more times, continuing from the current device-side positions (a
+ * timing helper: positions must stay below seq_len).  Enqueues only; the
+ * stream the steps run on is written to *stream_out when it is not NULL. */
+int lmc_model_replay(lmc_model *m, int n, void *stream_out);
+/* Kernel launches in one captured step (graph kernel nodes), -1 if none. */
+int lmc_model_graph_kernels(const lmc_model *m);
+/* Device-side buffers of the model, for callers that drive steps themselves:
+ * which = 0 logits [max_batch][V] fp32. */
+void *lmc_model_device_buffer(lmc_model *m, int which);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LMC_CUDA_H */

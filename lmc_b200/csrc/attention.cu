@@ -1,0 +1,199 @@
+// attention.cu - K4: decode-step attention over the head-major KV cache.
+//
+// Replaces the cache write and per-head read of LMc attention_forward
+// (src/ops.c:122-178) and llama_attention_forward (src/ops_llama.c:80-134):
+// scores = q . k_t / sqrt(Dh) for t <= pos, softmax, out = sum_t p_t v_t.
+//
+// Split-K over the context (flash-decoding): CTA (split, kv head, sequence)
+// covers CH positions and all G = H / Hkv query heads of its kv head, so each
+// K/V row is read from HBM once per group, not once per query head.  A split
+// writes (max, exp-sum, unnormalised accumulator) to the caller's workspace;
+// k_attn_combine merges the splits.  The CTA whose range holds `pos` first
+// appends the new K/V row to the cache (rounded to the cache type, so the
+// step reads exactly what later steps will read).
+#include <cuda_fp16.h>
+
+#include "lmc_common.cuh"
+#include "lmc_internal.h"
+
+#define ATT_THREADS 128
+#define ATT_MAX_SPLITS 16
+
+template <typename KV> __device__ __forceinline__ float kv_ld(const KV *p);
+template <> __device__ __forceinline__ float kv_ld<float>(const float *p) { return *p; }
+template <> __device__ __forceinline__ float kv_ld<__half>(const __half *p) { return __half2float(*p); }
+template <typename KV> __device__ __forceinline__ KV kv_cvt(float v);
+template <> __device__ __forceinline__ float kv_cvt<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half kv_cvt<__half>(float v) { return __float2half_rn(v); }
+
+struct AttnArgs {
+    float *out;
+    const float *q, *k_new, *v_new;
+    void *k_cache, *v_cache;
+    const int *pos;
+    float *ws;  // [batch][H][nsplit][Dh + 2]
+    int H, Hkv, Dh, S, CH, nsplit;
+    int ldo, ldq, ldkv;  // row strides (floats) between sequences
+};
+
+template <typename KV>
+__global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
+    extern __shared__ float sm[];
+    const int sp = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+    const int G = a.H / a.Hkv, Dh = a.Dh, CH = a.CH;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = ATT_THREADS / 32;
+    const int pos = a.pos[b];
+    if (pos < 0 || pos >= a.S) return;  // the host validates positions; never index outside the cache
+    const int t0 = sp * CH, t1 = min(t0 + CH, pos + 1);
+    float *qs = sm;               // [G][Dh]
+    float *sc = sm + G * Dh;      // [G][CH]
+    float *ml = sc + G * CH;      // [G][2]
+    float *wsb = a.ws + (((size_t)b * a.H + (size_t)kh * G) * a.nsplit + sp) * (Dh + 2);
+    const size_t hstride = (size_t)a.nsplit * (Dh + 2);
+    if (t0 > pos) {  // empty split: mark it so the combine skips it
+        if (a.nsplit > 1)
+            for (int g = threadIdx.x; g < G; g += ATT_THREADS) {
+                wsb[g * hstride + Dh] = -INFINITY;
+                wsb[g * hstride + Dh + 1] = 0.0f;
+            }
+        return;
+    }
+    KV *kc = reinterpret_cast<KV *>(a.k_cache) + ((size_t)b * a.Hkv + kh) * a.S * Dh;
+    KV *vc = reinterpret_cast<KV *>(a.v_cache) + ((size_t)b * a.Hkv + kh) * a.S * Dh;
+    if (pos >= t0 && pos < t1) {  // append this step's K/V row
+        const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
+        const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
+        for (int d = threadIdx.x; d < Dh; d += ATT_THREADS) {
+            kc[(size_t)pos * Dh + d] = kv_cvt<KV>(kn[d]);
+            vc[(size_t)pos * Dh + d] = kv_cvt<KV>(vn[d]);
+        }
+    }
+    const float *qb = a.q + (size_t)b * a.ldq + (size_t)kh * G * Dh;
+    for (int i = threadIdx.x; i < G * Dh; i += ATT_THREADS) qs[i] = qb[i];
+    __syncthreads();
+    const float scale = 1.0f / sqrtf((float)Dh);
+    const int per_lane = Dh / 32;
+    for (int t = t0 + warp; t < t1; t += nw) {
+        float kv[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            if (i < per_lane) kv[i] = kv_ld<KV>(kc + (size_t)t * Dh + lane + 32 * i);
+        for (int g = 0; g < G; g++) {
+            float dot = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if (i < per_lane) dot = fmaf(qs[g * Dh + lane + 32 * i], kv[i], dot);
+            dot = warp_sum(dot);
+            if (lane == 0) sc[g * CH + (t - t0)] = dot * scale;
+        }
+    }
+    __syncthreads();
+    const int n = t1 - t0;
+    for (int g = warp; g < G; g += nw) {
+        float m = -INFINITY;
+        for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[g * CH + t]);
+        m = warp_max(m);
+        float l = 0.0f;
+        for (int t = lane; t < n; t += 32) {
+            const float e = expf(sc[g * CH + t] - m);
+            sc[g * CH + t] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) { ml[2 * g] = m; ml[2 * g + 1] = l; }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * Dh; i += ATT_THREADS) {
+        const int g = i / Dh, d = i % Dh;
+        float acc = 0.0f;
+        const float *p = sc + g * CH;
+        for (int t = 0; t < n; t++) acc = fmaf(p[t], kv_ld<KV>(vc + (size_t)(t0 + t) * Dh + d), acc);
+        if (a.nsplit == 1) {
+            a.out[(size_t)b * a.ldo + ((size_t)kh * G + g) * Dh + d] = acc / ml[2 * g + 1];
+        } else {
+            wsb[g * hstride + d] = acc;
+            if (d == 0) { wsb[g * hstride + Dh] = ml[2 * g]; wsb[g * hstride + Dh + 1] = ml[2 * g + 1]; }
+        }
+    }
+}
+
+// Merge the splits of one (sequence, query head): rescale each split's sum
+// and accumulator to the global maximum.
+__global__ void k_attn_combine(AttnArgs a) {
+    const int h = blockIdx.x, b = blockIdx.y, Dh = a.Dh;
+    const float *w = a.ws + ((size_t)b * a.H + h) * a.nsplit * (Dh + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < a.nsplit; s++) M = fmaxf(M, w[s * (Dh + 2) + Dh]);
+    for (int d = threadIdx.x; d < Dh; d += blockDim.x) {
+        float L = 0.0f, acc = 0.0f;
+        for (int s = 0; s < a.nsplit; s++) {
+            const float l = w[s * (Dh + 2) + Dh + 1];
+            if (l == 0.0f) continue;
+            const float f = expf(w[s * (Dh + 2) + Dh] - M);
+            L += l * f;
+            acc += w[s * (Dh + 2) + d] * f;
+        }
+        a.out[(size_t)b * a.ldo + (size_t)h * Dh + d] = acc / L;
+    }
+}
+
+static void attn_plan(int S, int *CH, int *nsplit) {
+    int ch = 64;
+    while ((S + ch - 1) / ch > ATT_MAX_SPLITS) ch *= 2;
+    *CH = ch;
+    *nsplit = (S + ch - 1) / ch;
+}
+
+extern "C" size_t lmc_attention_workspace_bytes(int batch, int H, int Dh, int S) {
+    int CH, ns;
+    attn_plan(S, &CH, &ns);
+    return ns > 1 ? (size_t)batch * H * ns * (Dh + 2) * sizeof(float) : 0;
+}
+
+extern "C" int lmc_attention_launch(float *out, int ldo, const float *q, int ldq, const float *k_new,
+                                    const float *v_new, int ldkv, void *k_cache, void *v_cache, int kv_dtype,
+                                    const int *d_pos, int batch, int H, int Hkv, int Dh, int S, void *d_ws,
+                                    size_t ws_bytes, cudaStream_t s) {
+    if (!out || !q || !k_new || !v_new || !k_cache || !v_cache || !d_pos)
+        return lmc_set_error(LMC_ERR_INVALID, "attention: null pointer");
+    if (batch <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh % 32 || Dh > 256 || S <= 0)
+        return lmc_set_error(LMC_ERR_INVALID, "attention: H=%d Hkv=%d Dh=%d S=%d (need H%%Hkv==0, Dh%%32==0, Dh<=256)",
+                             H, Hkv, Dh, S);
+    if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16)
+        return lmc_set_error(LMC_ERR_UNSUPPORTED, "attention: kv dtype %d", kv_dtype);
+    AttnArgs a;
+    a.out = out; a.q = q; a.k_new = k_new; a.v_new = v_new; a.k_cache = k_cache; a.v_cache = v_cache;
+    a.pos = d_pos; a.H = H; a.Hkv = Hkv; a.Dh = Dh; a.S = S;
+    a.ldo = ldo; a.ldq = ldq; a.ldkv = ldkv;
+    attn_plan(S, &a.CH, &a.nsplit);
+    const size_t need = lmc_attention_workspace_bytes(batch, H, Dh, S);
+    if (need > ws_bytes || (need && !d_ws))
+        return lmc_set_error(LMC_ERR_INVALID, "attention: workspace %zu bytes < %zu needed", ws_bytes, need);
+    a.ws = (float *)d_ws;
+    const int G = H / Hkv;
+    const size_t smem = (size_t)(G * Dh + G * a.CH + 2 * G) * sizeof(float);
+    if (smem > 200 * 1024) return lmc_set_error(LMC_ERR_UNSUPPORTED, "attention: group too large");
+    dim3 grid(a.nsplit, Hkv, batch);
+    if (kv_dtype == LMC_KV_F32) {
+        if (smem > 48 * 1024)
+            LMC_CUDA_TRY(cudaFuncSetAttribute(k_attn_split<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        k_attn_split<float><<<grid, ATT_THREADS, smem, s>>>(a);
+    } else {
+        if (smem > 48 * 1024)
+            LMC_CUDA_TRY(cudaFuncSetAttribute(k_attn_split<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        k_attn_split<__half><<<grid, ATT_THREADS, smem, s>>>(a);
+    }
+    LMC_LAUNCH_CHECK("attention");
+    if (a.nsplit > 1) {
+        k_attn_combine<<<dim3(H, batch), Dh, 0, s>>>(a);
+        LMC_LAUNCH_CHECK("attention combine");
+    }
+    return LMC_OK;
+}
+
+extern "C" int lmc_attention_decode(float *out, const float *q, const float *k_new, const float *v_new,
+                                    void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, int batch,
+                                    int H, int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes, void *stream) {
+    return lmc_attention_launch(out, H * Dh, q, H * Dh, k_new, v_new, Hkv * Dh, k_cache, v_cache, kv_dtype, d_pos,
+                                batch, H, Hkv, Dh, S, d_ws, ws_bytes, lmc_stream(stream));
+}

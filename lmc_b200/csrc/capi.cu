@@ -1,0 +1,158 @@
+// capi.cu - C ABI plumbing: error reporting, device init, block geometry,
+// quantized tensors on the device and the matmul dispatcher.
+#include <stdarg.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "lmc_common.cuh"
+#include "lmc_internal.h"
+
+static thread_local char g_err[1024];
+
+extern "C" int lmc_set_error(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+extern "C" const char *lmc_last_error(void) { return g_err; }
+
+extern "C" int lmc_init(int device) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0)
+        return lmc_set_error(LMC_ERR_CUDA, "no CUDA device (%s)", cudaGetErrorString(e));
+    if (device < 0 || device >= n) return lmc_set_error(LMC_ERR_INVALID, "device %d of %d", device, n);
+    LMC_CUDA_TRY(cudaSetDevice(device));
+    int major = 0, minor = 0;
+    LMC_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+    LMC_CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+    if (major != 10 || minor != 0)
+        return lmc_set_error(LMC_ERR_CUDA, "device %d is sm_%d%d; this library is built for sm_100a only", device,
+                             major, minor);
+    LMC_CUDA_TRY(cudaFree(0));  // create the context now
+    return LMC_OK;
+}
+
+// src/quant.h:54-99 (F32/F16: one element of 4/2 bytes).
+extern "C" int lmc_block_geometry(uint32_t type, int *be, int *bb) {
+    int e, b;
+    switch (type) {
+    case LMC_TYPE_F32: e = 1; b = 4; break;
+    case LMC_TYPE_F16: e = 1; b = 2; break;
+    case LMC_TYPE_Q4_0: e = 32; b = 18; break;
+    case LMC_TYPE_Q4_1: e = 32; b = 20; break;
+    case LMC_TYPE_Q5_0: e = 32; b = 22; break;
+    case LMC_TYPE_Q5_1: e = 32; b = 24; break;
+    case LMC_TYPE_Q8_0: e = 32; b = 34; break;
+    case LMC_TYPE_Q2_K: e = 256; b = 84; break;
+    case LMC_TYPE_Q3_K: e = 256; b = 110; break;
+    case LMC_TYPE_Q4_K: e = 256; b = 144; break;
+    case LMC_TYPE_Q5_K: e = 256; b = 176; break;
+    case LMC_TYPE_Q6_K: e = 256; b = 210; break;
+    case LMC_TYPE_IQ3_XXS: e = 256; b = 98; break;
+    case LMC_TYPE_IQ3_S: e = 256; b = 110; break;
+    case LMC_TYPE_IQ4_XS: e = 256; b = 136; break;
+    default: return lmc_set_error(LMC_ERR_UNSUPPORTED, "unsupported tensor type %u", type);
+    }
+    if (be) *be = e;
+    if (bb) *bb = b;
+    return LMC_OK;
+}
+
+extern "C" int lmc_tensor_bytes(uint32_t type, size_t n_elements, size_t *bytes) {
+    int be, bb;
+    int rc = lmc_block_geometry(type, &be, &bb);
+    if (rc) return rc;
+    if (n_elements % (size_t)be)
+        return lmc_set_error(LMC_ERR_INVALID, "n_elements=%zu not a multiple of %d", n_elements, be);
+    *bytes = n_elements / (size_t)be * (size_t)bb;
+    return LMC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// qtensor: raw GGUF blocks on the device (+ a tiled copy for tensor-core GEMV)
+// ---------------------------------------------------------------------------
+extern "C" int lmc_qtensor_upload(uint32_t type, int rows, int cols, const void *h_blocks, size_t bytes,
+                                  lmc_qtensor **out) {
+    if (!out || !h_blocks || rows <= 0 || cols <= 0) return lmc_set_error(LMC_ERR_INVALID, "qtensor_upload: args");
+    *out = NULL;
+    size_t need;
+    int rc = lmc_tensor_bytes(type, (size_t)rows * cols, &need);
+    if (rc) return rc;
+    if (bytes < need) return lmc_set_error(LMC_ERR_INVALID, "qtensor_upload: %zu bytes < %zu needed", bytes, need);
+    lmc_qtensor *t = (lmc_qtensor *)calloc(1, sizeof(lmc_qtensor));
+    if (!t) return lmc_set_error(LMC_ERR_OOM, "qtensor_upload: host alloc");
+    t->type = type;
+    t->rows = rows;
+    t->cols = cols;
+    t->bytes = need;
+    // LMC_BLOCK_PAD zero bytes after the stream: IQ4_XS decoding reads two
+    // bytes past the last block (src/quant.c:506,515).
+    cudaError_t e = cudaMalloc(&t->blocks, need + LMC_BLOCK_PAD);
+    if (e != cudaSuccess) { free(t); return lmc_set_error(LMC_ERR_OOM, "qtensor_upload: %s", cudaGetErrorString(e)); }
+    e = cudaMemcpy(t->blocks, h_blocks, need, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset((char *)t->blocks + need, 0, LMC_BLOCK_PAD);
+    if (e != cudaSuccess) {
+        cudaFree(t->blocks);
+        free(t);
+        return lmc_set_error(LMC_ERR_CUDA, "qtensor_upload: %s", cudaGetErrorString(e));
+    }
+    rc = lmc_tiled_build(t);
+    if (rc) {
+        lmc_qtensor_free(t);
+        return rc;
+    }
+    *out = t;
+    return LMC_OK;
+}
+
+extern "C" int lmc_qtensor_free(lmc_qtensor *t) {
+    if (!t) return LMC_OK;
+    if (t->blocks) cudaFree(t->blocks);
+    if (t->tiled) cudaFree(t->tiled);
+    free(t);
+    return LMC_OK;
+}
+
+extern "C" const void *lmc_qtensor_blocks(const lmc_qtensor *t) { return t ? t->blocks : NULL; }
+extern "C" int lmc_qtensor_has_tiled(const lmc_qtensor *t) { return t && t->tiled ? 1 : 0; }
+
+// ---------------------------------------------------------------------------
+// matmul dispatch
+// ---------------------------------------------------------------------------
+static int check_mm(const float *x, int ldx, float *y, int ldy, int rows, int cols, int batch) {
+    if (!x || !y || rows <= 0 || cols <= 0 || batch <= 0)
+        return lmc_set_error(LMC_ERR_INVALID, "matmul: null pointer or empty shape");
+    if (ldx < cols || ldy < rows) return lmc_set_error(LMC_ERR_INVALID, "matmul: ldx %d < %d or ldy %d < %d", ldx, cols,
+                                                       ldy, rows);
+    return LMC_OK;
+}
+
+extern "C" int lmc_matmul_blocks(uint32_t type, const void *d_blocks, int rows, int cols, const float *d_x, int ldx,
+                                 const float *d_bias, float *d_y, int ldy, int batch, int epi, void *stream) {
+    int rc = check_mm(d_x, ldx, d_y, ldy, rows, cols, batch);
+    if (rc) return rc;
+    size_t need;
+    if ((rc = lmc_tensor_bytes(type, (size_t)rows * cols, &need))) return rc;
+    if (!d_blocks) return lmc_set_error(LMC_ERR_INVALID, "matmul: null weights");
+    if ((type == LMC_TYPE_F32 && ((uintptr_t)d_blocks & 15)) || ((uintptr_t)d_blocks & 1))
+        return lmc_set_error(LMC_ERR_INVALID, "matmul: misaligned weights");
+    if ((type == LMC_TYPE_F32 || type == LMC_TYPE_F16) && ((size_t)rows * cols) % 8)
+        return lmc_set_error(LMC_ERR_UNSUPPORTED, "matmul: raw F32/F16 weights need rows*cols %% 8 == 0 "
+                             "(upload a qtensor instead)");
+    return lmc_gemv_generic_launch(type, d_blocks, rows, cols, d_x, ldx, d_bias, d_y, ldy, batch, epi,
+                                   lmc_stream(stream));
+}
+
+extern "C" int lmc_matmul(const lmc_qtensor *w, const float *d_x, int ldx, const float *d_bias, float *d_y, int ldy,
+                          int batch, int epi, void *stream) {
+    if (!w) return lmc_set_error(LMC_ERR_INVALID, "matmul: null qtensor");
+    int rc = check_mm(d_x, ldx, d_y, ldy, w->rows, w->cols, batch);
+    if (rc) return rc;
+    if (w->tiled) return lmc_tiled_gemv_launch(w, d_x, ldx, d_bias, d_y, ldy, batch, epi, lmc_stream(stream));
+    return lmc_gemv_generic_launch(w->type, w->blocks, w->rows, w->cols, d_x, ldx, d_bias, d_y, ldy, batch, epi,
+                                   lmc_stream(stream));
+}

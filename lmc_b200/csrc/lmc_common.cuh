@@ -1,0 +1,68 @@
+// lmc_common.cuh - shared helpers for the CUDA side of liblmc_b200.so.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/lmc_cuda.h"
+
+// Records a formatted message for lmc_last_error() and returns `code`.
+extern "C" int lmc_set_error(int code, const char *fmt, ...);
+
+#define LMC_CUDA_TRY(expr)                                                        \
+    do {                                                                          \
+        cudaError_t _e = (expr);                                                  \
+        if (_e != cudaSuccess)                                                    \
+            return lmc_set_error(LMC_ERR_CUDA, "%s: %s (%s:%d)", #expr,           \
+                                 cudaGetErrorString(_e), __FILE__, __LINE__);     \
+    } while (0)
+
+// After a kernel launch: report launch-configuration errors.
+#define LMC_LAUNCH_CHECK(name)                                                    \
+    do {                                                                          \
+        cudaError_t _e = cudaGetLastError();                                      \
+        if (_e != cudaSuccess)                                                    \
+            return lmc_set_error(LMC_ERR_CUDA, "%s launch: %s", name,             \
+                                 cudaGetErrorString(_e));                         \
+    } while (0)
+
+static inline cudaStream_t lmc_stream(void *s) { return (cudaStream_t)s; }
+
+static inline unsigned lmc_cdiv(size_t a, size_t b) { return (unsigned)((a + b - 1) / b); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide sum; `red` must hold blockDim.x/32 floats.  All threads get it.
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    float t = lane < nw ? red[lane] : 0.0f;
+    return warp_sum(t);
+}
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    float t = lane < nw ? red[lane] : -INFINITY;
+    return warp_max(t);
+}
+
+// LMc activations (src/ops.c:20-29), same expression and operation order.
+__device__ __forceinline__ float lmc_gelu_f(float x) { return x * (1.0f / (1.0f + expf(-1.702f * x))); }
+__device__ __forceinline__ float lmc_silu_f(float x) { return x * (1.0f / (1.0f + expf(-x))); }

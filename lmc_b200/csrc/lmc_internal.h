@@ -1,0 +1,58 @@
+/* lmc_internal.h - declarations shared between the CUDA kernels (.cu) and
+ * the C99 host runtime (lmc_b200/host) inside liblmc_b200.so.  Not installed. */
+#ifndef LMC_INTERNAL_H
+#define LMC_INTERNAL_H
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/lmc_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Zero bytes kept readable after every device block stream: IQ4_XS reads
+ * two bytes past its last block (LMc src/quant.c:506,515), and the kernels
+ * address F32/F16 tensors in whole 8-element groups (up to 28 bytes past). */
+#define LMC_BLOCK_PAD 32
+
+struct lmc_qtensor {
+    uint32_t type;
+    int rows, cols;
+    size_t bytes;      /* raw GGUF block stream size */
+    void *blocks;      /* device: raw blocks + LMC_BLOCK_PAD */
+    void *tiled;       /* device: row-tiled copy for the tensor-core GEMV, or NULL */
+    size_t tiled_bytes;
+    int tiled_rows;    /* rows padded to the tile height */
+};
+
+int lmc_set_error(int code, const char *fmt, ...);
+int lmc_tensor_bytes(uint32_t type, size_t n_elements, size_t *bytes);
+int lmc_sm_count(void);
+
+int lmc_gemv_generic_launch(uint32_t type, const void *d_blocks, int M, int K, const float *d_x, int ldx,
+                            const float *d_bias, float *d_y, int ldy, int batch, int epi, cudaStream_t s);
+/* Builds t->tiled when the type/shape has a tensor-core GEMV (else leaves it NULL). */
+int lmc_tiled_build(struct lmc_qtensor *t);
+int lmc_tiled_gemv_launch(const struct lmc_qtensor *t, const float *d_x, int ldx, const float *d_bias, float *d_y,
+                          int ldy, int batch, int epi, cudaStream_t s);
+int lmc_embed_launch(uint32_t type, const void *wte, const float *wpe, const int *d_tok, const int *d_pos, int D,
+                     int V, int S, int batch, float *out, cudaStream_t s);
+/* RoPE on `batch` rows (row stride ld floats) of n_heads x Dh, each at its
+ * own position d_pos[b], from [S][Dh/2] cos/sin tables. */
+int lmc_rope_pos_launch(float *v, int ld, int n_heads, int Dh, const float *cos_tab, const float *sin_tab,
+                        const int *d_pos, int S, int batch, cudaStream_t s);
+/* Attention with explicit row strides for q/out (ldq) and k_new/v_new (ldkv). */
+int lmc_attention_launch(float *out, int ldo, const float *q, int ldq, const float *k_new, const float *v_new,
+                         int ldkv, void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, int batch, int H,
+                         int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes, cudaStream_t s);
+/* Generation bookkeeping after one step (see lmc_model_generate). */
+int lmc_advance_launch(const int *d_next, int *d_tok, int *d_pos, int *d_step, const int *d_prompt, int n_prompt,
+                       int *d_ids, int n_new, int batch, cudaStream_t s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LMC_INTERNAL_H */

@@ -1,0 +1,558 @@
+/* lmc_model.c - C99 host runtime: GGUF load onto the device and the
+ * decode-step driver (LMc load_model + model_forward + generate, on B200).
+ *
+ * LMc parses the GGUF header (src/gguf.c:114-282), dequantizes every tensor
+ * into an fp32 arena (src/gguf.c:290-347) and runs model_forward on the CPU
+ * (src/ops.c:212-237, src/ops_llama.c:157-192).  Here the same header rules
+ * pick the configuration, the raw blocks go to the device as qtensors, and a
+ * step is a fixed sequence of kernel launches on one stream that reads the
+ * token and position of each sequence from device memory - so a step can be
+ * captured once as a CUDA graph and replayed for every position, and greedy
+ * generation runs without the host waiting between tokens.
+ */
+#define _POSIX_C_SOURCE 200809L
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "../csrc/lmc_internal.h"
+
+typedef struct {
+    /* GPT-2 (src/models.h:79-117) */
+    lmc_qtensor *qkv, *proj, *fc, *fc2;
+    float *ln1_w, *ln1_b, *ln2_w, *ln2_b, *qkv_b, *proj_b, *fc_b, *fc2_b;
+    /* LLaMA */
+    lmc_qtensor *q, *k, *v, *o, *gate, *up, *down;
+    float *rms_attn, *rms_ffn;
+} Layer;
+
+struct lmc_model {
+    lmc_model_config cfg;
+    int max_batch, kv_dtype;
+    lmc_qtensor *wte, *lm_head;
+    float *wpe, *lnf_w, *lnf_b, *rmsf, *rope_cos, *rope_sin;
+    Layer *layers;
+    void *kc, *vc;
+    size_t kv_layer_elems;
+    float *x, *xn, *qkv, *att, *h, *h2, *logits;
+    void *ws;
+    size_t ws_bytes;
+    int *d_tok, *d_pos, *d_next, *d_step, *d_prompt, *d_ids;
+    int *h_stage; /* pinned: tokens, positions, next ids */
+    int prompt_cap, ids_cap;
+    cudaStream_t stream;
+    cudaGraphExec_t gexec;
+    int g_batch, g_nprompt, g_nnew; /* shape the captured graph was built for */
+    int g_kernels;                  /* kernel nodes in the captured step graph */
+};
+
+#define TRY(expr)                     \
+    do {                              \
+        int _rc = (expr);             \
+        if (_rc) return _rc;          \
+    } while (0)
+#define CUTRY(expr)                                                                              \
+    do {                                                                                         \
+        cudaError_t _e = (expr);                                                                 \
+        if (_e != cudaSuccess)                                                                   \
+            return lmc_set_error(LMC_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(_e));        \
+    } while (0)
+
+/* ------------------------------------------------------------------------ */
+/* GGUF reading (layout per src/gguf.c:114-287)                               */
+/* ------------------------------------------------------------------------ */
+typedef struct { const unsigned char *p, *end; int err; } Rd;
+static int need(Rd *r, size_t n) { if ((size_t)(r->end - r->p) < n) { r->err = 1; return 0; } return 1; }
+static uint32_t u32(Rd *r) { uint32_t v = 0; if (need(r, 4)) { memcpy(&v, r->p, 4); r->p += 4; } return v; }
+static uint64_t u64(Rd *r) { uint64_t v = 0; if (need(r, 8)) { memcpy(&v, r->p, 8); r->p += 8; } return v; }
+static float f32(Rd *r) { float v = 0; if (need(r, 4)) { memcpy(&v, r->p, 4); r->p += 4; } return v; }
+static const char *str(Rd *r, uint64_t *n) {
+    *n = u64(r);
+    if (!need(r, *n)) { *n = 0; return ""; }
+    const char *s = (const char *)r->p;
+    r->p += *n;
+    return s;
+}
+static int is(const char *s, uint64_t n, const char *lit) { return strlen(lit) == n && !memcmp(s, lit, n); }
+static void skip(Rd *r, uint32_t t) {
+    static const int sz[13] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+    if (t == 8) { uint64_t n; str(r, &n); return; }
+    if (t == 9) {
+        uint32_t et = u32(r);
+        uint64_t c = u64(r);
+        for (uint64_t i = 0; i < c && !r->err; i++) skip(r, et);
+        return;
+    }
+    if (t > 12) { r->err = 1; return; }
+    if (need(r, (size_t)sz[t])) r->p += sz[t];
+}
+
+typedef struct { char name[96]; uint32_t type; uint64_t dims[4]; uint32_t nd; uint64_t n, off; } TInfo;
+
+/* ------------------------------------------------------------------------ */
+static int upload_vec(const TInfo *t, const unsigned char *data, size_t fsz, int want, float **out) {
+    size_t bytes;
+    TRY(lmc_tensor_bytes(t->type, (size_t)t->n, &bytes));
+    if ((int64_t)t->n != want) return lmc_set_error(LMC_ERR_IO, "tensor %s: %llu elements, expected %d", t->name,
+                                                    (unsigned long long)t->n, want);
+    if (t->off + bytes > fsz) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
+    CUTRY(cudaMalloc((void **)out, sizeof(float) * (size_t)want + 16));
+    if (t->type == LMC_TYPE_F32) {
+        CUTRY(cudaMemcpy(*out, data + t->off, bytes, cudaMemcpyHostToDevice));
+        return LMC_OK;
+    }
+    void *tmp = NULL;
+    CUTRY(cudaMalloc(&tmp, bytes + LMC_BLOCK_PAD));
+    cudaMemset(tmp, 0, bytes + LMC_BLOCK_PAD);
+    cudaMemcpy(tmp, data + t->off, bytes, cudaMemcpyHostToDevice);
+    int rc = lmc_dequant(t->type, tmp, (size_t)t->n, *out, NULL);
+    cudaDeviceSynchronize();
+    cudaFree(tmp);
+    return rc;
+}
+
+static int upload_mat(const TInfo *t, const unsigned char *data, size_t fsz, int rows, int cols, lmc_qtensor **out) {
+    size_t bytes;
+    TRY(lmc_tensor_bytes(t->type, (size_t)t->n, &bytes));
+    if ((int64_t)t->n != (int64_t)rows * cols || (t->nd >= 2 && (t->dims[0] != (uint64_t)cols || t->dims[1] != (uint64_t)rows)))
+        return lmc_set_error(LMC_ERR_IO, "tensor %s: shape mismatch (expected %d x %d)", t->name, rows, cols);
+    if (t->off + bytes > fsz) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
+    return lmc_qtensor_upload(t->type, rows, cols, data + t->off, bytes, out);
+}
+
+static int dev_alloc(void **p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e != cudaSuccess) return lmc_set_error(LMC_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    return cudaMemset(*p, 0, bytes ? bytes : 16) == cudaSuccess ? LMC_OK : lmc_set_error(LMC_ERR_CUDA, "memset");
+}
+
+/* Slot lookup for a tensor name (src/gguf.c:62-97). */
+static int bind_tensor(lmc_model *m, const TInfo *t, const unsigned char *data, size_t fsz) {
+    const lmc_model_config *c = &m->cfg;
+    const int D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size, S = c->seq_len;
+    const int ll = c->arch == 2, KV = c->n_kv_heads * c->head_dim, QD = c->n_heads * c->head_dim;
+    const char *nm = t->name;
+    if (!strcmp(nm, "token_embd.weight")) return upload_mat(t, data, fsz, V, D, &m->wte);
+    if (!strcmp(nm, "position_embd.weight")) return ll ? 0 : upload_vec(t, data, fsz, S * D, &m->wpe);
+    if (!strcmp(nm, "output.weight")) return upload_mat(t, data, fsz, V, D, &m->lm_head);
+    if (!strcmp(nm, "output_norm.weight")) return upload_vec(t, data, fsz, D, ll ? &m->rmsf : &m->lnf_w);
+    if (!strcmp(nm, "output_norm.bias")) return ll ? 0 : upload_vec(t, data, fsz, D, &m->lnf_b);
+    if (strncmp(nm, "blk.", 4)) return 0;
+    int l = atoi(nm + 4);
+    if (l < 0 || l >= c->n_layers) return 0;
+    const char *r = strchr(nm + 4, '.');
+    if (!r) return 0;
+    r++;
+    Layer *w = &m->layers[l];
+    if (!ll) {
+        if (!strcmp(r, "attn_norm.weight")) return upload_vec(t, data, fsz, D, &w->ln1_w);
+        if (!strcmp(r, "attn_norm.bias")) return upload_vec(t, data, fsz, D, &w->ln1_b);
+        if (!strcmp(r, "attn_qkv.weight")) return upload_mat(t, data, fsz, 3 * D, D, &w->qkv);
+        if (!strcmp(r, "attn_qkv.bias")) return upload_vec(t, data, fsz, 3 * D, &w->qkv_b);
+        if (!strcmp(r, "attn_output.weight")) return upload_mat(t, data, fsz, D, D, &w->proj);
+        if (!strcmp(r, "attn_output.bias")) return upload_vec(t, data, fsz, D, &w->proj_b);
+        if (!strcmp(r, "ffn_norm.weight")) return upload_vec(t, data, fsz, D, &w->ln2_w);
+        if (!strcmp(r, "ffn_norm.bias")) return upload_vec(t, data, fsz, D, &w->ln2_b);
+        if (!strcmp(r, "ffn_up.weight")) return upload_mat(t, data, fsz, F, D, &w->fc);
+        if (!strcmp(r, "ffn_up.bias")) return upload_vec(t, data, fsz, F, &w->fc_b);
+        if (!strcmp(r, "ffn_down.weight")) return upload_mat(t, data, fsz, D, F, &w->fc2);
+        if (!strcmp(r, "ffn_down.bias")) return upload_vec(t, data, fsz, D, &w->fc2_b);
+    } else {
+        if (!strcmp(r, "attn_norm.weight")) return upload_vec(t, data, fsz, D, &w->rms_attn);
+        if (!strcmp(r, "attn_q.weight")) return upload_mat(t, data, fsz, QD, D, &w->q);
+        if (!strcmp(r, "attn_k.weight")) return upload_mat(t, data, fsz, KV, D, &w->k);
+        if (!strcmp(r, "attn_v.weight")) return upload_mat(t, data, fsz, KV, D, &w->v);
+        if (!strcmp(r, "attn_output.weight")) return upload_mat(t, data, fsz, D, QD, &w->o);
+        if (!strcmp(r, "ffn_norm.weight")) return upload_vec(t, data, fsz, D, &w->rms_ffn);
+        if (!strcmp(r, "ffn_gate.weight")) return upload_mat(t, data, fsz, F, D, &w->gate);
+        if (!strcmp(r, "ffn_up.weight")) return upload_mat(t, data, fsz, F, D, &w->up);
+        if (!strcmp(r, "ffn_down.weight")) return upload_mat(t, data, fsz, D, F, &w->down);
+    }
+    return 0;
+}
+
+static int check_complete(const lmc_model *m) {
+    const lmc_model_config *c = &m->cfg;
+    if (!m->wte || !m->lm_head) return lmc_set_error(LMC_ERR_IO, "GGUF lacks token_embd.weight or output.weight");
+    for (int l = 0; l < c->n_layers; l++) {
+        const Layer *w = &m->layers[l];
+        int ok = c->arch == 1 ? (w->qkv && w->proj && w->fc && w->fc2 && w->ln1_w && w->ln1_b && w->ln2_w &&
+                                 w->ln2_b && w->qkv_b && w->proj_b && w->fc_b && w->fc2_b)
+                              : (w->q && w->k && w->v && w->o && w->gate && w->up && w->down && w->rms_attn &&
+                                 w->rms_ffn);
+        if (!ok) return lmc_set_error(LMC_ERR_IO, "GGUF lacks tensors of layer %d", l);
+    }
+    if (c->arch == 1 && (!m->wpe || !m->lnf_w || !m->lnf_b))
+        return lmc_set_error(LMC_ERR_IO, "GGUF lacks position_embd or output_norm");
+    if (c->arch == 2 && !m->rmsf) return lmc_set_error(LMC_ERR_IO, "GGUF lacks output_norm.weight");
+    return LMC_OK;
+}
+
+static int load(lmc_model *m, const char *path) {
+    FILE *f = fopen(path, "rb");
+    if (!f) return lmc_set_error(LMC_ERR_IO, "cannot open %s", path);
+    fseek(f, 0, SEEK_END);
+    long fsz = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    unsigned char *buf = (unsigned char *)malloc((size_t)fsz + 64);
+    if (!buf) { fclose(f); return lmc_set_error(LMC_ERR_OOM, "host buffer for %s", path); }
+    size_t got = fread(buf, 1, (size_t)fsz, f);
+    fclose(f);
+    if (got != (size_t)fsz) { free(buf); return lmc_set_error(LMC_ERR_IO, "short read of %s", path); }
+    memset(buf + fsz, 0, 64);
+    Rd r = {buf, buf + fsz, 0};
+    lmc_model_config *c = &m->cfg;
+    int rc = LMC_OK;
+    TInfo *ti = NULL;
+    uint32_t magic = u32(&r), ver = u32(&r);
+    if (magic != 0x46554747u || ver < 1 || ver > 3) { rc = lmc_set_error(LMC_ERR_IO, "%s: not a GGUF v1-3 file", path); goto done; }
+    uint64_t nt = u64(&r), nkv = u64(&r);
+    /* defaults, src/gguf.c:131-140 */
+    c->arch = 0; c->vocab_size = 128256; c->seq_len = 8192; c->rope_theta = 10000.0f; c->norm_eps = 1e-5f;
+    int vocab_key = 0, tok_count = 0;
+    for (uint64_t i = 0; i < nkv && !r.err; i++) {
+        uint64_t kl;
+        const char *k = str(&r, &kl);
+        uint32_t t = u32(&r);
+        if (t == 4) { /* src/gguf.c:146-164 */
+            int v = (int)u32(&r);
+            if (is(k, kl, "gpt2.block_count") || is(k, kl, "llama.block_count")) c->n_layers = v;
+            else if (is(k, kl, "gpt2.attention.head_count") || is(k, kl, "llama.attention.head_count")) c->n_heads = v;
+            else if (is(k, kl, "gpt2.embedding_length") || is(k, kl, "llama.embedding_length")) c->embed_dim = v;
+            else if (is(k, kl, "gpt2.feed_forward_length") || is(k, kl, "llama.feed_forward_length")) c->ffn_dim = v;
+            else if (is(k, kl, "gpt2.context_length") || is(k, kl, "llama.context_length")) c->seq_len = v;
+            else if (is(k, kl, "gpt2.vocab_size")) c->vocab_size = v;
+            else if (is(k, kl, "llama.vocab_size")) { c->vocab_size = v; vocab_key = v; }
+            else if (is(k, kl, "llama.attention.head_count_kv")) c->n_kv_heads = v;
+        } else if (t == 6) { /* src/gguf.c:166-172 */
+            float v = f32(&r);
+            if (is(k, kl, "llama.rope.freq_base")) c->rope_theta = v;
+            else if (is(k, kl, "llama.attention.layer_norm_rms_epsilon")) c->norm_eps = v;
+        } else if (t == 8) { /* src/gguf.c:173-179 */
+            uint64_t vl;
+            const char *v = str(&r, &vl);
+            if (is(k, kl, "general.architecture")) {
+                if (is(v, vl, "llama")) c->arch = 2;
+                else if (is(v, vl, "gpt2")) c->arch = 1;
+            }
+        } else if (t == 9 && is(k, kl, "tokenizer.ggml.tokens")) { /* src/gguf.c:184-199 */
+            uint32_t et = u32(&r);
+            uint64_t cnt = u64(&r);
+            if (cnt <= 32768) tok_count = (int)cnt;
+            for (uint64_t j = 0; j < cnt && !r.err; j++) skip(&r, et);
+        } else {
+            skip(&r, t);
+        }
+    }
+    if (r.err) { rc = lmc_set_error(LMC_ERR_IO, "%s: truncated metadata", path); goto done; }
+    /* src/gguf.c:218-244 */
+    if (c->arch == 0) c->arch = c->n_kv_heads > 0 ? 2 : 1;
+    if (c->arch == 2 && c->n_kv_heads == 0) c->n_kv_heads = c->n_heads;
+    if (c->arch == 1) c->n_kv_heads = c->n_heads;
+    if (c->arch == 1 && c->vocab_size == 128256) c->vocab_size = 50257;
+    {
+        int vn = tok_count ? tok_count : vocab_key;
+        if (c->arch == 2 && vn > 0 && vn < c->vocab_size) c->vocab_size = vn;
+    }
+    if (!c->n_layers || !c->n_heads || !c->embed_dim) { rc = lmc_set_error(LMC_ERR_IO, "%s: missing L/H/D metadata", path); goto done; }
+    if (!c->ffn_dim) c->ffn_dim = 4 * c->embed_dim;
+    c->head_dim = c->embed_dim / c->n_heads;
+    if (c->n_heads % c->n_kv_heads) { rc = lmc_set_error(LMC_ERR_IO, "%s: heads %d not a multiple of kv heads %d", path, c->n_heads, c->n_kv_heads); goto done; }
+    m->layers = (Layer *)calloc((size_t)c->n_layers, sizeof(Layer));
+    ti = (TInfo *)calloc((size_t)nt ? (size_t)nt : 1, sizeof(TInfo));
+    if (!m->layers || !ti) { rc = lmc_set_error(LMC_ERR_OOM, "host tables"); goto done; }
+    for (uint64_t i = 0; i < nt && !r.err; i++) {
+        uint64_t nl;
+        const char *nm = str(&r, &nl);
+        if (nl >= sizeof ti[i].name) nl = sizeof ti[i].name - 1;
+        memcpy(ti[i].name, nm, nl);
+        ti[i].nd = u32(&r);
+        ti[i].n = 1;
+        for (uint32_t d = 0; d < ti[i].nd; d++) {
+            uint64_t v = u64(&r);
+            if (d < 4) ti[i].dims[d] = v;
+            ti[i].n *= v;
+        }
+        ti[i].type = u32(&r);
+        ti[i].off = u64(&r);
+    }
+    if (r.err) { rc = lmc_set_error(LMC_ERR_IO, "%s: truncated tensor table", path); goto done; }
+    {
+        size_t data = ((size_t)(r.p - buf) + 31) / 32 * 32; /* src/gguf.c:285-287 */
+        for (uint64_t i = 0; i < nt && !rc; i++) rc = bind_tensor(m, &ti[i], buf + data, (size_t)fsz - data);
+    }
+    if (!rc) rc = check_complete(m);
+done:
+    free(ti);
+    free(buf);
+    return rc;
+}
+
+/* RoPE table with LMc's expression (src/models.c:101-117). */
+static int build_rope(lmc_model *m) {
+    const int S = m->cfg.seq_len, half = m->cfg.head_dim / 2;
+    const float theta = m->cfg.rope_theta > 0.0f ? m->cfg.rope_theta : 10000.0f;
+    float *c = (float *)malloc(sizeof(float) * (size_t)S * half), *s = (float *)malloc(sizeof(float) * (size_t)S * half);
+    if (!c || !s) { free(c); free(s); return lmc_set_error(LMC_ERR_OOM, "rope table"); }
+    for (int p = 0; p < S; p++)
+        for (int d = 0; d < half; d++) {
+            float a = (float)p / powf(theta, 2.0f * (float)d / (float)m->cfg.head_dim);
+            c[(size_t)p * half + d] = cosf(a);
+            s[(size_t)p * half + d] = sinf(a);
+        }
+    int rc = dev_alloc((void **)&m->rope_cos, sizeof(float) * (size_t)S * half);
+    if (!rc) rc = dev_alloc((void **)&m->rope_sin, sizeof(float) * (size_t)S * half);
+    if (!rc && (cudaMemcpy(m->rope_cos, c, sizeof(float) * (size_t)S * half, cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemcpy(m->rope_sin, s, sizeof(float) * (size_t)S * half, cudaMemcpyHostToDevice) != cudaSuccess))
+        rc = lmc_set_error(LMC_ERR_CUDA, "rope upload");
+    free(c);
+    free(s);
+    return rc;
+}
+
+static int alloc_state(lmc_model *m) {
+    const lmc_model_config *c = &m->cfg;
+    const size_t B = (size_t)m->max_batch, D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size;
+    const size_t QD = (size_t)c->n_heads * c->head_dim, KV = (size_t)c->n_kv_heads * c->head_dim;
+    const size_t esz = m->kv_dtype == LMC_KV_F16 ? 2 : 4;
+    m->kv_layer_elems = B * KV * (size_t)c->seq_len;
+    TRY(dev_alloc(&m->kc, esz * m->kv_layer_elems * c->n_layers));
+    TRY(dev_alloc(&m->vc, esz * m->kv_layer_elems * c->n_layers));
+    TRY(dev_alloc((void **)&m->x, 4 * B * D));
+    TRY(dev_alloc((void **)&m->xn, 4 * B * D));
+    TRY(dev_alloc((void **)&m->qkv, 4 * B * (QD + 2 * KV + 3 * D)));
+    TRY(dev_alloc((void **)&m->att, 4 * B * (QD > D ? QD : D)));
+    TRY(dev_alloc((void **)&m->h, 4 * B * F));
+    TRY(dev_alloc((void **)&m->h2, 4 * B * F));
+    TRY(dev_alloc((void **)&m->logits, 4 * B * V));
+    m->ws_bytes = lmc_attention_workspace_bytes((int)B, c->n_heads, c->head_dim, c->seq_len);
+    TRY(dev_alloc(&m->ws, m->ws_bytes));
+    TRY(dev_alloc((void **)&m->d_tok, 4 * B));
+    TRY(dev_alloc((void **)&m->d_pos, 4 * B));
+    TRY(dev_alloc((void **)&m->d_next, 4 * B));
+    TRY(dev_alloc((void **)&m->d_step, 16));
+    CUTRY(cudaMallocHost((void **)&m->h_stage, 3 * sizeof(int) * B));
+    CUTRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    if (c->arch == 2) TRY(build_rope(m));
+    return LMC_OK;
+}
+
+int lmc_model_load(const char *path, int max_batch, int kv_dtype, lmc_model **out) {
+    if (!path || !out || max_batch <= 0) return lmc_set_error(LMC_ERR_INVALID, "model_load: args");
+    if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16) return lmc_set_error(LMC_ERR_INVALID, "model_load: kv dtype");
+    *out = NULL;
+    lmc_model *m = (lmc_model *)calloc(1, sizeof(lmc_model));
+    if (!m) return lmc_set_error(LMC_ERR_OOM, "model struct");
+    m->max_batch = max_batch;
+    m->kv_dtype = kv_dtype;
+    int rc = load(m, path);
+    if (!rc) rc = alloc_state(m);
+    if (!rc && cudaDeviceSynchronize() != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "load sync");
+    if (rc) {
+        char msg[1024];
+        snprintf(msg, sizeof msg, "%s", lmc_last_error());
+        lmc_model_free(m);
+        return lmc_set_error(rc, "%s", msg);
+    }
+    *out = m;
+    return LMC_OK;
+}
+
+int lmc_model_get_config(const lmc_model *m, lmc_model_config *c) {
+    if (!m || !c) return lmc_set_error(LMC_ERR_INVALID, "model_get_config: null");
+    *c = m->cfg;
+    return LMC_OK;
+}
+
+void *lmc_model_device_buffer(lmc_model *m, int which) { return m && which == 0 ? m->logits : NULL; }
+
+int lmc_model_free(lmc_model *m) {
+    if (!m) return LMC_OK;
+    if (m->gexec) cudaGraphExecDestroy(m->gexec);
+    if (m->layers) {
+        for (int l = 0; l < m->cfg.n_layers; l++) {
+            Layer *w = &m->layers[l];
+            lmc_qtensor *qs[] = {w->qkv, w->proj, w->fc, w->fc2, w->q, w->k, w->v, w->o, w->gate, w->up, w->down};
+            for (size_t i = 0; i < sizeof qs / sizeof qs[0]; i++) lmc_qtensor_free(qs[i]);
+            float *vs[] = {w->ln1_w, w->ln1_b, w->ln2_w, w->ln2_b, w->qkv_b, w->proj_b, w->fc_b, w->fc2_b, w->rms_attn, w->rms_ffn};
+            for (size_t i = 0; i < sizeof vs / sizeof vs[0]; i++) if (vs[i]) cudaFree(vs[i]);
+        }
+        free(m->layers);
+    }
+    lmc_qtensor_free(m->wte);
+    lmc_qtensor_free(m->lm_head);
+    void *ps[] = {m->wpe, m->lnf_w, m->lnf_b, m->rmsf, m->rope_cos, m->rope_sin, m->kc, m->vc, m->x, m->xn, m->qkv,
+                  m->att, m->h, m->h2, m->logits, m->ws, m->d_tok, m->d_pos, m->d_next, m->d_step, m->d_prompt, m->d_ids};
+    for (size_t i = 0; i < sizeof ps / sizeof ps[0]; i++) if (ps[i]) cudaFree(ps[i]);
+    if (m->h_stage) cudaFreeHost(m->h_stage);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    free(m);
+    return LMC_OK;
+}
+
+/* ------------------------------------------------------------------------ */
+/* One decode step for B sequences: tokens d_tok, positions d_pos -> logits   */
+/* and greedy ids in d_next.  Only kernel launches on m->stream (capturable). */
+/* ------------------------------------------------------------------------ */
+static int step(lmc_model *m, int B) {
+    const lmc_model_config *c = &m->cfg;
+    const int D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size, H = c->n_heads, Hkv = c->n_kv_heads;
+    const int Dh = c->head_dim, S = c->seq_len, QD = H * Dh, KVD = Hkv * Dh;
+    cudaStream_t s = m->stream;
+    const size_t esz = m->kv_dtype == LMC_KV_F16 ? 2 : 4;
+    TRY(lmc_embed_launch(m->wte->type, m->wte->blocks, c->arch == 1 ? m->wpe : NULL, m->d_tok, m->d_pos, D, V, S, B, m->x, s));
+    for (int l = 0; l < c->n_layers; l++) {
+        const Layer *w = &m->layers[l];
+        char *kc = (char *)m->kc + esz * m->kv_layer_elems * l, *vc = (char *)m->vc + esz * m->kv_layer_elems * l;
+        if (c->arch == 1) { /* src/ops.c:182-206 */
+            TRY(lmc_layer_norm(m->xn, m->x, w->ln1_w, w->ln1_b, D, B, s));
+            TRY(lmc_matmul(w->qkv, m->xn, D, w->qkv_b, m->qkv, 3 * D, B, LMC_EPI_NONE, s));
+            TRY(lmc_attention_launch(m->att, D, m->qkv, 3 * D, m->qkv + D, m->qkv + 2 * D, 3 * D, kc, vc, m->kv_dtype,
+                                     m->d_pos, B, H, H, Dh, S, m->ws, m->ws_bytes, s));
+            TRY(lmc_matmul(w->proj, m->att, D, w->proj_b, m->x, D, B, LMC_EPI_ACCUM, s));
+            TRY(lmc_layer_norm(m->xn, m->x, w->ln2_w, w->ln2_b, D, B, s));
+            TRY(lmc_matmul(w->fc, m->xn, D, w->fc_b, m->h, F, B, LMC_EPI_GELU, s));
+            TRY(lmc_matmul(w->fc2, m->h, F, w->fc2_b, m->x, D, B, LMC_EPI_ACCUM, s));
+        } else { /* src/ops_llama.c:165-187 */
+            float *q = m->qkv, *k = m->qkv + (size_t)B * QD, *v = k + (size_t)B * KVD;
+            TRY(lmc_rms_norm(m->xn, m->x, w->rms_attn, D, B, c->norm_eps, s));
+            TRY(lmc_matmul(w->q, m->xn, D, NULL, q, QD, B, LMC_EPI_NONE, s));
+            TRY(lmc_matmul(w->k, m->xn, D, NULL, k, KVD, B, LMC_EPI_NONE, s));
+            TRY(lmc_matmul(w->v, m->xn, D, NULL, v, KVD, B, LMC_EPI_NONE, s));
+            TRY(lmc_rope_pos_launch(q, QD, H, Dh, m->rope_cos, m->rope_sin, m->d_pos, S, B, s));
+            TRY(lmc_rope_pos_launch(k, KVD, Hkv, Dh, m->rope_cos, m->rope_sin, m->d_pos, S, B, s));
+            TRY(lmc_attention_launch(m->att, QD, q, QD, k, v, KVD, kc, vc, m->kv_dtype, m->d_pos, B, H, Hkv, Dh, S,
+                                     m->ws, m->ws_bytes, s));
+            TRY(lmc_matmul(w->o, m->att, QD, NULL, m->x, D, B, LMC_EPI_ACCUM, s));
+            TRY(lmc_rms_norm(m->xn, m->x, w->rms_ffn, D, B, c->norm_eps, s));
+            TRY(lmc_matmul(w->gate, m->xn, D, NULL, m->h, F, B, LMC_EPI_NONE, s));
+            TRY(lmc_matmul(w->up, m->xn, D, NULL, m->h2, F, B, LMC_EPI_NONE, s));
+            TRY(lmc_swiglu(m->h, m->h2, (size_t)B * F, s));
+            TRY(lmc_matmul(w->down, m->h, F, NULL, m->x, D, B, LMC_EPI_ACCUM, s));
+        }
+    }
+    if (c->arch == 1) TRY(lmc_layer_norm(m->xn, m->x, m->lnf_w, m->lnf_b, D, B, s));
+    else TRY(lmc_rms_norm(m->xn, m->x, m->rmsf, D, B, c->norm_eps, s));
+    TRY(lmc_matmul(m->lm_head, m->xn, D, NULL, m->logits, V, B, LMC_EPI_NONE, s));
+    TRY(lmc_argmax(m->logits, V, B, m->d_next, s));
+    return LMC_OK;
+}
+
+int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B, float *h_logits, int *h_next) {
+    if (!m || !h_tokens || !h_pos || B <= 0 || B > m->max_batch)
+        return lmc_set_error(LMC_ERR_INVALID, "model_forward: args (batch %d, max %d)", B, m ? m->max_batch : 0);
+    for (int b = 0; b < B; b++) {
+        if (h_tokens[b] < 0 || h_tokens[b] >= m->cfg.vocab_size)
+            return lmc_set_error(LMC_ERR_INVALID, "model_forward: token %d outside [0, %d)", h_tokens[b], m->cfg.vocab_size);
+        if (h_pos[b] < 0 || h_pos[b] >= m->cfg.seq_len)
+            return lmc_set_error(LMC_ERR_INVALID, "model_forward: position %d outside [0, %d)", h_pos[b], m->cfg.seq_len);
+    }
+    memcpy(m->h_stage, h_tokens, sizeof(int) * B);
+    memcpy(m->h_stage + B, h_pos, sizeof(int) * B);
+    CUTRY(cudaMemcpyAsync(m->d_tok, m->h_stage, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
+    CUTRY(cudaMemcpyAsync(m->d_pos, m->h_stage + B, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
+    TRY(step(m, B));
+    if (h_logits)
+        CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * (size_t)B * m->cfg.vocab_size,
+                              cudaMemcpyDeviceToHost, m->stream));
+    CUTRY(cudaMemcpyAsync(m->h_stage + 2 * B, m->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, m->stream));
+    CUTRY(cudaStreamSynchronize(m->stream));
+    if (h_next) memcpy(h_next, m->h_stage + 2 * B, sizeof(int) * B);
+    return LMC_OK;
+}
+
+/* step + bookkeeping, the unit that is captured as one graph */
+static int gen_step(lmc_model *m, int B, int n_prompt, int n_new) {
+    TRY(step(m, B));
+    return lmc_advance_launch(m->d_next, m->d_tok, m->d_pos, m->d_step, m->d_prompt, n_prompt, m->d_ids, n_new, B,
+                              m->stream);
+}
+
+static int ensure_gen_buffers(lmc_model *m, int B, int n_prompt, int n_new) {
+    if (m->prompt_cap < B * n_prompt) {
+        if (m->d_prompt) cudaFree(m->d_prompt);
+        m->d_prompt = NULL;
+        TRY(dev_alloc((void **)&m->d_prompt, sizeof(int) * (size_t)B * n_prompt));
+        m->prompt_cap = B * n_prompt;
+        if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = NULL; }
+    }
+    if (m->ids_cap < B * n_new) {
+        if (m->d_ids) cudaFree(m->d_ids);
+        m->d_ids = NULL;
+        TRY(dev_alloc((void **)&m->d_ids, sizeof(int) * (size_t)B * n_new));
+        m->ids_cap = B * n_new;
+        if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = NULL; }
+    }
+    return LMC_OK;
+}
+
+int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, int n_new, int use_graph,
+                       int *h_out_ids) {
+    if (!m || !h_prompt || n_prompt <= 0 || n_new <= 0 || B <= 0 || B > m->max_batch || !h_out_ids)
+        return lmc_set_error(LMC_ERR_INVALID, "model_generate: args");
+    if (n_prompt + n_new - 1 > m->cfg.seq_len)
+        return lmc_set_error(LMC_ERR_INVALID, "model_generate: %d + %d tokens exceed the context of %d", n_prompt,
+                             n_new, m->cfg.seq_len);
+    for (int i = 0; i < B * n_prompt; i++)
+        if (h_prompt[i] < 0 || h_prompt[i] >= m->cfg.vocab_size)
+            return lmc_set_error(LMC_ERR_INVALID, "model_generate: token %d out of range", h_prompt[i]);
+    TRY(ensure_gen_buffers(m, B, n_prompt, n_new));
+    cudaStream_t s = m->stream;
+    CUTRY(cudaMemcpyAsync(m->d_prompt, h_prompt, sizeof(int) * (size_t)B * n_prompt, cudaMemcpyHostToDevice, s));
+    for (int b = 0; b < B; b++) { m->h_stage[b] = h_prompt[(size_t)b * n_prompt]; m->h_stage[B + b] = 0; }
+    CUTRY(cudaMemcpyAsync(m->d_tok, m->h_stage, sizeof(int) * B, cudaMemcpyHostToDevice, s));
+    CUTRY(cudaMemcpyAsync(m->d_pos, m->h_stage + B, sizeof(int) * B, cudaMemcpyHostToDevice, s));
+    CUTRY(cudaMemsetAsync(m->d_step, 0, sizeof(int), s));
+    const int steps = n_prompt + n_new - 1;
+    if (use_graph) {
+        if (m->gexec && (m->g_batch != B || m->g_nprompt != n_prompt || m->g_nnew != n_new)) {
+            cudaGraphExecDestroy(m->gexec);
+            m->gexec = NULL;
+        }
+        if (!m->gexec) {
+            cudaGraph_t g;
+            CUTRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+            int rc = gen_step(m, B, n_prompt, n_new);
+            cudaError_t e = cudaStreamEndCapture(s, &g);
+            if (rc) { if (e == cudaSuccess) cudaGraphDestroy(g); return rc; }
+            if (e != cudaSuccess) return lmc_set_error(LMC_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+            size_t nn = 0;
+            m->g_kernels = 0;
+            if (cudaGraphGetNodes(g, NULL, &nn) == cudaSuccess && nn) {
+                cudaGraphNode_t *nodes = (cudaGraphNode_t *)malloc(sizeof(cudaGraphNode_t) * nn);
+                if (nodes && cudaGraphGetNodes(g, nodes, &nn) == cudaSuccess)
+                    for (size_t i = 0; i < nn; i++) {
+                        enum cudaGraphNodeType ty;
+                        if (cudaGraphNodeGetType(nodes[i], &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel)
+                            m->g_kernels++;
+                    }
+                free(nodes);
+            }
+            e = cudaGraphInstantiate(&m->gexec, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) return lmc_set_error(LMC_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+            m->g_batch = B; m->g_nprompt = n_prompt; m->g_nnew = n_new;
+        }
+        for (int i = 0; i < steps; i++) CUTRY(cudaGraphLaunch(m->gexec, s));
+    } else {
+        for (int i = 0; i < steps; i++) TRY(gen_step(m, B, n_prompt, n_new));
+    }
+    /* the last greedy pick needs no forward of its own: take it from the
+     * last step's argmax (the advance kernel recorded it as well) */
+    CUTRY(cudaMemcpyAsync(h_out_ids, m->d_ids, sizeof(int) * (size_t)B * n_new, cudaMemcpyDeviceToHost, s));
+    CUTRY(cudaStreamSynchronize(s));
+    return LMC_OK;
+}
+
+/* Replays the captured generation graph `n` more times without resetting
+ * state (bench helper: timed decode steps continue from the current
+ * position).  Returns LMC_ERR_INVALID when no graph has been captured. */
+int lmc_model_replay(lmc_model *m, int n, void *stream_out) {
+    if (!m || !m->gexec) return lmc_set_error(LMC_ERR_INVALID, "model_replay: no captured graph");
+    for (int i = 0; i < n; i++) CUTRY(cudaGraphLaunch(m->gexec, m->stream));
+    if (stream_out) *(cudaStream_t *)stream_out = m->stream;
+    return LMC_OK;
+}
+
+int lmc_model_graph_kernels(const lmc_model *m) { return m && m->gexec ? m->g_kernels : -1; }

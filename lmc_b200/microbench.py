@@ -1,0 +1,95 @@
+"""GEMV microbenchmark: one quantized matrix-vector product, timed on the
+device with CUDA events over rotated weight copies whose total exceeds twice
+the 126 MB L2 (so every launch streams its weights from HBM).
+
+    python -m lmc_b200.microbench --type Q4_K --rows 3072 --cols 768 --batch 1
+
+Prints one JSON line: average launch time, algorithmic bytes per launch
+(weights + fp32 x + fp32 y, as counted in the roofline), GB/s and the
+fraction of the measured HBM peak.  Weights are seeded random blocks (fp16
+scales |N(0,1e-3)|, uniform codes), x ~ N(0,1).
+"""
+import argparse
+import json
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from lmc_b200 import runtime as rt  # noqa: E402
+from lmc_b200 import synth  # noqa: E402
+
+L2_BYTES = 126e6
+
+
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+def algorithmic_bytes(qtype, rows, cols, batch):
+    return synth.tensor_bytes(qtype, rows * cols) + 4 * cols * batch + 4 * rows * batch
+
+
+def run(torch, qtype, rows, cols, batch=1, iters=50, stream=None, generic=False, seed=100):
+    """Returns dict(ms, gbs, bytes, tiled)."""
+    wbytes = synth.tensor_bytes(qtype, rows * cols)
+    copies = max(2, int(np.ceil(2.2 * L2_BYTES / wbytes)) + 1)
+    qs = [rt.QTensor(qtype, rows, cols, synth.random_blocks(qtype, rows * cols, seed=seed + i)) for i in range(copies)]
+    x = torch.randn(batch, cols, device="cuda")
+    y = torch.empty(batch, rows, device="cuda")
+    s = stream or torch.cuda.current_stream()
+
+    def launch(q):
+        if generic:
+            rt.call("lmc_matmul_blocks", qtype, rt.lib().lmc_qtensor_blocks(q.h), rows, cols, x.data_ptr(), cols,
+                    None, y.data_ptr(), rows, batch, 0, s.cuda_stream)
+        else:
+            q.matmul(x, y, batch=batch, stream=s.cuda_stream)
+
+    with torch.cuda.stream(s):
+        for q in qs:
+            launch(q)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        for i in range(iters):
+            evs[i][0].record(s)
+            launch(qs[i % copies])
+            evs[i][1].record(s)
+    torch.cuda.synchronize()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    alg = algorithmic_bytes(qtype, rows, cols, batch)
+    tiled = qs[0].tiled and not generic
+    for q in qs:
+        q.close()
+    return {"ms": ms, "gbs": alg / (ms * 1e-3) / 1e9, "bytes": alg, "tiled": tiled}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--type", default="Q4_K")
+    ap.add_argument("--rows", type=int, default=3072)
+    ap.add_argument("--cols", type=int, default=768)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--generic", action="store_true", help="time the generic CUDA-core kernel")
+    a = ap.parse_args()
+    import torch
+    qtype = {v: k for k, v in synth.NAMES.items()}[a.type]
+    torch.cuda.set_device(0)
+    rt.init(0)
+    r = run(torch, qtype, a.rows, a.cols, a.batch, a.iters, generic=a.generic)
+    peak, kind = hbm_peak()
+    r.update({"type": a.type, "rows": a.rows, "cols": a.cols, "batch": a.batch, "peak_gbs": peak,
+              "frac": r["gbs"] / peak, "peak_kind": kind})
+    print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()
