@@ -178,10 +178,11 @@ int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int b
  * launch and the host does not wait between steps. */
 int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int batch,
                        int n_new, int use_graph, int *h_out_ids);
-/* Replays the step graph captured by the last lmc_model_generate(use_graph=1)
- * `n` more times, continuing from the current device-side positions (a
- * timing helper: positions must stay below seq_len).  Enqueues only; the
- * stream the steps run on is written to *stream_out when it is not NULL. */
+/* Runs `n` more steps of the last lmc_model_generate (replaying its CUDA
+ * graph, or launching the kernels directly when it ran without one),
+ * continuing from the current device-side positions (a timing helper:
+ * positions must stay below seq_len).  Enqueues only; the stream the steps
+ * run on is written to *stream_out when it is not NULL. */
 int lmc_model_replay(lmc_model *m, int n, void *stream_out);
 /* Kernel launches in one captured step (graph kernel nodes), -1 if none. */
 int lmc_model_graph_kernels(const lmc_model *m);

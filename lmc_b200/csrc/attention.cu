@@ -42,6 +42,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
     const int sp = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int G = a.H / a.Hkv, Dh = a.Dh, CH = a.CH;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = ATT_THREADS / 32;
+    pdl_wait();
+    pdl_launch_dependents();
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.S) return;  // the host validates positions; never index outside the cache
     const int t0 = sp * CH, t1 = min(t0 + CH, pos + 1);
@@ -120,6 +122,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
 // Merge the splits of one (sequence, query head): rescale each split's sum
 // and accumulator to the global maximum.
 __global__ void k_attn_combine(AttnArgs a) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int h = blockIdx.x, b = blockIdx.y, Dh = a.Dh;
     const float *w = a.ws + ((size_t)b * a.H + h) * a.nsplit * (Dh + 2);
     float M = -INFINITY;
@@ -177,16 +181,14 @@ extern "C" int lmc_attention_launch(float *out, int ldo, const float *q, int ldq
     if (kv_dtype == LMC_KV_F32) {
         if (smem > 48 * 1024)
             LMC_CUDA_TRY(cudaFuncSetAttribute(k_attn_split<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_attn_split<float><<<grid, ATT_THREADS, smem, s>>>(a);
+        LMC_LAUNCH("attention", k_attn_split<float>, grid, ATT_THREADS, smem, s, a);
     } else {
         if (smem > 48 * 1024)
             LMC_CUDA_TRY(cudaFuncSetAttribute(k_attn_split<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_attn_split<__half><<<grid, ATT_THREADS, smem, s>>>(a);
+        LMC_LAUNCH("attention", k_attn_split<__half>, grid, ATT_THREADS, smem, s, a);
     }
-    LMC_LAUNCH_CHECK("attention");
     if (a.nsplit > 1) {
-        k_attn_combine<<<dim3(H, batch), Dh, 0, s>>>(a);
-        LMC_LAUNCH_CHECK("attention combine");
+        LMC_LAUNCH("attention combine", k_attn_combine, dim3(H, batch), Dh, 0, s, a);
     }
     return LMC_OK;
 }

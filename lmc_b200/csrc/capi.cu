@@ -19,6 +19,16 @@ extern "C" int lmc_set_error(int code, const char *fmt, ...) {
 
 extern "C" const char *lmc_last_error(void) { return g_err; }
 
+// Programmatic dependent launch is on unless LMC_PDL=0 (A/B timing switch).
+extern "C" int lmc_pdl_enabled(void) {
+    static int flag = -1;
+    if (flag < 0) {
+        const char *e = getenv("LMC_PDL");
+        flag = (e && e[0] == '0') ? 0 : 1;
+    }
+    return flag;
+}
+
 extern "C" int lmc_init(int device) {
     int n = 0;
     cudaError_t e = cudaGetDeviceCount(&n);

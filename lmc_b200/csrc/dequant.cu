@@ -6,6 +6,7 @@
 // loop over 8-weight groups, launched at a multiple of the SM count.
 #include "lmc_blocks.cuh"
 #include "lmc_common.cuh"
+#include "lmc_internal.h"
 
 #include <algorithm>
 
@@ -36,7 +37,7 @@ __global__ void k_dequant_tail(uint32_t type, const uint8_t *__restrict__ src, f
 }
 
 static int g_sm_count = 0;
-int lmc_sm_count() {
+extern "C" int lmc_sm_count(void) {
     if (!g_sm_count) {
         int dev = 0;
         cudaGetDevice(&dev);

@@ -21,6 +21,8 @@ __global__ void __launch_bounds__(GEN_WARPS * 32)
 k_gemv_generic(const uint8_t *__restrict__ W, int M, int K, const float *__restrict__ x, int ldx,
                const float *__restrict__ bias, float *__restrict__ y, int ldy, int nb, int epi) {
     using F = lmcq::Fmt<T>;
+    pdl_wait();
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int m = blockIdx.x * GEN_WARPS + (threadIdx.x >> 5);
     if (m >= M) return;
@@ -68,15 +70,14 @@ extern "C" int lmc_gemv_generic_launch(uint32_t type, const void *d_blocks, int 
         switch (type) {
 #define CASE(T)                                                                                       \
     case T:                                                                                           \
-        k_gemv_generic<T><<<grid, GEN_WARPS * 32, 0, s>>>((const uint8_t *)d_blocks, M, K, xb, ldx, d_bias, \
-                                                          yb, ldy, nb, epi);                          \
+        LMC_LAUNCH("gemv_generic", k_gemv_generic<T>, grid, GEN_WARPS * 32, 0, s, (const uint8_t *)d_blocks, M, K, \
+                   xb, ldx, d_bias, yb, ldy, nb, epi);                                                \
         break;
             LMC_FOR_EACH_TYPE(CASE)
 #undef CASE
         default:
             return lmc_set_error(LMC_ERR_UNSUPPORTED, "matmul: type %u", type);
         }
-        LMC_LAUNCH_CHECK("gemv_generic");
     }
     return LMC_OK;
 }

@@ -66,3 +66,39 @@ __device__ __forceinline__ float block_max(float v, float *red) {
 // LMc activations (src/ops.c:20-29), same expression and operation order.
 __device__ __forceinline__ float lmc_gelu_f(float x) { return x * (1.0f / (1.0f + expf(-1.702f * x))); }
 __device__ __forceinline__ float lmc_silu_f(float x) { return x * (1.0f / (1.0f + expf(-x))); }
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL).  Kernels of a decode step are launched
+// with the programmatic-serialization attribute, so kernel N+1 is scheduled
+// while kernel N drains; every kernel calls pdl_launch_dependents() early and
+// pdl_wait() before it touches memory written by earlier kernels.  Work that
+// only reads weights (loads, L2 prefetch) is issued before pdl_wait() and so
+// overlaps the previous kernel.  Every kernel calls pdl_wait(), so completion
+// stays transitive along the chain.  Without the attribute both are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+extern "C" int lmc_pdl_enabled(void);
+
+template <typename... KArgs, typename... Args>
+static inline cudaError_t lmc_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = lmc_pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+#define LMC_LAUNCH(name, kern, grid, block, smem, stream, ...)                                        \
+    do {                                                                                              \
+        cudaError_t _e = lmc_launch(kern, dim3(grid), dim3(block), (size_t)(smem), stream, __VA_ARGS__); \
+        if (_e != cudaSuccess) return lmc_set_error(LMC_ERR_CUDA, "%s launch: %s", name, cudaGetErrorString(_e)); \
+    } while (0)

@@ -11,6 +11,8 @@
 // src/ops.c:47-59: mean, variance, (x - mean) * inv_std * w + b, eps 1e-5.
 __global__ void k_layer_norm(float *__restrict__ out, const float *__restrict__ x, const float *__restrict__ w,
                              const float *__restrict__ b, int dim) {
+    pdl_wait();
+    pdl_launch_dependents();
     __shared__ float red[32];
     const float *xr = x + (size_t)blockIdx.x * dim;
     float *orow = out + (size_t)blockIdx.x * dim;
@@ -27,6 +29,8 @@ __global__ void k_layer_norm(float *__restrict__ out, const float *__restrict__ 
 // src/ops_llama.c:24-33
 __global__ void k_rms_norm(float *__restrict__ out, const float *__restrict__ x, const float *__restrict__ w,
                            int dim, float eps) {
+    pdl_wait();
+    pdl_launch_dependents();
     __shared__ float red[32];
     const float *xr = x + (size_t)blockIdx.x * dim;
     float *orow = out + (size_t)blockIdx.x * dim;
@@ -38,6 +42,8 @@ __global__ void k_rms_norm(float *__restrict__ out, const float *__restrict__ x,
 
 // src/ops.c:32-44
 __global__ void k_softmax(float *__restrict__ x, int n) {
+    pdl_wait();
+    pdl_launch_dependents();
     __shared__ float red[32];
     float *r = x + (size_t)blockIdx.x * n;
     float mx = -INFINITY;
@@ -55,12 +61,16 @@ __global__ void k_softmax(float *__restrict__ x, int n) {
 }
 
 __global__ void k_act(float *__restrict__ x, size_t n, int kind) {
+    pdl_wait();
+    pdl_launch_dependents();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         x[i] = kind == 0 ? lmc_gelu_f(x[i]) : lmc_silu_f(x[i]);
 }
 
 // src/ops_llama.c:150-151
 __global__ void k_swiglu(float *__restrict__ g, const float *__restrict__ u, size_t n) {
+    pdl_wait();
+    pdl_launch_dependents();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         g[i] = lmc_silu_f(g[i]) * u[i];
 }
@@ -68,6 +78,8 @@ __global__ void k_swiglu(float *__restrict__ g, const float *__restrict__ u, siz
 // src/ops_llama.c:39-48, for n_heads consecutive vectors sharing one row.
 __global__ void k_rope(float *__restrict__ v, const float *__restrict__ c, const float *__restrict__ s, int Dh,
                        int n_pairs) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_pairs) return;
     const int d = i % (Dh / 2);
@@ -83,6 +95,8 @@ __device__ __forceinline__ void am_merge(float &v, int &i, float v2, int i2) {
     if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; }
 }
 __global__ void k_argmax(const float *__restrict__ x, int n, int *__restrict__ idx) {
+    pdl_wait();
+    pdl_launch_dependents();
     __shared__ float sv[32];
     __shared__ int si[32];
     const float *r = x + (size_t)blockIdx.x * n;
@@ -122,6 +136,8 @@ __global__ void k_argmax(const float *__restrict__ x, int n, int *__restrict__ i
 template <int T>
 __global__ void k_embed(const uint8_t *__restrict__ wte, const float *__restrict__ wpe, const int *__restrict__ tok,
                         const int *__restrict__ pos, int D, int V, int S, float *__restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
     using F = lmcq::Fmt<T>;
     const int b = blockIdx.x;
     // the host validates tokens and positions; never index outside wte / wpe
@@ -147,13 +163,12 @@ extern "C" int lmc_embed_launch(uint32_t type, const void *wte, const float *wpe
                                 const int *d_pos, int D, int V, int S, int batch, float *out, cudaStream_t s) {
     switch (type) {
 #define CASE(T) \
-    case T: k_embed<T><<<batch, 256, 0, s>>>((const uint8_t *)wte, wpe, d_tok, d_pos, D, V, S, out); break;
+    case T: LMC_LAUNCH("embed", k_embed<T>, batch, 256, 0, s, (const uint8_t *)wte, wpe, d_tok, d_pos, D, V, S, out); break;
         LMC_FOR_EACH_TYPE(CASE)
 #undef CASE
     default:
         return lmc_set_error(LMC_ERR_UNSUPPORTED, "embed: type %u", type);
     }
-    LMC_LAUNCH_CHECK("embed");
     return LMC_OK;
 }
 
@@ -163,16 +178,14 @@ extern "C" int lmc_layer_norm(float *out, const float *x, const float *w, const 
                               void *stream) {
     if (!out || !x || !w || !b || dim <= 0 || rows < 0) return lmc_set_error(LMC_ERR_INVALID, "layer_norm: args");
     if (!rows) return LMC_OK;
-    k_layer_norm<<<rows, rows_threads(dim), 0, lmc_stream(stream)>>>(out, x, w, b, dim);
-    LMC_LAUNCH_CHECK("layer_norm");
+    LMC_LAUNCH("layer_norm", k_layer_norm, rows, rows_threads(dim), 0, lmc_stream(stream), out, x, w, b, dim);
     return LMC_OK;
 }
 
 extern "C" int lmc_rms_norm(float *out, const float *x, const float *w, int dim, int rows, float eps, void *stream) {
     if (!out || !x || !w || dim <= 0 || rows < 0) return lmc_set_error(LMC_ERR_INVALID, "rms_norm: args");
     if (!rows) return LMC_OK;
-    k_rms_norm<<<rows, rows_threads(dim), 0, lmc_stream(stream)>>>(out, x, w, dim, eps);
-    LMC_LAUNCH_CHECK("rms_norm");
+    LMC_LAUNCH("rms_norm", k_rms_norm, rows, rows_threads(dim), 0, lmc_stream(stream), out, x, w, dim, eps);
     return LMC_OK;
 }
 
@@ -197,8 +210,7 @@ extern "C" int lmc_silu(float *x, size_t n, void *stream) { return act(x, n, 1, 
 extern "C" int lmc_swiglu(float *g, const float *u, size_t n, void *stream) {
     if (!g || !u) return lmc_set_error(LMC_ERR_INVALID, "swiglu: null");
     if (!n) return LMC_OK;
-    k_swiglu<<<std::min<size_t>(lmc_cdiv(n, 256), 148 * 16), 256, 0, lmc_stream(stream)>>>(g, u, n);
-    LMC_LAUNCH_CHECK("swiglu");
+    LMC_LAUNCH("swiglu", k_swiglu, std::min<size_t>(lmc_cdiv(n, 256), 148 * 16), 256, 0, lmc_stream(stream), g, u, n);
     return LMC_OK;
 }
 
@@ -214,14 +226,15 @@ extern "C" int lmc_rope_apply(float *v, const float *c, const float *s, int Dh, 
 extern "C" int lmc_argmax(const float *x, int n, int rows, int *idx, void *stream) {
     if (!x || !idx || n <= 0 || rows < 0) return lmc_set_error(LMC_ERR_INVALID, "argmax: args");
     if (!rows) return LMC_OK;
-    k_argmax<<<rows, 1024, 0, lmc_stream(stream)>>>(x, n, idx);
-    LMC_LAUNCH_CHECK("argmax");
+    LMC_LAUNCH("argmax", k_argmax, rows, 1024, 0, lmc_stream(stream), x, n, idx);
     return LMC_OK;
 }
 
 // RoPE for a batch of rows, each at its own device-side position.
 __global__ void k_rope_pos(float *__restrict__ v, int ld, int n_heads, int Dh, const float *__restrict__ ct,
                            const float *__restrict__ st, const int *__restrict__ pos, int S) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int b = blockIdx.y, half = Dh / 2;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_heads * half || pos[b] < 0 || pos[b] >= S) return;
@@ -236,8 +249,7 @@ __global__ void k_rope_pos(float *__restrict__ v, int ld, int n_heads, int Dh, c
 extern "C" int lmc_rope_pos_launch(float *v, int ld, int n_heads, int Dh, const float *ct, const float *st,
                                    const int *d_pos, int S, int batch, cudaStream_t s) {
     const int pairs = n_heads * (Dh / 2);
-    k_rope_pos<<<dim3(lmc_cdiv(pairs, 128), batch), 128, 0, s>>>(v, ld, n_heads, Dh, ct, st, d_pos, S);
-    LMC_LAUNCH_CHECK("rope_pos");
+    LMC_LAUNCH("rope_pos", k_rope_pos, dim3(lmc_cdiv(pairs, 128), batch), 128, 0, s, v, ld, n_heads, Dh, ct, st, d_pos, S);
     return LMC_OK;
 }
 
@@ -248,6 +260,8 @@ extern "C" int lmc_rope_pos_launch(float *v, int ld, int n_heads, int Dh, const 
 __global__ void k_advance(const int *__restrict__ next, int *__restrict__ tok, int *__restrict__ pos,
                           int *__restrict__ step_p, const int *__restrict__ prompt, int n_prompt,
                           int *__restrict__ ids, int n_new, int batch) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int step = *step_p;
     for (int b = threadIdx.x; b < batch; b += blockDim.x) {
         if (step + 1 < n_prompt) {
@@ -265,7 +279,6 @@ __global__ void k_advance(const int *__restrict__ next, int *__restrict__ tok, i
 
 extern "C" int lmc_advance_launch(const int *d_next, int *d_tok, int *d_pos, int *d_step, const int *d_prompt,
                                   int n_prompt, int *d_ids, int n_new, int batch, cudaStream_t s) {
-    k_advance<<<1, 256, 0, s>>>(d_next, d_tok, d_pos, d_step, d_prompt, n_prompt, d_ids, n_new, batch);
-    LMC_LAUNCH_CHECK("advance");
+    LMC_LAUNCH("advance", k_advance, 1, 256, 0, s, d_next, d_tok, d_pos, d_step, d_prompt, n_prompt, d_ids, n_new, batch);
     return LMC_OK;
 }

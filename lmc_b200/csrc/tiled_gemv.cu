@@ -18,7 +18,7 @@
 //     with the 8 nibbles of its A fragment: rows g and g+8, k = 16j + 2c,
 //     2c+1, 2c+8, 2c+9, arranged so that (u & 0x000F000F), (u & 0x00F000F0),
 //     (u>>8 & ...) drop straight into fp16 mantissas.
-//   Q6_K unit (3360 B = 16 x 210):  [16 rows x 18 B header: 16 int8 scales,
+//   Q6_K unit (3360 B = 16 x 210):  [16 rows x 16 int8 scales] [16 rows x
 //     fp16 d] [32 lanes x 64 B low nibbles, same arrangement as Q4_K]
 //     [32 lanes x 32 B high 2-bit pairs: one u16 per chunk].
 // The bytes are the GGUF bytes rearranged (same count per weight), so the
@@ -34,7 +34,8 @@
 
 namespace {
 
-constexpr int WARPS = 8;
+constexpr int MAX_WARPS = 16;
+constexpr int PF_UNITS = 4;  // L2 prefetch distance, in units of the warp's own sequence
 constexpr int Q4K_UNIT = 2304, Q6K_UNIT = 3360;
 constexpr int SMEM_LIMIT = 200 * 1024;
 
@@ -72,6 +73,9 @@ __device__ __forceinline__ uint4 ld_stream(const void *p) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;
+}
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
@@ -149,12 +153,12 @@ __global__ void k_repack_q6k(const uint8_t *__restrict__ src, uint8_t *__restric
     const int unit = blockIdx.x;
     const int rt = unit / KB, kb = unit % KB, t = threadIdx.x;
     uint8_t *u = dst + (size_t)unit * Q6K_UNIT;
-    if (t < 16) {  // header: 16 int8 scales, fp16 d
+    if (t < 16) {  // header: 16 rows x 16 int8 scales, then 16 rows x fp16 d
         const int r = rt * 16 + t;
         const uint8_t *b = r < M ? src + ((size_t)r * KB + kb) * 210 : nullptr;
-        for (int i = 0; i < 16; i++) u[18 * t + i] = b ? b[192 + i] : 0;
-        u[18 * t + 16] = b ? b[208] : 0;
-        u[18 * t + 17] = b ? b[209] : 0;
+        for (int i = 0; i < 16; i++) u[16 * t + i] = b ? b[192 + i] : 0;
+        u[256 + 2 * t] = b ? b[208] : 0;
+        u[256 + 2 * t + 1] = b ? b[209] : 0;
     }
     if (t < 32) {
         const int g = t >> 2, c = t & 3;
@@ -178,11 +182,11 @@ __global__ void k_repack_q6k(const uint8_t *__restrict__ src, uint8_t *__restric
 // xf[kb][j][nt][lane] = B fragment (2 x f16x2) of chunk j: column n = 8nt + g
 // is the hi (n even) or lo (n odd) fp16 part of x[n/2]; rows k = 16j + 2c,
 // +1 (reg 0) and +8, +9 (reg 1).
-// xsum[kb][nt][lane] = B fragment of the per-32 sums used by the Q4_K min
-// term (rows = sub-block index 2c, 2c+1; rows 8..15 are zero).
-__device__ __forceinline__ void hi_lo(float v, int part, float &out) {
+// xs[kb][nt][lane] = B fragment of the per-32 sums used by the Q4_K min term
+// (rows = sub-block index 2c, 2c+1; rows 8..15 are zero).
+__device__ __forceinline__ float hi_lo(float v, int part) {
     const float h = __half2float(__float2half_rn(v));
-    out = part ? (v - h) : h;
+    return part ? (v - h) : h;
 }
 
 template <int NT>
@@ -194,56 +198,74 @@ __device__ void build_xfrags(uint2 *xf, uint32_t *xs, float *xsum_tmp, const flo
         const int g = lane >> 2, c = lane & 3, n = nt * 8 + g, b = n >> 1, part = n & 1;
         uint2 r = make_uint2(0u, 0u);
         if (b < nb) {
-            const float *xb = x + (size_t)b * ldx + kb * 256 + 16 * j + 2 * c;
-            float v0, v1, v2, v3;
-            hi_lo(xb[0], part, v0);
-            hi_lo(xb[1], part, v1);
-            hi_lo(xb[8], part, v2);
-            hi_lo(xb[9], part, v3);
-            r.x = pack_h2(v0, v1);
-            r.y = pack_h2(v2, v3);
+            const float2 *xb = reinterpret_cast<const float2 *>(x + (size_t)b * ldx + kb * 256 + 16 * j + 2 * c);
+            const float2 p0 = xb[0], p1 = xb[4];
+            r.x = pack_h2(hi_lo(p0.x, part), hi_lo(p0.y, part));
+            r.y = pack_h2(hi_lo(p1.x, part), hi_lo(p1.y, part));
         }
         xf[e] = r;
     }
     if (!want_sums) return;
-    // per-32 sums of x: xsum_tmp[kb][sub][b]
-    const int n_sums = KB * 8 * nb;
-    for (int e = threadIdx.x; e < n_sums; e += blockDim.x) {
+    // per-32 sums of x, one warp per (kb, sub, b): xsum_tmp[(kb*8 + sub)*nb + b]
+    const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int e = threadIdx.x >> 5; e < KB * 8 * nb; e += nw) {
         const int b = e % nb, sub = (e / nb) & 7, kb = e / (nb * 8);
-        const float *xb = x + (size_t)b * ldx + kb * 256 + 32 * sub;
-        float s = 0.0f;
-#pragma unroll 8
-        for (int i = 0; i < 32; i++) s += xb[i];
-        xsum_tmp[e] = s;
+        const float v = warp_sum(x[(size_t)b * ldx + kb * 256 + 32 * sub + lane]);
+        if (lane == 0) xsum_tmp[e] = v;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < KB * NT * 32; e += blockDim.x) {
-        const int lane = e & 31, nt = (e >> 5) % NT, kb = e / (32 * NT);
-        const int g = lane >> 2, c = lane & 3, n = nt * 8 + g, b = n >> 1, part = n & 1;
+        const int ln = e & 31, nt = (e >> 5) % NT, kb = e / (32 * NT);
+        const int g = ln >> 2, c = ln & 3, n = nt * 8 + g, b = n >> 1, part = n & 1;
         uint32_t r = 0u;
-        if (b < nb) {
-            float v0, v1;
-            hi_lo(xsum_tmp[(kb * 8 + 2 * c) * nb + b], part, v0);
-            hi_lo(xsum_tmp[(kb * 8 + 2 * c + 1) * nb + b], part, v1);
-            r = pack_h2(v0, v1);
-        }
+        if (b < nb)
+            r = pack_h2(hi_lo(xsum_tmp[(kb * 8 + 2 * c) * nb + b], part),
+                        hi_lo(xsum_tmp[(kb * 8 + 2 * c + 1) * nb + b], part));
         xs[e] = r;
     }
 }
 
 // ---------------------------------------------------------------------------
-// the GEMV kernels
+// the GEMV kernels: persistent CTAs, each owning `rpc` row tiles at a time;
+// the `ksplit` warps of a row tile take every ksplit-th 256-column unit and
+// their partial sums meet in shared memory.
 // ---------------------------------------------------------------------------
 struct TArgs {
     const uint8_t *w;
     const float *x, *bias;
     float *y;
-    int M, KB, RT, ldx, ldy, nb, epi, ksplit, rpc;
+    int M, KB, RT, ldx, ldy, nb, epi, ksplit, rpc, ngroups;
 };
 
+// The sequence of units one warp processes: row-tile groups grp = blockIdx.x,
+// blockIdx.x + gridDim.x, ...; inside a group, units kb = ks, ks + ksplit, ...
+struct UnitIter {
+    int grp, kb;
+    __device__ __forceinline__ bool valid(const TArgs &a, int rt_local) const {
+        return grp < a.ngroups && grp * a.rpc + rt_local < a.RT;
+    }
+    __device__ __forceinline__ void next(const TArgs &a, int ks) {
+        kb += a.ksplit;
+        if (kb >= a.KB) { kb = ks; grp += gridDim.x; }
+    }
+};
+
+// Issue L2 prefetches for the first PF_UNITS units of this warp (one lane
+// each) - used before pdl_wait(), so the weight stream of this kernel starts
+// while the previous kernel of the step is still running.
+__device__ __forceinline__ UnitIter prefetch_head(const TArgs &a, int rt_local, int ks, int lane, int unit_bytes) {
+    UnitIter it{(int)blockIdx.x, ks};
+    if (ks >= a.KB) { it.grp = a.ngroups; return it; }
+    for (int i = 0; i < PF_UNITS && it.valid(a, rt_local); i++) {
+        if (lane == i)
+            prefetch_l2(a.w + ((size_t)(it.grp * a.rpc + rt_local) * a.KB + it.kb) * unit_bytes, unit_bytes);
+        it.next(a, ks);
+    }
+    return it;
+}
+
 template <int NT>
-__device__ __forceinline__ void finish(const TArgs &a, float (&tot)[NT][4], float *red, int rt_local, int ks, int lane) {
-    // reduce the ksplit partial sums of this row tile, then epilogue
+__device__ __forceinline__ void finish(const TArgs &a, float (&tot)[NT][4], float *red, int rt, int ks, int lane) {
     const int wid = threadIdx.x >> 5;
     if (a.ksplit > 1) {
 #pragma unroll
@@ -252,207 +274,241 @@ __device__ __forceinline__ void finish(const TArgs &a, float (&tot)[NT][4], floa
             for (int i = 0; i < 4; i++) red[((wid * NT + nt) * 4 + i) * 32 + lane] = tot[nt][i];
     }
     __syncthreads();
-    if (ks != 0 || rt_local >= a.rpc) return;
-    if (a.ksplit > 1) {
+    if (ks == 0 && rt < a.RT) {
         for (int s = 1; s < a.ksplit; s++) {
-            const int w2 = wid + s;
 #pragma unroll
             for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-                for (int i = 0; i < 4; i++) tot[nt][i] += red[((w2 * NT + nt) * 4 + i) * 32 + lane];
+                for (int i = 0; i < 4; i++) tot[nt][i] += red[(((wid + s) * NT + nt) * 4 + i) * 32 + lane];
+        }
+        const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int b = nt * 4 + c;
+            if (b >= a.nb) continue;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int row = rt * 16 + g + 8 * h;
+                if (row >= a.M) continue;
+                float v = tot[nt][2 * h] + tot[nt][2 * h + 1];  // hi + lo halves of x
+                if (a.bias) v += a.bias[row];
+                if (a.epi & LMC_EPI_GELU) v = lmc_gelu_f(v);
+                float *o = a.y + (size_t)b * a.ldy + row;
+                *o = (a.epi & LMC_EPI_ACCUM) ? *o + v : v;
+            }
         }
     }
-    const int g = lane >> 2, c = lane & 3;
-    const int rt = blockIdx.x * a.rpc + rt_local;
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-        const int b = nt * 4 + c;
-        if (b >= a.nb) continue;
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int row = rt * 16 + g + 8 * h;
-            if (row >= a.M) continue;
-            float v = tot[nt][2 * h] + tot[nt][2 * h + 1];
-            if (a.bias) v += a.bias[row];
-            if (a.epi & LMC_EPI_GELU) v = lmc_gelu_f(v);
-            float *o = a.y + (size_t)b * a.ldy + row;
-            *o = (a.epi & LMC_EPI_ACCUM) ? *o + v : v;
-        }
-    }
+    __syncthreads();  // `red` is reused by the next row-tile group
 }
 
-// Q4_K: y = sum_blocks d * sum_k (sc*q) x  -  dmin * sum_sub m * X_sub
+// Q4_K (src/quant.c:275-303): y = sum_units d * sum_k (sc*q) x - dmin * sum_sub m * X_sub
 template <int NT>
-__global__ void __launch_bounds__(WARPS * 32) k_gemv_q4k(TArgs a) {
+__global__ void __launch_bounds__(MAX_WARPS * 32) k_gemv_q4k(TArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint2 *xf = reinterpret_cast<uint2 *>(smem);
     uint32_t *xs = reinterpret_cast<uint32_t *>(xf + a.KB * 16 * NT * 32);
-    float *tmp = reinterpret_cast<float *>(xs + a.KB * NT * 32);  // xsum temp, later the reduction area
-    build_xfrags<NT>(xf, xs, tmp, a.x, a.ldx, a.nb, a.KB, true);
-    __syncthreads();
+    float *tmp = reinterpret_cast<float *>(xs + a.KB * NT * 32);  // x sums, later the reduction area
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int rt_local = wid / a.ksplit, ks = wid % a.ksplit;
-    const int rt = blockIdx.x * a.rpc + rt_local;
     const int g = lane >> 2, c = lane & 3;
-    float tot[NT][4];
+    pdl_launch_dependents();
+    UnitIter pf = prefetch_head(a, rt_local, ks, lane, Q4K_UNIT);  // weights only: before the wait
+    pdl_wait();
+    build_xfrags<NT>(xf, xs, tmp, a.x, a.ldx, a.nb, a.KB, true);
+    __syncthreads();
+    for (int grp = blockIdx.x; grp < a.ngroups; grp += gridDim.x) {
+        const int rt = grp * a.rpc + rt_local;
+        float tot[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++)
+        for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) tot[nt][i] = 0.0f;
-    const bool active = rt_local < a.rpc && rt < a.RT;
-    if (active) {
-        const uint8_t *base = a.w + (size_t)rt * a.KB * Q4K_UNIT;
-        int kb = ks;
-        uint4 h0, h1, q0, q1, q2, q3;
-        if (kb < a.KB) {
-            const uint8_t *u = base + (size_t)kb * Q4K_UNIT;
-            h0 = __ldg(reinterpret_cast<const uint4 *>(u + 16 * g));
-            h1 = __ldg(reinterpret_cast<const uint4 *>(u + 16 * (g + 8)));
-            const uint8_t *q = u + 256 + 64 * lane;
-            q0 = ld_stream(q); q1 = ld_stream(q + 16); q2 = ld_stream(q + 32); q3 = ld_stream(q + 48);
-        }
-        for (; kb < a.KB; kb += a.ksplit) {
-            const uint4 H0 = h0, H1 = h1;
-            const uint32_t qs[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
-                                     q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
-            const int nk = kb + a.ksplit;
-            if (nk < a.KB) {  // prefetch the next unit
-                const uint8_t *u = base + (size_t)nk * Q4K_UNIT;
+            for (int i = 0; i < 4; i++) tot[nt][i] = 0.0f;
+        if (rt < a.RT && ks < a.KB) {
+            const uint8_t *base = a.w + (size_t)rt * a.KB * Q4K_UNIT;
+            uint4 h0, h1, q0, q1, q2, q3;
+            {
+                const uint8_t *u = base + (size_t)ks * Q4K_UNIT;
                 h0 = __ldg(reinterpret_cast<const uint4 *>(u + 16 * g));
                 h1 = __ldg(reinterpret_cast<const uint4 *>(u + 16 * (g + 8)));
                 const uint8_t *q = u + 256 + 64 * lane;
                 q0 = ld_stream(q); q1 = ld_stream(q + 16); q2 = ld_stream(q + 32); q3 = ld_stream(q + 48);
             }
-            // scales (src/quant.c:44-53, four at a time)
-            const uint32_t sc0a = H0.y & 0x3F3F3F3Fu, sc0b = (H0.w & 0x0F0F0F0Fu) | ((H0.y >> 2) & 0x30303030u);
-            const uint32_t sc1a = H1.y & 0x3F3F3F3Fu, sc1b = (H1.w & 0x0F0F0F0Fu) | ((H1.y >> 2) & 0x30303030u);
-            const uint32_t m0a = H0.z & 0x3F3F3F3Fu, m0b = ((H0.w >> 4) & 0x0F0F0F0Fu) | ((H0.z >> 2) & 0x30303030u);
-            const uint32_t m1a = H1.z & 0x3F3F3F3Fu, m1b = ((H1.w >> 4) & 0x0F0F0F0Fu) | ((H1.z >> 2) & 0x30303030u);
-            float acc[NT][4];
+            for (int kb = ks; kb < a.KB; kb += a.ksplit) {
+                if (pf.valid(a, rt_local)) {  // keep PF_UNITS units of this warp in flight to L2
+                    if (lane == 0)
+                        prefetch_l2(a.w + ((size_t)(pf.grp * a.rpc + rt_local) * a.KB + pf.kb) * Q4K_UNIT, Q4K_UNIT);
+                    pf.next(a, ks);
+                }
+                const uint4 H0 = h0, H1 = h1;
+                const uint32_t qs[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
+                                         q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+                const int nk = kb + a.ksplit;
+                if (nk < a.KB) {  // prefetch the next unit
+                    const uint8_t *u = base + (size_t)nk * Q4K_UNIT;
+                    h0 = __ldg(reinterpret_cast<const uint4 *>(u + 16 * g));
+                    h1 = __ldg(reinterpret_cast<const uint4 *>(u + 16 * (g + 8)));
+                    const uint8_t *q = u + 256 + 64 * lane;
+                    q0 = ld_stream(q); q1 = ld_stream(q + 16); q2 = ld_stream(q + 32); q3 = ld_stream(q + 48);
+                }
+                // 6-bit scales / mins of rows g and g+8, four at a time (src/quant.c:44-53)
+                const uint32_t sc0a = H0.y & 0x3F3F3F3Fu, sc0b = (H0.w & 0x0F0F0F0Fu) | ((H0.y >> 2) & 0x30303030u);
+                const uint32_t sc1a = H1.y & 0x3F3F3F3Fu, sc1b = (H1.w & 0x0F0F0F0Fu) | ((H1.y >> 2) & 0x30303030u);
+                const uint32_t m0a = H0.z & 0x3F3F3F3Fu, m0b = ((H0.w >> 4) & 0x0F0F0F0Fu) | ((H0.z >> 2) & 0x30303030u);
+                const uint32_t m1a = H1.z & 0x3F3F3F3Fu, m1b = ((H1.w >> 4) & 0x0F0F0F0Fu) | ((H1.z >> 2) & 0x30303030u);
+                float acc[NT][4];
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++)
+                for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-                for (int i = 0; i < 4; i++) acc[nt][i] = 0.0f;
-            const uint2 *xk = xf + (size_t)(kb * 16) * NT * 32 + lane;
+                    for (int i = 0; i < 4; i++) acc[nt][i] = 0.0f;
+                const uint2 *xk = xf + (size_t)(kb * 16) * NT * 32 + lane;
 #pragma unroll
-            for (int sb = 0; sb < 8; sb++) {
-                const uint32_t w0 = sb < 4 ? sc0a : sc0b, w1 = sb < 4 ? sc1a : sc1b;
-                const uint32_t s0 = byte_pair_h2(w0, sb & 3, sb & 3);   // {sc, sc} row g
-                const uint32_t s1 = byte_pair_h2(w1, sb & 3, sb & 3);   // {sc, sc} row g+8
-                const uint32_t b0 = s0, c0 = hmul2(s0, HNEG1024);
-                const uint32_t b1 = hmul2(s1, HSIXTEENTH), c1 = hmul2(s1, HNEG64);
+                for (int sb = 0; sb < 8; sb++) {
+                    const uint32_t w0 = sb < 4 ? sc0a : sc0b, w1 = sb < 4 ? sc1a : sc1b;
+                    const uint32_t s0 = byte_pair_h2(w0, sb & 3, sb & 3);  // {sc, sc} row g
+                    const uint32_t s1 = byte_pair_h2(w1, sb & 3, sb & 3);  // {sc, sc} row g+8
+                    const uint32_t b0 = s0, c0 = hmul2(s0, HNEG1024);
+                    const uint32_t b1 = hmul2(s1, HSIXTEENTH), c1 = hmul2(s1, HNEG64);
 #pragma unroll
-                for (int jj = 0; jj < 2; jj++) {
-                    const int j = 2 * sb + jj;
-                    const uint32_t u = qs[j], u8 = u >> 8;
-                    const uint32_t a0 = hfma2(lop_and_or(u, 0x000F000Fu, H1024), b0, c0);
-                    const uint32_t a1 = hfma2(lop_and_or(u, 0x00F000F0u, H1024), b1, c1);
-                    const uint32_t a2 = hfma2(lop_and_or(u8, 0x000F000Fu, H1024), b0, c0);
-                    const uint32_t a3 = hfma2(lop_and_or(u8, 0x00F000F0u, H1024), b1, c1);
+                    for (int jj = 0; jj < 2; jj++) {
+                        const int j = 2 * sb + jj;
+                        const uint32_t u = qs[j], u8 = u >> 8;
+                        // A = q * sc, exact: (1024 + q)*sc - 1024*sc, (1024 + 16q)*sc/16 - 64*sc
+                        const uint32_t a0 = hfma2(lop_and_or(u, 0x000F000Fu, H1024), b0, c0);
+                        const uint32_t a1 = hfma2(lop_and_or(u, 0x00F000F0u, H1024), b1, c1);
+                        const uint32_t a2 = hfma2(lop_and_or(u8, 0x000F000Fu, H1024), b0, c0);
+                        const uint32_t a3 = hfma2(lop_and_or(u8, 0x00F000F0u, H1024), b1, c1);
 #pragma unroll
-                    for (int nt = 0; nt < NT; nt++) {
-                        const uint2 bx = xk[(j * NT + nt) * 32];
-                        mma(acc[nt], a0, a1, a2, a3, bx.x, bx.y);
+                        for (int nt = 0; nt < NT; nt++) {
+                            const uint2 bx = xk[(j * NT + nt) * 32];
+                            mma(acc[nt], a0, a1, a2, a3, bx.x, bx.y);
+                        }
                     }
                 }
-            }
-            // min term: rows g / g+8, sub-blocks 2c, 2c+1 (k rows 8..15 zero)
-            const uint32_t mw0 = c < 2 ? m0a : m0b, mw1 = c < 2 ? m1a : m1b;
-            const int i0 = (2 * c) & 3, i1 = (2 * c + 1) & 3;
-            const uint32_t am0 = byte_pair_h2(mw0, i0, i1), am1 = byte_pair_h2(mw1, i0, i1);
-            const float2 dd0 = __half22float2(*reinterpret_cast<const __half2 *>(&H0.x));
-            const float2 dd1 = __half22float2(*reinterpret_cast<const __half2 *>(&H1.x));
+                // min term: rows g / g+8, sub-blocks 2c, 2c+1 (k rows 8..15 zero)
+                const uint32_t mw0 = c < 2 ? m0a : m0b, mw1 = c < 2 ? m1a : m1b;
+                const int i0 = (2 * c) & 3, i1 = (2 * c + 1) & 3;
+                const uint32_t am0 = byte_pair_h2(mw0, i0, i1), am1 = byte_pair_h2(mw1, i0, i1);
+                const float2 dd0 = __half22float2(*reinterpret_cast<const __half2 *>(&H0.x));
+                const float2 dd1 = __half22float2(*reinterpret_cast<const __half2 *>(&H1.x));
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                float accm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                mma(accm, am0, am1, 0u, 0u, xs[(kb * NT + nt) * 32 + lane], 0u);
-                tot[nt][0] += dd0.x * acc[nt][0] - dd0.y * accm[0];
-                tot[nt][1] += dd0.x * acc[nt][1] - dd0.y * accm[1];
-                tot[nt][2] += dd1.x * acc[nt][2] - dd1.y * accm[2];
-                tot[nt][3] += dd1.x * acc[nt][3] - dd1.y * accm[3];
+                for (int nt = 0; nt < NT; nt++) {
+                    float accm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    mma(accm, am0, am1, 0u, 0u, xs[(kb * NT + nt) * 32 + lane], 0u);
+                    tot[nt][0] += dd0.x * acc[nt][0] - dd0.y * accm[0];
+                    tot[nt][1] += dd0.x * acc[nt][1] - dd0.y * accm[1];
+                    tot[nt][2] += dd1.x * acc[nt][2] - dd1.y * accm[2];
+                    tot[nt][3] += dd1.x * acc[nt][3] - dd1.y * accm[3];
+                }
             }
         }
+        finish<NT>(a, tot, tmp, rt, ks, lane);
     }
-    float *red = tmp;
-    finish<NT>(a, tot, red, rt_local, ks, lane);
 }
 
-// Q6_K: y = sum_blocks sum_sub (d*sc) * sum_16 (q-32) x
+// int8 byte i of w as an exact float: (2^23 + 128 + b) - (2^23 + 128)
+__device__ __forceinline__ float s8_to_f(uint32_t w, int i) {
+    const uint32_t v = __byte_perm(w, 0x4Bu, (uint32_t)(i | (5 << 4) | (5 << 8) | (4 << 12))) ^ 0x80u;
+    return __uint_as_float(v) - 8388736.0f;
+}
+
+// Q6_K (src/quant.c:386-414): y = sum_units sum_chunks (d*sc) * sum_16 (q-32) x
 template <int NT>
-__global__ void __launch_bounds__(WARPS * 32) k_gemv_q6k(TArgs a) {
+__global__ void __launch_bounds__(MAX_WARPS * 32) k_gemv_q6k(TArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint2 *xf = reinterpret_cast<uint2 *>(smem);
     float *tmp = reinterpret_cast<float *>(xf + a.KB * 16 * NT * 32);
-    build_xfrags<NT>(xf, nullptr, nullptr, a.x, a.ldx, a.nb, a.KB, false);
-    __syncthreads();
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int rt_local = wid / a.ksplit, ks = wid % a.ksplit;
-    const int rt = blockIdx.x * a.rpc + rt_local;
     const int g = lane >> 2;
-    float tot[NT][4];
+    pdl_launch_dependents();
+    UnitIter pf = prefetch_head(a, rt_local, ks, lane, Q6K_UNIT);  // weights only: before the wait
+    pdl_wait();
+    build_xfrags<NT>(xf, nullptr, nullptr, a.x, a.ldx, a.nb, a.KB, false);
+    __syncthreads();
+    for (int grp = blockIdx.x; grp < a.ngroups; grp += gridDim.x) {
+        const int rt = grp * a.rpc + rt_local;
+        float tot[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++)
+        for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) tot[nt][i] = 0.0f;
-    const bool active = rt_local < a.rpc && rt < a.RT;
-    if (active) {
-        const uint8_t *base = a.w + (size_t)rt * a.KB * Q6K_UNIT;
-        for (int kb = ks; kb < a.KB; kb += a.ksplit) {
-            const uint8_t *u = base + (size_t)kb * Q6K_UNIT;
-            // header: 16 int8 scales + fp16 d per row (18 B rows, 2-byte aligned)
-            const uint8_t *h0 = u + 18 * g, *h1 = u + 18 * (g + 8);
-            const float d0 = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short *>(h0 + 16))));
-            const float d1 = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short *>(h1 + 16))));
-            const uint8_t *q = u + 288 + 64 * lane;
-            const uint4 q0 = ld_stream(q), q1 = ld_stream(q + 16), q2 = ld_stream(q + 32), q3 = ld_stream(q + 48);
-            const uint4 hq0 = ld_stream(u + 288 + 2048 + 32 * lane), hq1 = ld_stream(u + 288 + 2048 + 32 * lane + 16);
-            const uint32_t qs[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
-                                     q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
-            const uint32_t hs[8] = {hq0.x, hq0.y, hq0.z, hq0.w, hq1.x, hq1.y, hq1.z, hq1.w};
-            const uint2 *xk = xf + (size_t)(kb * 16) * NT * 32 + lane;
+            for (int i = 0; i < 4; i++) tot[nt][i] = 0.0f;
+        if (rt < a.RT && ks < a.KB) {
+            const uint8_t *base = a.w + (size_t)rt * a.KB * Q6K_UNIT;
+            uint4 s0v, s1v, q0, q1, q2, q3, hq0, hq1;
+            uint32_t dw;
+            auto load = [&](int kb) {
+                const uint8_t *u = base + (size_t)kb * Q6K_UNIT;
+                s0v = __ldg(reinterpret_cast<const uint4 *>(u + 16 * g));
+                s1v = __ldg(reinterpret_cast<const uint4 *>(u + 16 * (g + 8)));
+                dw = (uint32_t)__ldg(reinterpret_cast<const unsigned short *>(u + 256 + 2 * g)) |
+                     ((uint32_t)__ldg(reinterpret_cast<const unsigned short *>(u + 256 + 2 * (g + 8))) << 16);
+                const uint8_t *q = u + 288 + 64 * lane;
+                q0 = ld_stream(q); q1 = ld_stream(q + 16); q2 = ld_stream(q + 32); q3 = ld_stream(q + 48);
+                hq0 = ld_stream(u + 288 + 2048 + 32 * lane);
+                hq1 = ld_stream(u + 288 + 2048 + 32 * lane + 16);
+            };
+            load(ks);
+            for (int kb = ks; kb < a.KB; kb += a.ksplit) {
+                if (pf.valid(a, rt_local)) {  // keep PF_UNITS units of this warp in flight to L2
+                    if (lane == 0)
+                        prefetch_l2(a.w + ((size_t)(pf.grp * a.rpc + rt_local) * a.KB + pf.kb) * Q6K_UNIT, Q6K_UNIT);
+                    pf.next(a, ks);
+                }
+                const uint32_t qs[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
+                                         q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+                const uint32_t hs[8] = {hq0.x, hq0.y, hq0.z, hq0.w, hq1.x, hq1.y, hq1.z, hq1.w};
+                const uint32_t sw0[4] = {s0v.x, s0v.y, s0v.z, s0v.w}, sw1[4] = {s1v.x, s1v.y, s1v.z, s1v.w};
+                const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&dw));
+                if (kb + a.ksplit < a.KB) load(kb + a.ksplit);  // prefetch the next unit
+                const uint2 *xk = xf + (size_t)(kb * 16) * NT * 32 + lane;
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const float s0 = d0 * (float)(int8_t)__ldg(h0 + j);
-                const float s1 = d1 * (float)(int8_t)__ldg(h1 + j);
-                const uint32_t u4 = qs[j], u8 = u4 >> 8;
-                const uint32_t hb = (hs[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
-                // high 2-bit pairs of nib i are at bits 2i..2i+1 of hb; place them
-                // at mantissa bits 4-5 (x1 fields) / 8-9 (x16 fields)
-                const uint32_t h_a0 = ((hb & 0x3u) << 4) | ((hb & 0x300u) << 12);          // nib0, nib4
-                const uint32_t h_a1 = ((hb & 0xCu) << 6) | ((hb & 0xC00u) << 14);          // nib1, nib5 (x16)
-                const uint32_t h_a2 = ((hb & 0x30u)) | ((hb & 0x3000u) << 8);              // nib2, nib6
-                const uint32_t h_a3 = ((hb & 0xC0u) << 2) | ((hb & 0xC000u) << 10);        // nib3, nib7 (x16)
-                // 1024 + q (x1) or 1024 + 16q (x16) with q = lo | hi << 4
-                const uint32_t v0 = lop_and_or(u4, 0x000F000Fu, H1024) | h_a0;
-                const uint32_t v1 = lop_and_or(u4, 0x00F000F0u, H1024) | h_a1;
-                const uint32_t v2 = lop_and_or(u8, 0x000F000Fu, H1024) | h_a2;
-                const uint32_t v3 = lop_and_or(u8, 0x00F000F0u, H1024) | h_a3;
-                const uint32_t a0 = hsub2(v0, H1056);                         // q - 32
-                const uint32_t a1 = hfma2(v1, HSIXTEENTH, HNEG96);       // (1024+16q)/16 - 96 = q - 32
-                const uint32_t a2 = hsub2(v2, H1056);
-                const uint32_t a3 = hfma2(v3, HSIXTEENTH, HNEG96);
+                for (int j = 0; j < 16; j++) {
+                    const float s0 = dd.x * s8_to_f(sw0[j >> 2], j & 3);  // d * sc, as LMc (quant.c:407)
+                    const float s1 = dd.y * s8_to_f(sw1[j >> 2], j & 3);
+                    const uint32_t u4 = qs[j], u8 = u4 >> 8;
+                    const uint32_t hb = (hs[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
+                    // high 2 bits of nibble i sit at bits 2i..2i+1 of hb; move them to
+                    // mantissa bits 4-5 (plain fields) or 8-9 (x16 fields)
+                    const uint32_t h_a0 = ((hb & 0x3u) << 4) | ((hb & 0x300u) << 12);
+                    const uint32_t h_a1 = ((hb & 0xCu) << 6) | ((hb & 0xC00u) << 14);
+                    const uint32_t h_a2 = (hb & 0x30u) | ((hb & 0x3000u) << 8);
+                    const uint32_t h_a3 = ((hb & 0xC0u) << 2) | ((hb & 0xC000u) << 10);
+                    const uint32_t v0 = lop_and_or(u4, 0x000F000Fu, H1024) | h_a0;  // 1024 + q
+                    const uint32_t v1 = lop_and_or(u4, 0x00F000F0u, H1024) | h_a1;  // 1024 + 16q
+                    const uint32_t v2 = lop_and_or(u8, 0x000F000Fu, H1024) | h_a2;
+                    const uint32_t v3 = lop_and_or(u8, 0x00F000F0u, H1024) | h_a3;
+                    const uint32_t a0 = hsub2(v0, H1056);              // q - 32
+                    const uint32_t a1 = hfma2(v1, HSIXTEENTH, HNEG96);  // (1024+16q)/16 - 96 = q - 32
+                    const uint32_t a2 = hsub2(v2, H1056);
+                    const uint32_t a3 = hfma2(v3, HSIXTEENTH, HNEG96);
 #pragma unroll
-                for (int nt = 0; nt < NT; nt++) {
-                    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    const uint2 bx = xk[(j * NT + nt) * 32];
-                    mma(acc, a0, a1, a2, a3, bx.x, bx.y);
-                    tot[nt][0] += s0 * acc[0];
-                    tot[nt][1] += s0 * acc[1];
-                    tot[nt][2] += s1 * acc[2];
-                    tot[nt][3] += s1 * acc[3];
+                    for (int nt = 0; nt < NT; nt++) {
+                        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        const uint2 bx = xk[(j * NT + nt) * 32];
+                        mma(acc, a0, a1, a2, a3, bx.x, bx.y);
+                        tot[nt][0] += s0 * acc[0];
+                        tot[nt][1] += s0 * acc[1];
+                        tot[nt][2] += s1 * acc[2];
+                        tot[nt][3] += s1 * acc[3];
+                    }
                 }
             }
         }
+        finish<NT>(a, tot, tmp, rt, ks, lane);
     }
-    finish<NT>(a, tot, tmp, rt_local, ks, lane);
 }
 
-size_t smem_bytes(uint32_t type, int KB, int NT) {
+size_t smem_bytes(uint32_t type, int KB, int NT, int warps) {
     size_t xf = (size_t)KB * 16 * NT * 32 * sizeof(uint2);
     size_t xs = type == LMC_TYPE_Q4_K ? (size_t)KB * NT * 32 * 4 : 0;
-    size_t red = (size_t)WARPS * NT * 4 * 32 * 4;
+    size_t red = (size_t)warps * NT * 4 * 32 * 4;
     size_t sums = type == LMC_TYPE_Q4_K ? (size_t)KB * 8 * 4 * NT * 4 : 0;
     return xf + xs + std::max(red, sums);
+}
+
+void plan(int KB, int *ksplit, int *rpc) {
+    *ksplit = std::min(KB, MAX_WARPS);
+    *rpc = std::max(1, MAX_WARPS / *ksplit);
 }
 
 }  // namespace
@@ -461,7 +517,7 @@ extern "C" int lmc_tiled_build(lmc_qtensor *t) {
     t->tiled = NULL;
     if ((t->type != LMC_TYPE_Q4_K && t->type != LMC_TYPE_Q6_K) || t->cols % 256) return LMC_OK;
     const int KB = t->cols / 256, RT = (t->rows + 15) / 16;
-    if (smem_bytes(t->type, KB, 1) > SMEM_LIMIT) return LMC_OK;  // very long rows: generic path
+    if (smem_bytes(t->type, KB, 1, MAX_WARPS) > SMEM_LIMIT) return LMC_OK;  // very long rows: generic path
     const size_t unit = t->type == LMC_TYPE_Q4_K ? Q4K_UNIT : Q6K_UNIT;
     const size_t bytes = (size_t)RT * KB * unit;
     LMC_CUDA_TRY(cudaMalloc(&t->tiled, bytes));
@@ -478,22 +534,25 @@ extern "C" int lmc_tiled_build(lmc_qtensor *t) {
 
 template <int NT>
 static int launch_nt(const lmc_qtensor *t, TArgs a, cudaStream_t s) {
-    const size_t smem = smem_bytes(t->type, a.KB, NT);
+    const int threads = a.ksplit * a.rpc * 32;
+    const size_t smem = smem_bytes(t->type, a.KB, NT, threads / 32);
     if (smem > SMEM_LIMIT) return LMC_ERR_UNSUPPORTED;
-    const unsigned grid = lmc_cdiv((size_t)a.RT, (size_t)a.rpc);
-    if (t->type == LMC_TYPE_Q4_K) {
-        LMC_CUDA_TRY(cudaFuncSetAttribute(k_gemv_q4k<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_gemv_q4k<NT><<<grid, WARPS * 32, smem, s>>>(a);
-    } else {
-        LMC_CUDA_TRY(cudaFuncSetAttribute(k_gemv_q6k<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_gemv_q6k<NT><<<grid, WARPS * 32, smem, s>>>(a);
-    }
-    LMC_LAUNCH_CHECK("tiled gemv");
+    const void *fn = t->type == LMC_TYPE_Q4_K ? (const void *)k_gemv_q4k<NT> : (const void *)k_gemv_q6k<NT>;
+    LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    LMC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));
+    const int grid = std::max(1, std::min(a.ngroups, std::max(per_sm, 1) * lmc_sm_count()));
+    if (t->type == LMC_TYPE_Q4_K)
+        LMC_LAUNCH("tiled gemv q4k", k_gemv_q4k<NT>, grid, threads, smem, s, a);
+    else
+        LMC_LAUNCH("tiled gemv q6k", k_gemv_q6k<NT>, grid, threads, smem, s, a);
     return LMC_OK;
 }
 
 extern "C" int lmc_tiled_gemv_launch(const lmc_qtensor *t, const float *d_x, int ldx, const float *d_bias, float *d_y,
                                      int ldy, int batch, int epi, cudaStream_t s) {
+    if (((uintptr_t)d_x & 7) || (ldx & 1))  // float2 fragment loads
+        return lmc_gemv_generic_launch(t->type, t->blocks, t->rows, t->cols, d_x, ldx, d_bias, d_y, ldy, batch, epi, s);
     TArgs a;
     a.w = (const uint8_t *)t->tiled;
     a.bias = d_bias;
@@ -503,18 +562,17 @@ extern "C" int lmc_tiled_gemv_launch(const lmc_qtensor *t, const float *d_x, int
     a.ldx = ldx;
     a.ldy = ldy;
     a.epi = epi;
-    a.ksplit = std::min(a.KB, WARPS);
-    a.rpc = std::max(1, WARPS / a.ksplit);
+    plan(a.KB, &a.ksplit, &a.rpc);
+    a.ngroups = (a.RT + a.rpc - 1) / a.rpc;
     for (int b0 = 0; b0 < batch;) {
         const int nb = std::min(batch - b0, 8);
         a.x = d_x + (size_t)b0 * ldx;
         a.y = d_y + (size_t)b0 * ldy;
         int rc;
+        a.nb = nb;
         if (nb <= 4) {
-            a.nb = nb;
             rc = launch_nt<1>(t, a, s);
         } else {
-            a.nb = nb;
             rc = launch_nt<2>(t, a, s);
             if (rc == LMC_ERR_UNSUPPORTED) {  // not enough shared memory for 2 n-tiles: two passes of 4
                 a.nb = 4;

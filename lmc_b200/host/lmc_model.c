@@ -498,6 +498,10 @@ int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, i
         if (h_prompt[i] < 0 || h_prompt[i] >= m->cfg.vocab_size)
             return lmc_set_error(LMC_ERR_INVALID, "model_generate: token %d out of range", h_prompt[i]);
     TRY(ensure_gen_buffers(m, B, n_prompt, n_new));
+    /* LMC_NO_GRAPH=1 launches the kernels directly (profilers that cannot
+     * replay graph kernel nodes one by one); the kernels are the same. */
+    const char *ng = getenv("LMC_NO_GRAPH");
+    if (ng && ng[0] == '1') use_graph = 0;
     cudaStream_t s = m->stream;
     CUTRY(cudaMemcpyAsync(m->d_prompt, h_prompt, sizeof(int) * (size_t)B * n_prompt, cudaMemcpyHostToDevice, s));
     for (int b = 0; b < B; b++) { m->h_stage[b] = h_prompt[(size_t)b * n_prompt]; m->h_stage[B + b] = 0; }
@@ -536,6 +540,8 @@ int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, i
         }
         for (int i = 0; i < steps; i++) CUTRY(cudaGraphLaunch(m->gexec, s));
     } else {
+        if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = NULL; }
+        m->g_batch = B; m->g_nprompt = n_prompt; m->g_nnew = n_new;
         for (int i = 0; i < steps; i++) TRY(gen_step(m, B, n_prompt, n_new));
     }
     /* the last greedy pick needs no forward of its own: take it from the
@@ -545,12 +551,15 @@ int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, i
     return LMC_OK;
 }
 
-/* Replays the captured generation graph `n` more times without resetting
- * state (bench helper: timed decode steps continue from the current
- * position).  Returns LMC_ERR_INVALID when no graph has been captured. */
+/* Runs `n` more steps of the last generation (its captured graph, or direct
+ * launches when it ran without one) without resetting state: timed decode
+ * steps continue from the current device-side position. */
 int lmc_model_replay(lmc_model *m, int n, void *stream_out) {
-    if (!m || !m->gexec) return lmc_set_error(LMC_ERR_INVALID, "model_replay: no captured graph");
-    for (int i = 0; i < n; i++) CUTRY(cudaGraphLaunch(m->gexec, m->stream));
+    if (!m || !m->g_batch) return lmc_set_error(LMC_ERR_INVALID, "model_replay: no generation to continue");
+    for (int i = 0; i < n; i++) {
+        if (m->gexec) CUTRY(cudaGraphLaunch(m->gexec, m->stream));
+        else TRY(gen_step(m, m->g_batch, m->g_nprompt, m->g_nnew));
+    }
     if (stream_out) *(cudaStream_t *)stream_out = m->stream;
     return LMC_OK;
 }

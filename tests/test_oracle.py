@@ -1,0 +1,101 @@
+"""The oracle (oracle/lmc_oracle.c) pinned against LMc itself: the committed
+golden fixtures (LMc's own outputs, tests/golden/make_golden.py) and, when
+the compiled LMc sources are present (oracle/_ref), random inputs."""
+import os
+import tempfile
+
+import numpy as np
+import pytest
+
+from lmc_b200 import synth
+from tests.conftest import ROOT, rel_err
+
+GOLD = os.path.join(ROOT, "tests", "golden")
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return np.load(os.path.join(GOLD, "kernels.npz"))
+
+
+@pytest.fixture(scope="module")
+def ref():
+    from oracle import Ref, ref_library_path
+    if not os.path.exists(ref_library_path()):
+        pytest.skip("LMc reference build (oracle/_ref) not present")
+    return Ref()
+
+
+@pytest.mark.parametrize("t", synth.ALL_TYPES, ids=lambda t: synth.NAMES[t])
+def test_dequant_golden(orc, gold, t):
+    blk = gold[f"dq_{synth.NAMES[t]}_blocks"]
+    want = gold[f"dq_{synth.NAMES[t]}_out"]
+    got = orc.dequant(t, blk, want.size)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_gemv_and_ops_golden(orc, gold):
+    w = orc.dequant(synth.Q4_K, gold["gemv_blocks"], 48 * 512).reshape(48, 512)
+    assert rel_err(orc.matmul_vec(w, gold["gemv_x"], gold["gemv_bias"]), gold["gemv_y"]) < 1e-6
+    x, w, b = gold["ops_x"], gold["ops_w"], gold["ops_b"]
+    assert rel_err(orc.layer_norm(x, w, b), gold["ops_layer_norm"]) < 1e-6
+    assert rel_err(orc.rms_norm(x, w, 1e-5), gold["ops_rms_norm"]) < 1e-6
+    assert rel_err(orc.softmax(x), gold["ops_softmax"]) < 1e-6
+    assert np.allclose(orc.gelu(x[:64]), gold["ops_gelu"], rtol=1e-6, atol=1e-7)
+    assert np.allclose(orc.silu(x[:64]), gold["ops_silu"], rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("kind", ["gpt2", "llama"])
+def test_model_golden(orc, kind):
+    g = np.load(os.path.join(GOLD, f"model_{kind}.npz"))
+    with tempfile.TemporaryDirectory() as d:
+        p = os.path.join(d, "m.gguf")
+        g["gguf"].tofile(p)
+        m = orc.model(p)
+        for pos, t in enumerate(g["tokens"]):
+            assert rel_err(m.forward(int(t), pos), g["logits"][pos]) < 1e-5
+        m.close()
+        m = orc.model(p)
+        lg = None
+        for pos, t in enumerate(g["prompt"]):
+            lg = m.forward(int(t), pos)
+        ids, pos = [], len(g["prompt"])
+        for _ in range(len(g["ids"])):
+            ids.append(orc.argmax(lg))
+            lg = m.forward(ids[-1], pos)
+            pos += 1
+        assert ids == g["ids"].tolist()
+
+
+@pytest.mark.parametrize("t", synth.ALL_TYPES, ids=lambda t: synth.NAMES[t])
+def test_dequant_vs_lmc_random(orc, ref, t):
+    be = max(synth.GEOMETRY[t][0], 8)
+    for seed in range(4):
+        n = be * 512
+        blk = synth.random_blocks(t, n, seed=seed)
+        assert np.array_equal(orc.dequant(t, blk, n).view(np.uint32), ref.dequant(t, blk, n).view(np.uint32))
+
+
+def test_edge_scales_vs_lmc(orc, ref):
+    """Zero, subnormal, max-finite and negative fp16 scales decode like LMc
+    (scales kept finite: LMc's fast-math build is only flag-stable there)."""
+    specials = np.array([0x0000, 0x8000, 0x0001, 0x03FF, 0x0400, 0x7BFF, 0xFBFF, 0x3C00, 0xBC00], np.uint16)
+    for t in synth.BLOCK_TYPES:
+        be, bb, offs = synth.GEOMETRY[t]
+        nb = len(specials)
+        blk = synth.random_blocks(t, be * nb, seed=9)
+        body = blk[:-synth.PAD].reshape(nb, bb)
+        for o in offs:
+            body[:, o:o + 2] = specials.view(np.uint8).reshape(nb, 2)
+        blk = np.concatenate([body.reshape(-1), blk[-synth.PAD:]])
+        a, b = orc.dequant(t, blk, be * nb), ref.dequant(t, blk, be * nb)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), synth.NAMES[t]
+
+
+def test_matmul_vs_lmc(orc, ref):
+    rng = np.random.default_rng(1)
+    for M, K in ((7, 1600), (300, 768), (3, 17)):
+        w = rng.normal(0, 1, (M, K)).astype(np.float32)
+        x = rng.normal(0, 1, K).astype(np.float32)
+        b = rng.normal(0, 1, M).astype(np.float32)
+        assert rel_err(orc.matmul_vec(w, x, b), ref.matmul_vec(w, x, b)) < 1e-5
