@@ -148,6 +148,22 @@ int lmc_attention_decode(float *d_out, const float *d_q, const float *d_k_new,
                          int kv_dtype, const int *d_pos, int batch, int H, int Hkv,
                          int Dh, int S, void *d_workspace, size_t workspace_bytes,
                          void *stream);
+/* lmc_attention_decode without a workspace, for callers that cannot
+ * allocate device memory where they decode (inside CUDA-graph capture,
+ * loops that must not let cudaMalloc/cudaFree synchronize the device, hosts
+ * that own every device allocation).  No counterpart in LMc: it is an
+ * addition of this library.  The split-context scratch is a fixed 4 MiB
+ * array compiled into liblmc_b200.so (held by every GPU that loads the
+ * library until exit); shapes whose lmc_attention_workspace_bytes exceed it
+ * are rejected with LMC_ERR_INVALID.  The first call on each device looks up
+ * the array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture.  The call allocates nothing.  All calls on a
+ * device share the one array, which keeps the last call's contents: calls
+ * that may overlap on the GPU (different streams without ordering) race. */
+int lmc_attention_decode_noalloc(float *d_out, const float *d_q, const float *d_k_new,
+                                 const float *d_v_new, void *d_k_cache, void *d_v_cache,
+                                 int kv_dtype, const int *d_pos, int batch, int H, int Hkv,
+                                 int Dh, int S, void *stream);
 
 /* ---- whole model: load_model + model_forward on the device -------------------
  * lmc_model_load parses a GGUF v1-3 file the way load_model does

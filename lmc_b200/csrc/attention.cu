@@ -199,3 +199,62 @@ extern "C" int lmc_attention_decode(float *out, const float *q, const float *k_n
     return lmc_attention_launch(out, H * Dh, q, H * Dh, k_new, v_new, Hkv * Dh, k_cache, v_cache, kv_dtype, d_pos,
                                 batch, H, Hkv, Dh, S, d_ws, ws_bytes, lmc_stream(stream));
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of lmc_attention_decode.
+//
+// Some callers cannot allocate device memory at the point where they decode:
+// code recorded into a CUDA graph (cudaMalloc is not a stream operation and
+// cannot be captured), latency-critical loops that must not let cudaMalloc /
+// cudaFree synchronize the device, and host applications that hand out all
+// device memory themselves and forbid other allocations.  For them this entry
+// point takes its split-context scratch from a fixed array compiled into the
+// library instead of a caller-supplied workspace.
+//
+// The array below is file-scope device memory: every GPU that loads the
+// library holds these 4 MiB until the process exits.  In host code its name
+// is only a host-side stand-in, so its device address is looked up with
+// cudaGetSymbolAddress once per device (on the first call made with that
+// device current) and that address is what the kernels receive.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+#define LMC_ATTN_STATIC_SCRATCH_BYTES (4u << 20)
+#define LMC_MAX_DEVICES 64
+
+static __device__ __align__(256) unsigned char g_attn_static_scratch[LMC_ATTN_STATIC_SCRATCH_BYTES];
+static void *g_attn_static_ptr[LMC_MAX_DEVICES];
+static std::mutex g_attn_static_mu;
+
+extern "C" int lmc_attention_decode_noalloc(float *out, const float *q, const float *k_new, const float *v_new,
+                                            void *k_cache, void *v_cache, int kv_dtype, const int *d_pos,
+                                            int batch, int H, int Hkv, int Dh, int S, void *stream) {
+    if (batch <= 0 || H <= 0 || Dh <= 0 || S <= 0)
+        return lmc_set_error(LMC_ERR_INVALID, "attention_noalloc: batch=%d H=%d Dh=%d S=%d", batch, H, Dh, S);
+    const size_t need = lmc_attention_workspace_bytes(batch, H, Dh, S);
+    if (need > LMC_ATTN_STATIC_SCRATCH_BYTES)
+        return lmc_set_error(LMC_ERR_INVALID,
+                             "attention_noalloc: this shape needs %zu bytes of scratch, more than the fixed %u "
+                             "(batch x heads x context splits x (head_dim + 2) x 4 bytes); use "
+                             "lmc_attention_decode with a workspace",
+                             need, LMC_ATTN_STATIC_SCRATCH_BYTES);
+    int dev = 0;
+    LMC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= LMC_MAX_DEVICES)
+        return lmc_set_error(LMC_ERR_INVALID, "attention_noalloc: device %d beyond %d", dev, LMC_MAX_DEVICES);
+    void *scratch;
+    {
+        std::lock_guard<std::mutex> lock(g_attn_static_mu);
+        if (!g_attn_static_ptr[dev]) {
+            void *p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+            if (e != cudaSuccess || !p)
+                return lmc_set_error(LMC_ERR_CUDA, "attention_noalloc: cudaGetSymbolAddress: %s",
+                                     cudaGetErrorString(e));
+            g_attn_static_ptr[dev] = p;
+        }
+        scratch = g_attn_static_ptr[dev];
+    }
+    return lmc_attention_launch(out, H * Dh, q, H * Dh, k_new, v_new, Hkv * Dh, k_cache, v_cache, kv_dtype, d_pos,
+                                batch, H, Hkv, Dh, S, scratch, LMC_ATTN_STATIC_SCRATCH_BYTES, lmc_stream(stream));
+}
