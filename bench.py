@@ -214,7 +214,7 @@ def run_lmc(args, rank, world, local_rank, dist):
 
     from lmc_b200 import microbench
     # the dominant kernel of the step: the largest GEMV (lm_head shape)
-    r = microbench.run(torch, synth.Q6_K, 50257, 768, 1, iters=60, stream=s)
+    r = microbench.run(torch, synth.Q6_K, 50257, 768, 1, iters=60)
     gbs, gemv_ms, alg, tiled = r["gbs"], r["ms"], r["bytes"], r["tiled"]
     peak, peak_kind = measured_peaks()
     cpu = None

@@ -52,6 +52,11 @@ extern "C" {
 /* Message for the last failing call on this host thread ("" if none). */
 const char *lmc_last_error(void);
 
+/* LMC_OK, or LMC_ERR_TIMEOUT (once; the flag is then cleared) when a kernel
+ * of this library gave up one of its bounded waits on the device - every
+ * spin-wait in the kernels has an iteration limit instead of hanging. */
+int lmc_device_status(void);
+
 /* Select and initialise CUDA device `device` for the calling thread.
  * Fails with LMC_ERR_CUDA when no sm_100 device is present. */
 int lmc_init(int device);

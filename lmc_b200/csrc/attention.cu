@@ -34,6 +34,9 @@ struct AttnArgs {
     float *ws;  // [batch][H][nsplit][Dh + 2]
     int H, Hkv, Dh, S, CH, nsplit;
     int ldo, ldq, ldkv;  // row strides (floats) between sequences
+    // RoPE tables [S][Dh/2] (LLaMA, src/ops_llama.c:75-78) applied to q and to
+    // the new K row here, or NULL
+    const float *rope_cos, *rope_sin;
 };
 
 template <typename KV>
@@ -62,16 +65,38 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
     }
     KV *kc = reinterpret_cast<KV *>(a.k_cache) + ((size_t)b * a.Hkv + kh) * a.S * Dh;
     KV *vc = reinterpret_cast<KV *>(a.v_cache) + ((size_t)b * a.Hkv + kh) * a.S * Dh;
-    if (pos >= t0 && pos < t1) {  // append this step's K/V row
+    const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (Dh / 2) : nullptr;
+    const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (Dh / 2) : nullptr;
+    if (pos >= t0 && pos < t1) {  // append this step's K/V row (K rotated first when RoPE applies)
         const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
         const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
-        for (int d = threadIdx.x; d < Dh; d += ATT_THREADS) {
-            kc[(size_t)pos * Dh + d] = kv_cvt<KV>(kn[d]);
-            vc[(size_t)pos * Dh + d] = kv_cvt<KV>(vn[d]);
+        for (int d = threadIdx.x; d < Dh / 2; d += ATT_THREADS) {
+            float k0 = kn[2 * d], k1 = kn[2 * d + 1];
+            if (rc) {
+                const float c = rc[d], sn = rs[d];
+                const float r0 = k0 * c - k1 * sn, r1 = k0 * sn + k1 * c;
+                k0 = r0;
+                k1 = r1;
+            }
+            kc[(size_t)pos * Dh + 2 * d] = kv_cvt<KV>(k0);
+            kc[(size_t)pos * Dh + 2 * d + 1] = kv_cvt<KV>(k1);
+            vc[(size_t)pos * Dh + 2 * d] = kv_cvt<KV>(vn[2 * d]);
+            vc[(size_t)pos * Dh + 2 * d + 1] = kv_cvt<KV>(vn[2 * d + 1]);
         }
     }
     const float *qb = a.q + (size_t)b * a.ldq + (size_t)kh * G * Dh;
-    for (int i = threadIdx.x; i < G * Dh; i += ATT_THREADS) qs[i] = qb[i];
+    for (int i = threadIdx.x; i < G * Dh / 2; i += ATT_THREADS) {  // q pairs (rotated when RoPE applies)
+        const int gq = i / (Dh / 2), d = i % (Dh / 2);
+        float q0 = qb[gq * Dh + 2 * d], q1 = qb[gq * Dh + 2 * d + 1];
+        if (rc) {
+            const float c = rc[d], sn = rs[d];
+            const float r0 = q0 * c - q1 * sn, r1 = q0 * sn + q1 * c;
+            q0 = r0;
+            q1 = r1;
+        }
+        qs[gq * Dh + 2 * d] = q0;
+        qs[gq * Dh + 2 * d + 1] = q1;
+    }
     __syncthreads();
     const float scale = 1.0f / sqrtf((float)Dh);
     const int per_lane = Dh / 32;
@@ -158,6 +183,15 @@ extern "C" int lmc_attention_launch(float *out, int ldo, const float *q, int ldq
                                     const float *v_new, int ldkv, void *k_cache, void *v_cache, int kv_dtype,
                                     const int *d_pos, int batch, int H, int Hkv, int Dh, int S, void *d_ws,
                                     size_t ws_bytes, cudaStream_t s) {
+    return lmc_attention_rope_launch(out, ldo, q, ldq, k_new, v_new, ldkv, k_cache, v_cache, kv_dtype, d_pos, batch, H,
+                                     Hkv, Dh, S, d_ws, ws_bytes, NULL, NULL, s);
+}
+
+extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, int ldq, const float *k_new,
+                                         const float *v_new, int ldkv, void *k_cache, void *v_cache, int kv_dtype,
+                                         const int *d_pos, int batch, int H, int Hkv, int Dh, int S, void *d_ws,
+                                         size_t ws_bytes, const float *rope_cos, const float *rope_sin,
+                                         cudaStream_t s) {
     if (!out || !q || !k_new || !v_new || !k_cache || !v_cache || !d_pos)
         return lmc_set_error(LMC_ERR_INVALID, "attention: null pointer");
     if (batch <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh % 32 || Dh > 256 || S <= 0)
@@ -169,6 +203,7 @@ extern "C" int lmc_attention_launch(float *out, int ldo, const float *q, int ldq
     a.out = out; a.q = q; a.k_new = k_new; a.v_new = v_new; a.k_cache = k_cache; a.v_cache = v_cache;
     a.pos = d_pos; a.H = H; a.Hkv = Hkv; a.Dh = Dh; a.S = S;
     a.ldo = ldo; a.ldq = ldq; a.ldkv = ldkv;
+    a.rope_cos = rope_cos; a.rope_sin = rope_sin;
     attn_plan(S, &a.CH, &a.nsplit);
     const size_t need = lmc_attention_workspace_bytes(batch, H, Dh, S);
     if (need > ws_bytes || (need && !d_ws))

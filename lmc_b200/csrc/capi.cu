@@ -119,6 +119,44 @@ extern "C" int lmc_qtensor_upload(uint32_t type, int rows, int cols, const void 
     return LMC_OK;
 }
 
+// Rows of several tensors of the same type and width stacked into one tensor
+// (block streams concatenated; each part's n_elements is a multiple of the
+// block size, so the result is a valid block stream).  *out = NULL when the
+// parts do not match.
+extern "C" int lmc_qtensor_concat(const lmc_qtensor *const *parts, int n, lmc_qtensor **out) {
+    *out = NULL;
+    if (n <= 0 || !parts[0]) return LMC_OK;
+    int rows = 0;
+    size_t bytes = 0;
+    for (int i = 0; i < n; i++) {
+        if (!parts[i] || parts[i]->type != parts[0]->type || parts[i]->cols != parts[0]->cols) return LMC_OK;
+        rows += parts[i]->rows;
+        bytes += parts[i]->bytes;
+    }
+    lmc_qtensor *t = (lmc_qtensor *)calloc(1, sizeof(lmc_qtensor));
+    if (!t) return lmc_set_error(LMC_ERR_OOM, "qtensor_concat: host alloc");
+    t->type = parts[0]->type;
+    t->rows = rows;
+    t->cols = parts[0]->cols;
+    t->bytes = bytes;
+    cudaError_t e = cudaMalloc(&t->blocks, bytes + LMC_BLOCK_PAD);
+    if (e != cudaSuccess) { free(t); return lmc_set_error(LMC_ERR_OOM, "qtensor_concat: %s", cudaGetErrorString(e)); }
+    size_t off = 0;
+    for (int i = 0; i < n && e == cudaSuccess; i++) {
+        e = cudaMemcpy((char *)t->blocks + off, parts[i]->blocks, parts[i]->bytes, cudaMemcpyDeviceToDevice);
+        off += parts[i]->bytes;
+    }
+    if (e == cudaSuccess) e = cudaMemset((char *)t->blocks + bytes, 0, LMC_BLOCK_PAD);
+    if (e != cudaSuccess) {
+        lmc_qtensor_free(t);
+        return lmc_set_error(LMC_ERR_CUDA, "qtensor_concat: %s", cudaGetErrorString(e));
+    }
+    int rc = lmc_tiled_build(t);
+    if (rc) { lmc_qtensor_free(t); return rc; }
+    *out = t;
+    return LMC_OK;
+}
+
 extern "C" int lmc_qtensor_free(lmc_qtensor *t) {
     if (!t) return LMC_OK;
     if (t->blocks) cudaFree(t->blocks);

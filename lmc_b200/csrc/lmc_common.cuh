@@ -63,6 +63,16 @@ __device__ __forceinline__ float block_max(float v, float *red) {
     return warp_max(t);
 }
 
+// Greedy-pick key (src/lmc.c:45-47: largest value, first index on ties):
+// high word = the float's bits mapped to an order-preserving unsigned,
+// low word = ~index, so the unsigned 64-bit maximum is the first maximum.
+__device__ __forceinline__ unsigned long long lmc_argmax_key(float v, int idx) {
+    const unsigned int f = __float_as_uint(v);
+    const unsigned int o = (f & 0x80000000u) ? ~f : (f | 0x80000000u);
+    return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned int)idx);
+}
+__device__ __forceinline__ int lmc_key_index(unsigned long long k) { return (int)(0xFFFFFFFFu - (unsigned int)(k & 0xFFFFFFFFu)); }
+
 // LMc activations (src/ops.c:20-29), same expression and operation order.
 __device__ __forceinline__ float lmc_gelu_f(float x) { return x * (1.0f / (1.0f + expf(-1.702f * x))); }
 __device__ __forceinline__ float lmc_silu_f(float x) { return x * (1.0f / (1.0f + expf(-x))); }

@@ -29,6 +29,7 @@ struct lmc_qtensor {
 };
 
 int lmc_set_error(int code, const char *fmt, ...);
+int lmc_qtensor_concat(const struct lmc_qtensor *const *parts, int n, struct lmc_qtensor **out);
 int lmc_tensor_bytes(uint32_t type, size_t n_elements, size_t *bytes);
 int lmc_sm_count(void);
 
@@ -38,6 +39,25 @@ int lmc_gemv_generic_launch(uint32_t type, const void *d_blocks, int M, int K, c
 int lmc_tiled_build(struct lmc_qtensor *t);
 int lmc_tiled_gemv_launch(const struct lmc_qtensor *t, const float *d_x, int ldx, const float *d_bias, float *d_y,
                           int ldy, int batch, int epi, cudaStream_t s);
+/* Fused work around a tensor-core GEMV (tiled tensors only): a prologue op
+ * applied to x as it is loaded, and a greedy-argmax epilogue. */
+#define LMC_PRO_NONE 0
+#define LMC_PRO_LAYERNORM 1 /* (x - mean) * rstd * w + b, eps 1e-5 (src/ops.c:47-59) */
+#define LMC_PRO_RMSNORM 2   /* w * rs * x (src/ops_llama.c:24-33) */
+#define LMC_PRO_SWIGLU 3    /* silu(x) * x2 (src/ops_llama.c:150-151) */
+typedef struct {
+    int pro;
+    const float *w, *b, *x2;
+    float eps;
+    unsigned long long *keys; /* non-NULL: atomicMax of lmc_argmax_key(y, row) per batch row */
+} lmc_gemv_extra;
+int lmc_tiled_gemv_ex(const struct lmc_qtensor *t, const float *d_x, int ldx, const float *d_bias, float *d_y, int ldy,
+                      int batch, int epi, const lmc_gemv_extra *ex, cudaStream_t s);
+/* Argmax over keys: reads each batch row's key (written by the fused
+ * epilogue or by lmc_argmax_keys_launch), stores the row index in d_next and
+ * resets the key to 0 for the next step. */
+int lmc_argmax_keys_launch(const float *d_x, int n, int rows, unsigned long long *d_keys, cudaStream_t s);
+int lmc_keys_to_ids_launch(unsigned long long *d_keys, int *d_next, int batch, cudaStream_t s);
 int lmc_embed_launch(uint32_t type, const void *wte, const float *wpe, const int *d_tok, const int *d_pos, int D,
                      int V, int S, int batch, float *out, cudaStream_t s);
 /* RoPE on `batch` rows (row stride ld floats) of n_heads x Dh, each at its
@@ -48,9 +68,16 @@ int lmc_rope_pos_launch(float *v, int ld, int n_heads, int Dh, const float *cos_
 int lmc_attention_launch(float *out, int ldo, const float *q, int ldq, const float *k_new, const float *v_new,
                          int ldkv, void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, int batch, int H,
                          int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes, cudaStream_t s);
-/* Generation bookkeeping after one step (see lmc_model_generate). */
-int lmc_advance_launch(const int *d_next, int *d_tok, int *d_pos, int *d_step, const int *d_prompt, int n_prompt,
-                       int *d_ids, int n_new, int batch, cudaStream_t s);
+/* Same, applying RoPE (src/ops_llama.c:39-48,75-78) from [S][Dh/2] tables to
+ * q and to the new K row on the fly (no separate rope launch). */
+int lmc_attention_rope_launch(float *out, int ldo, const float *q, int ldq, const float *k_new, const float *v_new,
+                              int ldkv, void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, int batch, int H,
+                              int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes, const float *rope_cos,
+                              const float *rope_sin, cudaStream_t s);
+/* Generation bookkeeping after one step (see lmc_model_generate): the greedy
+ * id of each sequence is read from (and reset in) d_keys. */
+int lmc_advance_launch(unsigned long long *d_keys, int *d_next, int *d_tok, int *d_pos, int *d_step,
+                       const int *d_prompt, int n_prompt, int *d_ids, int n_new, int batch, cudaStream_t s);
 
 #ifdef __cplusplus
 }

@@ -253,23 +253,73 @@ extern "C" int lmc_rope_pos_launch(float *v, int ld, int n_heads, int Dh, const 
     return LMC_OK;
 }
 
+// Greedy argmax producing the pick key of each row (see lmc_argmax_key):
+// used when the lm_head GEMV cannot fuse the argmax itself.
+__global__ void k_argmax_keys(const float *__restrict__ x, int n, unsigned long long *__restrict__ keys) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ unsigned long long sk[32];
+    const float *r = x + (size_t)blockIdx.x * n;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const unsigned long long k = lmc_argmax_key(r[i], i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+    }
+    if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = sk[w] > best ? sk[w] : best;
+        best = sk[0] > best ? sk[0] : best;
+        keys[blockIdx.x] = best;
+    }
+}
+
+extern "C" int lmc_argmax_keys_launch(const float *d_x, int n, int rows, unsigned long long *d_keys, cudaStream_t s) {
+    LMC_LAUNCH("argmax_keys", k_argmax_keys, rows, 1024, 0, s, d_x, n, d_keys);
+    return LMC_OK;
+}
+
+// key -> id, and reset the key for the next step
+__global__ void k_keys_to_ids(unsigned long long *__restrict__ keys, int *__restrict__ next, int batch) {
+    pdl_wait();
+    pdl_launch_dependents();
+    for (int b = threadIdx.x; b < batch; b += blockDim.x) {
+        next[b] = lmc_key_index(keys[b]);
+        keys[b] = 0ull;
+    }
+}
+
+extern "C" int lmc_keys_to_ids_launch(unsigned long long *d_keys, int *d_next, int batch, cudaStream_t s) {
+    LMC_LAUNCH("keys_to_ids", k_keys_to_ids, 1, 256, 0, s, d_keys, d_next, batch);
+    return LMC_OK;
+}
+
 // Generation bookkeeping run after every step of lmc_model_generate: the
 // step just computed position `step`; the next step feeds the next prompt
 // token while the prompt lasts (token-by-token prefill, src/lmc.c:109-112),
-// then the greedy pick (src/lmc.c:123,129), which is also recorded.
-__global__ void k_advance(const int *__restrict__ next, int *__restrict__ tok, int *__restrict__ pos,
-                          int *__restrict__ step_p, const int *__restrict__ prompt, int n_prompt,
+// then the greedy pick (src/lmc.c:123,129), which is also recorded.  The
+// pick is read from the step's argmax key, which is reset for the next step.
+__global__ void k_advance(unsigned long long *__restrict__ keys, int *__restrict__ next, int *__restrict__ tok,
+                          int *__restrict__ pos, int *__restrict__ step_p, const int *__restrict__ prompt, int n_prompt,
                           int *__restrict__ ids, int n_new, int batch) {
     pdl_wait();
     pdl_launch_dependents();
     const int step = *step_p;
     for (int b = threadIdx.x; b < batch; b += blockDim.x) {
+        const int nx = lmc_key_index(keys[b]);
+        keys[b] = 0ull;
+        next[b] = nx;
         if (step + 1 < n_prompt) {
             tok[b] = prompt[(size_t)b * n_prompt + step + 1];
         } else {
             const int k = step + 1 - n_prompt;
-            tok[b] = next[b];
-            if (k < n_new) ids[(size_t)b * n_new + k] = next[b];
+            tok[b] = nx;
+            if (k < n_new) ids[(size_t)b * n_new + k] = nx;
         }
         pos[b] = step + 1;
     }
@@ -277,8 +327,10 @@ __global__ void k_advance(const int *__restrict__ next, int *__restrict__ tok, i
     if (threadIdx.x == 0) *step_p = step + 1;
 }
 
-extern "C" int lmc_advance_launch(const int *d_next, int *d_tok, int *d_pos, int *d_step, const int *d_prompt,
-                                  int n_prompt, int *d_ids, int n_new, int batch, cudaStream_t s) {
-    LMC_LAUNCH("advance", k_advance, 1, 256, 0, s, d_next, d_tok, d_pos, d_step, d_prompt, n_prompt, d_ids, n_new, batch);
+extern "C" int lmc_advance_launch(unsigned long long *d_keys, int *d_next, int *d_tok, int *d_pos, int *d_step,
+                                  const int *d_prompt, int n_prompt, int *d_ids, int n_new, int batch,
+                                  cudaStream_t s) {
+    LMC_LAUNCH("advance", k_advance, 1, 256, 0, s, d_keys, d_next, d_tok, d_pos, d_step, d_prompt, n_prompt, d_ids,
+               n_new, batch);
     return LMC_OK;
 }

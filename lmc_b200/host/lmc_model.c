@@ -25,6 +25,9 @@ typedef struct {
     /* LLaMA */
     lmc_qtensor *q, *k, *v, *o, *gate, *up, *down;
     float *rms_attn, *rms_ffn;
+    /* q|k|v and gate|up concatenated by rows (same type and width), so each
+     * pair of projections is one launch; NULL when they cannot be fused */
+    lmc_qtensor *qkv_cat, *gateup_cat;
 } Layer;
 
 struct lmc_model {
@@ -39,6 +42,7 @@ struct lmc_model {
     void *ws;
     size_t ws_bytes;
     int *d_tok, *d_pos, *d_next, *d_step, *d_prompt, *d_ids;
+    unsigned long long *d_keys; /* per sequence greedy-pick key of the step */
     int *h_stage; /* pinned: tokens, positions, next ids */
     int prompt_cap, ids_cap;
     cudaStream_t stream;
@@ -283,6 +287,14 @@ static int load(lmc_model *m, const char *path) {
         for (uint64_t i = 0; i < nt && !rc; i++) rc = bind_tensor(m, &ti[i], buf + data, (size_t)fsz - data);
     }
     if (!rc) rc = check_complete(m);
+    if (!rc && c->arch == 2) { /* fuse q|k|v and gate|up (LMc keeps them separate, ops_llama.c:70-72,148-149) */
+        for (int l = 0; l < c->n_layers && !rc; l++) {
+            Layer *w = &m->layers[l];
+            const lmc_qtensor *qkv[3] = {w->q, w->k, w->v}, *gu[2] = {w->gate, w->up};
+            rc = lmc_qtensor_concat(qkv, 3, &w->qkv_cat);
+            if (!rc) rc = lmc_qtensor_concat(gu, 2, &w->gateup_cat);
+        }
+    }
 done:
     free(ti);
     free(buf);
@@ -323,8 +335,9 @@ static int alloc_state(lmc_model *m) {
     TRY(dev_alloc((void **)&m->xn, 4 * B * D));
     TRY(dev_alloc((void **)&m->qkv, 4 * B * (QD + 2 * KV + 3 * D)));
     TRY(dev_alloc((void **)&m->att, 4 * B * (QD > D ? QD : D)));
-    TRY(dev_alloc((void **)&m->h, 4 * B * F));
+    TRY(dev_alloc((void **)&m->h, 4 * B * 2 * F)); /* gate | up rows */
     TRY(dev_alloc((void **)&m->h2, 4 * B * F));
+    TRY(dev_alloc((void **)&m->d_keys, 8 * B));
     TRY(dev_alloc((void **)&m->logits, 4 * B * V));
     m->ws_bytes = lmc_attention_workspace_bytes((int)B, c->n_heads, c->head_dim, c->seq_len);
     TRY(dev_alloc(&m->ws, m->ws_bytes));
@@ -373,7 +386,8 @@ int lmc_model_free(lmc_model *m) {
     if (m->layers) {
         for (int l = 0; l < m->cfg.n_layers; l++) {
             Layer *w = &m->layers[l];
-            lmc_qtensor *qs[] = {w->qkv, w->proj, w->fc, w->fc2, w->q, w->k, w->v, w->o, w->gate, w->up, w->down};
+            lmc_qtensor *qs[] = {w->qkv, w->proj, w->fc, w->fc2, w->q, w->k, w->v, w->o, w->gate, w->up, w->down,
+                                 w->qkv_cat, w->gateup_cat};
             for (size_t i = 0; i < sizeof qs / sizeof qs[0]; i++) lmc_qtensor_free(qs[i]);
             float *vs[] = {w->ln1_w, w->ln1_b, w->ln2_w, w->ln2_b, w->qkv_b, w->proj_b, w->fc_b, w->fc2_b, w->rms_attn, w->rms_ffn};
             for (size_t i = 0; i < sizeof vs / sizeof vs[0]; i++) if (vs[i]) cudaFree(vs[i]);
@@ -383,7 +397,8 @@ int lmc_model_free(lmc_model *m) {
     lmc_qtensor_free(m->wte);
     lmc_qtensor_free(m->lm_head);
     void *ps[] = {m->wpe, m->lnf_w, m->lnf_b, m->rmsf, m->rope_cos, m->rope_sin, m->kc, m->vc, m->x, m->xn, m->qkv,
-                  m->att, m->h, m->h2, m->logits, m->ws, m->d_tok, m->d_pos, m->d_next, m->d_step, m->d_prompt, m->d_ids};
+                  m->att, m->h, m->h2, m->logits, m->ws, m->d_tok, m->d_pos, m->d_next, m->d_step, m->d_prompt, m->d_ids,
+                  m->d_keys};
     for (size_t i = 0; i < sizeof ps / sizeof ps[0]; i++) if (ps[i]) cudaFree(ps[i]);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -395,47 +410,92 @@ int lmc_model_free(lmc_model *m) {
 /* One decode step for B sequences: tokens d_tok, positions d_pos -> logits   */
 /* and greedy ids in d_next.  Only kernel launches on m->stream (capturable). */
 /* ------------------------------------------------------------------------ */
+/* x -> norm -> W, as one tensor-core launch with the norm as its prologue
+ * when W has the tiled layout, else a norm kernel and a plain matmul. */
+static int norm_matmul(lmc_model *m, const lmc_qtensor *W, int pro, const float *nw, const float *nb, float eps,
+                       const float *bias, float *y, int ldy, int B, int epi, unsigned long long *keys) {
+    const int D = m->cfg.embed_dim;
+    cudaStream_t s = m->stream;
+    if (lmc_qtensor_has_tiled(W) && (keys == NULL || B <= 8)) {
+        lmc_gemv_extra ex = {pro, nw, nb, NULL, eps, keys};
+        return lmc_tiled_gemv_ex(W, m->x, D, bias, y, ldy, B, epi, &ex, s);
+    }
+    if (pro == LMC_PRO_LAYERNORM) TRY(lmc_layer_norm(m->xn, m->x, nw, nb, D, B, s));
+    else TRY(lmc_rms_norm(m->xn, m->x, nw, D, B, eps, s));
+    TRY(lmc_matmul(W, m->xn, D, bias, y, ldy, B, epi, s));
+    if (keys) TRY(lmc_argmax_keys_launch(y, W->rows, B, keys, s));
+    return LMC_OK;
+}
+
+/* One decode step for B sequences: tokens d_tok, positions d_pos -> logits
+ * and each sequence's greedy-pick key in d_keys.  Only kernel launches on
+ * m->stream, so it can be captured as a graph.  LayerNorm / RMSNorm run as
+ * the prologue of the projection that follows them, SwiGLU as the prologue
+ * of ffn_down, and the greedy argmax as the epilogue of lm_head, whenever the
+ * weights have the tensor-core layout. */
 static int step(lmc_model *m, int B) {
     const lmc_model_config *c = &m->cfg;
     const int D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size, H = c->n_heads, Hkv = c->n_kv_heads;
     const int Dh = c->head_dim, S = c->seq_len, QD = H * Dh, KVD = Hkv * Dh;
     cudaStream_t s = m->stream;
     const size_t esz = m->kv_dtype == LMC_KV_F16 ? 2 : 4;
-    TRY(lmc_embed_launch(m->wte->type, m->wte->blocks, c->arch == 1 ? m->wpe : NULL, m->d_tok, m->d_pos, D, V, S, B, m->x, s));
+    TRY(lmc_embed_launch(m->wte->type, m->wte->blocks, c->arch == 1 ? m->wpe : NULL, m->d_tok, m->d_pos, D, V, S, B,
+                         m->x, s));
     for (int l = 0; l < c->n_layers; l++) {
         const Layer *w = &m->layers[l];
         char *kc = (char *)m->kc + esz * m->kv_layer_elems * l, *vc = (char *)m->vc + esz * m->kv_layer_elems * l;
         if (c->arch == 1) { /* src/ops.c:182-206 */
-            TRY(lmc_layer_norm(m->xn, m->x, w->ln1_w, w->ln1_b, D, B, s));
-            TRY(lmc_matmul(w->qkv, m->xn, D, w->qkv_b, m->qkv, 3 * D, B, LMC_EPI_NONE, s));
+            TRY(norm_matmul(m, w->qkv, LMC_PRO_LAYERNORM, w->ln1_w, w->ln1_b, 1e-5f, w->qkv_b, m->qkv, 3 * D, B,
+                            LMC_EPI_NONE, NULL));
             TRY(lmc_attention_launch(m->att, D, m->qkv, 3 * D, m->qkv + D, m->qkv + 2 * D, 3 * D, kc, vc, m->kv_dtype,
                                      m->d_pos, B, H, H, Dh, S, m->ws, m->ws_bytes, s));
             TRY(lmc_matmul(w->proj, m->att, D, w->proj_b, m->x, D, B, LMC_EPI_ACCUM, s));
-            TRY(lmc_layer_norm(m->xn, m->x, w->ln2_w, w->ln2_b, D, B, s));
-            TRY(lmc_matmul(w->fc, m->xn, D, w->fc_b, m->h, F, B, LMC_EPI_GELU, s));
+            TRY(norm_matmul(m, w->fc, LMC_PRO_LAYERNORM, w->ln2_w, w->ln2_b, 1e-5f, w->fc_b, m->h, F, B, LMC_EPI_GELU,
+                            NULL));
             TRY(lmc_matmul(w->fc2, m->h, F, w->fc2_b, m->x, D, B, LMC_EPI_ACCUM, s));
         } else { /* src/ops_llama.c:165-187 */
-            float *q = m->qkv, *k = m->qkv + (size_t)B * QD, *v = k + (size_t)B * KVD;
-            TRY(lmc_rms_norm(m->xn, m->x, w->rms_attn, D, B, c->norm_eps, s));
-            TRY(lmc_matmul(w->q, m->xn, D, NULL, q, QD, B, LMC_EPI_NONE, s));
-            TRY(lmc_matmul(w->k, m->xn, D, NULL, k, KVD, B, LMC_EPI_NONE, s));
-            TRY(lmc_matmul(w->v, m->xn, D, NULL, v, KVD, B, LMC_EPI_NONE, s));
-            TRY(lmc_rope_pos_launch(q, QD, H, Dh, m->rope_cos, m->rope_sin, m->d_pos, S, B, s));
-            TRY(lmc_rope_pos_launch(k, KVD, Hkv, Dh, m->rope_cos, m->rope_sin, m->d_pos, S, B, s));
-            TRY(lmc_attention_launch(m->att, QD, q, QD, k, v, KVD, kc, vc, m->kv_dtype, m->d_pos, B, H, Hkv, Dh, S,
-                                     m->ws, m->ws_bytes, s));
+            const int LQ = QD + 2 * KVD;
+            float *q = m->qkv, *k, *v;
+            int ld;
+            if (w->qkv_cat) {
+                TRY(norm_matmul(m, w->qkv_cat, LMC_PRO_RMSNORM, w->rms_attn, NULL, c->norm_eps, NULL, q, LQ, B,
+                                LMC_EPI_NONE, NULL));
+                k = q + QD;
+                v = q + QD + KVD;
+                ld = LQ;
+            } else {
+                k = m->qkv + (size_t)B * QD;
+                v = k + (size_t)B * KVD;
+                TRY(lmc_rms_norm(m->xn, m->x, w->rms_attn, D, B, c->norm_eps, s));
+                TRY(lmc_matmul(w->q, m->xn, D, NULL, q, QD, B, LMC_EPI_NONE, s));
+                TRY(lmc_matmul(w->k, m->xn, D, NULL, k, KVD, B, LMC_EPI_NONE, s));
+                TRY(lmc_matmul(w->v, m->xn, D, NULL, v, KVD, B, LMC_EPI_NONE, s));
+                ld = 0;
+            }
+            /* RoPE on q and the new K row happens inside the attention kernel */
+            TRY(lmc_attention_rope_launch(m->att, QD, q, ld ? ld : QD, k, v, ld ? ld : KVD, kc, vc, m->kv_dtype,
+                                          m->d_pos, B, H, Hkv, Dh, S, m->ws, m->ws_bytes, m->rope_cos, m->rope_sin, s));
             TRY(lmc_matmul(w->o, m->att, QD, NULL, m->x, D, B, LMC_EPI_ACCUM, s));
-            TRY(lmc_rms_norm(m->xn, m->x, w->rms_ffn, D, B, c->norm_eps, s));
-            TRY(lmc_matmul(w->gate, m->xn, D, NULL, m->h, F, B, LMC_EPI_NONE, s));
-            TRY(lmc_matmul(w->up, m->xn, D, NULL, m->h2, F, B, LMC_EPI_NONE, s));
-            TRY(lmc_swiglu(m->h, m->h2, (size_t)B * F, s));
-            TRY(lmc_matmul(w->down, m->h, F, NULL, m->x, D, B, LMC_EPI_ACCUM, s));
+            if (w->gateup_cat && lmc_qtensor_has_tiled(w->down)) {
+                TRY(norm_matmul(m, w->gateup_cat, LMC_PRO_RMSNORM, w->rms_ffn, NULL, c->norm_eps, NULL, m->h, 2 * F,
+                                B, LMC_EPI_NONE, NULL));
+                lmc_gemv_extra ex = {LMC_PRO_SWIGLU, NULL, NULL, m->h + F, 0.0f, NULL};
+                TRY(lmc_tiled_gemv_ex(w->down, m->h, 2 * F, NULL, m->x, D, B, LMC_EPI_ACCUM, &ex, s));
+            } else {
+                TRY(lmc_rms_norm(m->xn, m->x, w->rms_ffn, D, B, c->norm_eps, s));
+                TRY(lmc_matmul(w->gate, m->xn, D, NULL, m->h, F, B, LMC_EPI_NONE, s));
+                TRY(lmc_matmul(w->up, m->xn, D, NULL, m->h2, F, B, LMC_EPI_NONE, s));
+                TRY(lmc_swiglu(m->h, m->h2, (size_t)B * F, s));
+                TRY(lmc_matmul(w->down, m->h, F, NULL, m->x, D, B, LMC_EPI_ACCUM, s));
+            }
         }
     }
-    if (c->arch == 1) TRY(lmc_layer_norm(m->xn, m->x, m->lnf_w, m->lnf_b, D, B, s));
-    else TRY(lmc_rms_norm(m->xn, m->x, m->rmsf, D, B, c->norm_eps, s));
-    TRY(lmc_matmul(m->lm_head, m->xn, D, NULL, m->logits, V, B, LMC_EPI_NONE, s));
-    TRY(lmc_argmax(m->logits, V, B, m->d_next, s));
+    if (c->arch == 1)
+        TRY(norm_matmul(m, m->lm_head, LMC_PRO_LAYERNORM, m->lnf_w, m->lnf_b, 1e-5f, NULL, m->logits, V, B,
+                        LMC_EPI_NONE, m->d_keys));
+    else
+        TRY(norm_matmul(m, m->lm_head, LMC_PRO_RMSNORM, m->rmsf, NULL, c->norm_eps, NULL, m->logits, V, B,
+                        LMC_EPI_NONE, m->d_keys));
     return LMC_OK;
 }
 
@@ -453,6 +513,7 @@ int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B
     CUTRY(cudaMemcpyAsync(m->d_tok, m->h_stage, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
     CUTRY(cudaMemcpyAsync(m->d_pos, m->h_stage + B, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
     TRY(step(m, B));
+    TRY(lmc_keys_to_ids_launch(m->d_keys, m->d_next, B, m->stream));
     if (h_logits)
         CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * (size_t)B * m->cfg.vocab_size,
                               cudaMemcpyDeviceToHost, m->stream));
@@ -465,7 +526,7 @@ int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B
 /* step + bookkeeping, the unit that is captured as one graph */
 static int gen_step(lmc_model *m, int B, int n_prompt, int n_new) {
     TRY(step(m, B));
-    return lmc_advance_launch(m->d_next, m->d_tok, m->d_pos, m->d_step, m->d_prompt, n_prompt, m->d_ids, n_new, B,
+    return lmc_advance_launch(m->d_keys, m->d_next, m->d_tok, m->d_pos, m->d_step, m->d_prompt, n_prompt, m->d_ids, n_new, B,
                               m->stream);
 }
 

@@ -1,6 +1,7 @@
 """GEMV microbenchmark: one quantized matrix-vector product, timed on the
-device with CUDA events over rotated weight copies whose total exceeds twice
-the 126 MB L2 (so every launch streams its weights from HBM).
+device with CUDA events around a CUDA graph of back-to-back launches over
+rotated weight copies whose total exceeds twice the 126 MB L2 (so every
+launch streams its weights from HBM and host launch cost is excluded).
 
     python -m lmc_b200.microbench --type Q4_K --rows 3072 --cols 768 --batch 1
 
@@ -39,33 +40,46 @@ def algorithmic_bytes(qtype, rows, cols, batch):
 
 
 def run(torch, qtype, rows, cols, batch=1, iters=50, stream=None, generic=False, seed=100):
-    """Returns dict(ms, gbs, bytes, tiled)."""
+    """Returns dict(ms, gbs, bytes, tiled).  The `iters` launches (round robin
+    over the weight copies) are captured once as a CUDA graph and the graph
+    replay is timed, so host launch overhead is not in the number."""
     wbytes = synth.tensor_bytes(qtype, rows * cols)
     copies = max(2, int(np.ceil(2.2 * L2_BYTES / wbytes)) + 1)
     qs = [rt.QTensor(qtype, rows, cols, synth.random_blocks(qtype, rows * cols, seed=seed + i)) for i in range(copies)]
     x = torch.randn(batch, cols, device="cuda")
     y = torch.empty(batch, rows, device="cuda")
-    s = stream or torch.cuda.current_stream()
 
-    def launch(q):
+    def launch(q, st):
         if generic:
             rt.call("lmc_matmul_blocks", qtype, rt.lib().lmc_qtensor_blocks(q.h), rows, cols, x.data_ptr(), cols,
-                    None, y.data_ptr(), rows, batch, 0, s.cuda_stream)
+                    None, y.data_ptr(), rows, batch, 0, st)
         else:
-            q.matmul(x, y, batch=batch, stream=s.cuda_stream)
+            q.matmul(x, y, batch=batch, stream=st)
 
+    s = stream or torch.cuda.Stream()
     with torch.cuda.stream(s):
         for q in qs:
-            launch(q)
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
-        for i in range(iters):
-            evs[i][0].record(s)
-            launch(qs[i % copies])
-            evs[i][1].record(s)
+            launch(q, s.cuda_stream)
     torch.cuda.synchronize()
-    ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        cs = torch.cuda.current_stream().cuda_stream
+        for i in range(iters):
+            launch(qs[i % copies], cs)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * iters)
     alg = algorithmic_bytes(qtype, rows, cols, batch)
     tiled = qs[0].tiled and not generic
+    del g
     for q in qs:
         q.close()
     return {"ms": ms, "gbs": alg / (ms * 1e-3) / 1e9, "bytes": alg, "tiled": tiled}

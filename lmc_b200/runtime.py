@@ -22,6 +22,7 @@ _ip = _c.POINTER(_c.c_int)
 SIGNATURES = {
     "lmc_last_error": ([], _c.c_char_p),
     "lmc_init": ([_i], _i),
+    "lmc_device_status": ([], _i),
     "lmc_block_geometry": ([_u32, _ip, _ip], _i),
     "lmc_dequant": ([_u32, _vp, _sz, _vp, _vp], _i),
     "lmc_qtensor_upload": ([_u32, _i, _i, _vp, _sz, _c.POINTER(_vp)], _i),
