@@ -72,7 +72,7 @@ def ref_gemv(orc, t, blk, M, K, x, bias=None):
 
 
 GEMV_CASES = [
-    (synth.Q4_K, 3072, 768), (synth.Q6_K, 768, 3072), (synth.Q8_0, 1000, 512),
+    (synth.Q4_K, 3072, 768), (synth.Q6_K, 768, 3072), (synth.Q8_0, 1000, 512), (synth.Q8_0, 3072, 768),
     (synth.Q4_K, 6400, 1600), (synth.Q5_K, 1600, 6400),  # 6400x1600: K-quant blocks straddle rows
 ] + [(t, 256, 512) for t in synth.ALL_TYPES] + [(t, 96, 1600) for t in synth.BLOCK_TYPES]
 
@@ -96,6 +96,30 @@ def test_gemv(cuda, orc, t, M, K, B):
     rt.call("lmc_matmul_blocks", t, rt.lib().lmc_qtensor_blocks(q.h), M, K, dx.data_ptr(), K, db.data_ptr(),
             y2.data_ptr(), M, B, 0, None)
     assert rel_err(y2.cpu().numpy(), want) < RTOL
+
+
+# Shapes of the tensor-core path (Q4_K / Q6_K / Q8_0, cols % 256 == 0) that
+# exercise its work split: long rows (K = 14336), ragged row count, many row
+# tiles per cluster, and batch widths 2 and 5 (two rows per fragment, and an
+# odd row in the last fragment).
+TILED_CASES = [(synth.Q4_K, 4096, 14336), (synth.Q6_K, 50257, 768), (synth.Q8_0, 2048, 4096),
+               (synth.Q4_K, 14336, 2048), (synth.Q8_0, 520, 768)]
+
+
+@pytest.mark.parametrize("t,M,K", TILED_CASES, ids=lambda v: str(v))
+@pytest.mark.parametrize("B", [1, 2, 5])
+def test_gemv_tiled_shapes(cuda, orc, t, M, K, B):
+    rng = np.random.default_rng(M * 7 + K + B)
+    blk = synth.random_blocks(t, M * K, seed=M + 3 * K)
+    x = rng.normal(0, 1, (B, K)).astype(np.float32)
+    want = ref_gemv(orc, t, blk, M, K, x)
+    q = rt.QTensor(t, M, K, blk)
+    assert q.tiled
+    y = cuda.empty((B, M), dtype=cuda.float32, device="cuda")
+    dx = dev(cuda, x)
+    q.matmul(dx, y, batch=B)
+    assert rel_err(y.cpu().numpy(), want) < RTOL
+    assert rt.lib().lmc_device_status() == 0
 
 
 def test_gemv_epilogues(cuda, orc):
