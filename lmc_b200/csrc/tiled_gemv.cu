@@ -1031,7 +1031,9 @@ static int plan_for(uint32_t type, int rows_tiled, int cols, int nb, Plan *P) {
                 }
             }
         if (!stages) continue;
-        const long long score = per_cta * 4096 - (long long)NC * cl * 8 + cl;  // lower is better
+        // lower is better: the busiest CTA's units, plus about one unit for the
+        // two cluster barriers of a split, minus a little per CTA engaged
+        const long long score = (per_cta + (cl > 1 ? 1 : 0)) * 4096 - (long long)NC * cl * 8 + cl;
         if (best < 0 || score < best) {
             best = score;
             bestp = Plan{NT, XL, cl, NC, maxrt, stages, smem};
