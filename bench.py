@@ -70,6 +70,12 @@ def prompt_ids():
     return np.random.default_rng(0).integers(0, 50257, N_PROMPT).astype(np.int32)
 
 
+# DRAM bytes (read + write) of one lm_head-shape GEMV launch, from the ncu
+# capture summarised in profiles/gemv_q6k_50257x768.md (same kernel and shape
+# as the roofline line below).
+LM_HEAD_DRAM_BYTES = 31747584
+
+
 class Clocks:
     """SM clock and clock-event (throttle) reasons sampled through NVML every
     millisecond while the timed region runs (the region can be a few tens of
@@ -252,7 +258,8 @@ def run_lmc(args, rank, world, local_rank, dist):
                              " Q6_K 50257x768 (lm_head shape), rotated copies > 2x L2",
                              "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(gbs / peak, 4), "peak_kind": peak_kind + " (hbm_gbs, burst)",
-                             "traffic": None, "algorithmic_bytes": alg, "avg_launch_ms": round(gemv_ms, 5)},
+                             "traffic": LM_HEAD_DRAM_BYTES, "traffic_source": "profiles/gemv_q6k_50257x768.md",
+                             "algorithmic_bytes": alg, "avg_launch_ms": round(gemv_ms, 5)},
                 "cpu_baseline": cpu,
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
