@@ -111,6 +111,7 @@ extern "C" int lmc_qtensor_upload(uint32_t type, int rows, int cols, const void 
         return lmc_set_error(LMC_ERR_CUDA, "qtensor_upload: %s", cudaGetErrorString(e));
     }
     rc = lmc_tiled_build(t);
+    if (!rc) rc = lmc_gemm_prepare(t);
     if (rc) {
         lmc_qtensor_free(t);
         return rc;
@@ -152,6 +153,7 @@ extern "C" int lmc_qtensor_concat(const lmc_qtensor *const *parts, int n, lmc_qt
         return lmc_set_error(LMC_ERR_CUDA, "qtensor_concat: %s", cudaGetErrorString(e));
     }
     int rc = lmc_tiled_build(t);
+    if (!rc) rc = lmc_gemm_prepare(t);
     if (rc) { lmc_qtensor_free(t); return rc; }
     *out = t;
     return LMC_OK;
@@ -200,6 +202,9 @@ extern "C" int lmc_matmul(const lmc_qtensor *w, const float *d_x, int ldx, const
     if (!w) return lmc_set_error(LMC_ERR_INVALID, "matmul: null qtensor");
     int rc = check_mm(d_x, ldx, d_y, ldy, w->rows, w->cols, batch);
     if (rc) return rc;
+    // batch widths above the GEMV's 8 rows: the tensor-core GEMM
+    if (batch > 8 && w->gemm_wscale > 0.0f && !((uintptr_t)d_x & 15) && !(ldx & 3))
+        return lmc_gemm_launch(w, d_x, ldx, d_bias, d_y, ldy, batch, epi, NULL, lmc_stream(stream));
     if (w->tiled) return lmc_tiled_gemv_launch(w, d_x, ldx, d_bias, d_y, ldy, batch, epi, lmc_stream(stream));
     return lmc_gemv_generic_launch(w->type, w->blocks, w->rows, w->cols, d_x, ldx, d_bias, d_y, ldy, batch, epi,
                                    lmc_stream(stream));

@@ -26,6 +26,7 @@ struct lmc_qtensor {
     void *tiled;       /* device: row-tiled copy for the tensor-core GEMV, or NULL */
     size_t tiled_bytes;
     int tiled_rows;    /* rows padded to the tile height */
+    float gemm_wscale; /* power-of-two prescale of the fp16 weights in the batched GEMM (0: no GEMM) */
 };
 
 int lmc_set_error(int code, const char *fmt, ...);
@@ -53,6 +54,15 @@ typedef struct {
 } lmc_gemv_extra;
 int lmc_tiled_gemv_ex(const struct lmc_qtensor *t, const float *d_x, int ldx, const float *d_bias, float *d_y, int ldy,
                       int batch, int epi, const lmc_gemv_extra *ex, cudaStream_t s);
+/* Batched GEMM on the tcgen05 tensor cores (batch widths > 8; gemm_tc.cu).
+ * lmc_gemm_prepare sets t->gemm_wscale (needs cols % 64 == 0);
+ * lmc_gemm_reserve sizes the activation workspace (call before any capture);
+ * lmc_gemm_launch applies the prologue of `ex` (may be NULL) and the epilogue. */
+int lmc_gemm_prepare(struct lmc_qtensor *t);
+int lmc_gemm_reserve(int N, int K, cudaStream_t s);
+int lmc_gemm_launch(const struct lmc_qtensor *t, const float *d_x, int ldx, const float *d_bias, float *d_y, int ldy,
+                    int N, int epi, const lmc_gemv_extra *ex, cudaStream_t s);
+int lmc_gemm_status(void);
 /* Argmax over keys: reads each batch row's key (written by the fused
  * epilogue or by lmc_argmax_keys_launch), stores the row index in d_next and
  * resets the key to 0 for the next step. */

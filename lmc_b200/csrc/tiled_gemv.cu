@@ -930,10 +930,13 @@ __global__ void __launch_bounds__(NTHR, 2) k_gemv_tiled(TArgs a) {
 extern "C" int lmc_device_status(void) {
     int v = 0;
     LMC_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_tiled_timeout, sizeof(int)));
-    if (!v) return LMC_OK;
+    const int g = lmc_gemm_status();
+    if (g != LMC_OK && g != LMC_ERR_TIMEOUT) return g;
+    if (!v && g == LMC_OK) return LMC_OK;
     const int zero = 0;
     LMC_CUDA_TRY(cudaMemcpyToSymbol(g_tiled_timeout, &zero, sizeof(int)));
-    return lmc_set_error(LMC_ERR_TIMEOUT, "a kernel gave up a bounded wait (bulk copy not completed)");
+    return lmc_set_error(LMC_ERR_TIMEOUT, "a kernel gave up a bounded wait (%s)",
+                         v ? "bulk copy not completed" : "tensor-core MMA not completed");
 }
 
 static int qt_of(uint32_t type) { return type == LMC_TYPE_Q4_K ? 4 : type == LMC_TYPE_Q6_K ? 6 : 8; }
@@ -1141,6 +1144,7 @@ extern "C" int lmc_tiled_gemv_launch(const lmc_qtensor *t, const float *d_x, int
 
 extern "C" int lmc_tiled_gemv_ex(const lmc_qtensor *t, const float *d_x, int ldx, const float *d_bias, float *d_y,
                                  int ldy, int batch, int epi, const lmc_gemv_extra *ex, cudaStream_t s) {
+    if (batch > 8 && t->gemm_wscale > 0.0f) return lmc_gemm_launch(t, d_x, ldx, d_bias, d_y, ldy, batch, epi, ex, s);
     if (!t->tiled) return lmc_set_error(LMC_ERR_UNSUPPORTED, "gemv_ex: no tiled layout");
     if (((uintptr_t)d_x & 15) || (ldx & 3) || (ex->x2 && ((uintptr_t)ex->x2 & 15)) ||
         (ex->w && ((uintptr_t)ex->w & 15)) || (ex->b && ((uintptr_t)ex->b & 15)))

@@ -347,6 +347,10 @@ static int alloc_state(lmc_model *m) {
     TRY(dev_alloc((void **)&m->d_step, 16));
     CUTRY(cudaMallocHost((void **)&m->h_stage, 3 * sizeof(int) * B));
     CUTRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    if (B > 8) { /* the batched GEMM's activation workspace, sized before any graph capture */
+        const size_t kmax = D > F ? (D > QD ? D : QD) : (F > QD ? F : QD);
+        TRY(lmc_gemm_reserve((int)B, (int)kmax, m->stream));
+    }
     if (c->arch == 2) TRY(build_rope(m));
     return LMC_OK;
 }
@@ -411,12 +415,13 @@ int lmc_model_free(lmc_model *m) {
 /* and greedy ids in d_next.  Only kernel launches on m->stream (capturable). */
 /* ------------------------------------------------------------------------ */
 /* x -> norm -> W, as one tensor-core launch with the norm as its prologue
- * when W has the tiled layout, else a norm kernel and a plain matmul. */
+ * when W has the tiled layout (batch <= 8: the GEMV) or the batched GEMM
+ * applies (batch > 8), else a norm kernel and a plain matmul. */
 static int norm_matmul(lmc_model *m, const lmc_qtensor *W, int pro, const float *nw, const float *nb, float eps,
                        const float *bias, float *y, int ldy, int B, int epi, unsigned long long *keys) {
     const int D = m->cfg.embed_dim;
     cudaStream_t s = m->stream;
-    if (lmc_qtensor_has_tiled(W) && (keys == NULL || B <= 8)) {
+    if ((B > 8 && W->gemm_wscale > 0.0f) || (lmc_qtensor_has_tiled(W) && (keys == NULL || B <= 8))) {
         lmc_gemv_extra ex = {pro, nw, nb, NULL, eps, keys};
         return lmc_tiled_gemv_ex(W, m->x, D, bias, y, ldy, B, epi, &ex, s);
     }
@@ -476,7 +481,7 @@ static int step(lmc_model *m, int B) {
             TRY(lmc_attention_rope_launch(m->att, QD, q, ld ? ld : QD, k, v, ld ? ld : KVD, kc, vc, m->kv_dtype,
                                           m->d_pos, B, H, Hkv, Dh, S, m->ws, m->ws_bytes, m->rope_cos, m->rope_sin, s));
             TRY(lmc_matmul(w->o, m->att, QD, NULL, m->x, D, B, LMC_EPI_ACCUM, s));
-            if (w->gateup_cat && lmc_qtensor_has_tiled(w->down)) {
+            if (w->gateup_cat && (lmc_qtensor_has_tiled(w->down) || (B > 8 && w->down->gemm_wscale > 0.0f))) {
                 TRY(norm_matmul(m, w->gateup_cat, LMC_PRO_RMSNORM, w->rms_ffn, NULL, c->norm_eps, NULL, m->h, 2 * F,
                                 B, LMC_EPI_NONE, NULL));
                 lmc_gemv_extra ex = {LMC_PRO_SWIGLU, NULL, NULL, m->h + F, 0.0f, NULL};

@@ -101,7 +101,8 @@ def main():
     r = run(torch, qtype, a.rows, a.cols, a.batch, a.iters, generic=a.generic)
     peak, kind = hbm_peak()
     r.update({"type": a.type, "rows": a.rows, "cols": a.cols, "batch": a.batch, "peak_gbs": peak,
-              "frac": r["gbs"] / peak, "peak_kind": kind})
+              "frac": r["gbs"] / peak, "peak_kind": kind,
+              "tflops": 2.0 * a.rows * a.cols * a.batch / (r["ms"] * 1e-3) / 1e12})
     print(json.dumps(r), flush=True)
 
 

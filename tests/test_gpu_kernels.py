@@ -122,6 +122,48 @@ def test_gemv_tiled_shapes(cuda, orc, t, M, K, B):
     assert rt.lib().lmc_device_status() == 0
 
 
+# Batched GEMM on the tcgen05 tensor cores (batch widths above the GEMV's 8
+# rows).  The weights enter as fp16 (relative rounding <= 2^-11) and x as fp16
+# hi + lo, fp32 accumulation: the norm-wise relative error is ~3e-4, checked
+# against the 1e-3 bound of the GEMV.
+GEMM_CASES = [(synth.Q4_K, 3072, 768, 64), (synth.Q6_K, 768, 3072, 64), (synth.Q8_0, 1000, 512, 200),
+              (synth.Q4_0, 6400, 1600, 16), (synth.Q5_1, 512, 1024, 512), (synth.Q3_K, 520, 1024, 9),
+              (synth.Q5_K, 640, 2048, 100), (synth.IQ4_XS, 384, 1024, 64), (synth.F16, 256, 512, 33),
+              (synth.Q2_K, 256, 768, 24), (synth.IQ3_XXS, 300, 512, 40), (synth.Q4_1, 256, 4096, 130)]
+
+
+@pytest.mark.parametrize("t,M,K,N", GEMM_CASES, ids=lambda v: str(v))
+def test_gemm(cuda, orc, t, M, K, N):
+    rng = np.random.default_rng(M + 3 * K + N)
+    blk = synth.random_blocks(t, M * K, seed=M + K)
+    x = rng.normal(0, 1, (N, K)).astype(np.float32)
+    bias = rng.normal(0, 1, M).astype(np.float32)
+    want = ref_gemv(orc, t, blk, M, K, x, bias)
+    q = rt.QTensor(t, M, K, blk)
+    y = cuda.empty((N, M), dtype=cuda.float32, device="cuda")
+    dx, db = dev(cuda, x), dev(cuda, bias)
+    q.matmul(dx, y, batch=N, bias=db)
+    assert rel_err(y.cpu().numpy(), want) < RTOL
+    assert rt.lib().lmc_device_status() == 0
+
+
+def test_gemm_epilogues(cuda, orc):
+    t, M, K, N = synth.Q4_K, 640, 1024, 24
+    rng = np.random.default_rng(5)
+    blk = synth.random_blocks(t, M * K, seed=5)
+    x = rng.normal(0, 1, (N, K)).astype(np.float32)
+    bias = rng.normal(0, 1, M).astype(np.float32)
+    base = ref_gemv(orc, t, blk, M, K, x, bias)
+    q = rt.QTensor(t, M, K, blk)
+    y = cuda.empty((N, M), dtype=cuda.float32, device="cuda")
+    q.matmul(dev(cuda, x), y, batch=N, bias=dev(cuda, bias), epilogue=rt.EPI_GELU)
+    assert rel_err(y.cpu().numpy(), orc.gelu(base)) < RTOL
+    resid = rng.normal(0, 1, (N, M)).astype(np.float32)
+    y = dev(cuda, resid)
+    q.matmul(dev(cuda, x), y, batch=N, bias=dev(cuda, bias), epilogue=rt.EPI_ACCUM)
+    assert rel_err(y.cpu().numpy(), resid + base) < RTOL
+
+
 def test_gemv_epilogues(cuda, orc):
     t, M, K, B = synth.Q4_K, 512, 1024, 2
     rng = np.random.default_rng(3)
