@@ -1,0 +1,90 @@
+"""Whole-model throughput on one GPU: batched prompt feed + greedy decode
+through lmc_model_generate (one CUDA-graph launch per step for the whole
+batch), for the model shapes of the workloads:
+
+    python -m lmc_b200.modelbench --model tinyllama --batch 64 --prompt 512 --gen 256
+    python -m lmc_b200.modelbench --model llama8b --batch 1 --prompt 1024 --gen 64
+
+Weights: seeded random blocks of the named formats (Q4_K matrices, Q6_K
+output and token embedding), written as GGUF into --dir once.  Prompts are
+uniform random ids.  The prompt is fed one position per step for all
+sequences (LMc's token-by-token prefill), so a step is one forward of
+`batch` tokens; batches above 8 rows run their projections on the
+tcgen05 GEMM.  Prints one JSON line: prompt-feed and decode tokens/s (host
+clock around synchronised runs, second of two identical runs).
+"""
+import argparse
+import json
+import os
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from lmc_b200 import runtime as rt  # noqa: E402
+from lmc_b200 import synth  # noqa: E402
+
+SHAPES = {
+    # TinyLlama-1.1B architecture: 22 x 2048, FFN 5632, 32 / 4 heads, vocab 32000
+    "tinyllama": dict(kind="llama", L=22, D=2048, H=32, Hkv=4, F=5632, S=2048, V=32000),
+    # Llama-style 8B shape: 32 x 4096, FFN 14336, 32 / 8 heads, vocab 128256, ctx 4096
+    "llama8b": dict(kind="llama", L=32, D=4096, H=32, Hkv=8, F=14336, S=4096, V=128256),
+    # GPT-2 Small: 12 x 768, 12 heads, vocab 50257, ctx 1024
+    "gpt2": dict(kind="gpt2", L=12, D=768, H=12, S=1024, V=50257),
+}
+
+
+def model_file(name, directory):
+    kw = dict(SHAPES[name])
+    kind = kw.pop("kind")
+    if kind == "llama":
+        kw["blocks"] = "random"
+    return synth.cached_model(kind, directory, **kw)
+
+
+def run(name, batch, n_prompt, n_gen, kv, directory):
+    import torch
+    path = model_file(name, directory)
+    torch.cuda.set_device(0)
+    rt.init(0)
+    m = rt.Model(path, max_batch=batch, kv_dtype=rt.KV_F16 if kv == "f16" else rt.KV_F32)
+    rng = np.random.default_rng(0)
+    prompts = rng.integers(0, m.cfg.vocab_size, (batch, n_prompt)).astype(np.int32)
+
+    def timed(n_new):
+        m.generate(prompts, n_new)  # captures this shape's step graph
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        m.generate(prompts, n_new)
+        torch.cuda.synchronize()
+        return time.perf_counter() - t0
+
+    t_feed = timed(1)        # n_prompt steps
+    t_all = timed(n_gen)     # n_prompt + n_gen - 1 steps
+    t_dec = max(t_all - t_feed, 1e-9)
+    res = {"model": name, "batch": batch, "prompt": n_prompt, "gen": n_gen, "kv": kv,
+           "prompt_tok_s": batch * n_prompt / t_feed, "decode_tok_s": batch * (n_gen - 1) / t_dec,
+           "ms_per_step_prompt": 1e3 * t_feed / n_prompt, "ms_per_step_decode": 1e3 * t_dec / max(n_gen - 1, 1),
+           "graph_kernels_per_step": m.graph_kernels(), "weights_bytes": os.path.getsize(path)}
+    m.close()
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", choices=sorted(SHAPES), default="tinyllama")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--gen", type=int, default=256)
+    ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
+    ap.add_argument("--dir", default=os.environ.get("LMC_BENCH_DIR", "/tmp/lmc_models"))
+    a = ap.parse_args()
+    print(json.dumps(run(a.model, a.batch, a.prompt, a.gen, a.kv, a.dir)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

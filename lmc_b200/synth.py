@@ -250,26 +250,37 @@ def make_gpt2(path, L=12, D=768, H=12, S=1024, V=50257, F=None, seed=0,
 
 
 def make_llama(path, L=22, D=2048, H=32, Hkv=4, F=5632, S=2048, V=32000, theta=10000.0,
-               eps=1e-5, seed=0, wtype=Q4_K, out_type=Q6_K, emb_type=Q6_K, std=0.02):
-    """LLaMA-architecture GGUF: RMSNorm, RoPE, GQA, SwiGLU; weights
-    N(0, std) then quantized; RMS weights 1 + N(0, std)."""
+               eps=1e-5, seed=0, wtype=Q4_K, out_type=Q6_K, emb_type=Q6_K, std=0.02, blocks="quantized"):
+    """LLaMA-architecture GGUF: RMSNorm, RoPE, GQA, SwiGLU; RMS weights
+    1 + N(0, std).  blocks="quantized": matrices N(0, std) then quantized;
+    blocks="random": matrices are random blocks (uniform codes, fp16 scales
+    |N(0, 1e-3)|, as random_blocks) -- the same bytes per weight, written in
+    seconds for the billion-parameter shapes used by the throughput runs."""
     rng = np.random.default_rng(seed)
     nrm = lambda *s: rng.normal(0.0, std, s).astype(np.float32)
+    salt = [0]
+
+    def mat(t, rows, cols):
+        if blocks == "random":
+            salt[0] += 1
+            return random_blocks(t, rows * cols, seed=seed * 7919 + salt[0])[:tensor_bytes(t, rows * cols)]
+        return _q(t, nrm(rows, cols))
+
     Dh = D // H
-    T = [("token_embd.weight", (D, V), emb_type, _q(emb_type, nrm(V, D)))]
+    T = [("token_embd.weight", (D, V), emb_type, mat(emb_type, V, D))]
     for l in range(L):
         p = f"blk.{l}."
         T += [(p + "attn_norm.weight", (D,), F32, _q(F32, 1.0 + nrm(D))),
-              (p + "attn_q.weight", (D, H * Dh), wtype, _q(wtype, nrm(H * Dh, D))),
-              (p + "attn_k.weight", (D, Hkv * Dh), wtype, _q(wtype, nrm(Hkv * Dh, D))),
-              (p + "attn_v.weight", (D, Hkv * Dh), wtype, _q(wtype, nrm(Hkv * Dh, D))),
-              (p + "attn_output.weight", (D, D), wtype, _q(wtype, nrm(D, D))),
+              (p + "attn_q.weight", (D, H * Dh), wtype, mat(wtype, H * Dh, D)),
+              (p + "attn_k.weight", (D, Hkv * Dh), wtype, mat(wtype, Hkv * Dh, D)),
+              (p + "attn_v.weight", (D, Hkv * Dh), wtype, mat(wtype, Hkv * Dh, D)),
+              (p + "attn_output.weight", (D, D), wtype, mat(wtype, D, D)),
               (p + "ffn_norm.weight", (D,), F32, _q(F32, 1.0 + nrm(D))),
-              (p + "ffn_gate.weight", (D, F), wtype, _q(wtype, nrm(F, D))),
-              (p + "ffn_up.weight", (D, F), wtype, _q(wtype, nrm(F, D))),
-              (p + "ffn_down.weight", (F, D), wtype, _q(wtype, nrm(D, F)))]
+              (p + "ffn_gate.weight", (D, F), wtype, mat(wtype, F, D)),
+              (p + "ffn_up.weight", (D, F), wtype, mat(wtype, F, D)),
+              (p + "ffn_down.weight", (F, D), wtype, mat(wtype, D, F))]
     T += [("output_norm.weight", (D,), F32, _q(F32, 1.0 + nrm(D))),
-          ("output.weight", (D, V), out_type, _q(out_type, nrm(V, D)))]
+          ("output.weight", (D, V), out_type, mat(out_type, V, D))]
     meta = {"llama.block_count": L, "llama.attention.head_count": H, "llama.attention.head_count_kv": Hkv,
             "llama.embedding_length": D, "llama.feed_forward_length": F, "llama.context_length": S,
             "llama.vocab_size": V}
