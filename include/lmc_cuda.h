@@ -184,6 +184,21 @@ typedef struct {
 } lmc_model_config;
 
 int lmc_model_load(const char *gguf_path, int max_batch, int kv_dtype, lmc_model **out);
+/* Tensor-parallel shard tp_rank of tp_size (LLaMA; one process per GPU, the
+ * caller selects the device first).  No counterpart in LMc, which runs on
+ * one CPU: q/k/v rows by heads (attention local to a rank), ffn gate/up rows
+ * and the lm_head vocabulary split by rows, attn_output and ffn_down split by
+ * columns; each layer sums the ranks' partial residual with one NCCL
+ * all-reduce after attn_output and one after ffn_down (NVLink), and the
+ * greedy pick is an all-reduce max of 64-bit (logit, index) keys.  nccl_id:
+ * 128 bytes from lmc_nccl_unique_id on one rank, given to all.  Every rank
+ * makes the same calls (forward / generate) in the same order.  h_logits of
+ * lmc_model_forward then receives batch x vocab_rows (this rank's slice,
+ * lmc_model_shard). */
+int lmc_nccl_unique_id(void *nccl_id_128);
+int lmc_model_load_tp(const char *gguf_path, int max_batch, int kv_dtype, int tp_rank, int tp_size,
+                      const void *nccl_id_128, lmc_model **out);
+int lmc_model_shard(const lmc_model *m, int *tp_rank, int *tp_size, int *vocab_begin, int *vocab_rows);
 int lmc_model_get_config(const lmc_model *m, lmc_model_config *cfg);
 int lmc_model_free(lmc_model *m);
 /* model_forward (src/ops.c:212-237, src/ops_llama.c:157-192) for `batch`

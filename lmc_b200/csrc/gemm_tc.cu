@@ -48,6 +48,7 @@ struct GArgs {
     float *y;
     int ldy, epi;
     unsigned long long *keys;
+    int key_base;  // global index of row 0 in the keys
     int BN, MT, CL, nkb;
     const uint8_t *wt;  // tiled copy (16-row x 256-column units), or NULL
     int RT, KBU;        // row tiles and unit columns of the tiled copy
@@ -136,7 +137,7 @@ __device__ __forceinline__ void epi_store(const GArgs &a, int n, int m, float v)
     if (a.epi & LMC_EPI_GELU) v = lmc_gelu_f(v);
     float *o = a.y + (size_t)n * a.ldy + m;
     *o = (a.epi & LMC_EPI_ACCUM) ? *o + v : v;
-    if (a.keys) atomicMax(a.keys + n, lmc_argmax_key(v, m));
+    if (a.keys) atomicMax(a.keys + n, lmc_argmax_key(v, m + a.key_base));
 }
 
 // Accumulator (TMEM lanes = tile rows, columns = tokens) -> Y.  Warp w reads
@@ -847,7 +848,7 @@ extern "C" int lmc_gemm_launch(const lmc_qtensor *t, const float *d_x, int ldx, 
                ex ? ex->eps : 0.0f, g_xh, g_xl, g_xinv, fast ? 1 : 0,
                fast && t->type == LMC_TYPE_Q4_K ? g_xsh : (__half *)NULL,
                fast && t->type == LMC_TYPE_Q4_K ? g_xsl : (__half *)NULL, N, Npad);
-    GArgs a;
+    GArgs a = {};
     a.w = (const uint8_t *)t->blocks;
     a.M = M;
     a.K = K;
@@ -862,6 +863,7 @@ extern "C" int lmc_gemm_launch(const lmc_qtensor *t, const float *d_x, int ldx, 
     a.ldy = ldy;
     a.epi = epi;
     a.keys = ex ? ex->keys : NULL;
+    a.key_base = ex ? ex->key_base : 0;
     a.MT = (M + BM - 1) / BM;
     a.wt = (const uint8_t *)t->tiled;
     a.RT = t->tiled_rows / 16;

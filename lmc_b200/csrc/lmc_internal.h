@@ -50,7 +50,8 @@ typedef struct {
     int pro;
     const float *w, *b, *x2;
     float eps;
-    unsigned long long *keys; /* non-NULL: atomicMax of lmc_argmax_key(y, row) per batch row */
+    unsigned long long *keys; /* non-NULL: atomicMax of lmc_argmax_key(y, row + key_base) per batch row */
+    int key_base;             /* global index of row 0 (a vocabulary shard of the lm_head) */
 } lmc_gemv_extra;
 int lmc_tiled_gemv_ex(const struct lmc_qtensor *t, const float *d_x, int ldx, const float *d_bias, float *d_y, int ldy,
                       int batch, int epi, const lmc_gemv_extra *ex, cudaStream_t s);

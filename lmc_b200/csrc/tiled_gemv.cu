@@ -199,6 +199,7 @@ struct TArgs {
     const float *pw, *pb, *x2;
     float eps;
     unsigned long long *keys;  // non-NULL: greedy-pick key per batch row (argmax epilogue)
+    int key_base;              // global index of row 0 in the keys
     int XL;      // B-fragment lanes stored per chunk: 12 per batch row (3 limbs x 4), 24 for two
     int CL;      // CTAs per cluster
     int NC;      // clusters; cluster c owns row tiles [c*RT/NC, (c+1)*RT/NC)
@@ -584,7 +585,7 @@ __device__ __forceinline__ void epilogue(const TArgs &a, int b, int row, float v
     if (a.epi & LMC_EPI_GELU) v = lmc_gelu_f(v);
     float *o = a.y + (size_t)b * a.ldy + row;
     *o = (a.epi & LMC_EPI_ACCUM) ? *o + v : v;
-    if (a.keys) atomicMax(a.keys + b, lmc_argmax_key(v, row));
+    if (a.keys) atomicMax(a.keys + b, lmc_argmax_key(v, row + a.key_base));
 }
 
 // Byte i of w, zero-extended / sign-extended (one PRMT each).
@@ -1138,7 +1139,7 @@ extern "C" int lmc_tiled_gemv_launch(const lmc_qtensor *t, const float *d_x, int
                                      int ldy, int batch, int epi, cudaStream_t s) {
     if (((uintptr_t)d_x & 15) || (ldx & 3))  // float4 activation loads
         return lmc_gemv_generic_launch(t->type, t->blocks, t->rows, t->cols, d_x, ldx, d_bias, d_y, ldy, batch, epi, s);
-    lmc_gemv_extra ex = {LMC_PRO_NONE, NULL, NULL, NULL, 0.0f, NULL};
+    lmc_gemv_extra ex = {LMC_PRO_NONE, NULL, NULL, NULL, 0.0f, NULL, 0};
     return lmc_tiled_gemv_ex(t, d_x, ldx, d_bias, d_y, ldy, batch, epi, &ex, s);
 }
 
@@ -1162,6 +1163,7 @@ extern "C" int lmc_tiled_gemv_ex(const lmc_qtensor *t, const float *d_x, int ldx
     a.pw = ex->w;
     a.pb = ex->b;
     a.eps = ex->eps;
+    a.key_base = ex->key_base;
     for (int b0 = 0; b0 < batch;) {
         int nb = std::min(batch - b0, 8);
         Plan P;

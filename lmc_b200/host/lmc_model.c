@@ -16,6 +16,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <nccl.h>
+
 #include "../csrc/lmc_internal.h"
 
 typedef struct {
@@ -49,6 +51,12 @@ struct lmc_model {
     cudaGraphExec_t gexec;
     int g_batch, g_nprompt, g_nnew; /* shape the captured graph was built for */
     int g_kernels;                  /* kernel nodes in the captured step graph */
+    /* tensor-parallel shard (tp_size 1: the whole model on this GPU).  This
+     * rank holds heads [rank hl, +hl) with their kv heads, ffn rows
+     * [rank fl, +fl) of gate / up (columns of down), attn_output columns of
+     * its heads, and lm_head rows [v0, v0 + vl). */
+    int tp_rank, tp_size, hl, hkvl, fl, vl, v0;
+    ncclComm_t comm;
 };
 
 #define TRY(expr)                     \
@@ -125,6 +133,39 @@ static int upload_mat(const TInfo *t, const unsigned char *data, size_t fsz, int
     return lmc_qtensor_upload(t->type, rows, cols, data + t->off, bytes, out);
 }
 
+/* Rows [r0, r0 + nr) of a row-major block matrix (rows must not share blocks). */
+static int upload_rows(const TInfo *t, const unsigned char *data, size_t fsz, int rows, int cols, int r0, int nr,
+                       lmc_qtensor **out) {
+    size_t bytes, rb;
+    TRY(lmc_tensor_bytes(t->type, (size_t)t->n, &bytes));
+    if ((int64_t)t->n != (int64_t)rows * cols || (t->nd >= 2 && (t->dims[0] != (uint64_t)cols || t->dims[1] != (uint64_t)rows)))
+        return lmc_set_error(LMC_ERR_IO, "tensor %s: shape mismatch (expected %d x %d)", t->name, rows, cols);
+    if (t->off + bytes > fsz) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
+    if (lmc_tensor_bytes(t->type, (size_t)cols, &rb))
+        return lmc_set_error(LMC_ERR_UNSUPPORTED, "tensor %s: rows share blocks, cannot shard by rows", t->name);
+    return lmc_qtensor_upload(t->type, nr, cols, data + t->off + (size_t)r0 * rb, (size_t)nr * rb, out);
+}
+
+/* Columns [c0, c0 + nc) of every row (block-aligned). */
+static int upload_cols(const TInfo *t, const unsigned char *data, size_t fsz, int rows, int cols, int c0, int nc,
+                       lmc_qtensor **out) {
+    size_t bytes, rb, cb0, cbn;
+    TRY(lmc_tensor_bytes(t->type, (size_t)t->n, &bytes));
+    if ((int64_t)t->n != (int64_t)rows * cols || (t->nd >= 2 && (t->dims[0] != (uint64_t)cols || t->dims[1] != (uint64_t)rows)))
+        return lmc_set_error(LMC_ERR_IO, "tensor %s: shape mismatch (expected %d x %d)", t->name, rows, cols);
+    if (t->off + bytes > fsz) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
+    if (lmc_tensor_bytes(t->type, (size_t)cols, &rb) || lmc_tensor_bytes(t->type, (size_t)c0, &cb0) ||
+        lmc_tensor_bytes(t->type, (size_t)nc, &cbn))
+        return lmc_set_error(LMC_ERR_UNSUPPORTED, "tensor %s: column shard [%d, %d) is not block-aligned", t->name, c0,
+                             c0 + nc);
+    unsigned char *buf = (unsigned char *)malloc((size_t)rows * cbn + 1);
+    if (!buf) return lmc_set_error(LMC_ERR_OOM, "column shard of %s", t->name);
+    for (int r = 0; r < rows; r++) memcpy(buf + (size_t)r * cbn, data + t->off + (size_t)r * rb + cb0, cbn);
+    int rc = lmc_qtensor_upload(t->type, rows, nc, buf, (size_t)rows * cbn, out);
+    free(buf);
+    return rc;
+}
+
 static int dev_alloc(void **p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
     if (e != cudaSuccess) return lmc_set_error(LMC_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
@@ -139,7 +180,9 @@ static int bind_tensor(lmc_model *m, const TInfo *t, const unsigned char *data, 
     const char *nm = t->name;
     if (!strcmp(nm, "token_embd.weight")) return upload_mat(t, data, fsz, V, D, &m->wte);
     if (!strcmp(nm, "position_embd.weight")) return ll ? 0 : upload_vec(t, data, fsz, S * D, &m->wpe);
-    if (!strcmp(nm, "output.weight")) return upload_mat(t, data, fsz, V, D, &m->lm_head);
+    if (!strcmp(nm, "output.weight"))
+        return m->tp_size > 1 ? upload_rows(t, data, fsz, V, D, m->v0, m->vl, &m->lm_head)
+                              : upload_mat(t, data, fsz, V, D, &m->lm_head);
     if (!strcmp(nm, "output_norm.weight")) return upload_vec(t, data, fsz, D, ll ? &m->rmsf : &m->lnf_w);
     if (!strcmp(nm, "output_norm.bias")) return ll ? 0 : upload_vec(t, data, fsz, D, &m->lnf_b);
     if (strncmp(nm, "blk.", 4)) return 0;
@@ -163,12 +206,26 @@ static int bind_tensor(lmc_model *m, const TInfo *t, const unsigned char *data, 
         if (!strcmp(r, "ffn_down.weight")) return upload_mat(t, data, fsz, D, F, &w->fc2);
         if (!strcmp(r, "ffn_down.bias")) return upload_vec(t, data, fsz, D, &w->fc2_b);
     } else {
+        const int Dh = c->head_dim, tr = m->tp_rank;
         if (!strcmp(r, "attn_norm.weight")) return upload_vec(t, data, fsz, D, &w->rms_attn);
+        if (!strcmp(r, "ffn_norm.weight")) return upload_vec(t, data, fsz, D, &w->rms_ffn);
+        if (m->tp_size > 1) { /* this rank's shard (see struct lmc_model) */
+            if (!strcmp(r, "attn_q.weight")) return upload_rows(t, data, fsz, QD, D, tr * m->hl * Dh, m->hl * Dh, &w->q);
+            if (!strcmp(r, "attn_k.weight"))
+                return upload_rows(t, data, fsz, KV, D, tr * m->hkvl * Dh, m->hkvl * Dh, &w->k);
+            if (!strcmp(r, "attn_v.weight"))
+                return upload_rows(t, data, fsz, KV, D, tr * m->hkvl * Dh, m->hkvl * Dh, &w->v);
+            if (!strcmp(r, "attn_output.weight"))
+                return upload_cols(t, data, fsz, D, QD, tr * m->hl * Dh, m->hl * Dh, &w->o);
+            if (!strcmp(r, "ffn_gate.weight")) return upload_rows(t, data, fsz, F, D, tr * m->fl, m->fl, &w->gate);
+            if (!strcmp(r, "ffn_up.weight")) return upload_rows(t, data, fsz, F, D, tr * m->fl, m->fl, &w->up);
+            if (!strcmp(r, "ffn_down.weight")) return upload_cols(t, data, fsz, D, F, tr * m->fl, m->fl, &w->down);
+            return 0;
+        }
         if (!strcmp(r, "attn_q.weight")) return upload_mat(t, data, fsz, QD, D, &w->q);
         if (!strcmp(r, "attn_k.weight")) return upload_mat(t, data, fsz, KV, D, &w->k);
         if (!strcmp(r, "attn_v.weight")) return upload_mat(t, data, fsz, KV, D, &w->v);
         if (!strcmp(r, "attn_output.weight")) return upload_mat(t, data, fsz, D, QD, &w->o);
-        if (!strcmp(r, "ffn_norm.weight")) return upload_vec(t, data, fsz, D, &w->rms_ffn);
         if (!strcmp(r, "ffn_gate.weight")) return upload_mat(t, data, fsz, F, D, &w->gate);
         if (!strcmp(r, "ffn_up.weight")) return upload_mat(t, data, fsz, F, D, &w->up);
         if (!strcmp(r, "ffn_down.weight")) return upload_mat(t, data, fsz, D, F, &w->down);
@@ -263,6 +320,21 @@ static int load(lmc_model *m, const char *path) {
     if (!c->ffn_dim) c->ffn_dim = 4 * c->embed_dim;
     c->head_dim = c->embed_dim / c->n_heads;
     if (c->n_heads % c->n_kv_heads) { rc = lmc_set_error(LMC_ERR_IO, "%s: heads %d not a multiple of kv heads %d", path, c->n_heads, c->n_kv_heads); goto done; }
+    /* shard geometry (tensor parallel: LLaMA only, whole heads per rank) */
+    m->hl = c->n_heads; m->hkvl = c->n_kv_heads; m->fl = c->ffn_dim; m->vl = c->vocab_size; m->v0 = 0;
+    if (m->tp_size > 1) {
+        const int N = m->tp_size;
+        if (c->arch != 2) { rc = lmc_set_error(LMC_ERR_UNSUPPORTED, "tensor parallel: LLaMA models only"); goto done; }
+        if (c->n_heads % N || c->n_kv_heads % N || c->ffn_dim % N) {
+            rc = lmc_set_error(LMC_ERR_UNSUPPORTED, "tensor parallel: heads %d / kv heads %d / ffn %d not divisible by %d",
+                               c->n_heads, c->n_kv_heads, c->ffn_dim, N);
+            goto done;
+        }
+        m->hl = c->n_heads / N; m->hkvl = c->n_kv_heads / N; m->fl = c->ffn_dim / N;
+        const int vr = (c->vocab_size + N - 1) / N;
+        m->v0 = m->tp_rank * vr;
+        m->vl = c->vocab_size - m->v0 < vr ? c->vocab_size - m->v0 : vr;
+    }
     m->layers = (Layer *)calloc((size_t)c->n_layers, sizeof(Layer));
     ti = (TInfo *)calloc((size_t)nt ? (size_t)nt : 1, sizeof(TInfo));
     if (!m->layers || !ti) { rc = lmc_set_error(LMC_ERR_OOM, "host tables"); goto done; }
@@ -328,7 +400,7 @@ static int alloc_state(lmc_model *m) {
     const size_t B = (size_t)m->max_batch, D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size;
     const size_t QD = (size_t)c->n_heads * c->head_dim, KV = (size_t)c->n_kv_heads * c->head_dim;
     const size_t esz = m->kv_dtype == LMC_KV_F16 ? 2 : 4;
-    m->kv_layer_elems = B * KV * (size_t)c->seq_len;
+    m->kv_layer_elems = B * (size_t)m->hkvl * c->head_dim * (size_t)c->seq_len;  /* this rank's kv heads */
     TRY(dev_alloc(&m->kc, esz * m->kv_layer_elems * c->n_layers));
     TRY(dev_alloc(&m->vc, esz * m->kv_layer_elems * c->n_layers));
     TRY(dev_alloc((void **)&m->x, 4 * B * D));
@@ -355,16 +427,36 @@ static int alloc_state(lmc_model *m) {
     return LMC_OK;
 }
 
-int lmc_model_load(const char *path, int max_batch, int kv_dtype, lmc_model **out) {
+int lmc_nccl_unique_id(void *id) {
+    if (!id) return lmc_set_error(LMC_ERR_INVALID, "nccl_unique_id: null");
+    ncclUniqueId u;
+    ncclResult_t r = ncclGetUniqueId(&u);
+    if (r != ncclSuccess) return lmc_set_error(LMC_ERR_CUDA, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+    memcpy(id, &u, sizeof u);
+    return LMC_OK;
+}
+
+static int model_load(const char *path, int max_batch, int kv_dtype, int tp_rank, int tp_size, const void *nccl_id,
+                      lmc_model **out) {
     if (!path || !out || max_batch <= 0) return lmc_set_error(LMC_ERR_INVALID, "model_load: args");
     if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16) return lmc_set_error(LMC_ERR_INVALID, "model_load: kv dtype");
+    if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size || (tp_size > 1 && !nccl_id))
+        return lmc_set_error(LMC_ERR_INVALID, "model_load: shard %d of %d", tp_rank, tp_size);
     *out = NULL;
     lmc_model *m = (lmc_model *)calloc(1, sizeof(lmc_model));
     if (!m) return lmc_set_error(LMC_ERR_OOM, "model struct");
     m->max_batch = max_batch;
     m->kv_dtype = kv_dtype;
+    m->tp_rank = tp_rank;
+    m->tp_size = tp_size;
     int rc = load(m, path);
     if (!rc) rc = alloc_state(m);
+    if (!rc && tp_size > 1) { /* every rank of the group calls this (collective) */
+        ncclUniqueId u;
+        memcpy(&u, nccl_id, sizeof u);
+        ncclResult_t r = ncclCommInitRank(&m->comm, tp_size, u, tp_rank);
+        if (r != ncclSuccess) { m->comm = NULL; rc = lmc_set_error(LMC_ERR_CUDA, "ncclCommInitRank: %s", ncclGetErrorString(r)); }
+    }
     if (!rc && cudaDeviceSynchronize() != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "load sync");
     if (rc) {
         char msg[1024];
@@ -373,6 +465,24 @@ int lmc_model_load(const char *path, int max_batch, int kv_dtype, lmc_model **ou
         return lmc_set_error(rc, "%s", msg);
     }
     *out = m;
+    return LMC_OK;
+}
+
+int lmc_model_load(const char *path, int max_batch, int kv_dtype, lmc_model **out) {
+    return model_load(path, max_batch, kv_dtype, 0, 1, NULL, out);
+}
+
+int lmc_model_load_tp(const char *path, int max_batch, int kv_dtype, int tp_rank, int tp_size, const void *nccl_id,
+                      lmc_model **out) {
+    return model_load(path, max_batch, kv_dtype, tp_rank, tp_size, nccl_id, out);
+}
+
+int lmc_model_shard(const lmc_model *m, int *tp_rank, int *tp_size, int *vocab_begin, int *vocab_rows) {
+    if (!m) return lmc_set_error(LMC_ERR_INVALID, "model_shard: null");
+    if (tp_rank) *tp_rank = m->tp_rank;
+    if (tp_size) *tp_size = m->tp_size;
+    if (vocab_begin) *vocab_begin = m->v0;
+    if (vocab_rows) *vocab_rows = m->vl;
     return LMC_OK;
 }
 
@@ -386,7 +496,8 @@ void *lmc_model_device_buffer(lmc_model *m, int which) { return m && which == 0 
 
 int lmc_model_free(lmc_model *m) {
     if (!m) return LMC_OK;
-    if (m->gexec) cudaGraphExecDestroy(m->gexec);
+    if (m->gexec) cudaGraphExecDestroy(m->gexec); /* (it may hold the communicator's calls) */
+    if (m->comm) ncclCommDestroy(m->comm);
     if (m->layers) {
         for (int l = 0; l < m->cfg.n_layers; l++) {
             Layer *w = &m->layers[l];
@@ -422,14 +533,24 @@ static int norm_matmul(lmc_model *m, const lmc_qtensor *W, int pro, const float 
     const int D = m->cfg.embed_dim;
     cudaStream_t s = m->stream;
     if ((B > 8 && W->gemm_wscale > 0.0f) || (lmc_qtensor_has_tiled(W) && (keys == NULL || B <= 8))) {
-        lmc_gemv_extra ex = {pro, nw, nb, NULL, eps, keys};
+        lmc_gemv_extra ex = {pro, nw, nb, NULL, eps, keys, keys ? m->v0 : 0};
         return lmc_tiled_gemv_ex(W, m->x, D, bias, y, ldy, B, epi, &ex, s);
     }
+    if (keys && m->v0) return lmc_set_error(LMC_ERR_UNSUPPORTED, "sharded lm_head needs the tensor-core layout");
     if (pro == LMC_PRO_LAYERNORM) TRY(lmc_layer_norm(m->xn, m->x, nw, nb, D, B, s));
     else TRY(lmc_rms_norm(m->xn, m->x, nw, D, B, eps, s));
     TRY(lmc_matmul(W, m->xn, D, bias, y, ldy, B, epi, s));
     if (keys) TRY(lmc_argmax_keys_launch(y, W->rows, B, keys, s));
     return LMC_OK;
+}
+
+/* Sum of the ranks' partial x (tensor parallel): rank 0 added its partial to
+ * the residual, the others wrote theirs over it, so the in-place sum is the
+ * next residual on every rank. */
+static int tp_sum_x(lmc_model *m, int B) {
+    if (m->tp_size <= 1) return LMC_OK;
+    ncclResult_t r = ncclAllReduce(m->x, m->x, (size_t)B * m->cfg.embed_dim, ncclFloat32, ncclSum, m->comm, m->stream);
+    return r == ncclSuccess ? LMC_OK : lmc_set_error(LMC_ERR_CUDA, "ncclAllReduce: %s", ncclGetErrorString(r));
 }
 
 /* One decode step for B sequences: tokens d_tok, positions d_pos -> logits
@@ -440,8 +561,8 @@ static int norm_matmul(lmc_model *m, const lmc_qtensor *W, int pro, const float 
  * weights have the tensor-core layout. */
 static int step(lmc_model *m, int B) {
     const lmc_model_config *c = &m->cfg;
-    const int D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size, H = c->n_heads, Hkv = c->n_kv_heads;
-    const int Dh = c->head_dim, S = c->seq_len, QD = H * Dh, KVD = Hkv * Dh;
+    const int D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size, H = c->n_heads;
+    const int Dh = c->head_dim, S = c->seq_len;
     cudaStream_t s = m->stream;
     const size_t esz = m->kv_dtype == LMC_KV_F16 ? 2 : 4;
     TRY(lmc_embed_launch(m->wte->type, m->wte->blocks, c->arch == 1 ? m->wpe : NULL, m->d_tok, m->d_pos, D, V, S, B,
@@ -458,7 +579,9 @@ static int step(lmc_model *m, int B) {
             TRY(norm_matmul(m, w->fc, LMC_PRO_LAYERNORM, w->ln2_w, w->ln2_b, 1e-5f, w->fc_b, m->h, F, B, LMC_EPI_GELU,
                             NULL));
             TRY(lmc_matmul(w->fc2, m->h, F, w->fc2_b, m->x, D, B, LMC_EPI_ACCUM, s));
-        } else { /* src/ops_llama.c:165-187 */
+        } else { /* src/ops_llama.c:165-187 (this rank's heads and ffn rows when sharded) */
+            const int QD = m->hl * Dh, KVD = m->hkvl * Dh, F = m->fl, H = m->hl, Hkv = m->hkvl;
+            const int rp = m->tp_size > 1 && m->tp_rank > 0 ? LMC_EPI_NONE : LMC_EPI_ACCUM; /* residual add */
             const int LQ = QD + 2 * KVD;
             float *q = m->qkv, *k, *v;
             int ld;
@@ -480,27 +603,33 @@ static int step(lmc_model *m, int B) {
             /* RoPE on q and the new K row happens inside the attention kernel */
             TRY(lmc_attention_rope_launch(m->att, QD, q, ld ? ld : QD, k, v, ld ? ld : KVD, kc, vc, m->kv_dtype,
                                           m->d_pos, B, H, Hkv, Dh, S, m->ws, m->ws_bytes, m->rope_cos, m->rope_sin, s));
-            TRY(lmc_matmul(w->o, m->att, QD, NULL, m->x, D, B, LMC_EPI_ACCUM, s));
+            TRY(lmc_matmul(w->o, m->att, QD, NULL, m->x, D, B, rp, s));
+            TRY(tp_sum_x(m, B));
             if (w->gateup_cat && (lmc_qtensor_has_tiled(w->down) || (B > 8 && w->down->gemm_wscale > 0.0f))) {
                 TRY(norm_matmul(m, w->gateup_cat, LMC_PRO_RMSNORM, w->rms_ffn, NULL, c->norm_eps, NULL, m->h, 2 * F,
                                 B, LMC_EPI_NONE, NULL));
-                lmc_gemv_extra ex = {LMC_PRO_SWIGLU, NULL, NULL, m->h + F, 0.0f, NULL};
-                TRY(lmc_tiled_gemv_ex(w->down, m->h, 2 * F, NULL, m->x, D, B, LMC_EPI_ACCUM, &ex, s));
+                lmc_gemv_extra ex = {LMC_PRO_SWIGLU, NULL, NULL, m->h + F, 0.0f, NULL, 0};
+                TRY(lmc_tiled_gemv_ex(w->down, m->h, 2 * F, NULL, m->x, D, B, rp, &ex, s));
             } else {
                 TRY(lmc_rms_norm(m->xn, m->x, w->rms_ffn, D, B, c->norm_eps, s));
                 TRY(lmc_matmul(w->gate, m->xn, D, NULL, m->h, F, B, LMC_EPI_NONE, s));
                 TRY(lmc_matmul(w->up, m->xn, D, NULL, m->h2, F, B, LMC_EPI_NONE, s));
                 TRY(lmc_swiglu(m->h, m->h2, (size_t)B * F, s));
-                TRY(lmc_matmul(w->down, m->h, F, NULL, m->x, D, B, LMC_EPI_ACCUM, s));
+                TRY(lmc_matmul(w->down, m->h, F, NULL, m->x, D, B, rp, s));
             }
+            TRY(tp_sum_x(m, B));
         }
     }
     if (c->arch == 1)
         TRY(norm_matmul(m, m->lm_head, LMC_PRO_LAYERNORM, m->lnf_w, m->lnf_b, 1e-5f, NULL, m->logits, V, B,
                         LMC_EPI_NONE, m->d_keys));
     else
-        TRY(norm_matmul(m, m->lm_head, LMC_PRO_RMSNORM, m->rmsf, NULL, c->norm_eps, NULL, m->logits, V, B,
+        TRY(norm_matmul(m, m->lm_head, LMC_PRO_RMSNORM, m->rmsf, NULL, c->norm_eps, NULL, m->logits, m->vl, B,
                         LMC_EPI_NONE, m->d_keys));
+    if (m->tp_size > 1) { /* greedy pick over the vocabulary shards: max of the 64-bit keys */
+        ncclResult_t r = ncclAllReduce(m->d_keys, m->d_keys, (size_t)B, ncclUint64, ncclMax, m->comm, m->stream);
+        if (r != ncclSuccess) return lmc_set_error(LMC_ERR_CUDA, "ncclAllReduce(keys): %s", ncclGetErrorString(r));
+    }
     return LMC_OK;
 }
 
@@ -519,9 +648,9 @@ int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B
     CUTRY(cudaMemcpyAsync(m->d_pos, m->h_stage + B, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
     TRY(step(m, B));
     TRY(lmc_keys_to_ids_launch(m->d_keys, m->d_next, B, m->stream));
-    if (h_logits)
-        CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * (size_t)B * m->cfg.vocab_size,
-                              cudaMemcpyDeviceToHost, m->stream));
+    if (h_logits) /* [B][vocab rows of this rank] (the whole vocabulary without sharding) */
+        CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * (size_t)B * m->vl, cudaMemcpyDeviceToHost,
+                              m->stream));
     CUTRY(cudaMemcpyAsync(m->h_stage + 2 * B, m->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, m->stream));
     CUTRY(cudaStreamSynchronize(m->stream));
     if (h_next) memcpy(h_next, m->h_stage + 2 * B, sizeof(int) * B);

@@ -4,6 +4,11 @@ batch), for the model shapes of the workloads:
 
     python -m lmc_b200.modelbench --model tinyllama --batch 64 --prompt 512 --gen 256
     python -m lmc_b200.modelbench --model llama8b --batch 1 --prompt 1024 --gen 64
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m lmc_b200.modelbench --model llama8b --tp
+
+With --tp (under torchrun, one process per GPU) every rank loads its
+tensor-parallel shard (lmc_model_load_tp) and the times are the maximum
+over the ranks.
 
 Weights: seeded random blocks of the named formats (Q4_K matrices, Q6_K
 output and token embedding), written as GGUF into --dir once.  Prompts are
@@ -46,22 +51,47 @@ def model_file(name, directory):
     return synth.cached_model(kind, directory, **kw)
 
 
-def run(name, batch, n_prompt, n_gen, kv, directory):
+def run(name, batch, n_prompt, n_gen, kv, directory, tp=False):
     import torch
-    path = model_file(name, directory)
-    torch.cuda.set_device(0)
-    rt.init(0)
-    m = rt.Model(path, max_batch=batch, kv_dtype=rt.KV_F16 if kv == "f16" else rt.KV_F32)
+    dist, rank, world, dev = None, 0, 1, 0
+    if tp:
+        import datetime
+
+        import torch.distributed as dist
+        rank, world, dev = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+        torch.cuda.set_device(dev)
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    path = model_file(name, directory) if rank == 0 else None
+    if dist:
+        obj = [path]
+        dist.broadcast_object_list(obj, src=0)
+        path = obj[0]
+    torch.cuda.set_device(dev)
+    rt.init(dev)
+    kvd = rt.KV_F16 if kv == "f16" else rt.KV_F32
+    if dist:
+        from lmc_b200 import tp as tpm
+        nid = tpm.exchange_id(dist, rt.nccl_unique_id)
+        m = rt.Model(path, max_batch=batch, kv_dtype=kvd, tp=(rank, world, nid))
+    else:
+        m = rt.Model(path, max_batch=batch, kv_dtype=kvd)
     rng = np.random.default_rng(0)
     prompts = rng.integers(0, m.cfg.vocab_size, (batch, n_prompt)).astype(np.int32)
 
     def timed(n_new):
         m.generate(prompts, n_new)  # captures this shape's step graph
         torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
         t0 = time.perf_counter()
         m.generate(prompts, n_new)
         torch.cuda.synchronize()
-        return time.perf_counter() - t0
+        dt = time.perf_counter() - t0
+        if dist:  # the slowest rank
+            t = torch.tensor([dt])
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+        return dt
 
     t_feed = timed(1)        # n_prompt steps
     t_all = timed(n_gen)     # n_prompt + n_gen - 1 steps
@@ -69,9 +99,13 @@ def run(name, batch, n_prompt, n_gen, kv, directory):
     res = {"model": name, "batch": batch, "prompt": n_prompt, "gen": n_gen, "kv": kv,
            "prompt_tok_s": batch * n_prompt / t_feed, "decode_tok_s": batch * (n_gen - 1) / t_dec,
            "ms_per_step_prompt": 1e3 * t_feed / n_prompt, "ms_per_step_decode": 1e3 * t_dec / max(n_gen - 1, 1),
-           "graph_kernels_per_step": m.graph_kernels(), "weights_bytes": os.path.getsize(path)}
+           "graph_kernels_per_step": m.graph_kernels(), "weights_bytes": os.path.getsize(path),
+           "tensor_parallel": world}
     m.close()
-    return res
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res if rank == 0 else None
 
 
 def main():
@@ -82,8 +116,11 @@ def main():
     ap.add_argument("--gen", type=int, default=256)
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
     ap.add_argument("--dir", default=os.environ.get("LMC_BENCH_DIR", "/tmp/lmc_models"))
+    ap.add_argument("--tp", action="store_true", help="tensor parallel over the torchrun ranks")
     a = ap.parse_args()
-    print(json.dumps(run(a.model, a.batch, a.prompt, a.gen, a.kv, a.dir)), flush=True)
+    r = run(a.model, a.batch, a.prompt, a.gen, a.kv, a.dir, tp=a.tp)
+    if r is not None:
+        print(json.dumps(r), flush=True)
 
 
 if __name__ == "__main__":

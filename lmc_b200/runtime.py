@@ -43,6 +43,9 @@ SIGNATURES = {
     "lmc_attention_decode": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp], _i),
     "lmc_attention_decode_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _vp], _i),
     "lmc_model_load": ([_c.c_char_p, _i, _i, _c.POINTER(_vp)], _i),
+    "lmc_nccl_unique_id": ([_vp], _i),
+    "lmc_model_load_tp": ([_c.c_char_p, _i, _i, _i, _i, _vp, _c.POINTER(_vp)], _i),
+    "lmc_model_shard": ([_vp, _ip, _ip, _ip, _ip], _i),
     "lmc_model_get_config": ([_vp, _vp], _i),
     "lmc_model_free": ([_vp], _i),
     "lmc_model_forward": ([_vp, _ip, _ip, _i, _vp, _ip], _i),
@@ -135,23 +138,42 @@ class QTensor:
             pass
 
 
-class Model:
-    """A GGUF model loaded onto the device (lmc_model_load)."""
+def nccl_unique_id():
+    """128-byte NCCL group id (lmc_nccl_unique_id), made on one rank and
+    handed to every rank of a tensor-parallel group."""
+    buf = ctypes.create_string_buffer(128)
+    call("lmc_nccl_unique_id", ctypes.cast(buf, _vp))
+    return buf.raw
 
-    def __init__(self, path, max_batch=1, kv_dtype=KV_F32):
+
+class Model:
+    """A GGUF model loaded onto the device (lmc_model_load), or one
+    tensor-parallel shard of it when tp = (rank, size, nccl_id) is given
+    (lmc_model_load_tp; every rank of the group constructs its shard)."""
+
+    def __init__(self, path, max_batch=1, kv_dtype=KV_F32, tp=None):
         h = _vp()
-        call("lmc_model_load", path.encode(), max_batch, kv_dtype, ctypes.byref(h))
+        if tp is None:
+            call("lmc_model_load", path.encode(), max_batch, kv_dtype, ctypes.byref(h))
+        else:
+            rank, size, nid = tp
+            idbuf = ctypes.create_string_buffer(bytes(nid), 128)
+            call("lmc_model_load_tp", path.encode(), max_batch, kv_dtype, rank, size, ctypes.cast(idbuf, _vp),
+                 ctypes.byref(h))
         self.h = h
         self.cfg = ModelConfig()
         call("lmc_model_get_config", self.h, ctypes.byref(self.cfg))
         self.max_batch = max_batch
+        r, n, v0, vl = (ctypes.c_int() for _ in range(4))
+        call("lmc_model_shard", self.h, ctypes.byref(r), ctypes.byref(n), ctypes.byref(v0), ctypes.byref(vl))
+        self.tp_rank, self.tp_size, self.vocab_begin, self.vocab_rows = r.value, n.value, v0.value, vl.value
 
     def forward(self, tokens, positions, want_logits=True):
         import numpy as np
         tokens = np.ascontiguousarray(tokens, np.int32)
         positions = np.ascontiguousarray(positions, np.int32)
         B = tokens.size
-        logits = np.empty((B, self.cfg.vocab_size), np.float32) if want_logits else None
+        logits = np.empty((B, self.vocab_rows), np.float32) if want_logits else None
         nxt = np.empty(B, np.int32)
         call("lmc_model_forward", self.h, tokens.ctypes.data_as(_ip), positions.ctypes.data_as(_ip), B,
              None if logits is None else logits.ctypes.data, nxt.ctypes.data_as(_ip))
