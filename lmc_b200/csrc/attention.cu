@@ -8,7 +8,9 @@
 // covers CH positions and all G = H / Hkv query heads of its kv head, so each
 // K/V row is read from HBM once per group, not once per query head.  A split
 // writes (max, exp-sum, unnormalised accumulator) to the caller's workspace;
-// k_attn_combine merges the splits.  The CTA whose range holds `pos` first
+// k_attn_combine merges the splits -- or, with arrival counters (the model's
+// step), the last split CTA of each (sequence, kv head) to finish merges them
+// in the same launch.  The CTA whose range holds `pos` first
 // appends the new K/V row to the cache (rounded to the cache type, so the
 // step reads exactly what later steps will read).
 #include <cuda_fp16.h>
@@ -37,32 +39,82 @@ struct AttnArgs {
     // RoPE tables [S][Dh/2] (LLaMA, src/ops_llama.c:75-78) applied to q and to
     // the new K row here, or NULL
     const float *rope_cos, *rope_sin;
+    int *cnt;  // [batch][Hkv] arrival counters, zero between launches, or NULL (separate combine kernel)
 };
+
+template <typename KV>
+__device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp, int kh, int b, int pos, int t0, int t1,
+                                           float *wsb, size_t hstride);
 
 template <typename KV>
 __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
     extern __shared__ float sm[];
     const int sp = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int G = a.H / a.Hkv, Dh = a.Dh, CH = a.CH;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = ATT_THREADS / 32;
     pdl_wait();
     pdl_launch_dependents();
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.S) return;  // the host validates positions; never index outside the cache
     const int t0 = sp * CH, t1 = min(t0 + CH, pos + 1);
-    float *qs = sm;               // [G][Dh]
-    float *sc = sm + G * Dh;      // [G][CH]
-    float *ml = sc + G * CH;      // [G][2]
     float *wsb = a.ws + (((size_t)b * a.H + (size_t)kh * G) * a.nsplit + sp) * (Dh + 2);
     const size_t hstride = (size_t)a.nsplit * (Dh + 2);
-    if (t0 > pos) {  // empty split: mark it so the combine skips it
-        if (a.nsplit > 1)
+    if (t0 > pos) {  // empty split
+        if (a.nsplit > 1 && !a.cnt)  // mark it so the combine kernel skips it
             for (int g = threadIdx.x; g < G; g += ATT_THREADS) {
                 wsb[g * hstride + Dh] = -INFINITY;
                 wsb[g * hstride + Dh + 1] = 0.0f;
             }
         return;
     }
+    split_body<KV>(a, sm, sp, kh, b, pos, t0, t1, wsb, hstride);
+    if (!a.cnt || a.nsplit == 1) return;
+    // the last of the splits that hold positions (0..pos) to arrive merges
+    // them (as k_attn_combine); empty splits took no part
+    const int active = min(a.nsplit, pos / CH + 1);
+    if (active == 1) {  // the only split: normalise its own accumulator
+        __syncthreads();
+        for (int i = threadIdx.x; i < G * Dh; i += ATT_THREADS) {
+            const int g = i / Dh, d = i % Dh;
+            a.out[(size_t)b * a.ldo + ((size_t)kh * G + g) * Dh + d] = wsb[g * hstride + d] / wsb[g * hstride + Dh + 1];
+        }
+        return;
+    }
+    __shared__ int last;
+    __threadfence();  // this CTA's partials are visible to the merging CTA
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(a.cnt + (size_t)b * a.Hkv + kh, 1) == active - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < G * Dh; i += ATT_THREADS) {
+        const int g = i / Dh, d = i % Dh;
+        const float *w = a.ws + ((size_t)b * a.H + (size_t)kh * G + g) * hstride;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < active; s2++) M = fmaxf(M, __ldcg(w + s2 * (Dh + 2) + Dh));
+        float L = 0.0f, acc = 0.0f;
+        for (int s2 = 0; s2 < active; s2++) {
+            const float l = __ldcg(w + s2 * (Dh + 2) + Dh + 1);
+            if (l == 0.0f) continue;
+            const float f = expf(__ldcg(w + s2 * (Dh + 2) + Dh) - M);
+            L += l * f;
+            acc += __ldcg(w + s2 * (Dh + 2) + d) * f;
+        }
+        a.out[(size_t)b * a.ldo + ((size_t)kh * G + g) * Dh + d] = acc / L;
+    }
+    if (threadIdx.x == 0) a.cnt[(size_t)b * a.Hkv + kh] = 0;  // ready for the next step
+}
+
+// One non-empty split: append the new K/V row when it falls here, scores,
+// softmax statistics and the unnormalised accumulator (or the final output
+// when there is one split).
+template <typename KV>
+__device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp, int kh, int b, int pos, int t0, int t1,
+                                           float *wsb, size_t hstride) {
+    const int G = a.H / a.Hkv, Dh = a.Dh, CH = a.CH;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = ATT_THREADS / 32;
+    float *qs = sm;               // [G][Dh]
+    float *sc = sm + G * Dh;      // [G][CH]
+    float *ml = sc + G * CH;      // [G][2]
     KV *kc = reinterpret_cast<KV *>(a.k_cache) + ((size_t)b * a.Hkv + kh) * a.S * Dh;
     KV *vc = reinterpret_cast<KV *>(a.v_cache) + ((size_t)b * a.Hkv + kh) * a.S * Dh;
     const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (Dh / 2) : nullptr;
@@ -182,15 +234,15 @@ extern "C" size_t lmc_attention_workspace_bytes(int batch, int H, int Dh, int S)
 extern "C" int lmc_attention_launch(float *out, int ldo, const float *q, int ldq, const float *k_new,
                                     const float *v_new, int ldkv, void *k_cache, void *v_cache, int kv_dtype,
                                     const int *d_pos, int batch, int H, int Hkv, int Dh, int S, void *d_ws,
-                                    size_t ws_bytes, cudaStream_t s) {
+                                    size_t ws_bytes, int *d_cnt, cudaStream_t s) {
     return lmc_attention_rope_launch(out, ldo, q, ldq, k_new, v_new, ldkv, k_cache, v_cache, kv_dtype, d_pos, batch, H,
-                                     Hkv, Dh, S, d_ws, ws_bytes, NULL, NULL, s);
+                                     Hkv, Dh, S, d_ws, ws_bytes, NULL, NULL, d_cnt, s);
 }
 
 extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, int ldq, const float *k_new,
                                          const float *v_new, int ldkv, void *k_cache, void *v_cache, int kv_dtype,
                                          const int *d_pos, int batch, int H, int Hkv, int Dh, int S, void *d_ws,
-                                         size_t ws_bytes, const float *rope_cos, const float *rope_sin,
+                                         size_t ws_bytes, const float *rope_cos, const float *rope_sin, int *d_cnt,
                                          cudaStream_t s) {
     if (!out || !q || !k_new || !v_new || !k_cache || !v_cache || !d_pos)
         return lmc_set_error(LMC_ERR_INVALID, "attention: null pointer");
@@ -204,6 +256,7 @@ extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, in
     a.pos = d_pos; a.H = H; a.Hkv = Hkv; a.Dh = Dh; a.S = S;
     a.ldo = ldo; a.ldq = ldq; a.ldkv = ldkv;
     a.rope_cos = rope_cos; a.rope_sin = rope_sin;
+    a.cnt = d_cnt;
     attn_plan(S, &a.CH, &a.nsplit);
     const size_t need = lmc_attention_workspace_bytes(batch, H, Dh, S);
     if (need > ws_bytes || (need && !d_ws))
@@ -222,7 +275,7 @@ extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, in
             LMC_CUDA_TRY(cudaFuncSetAttribute(k_attn_split<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         LMC_LAUNCH("attention", k_attn_split<__half>, grid, ATT_THREADS, smem, s, a);
     }
-    if (a.nsplit > 1) {
+    if (a.nsplit > 1 && !d_cnt) {
         LMC_LAUNCH("attention combine", k_attn_combine, dim3(H, batch), Dh, 0, s, a);
     }
     return LMC_OK;
@@ -232,7 +285,7 @@ extern "C" int lmc_attention_decode(float *out, const float *q, const float *k_n
                                     void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, int batch,
                                     int H, int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes, void *stream) {
     return lmc_attention_launch(out, H * Dh, q, H * Dh, k_new, v_new, Hkv * Dh, k_cache, v_cache, kv_dtype, d_pos,
-                                batch, H, Hkv, Dh, S, d_ws, ws_bytes, lmc_stream(stream));
+                                batch, H, Hkv, Dh, S, d_ws, ws_bytes, NULL, lmc_stream(stream));
 }
 
 // ---------------------------------------------------------------------------
@@ -291,5 +344,5 @@ extern "C" int lmc_attention_decode_noalloc(float *out, const float *q, const fl
         scratch = g_attn_static_ptr[dev];
     }
     return lmc_attention_launch(out, H * Dh, q, H * Dh, k_new, v_new, Hkv * Dh, k_cache, v_cache, kv_dtype, d_pos,
-                                batch, H, Hkv, Dh, S, scratch, LMC_ATTN_STATIC_SCRATCH_BYTES, lmc_stream(stream));
+                                batch, H, Hkv, Dh, S, scratch, LMC_ATTN_STATIC_SCRATCH_BYTES, NULL, lmc_stream(stream));
 }

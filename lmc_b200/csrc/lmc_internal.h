@@ -75,16 +75,19 @@ int lmc_embed_launch(uint32_t type, const void *wte, const float *wpe, const int
  * own position d_pos[b], from [S][Dh/2] cos/sin tables. */
 int lmc_rope_pos_launch(float *v, int ld, int n_heads, int Dh, const float *cos_tab, const float *sin_tab,
                         const int *d_pos, int S, int batch, cudaStream_t s);
-/* Attention with explicit row strides for q/out (ldq) and k_new/v_new (ldkv). */
+/* Attention with explicit row strides for q/out (ldq) and k_new/v_new (ldkv).
+ * d_cnt: [batch][Hkv] arrival counters, zero before the first call, or NULL.
+ * With counters the last split CTA of each (sequence, kv head) merges the
+ * splits in the same launch (no separate combine kernel). */
 int lmc_attention_launch(float *out, int ldo, const float *q, int ldq, const float *k_new, const float *v_new,
                          int ldkv, void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, int batch, int H,
-                         int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes, cudaStream_t s);
+                         int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes, int *d_cnt, cudaStream_t s);
 /* Same, applying RoPE (src/ops_llama.c:39-48,75-78) from [S][Dh/2] tables to
  * q and to the new K row on the fly (no separate rope launch). */
 int lmc_attention_rope_launch(float *out, int ldo, const float *q, int ldq, const float *k_new, const float *v_new,
                               int ldkv, void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, int batch, int H,
                               int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes, const float *rope_cos,
-                              const float *rope_sin, cudaStream_t s);
+                              const float *rope_sin, int *d_cnt, cudaStream_t s);
 /* Generation bookkeeping after one step (see lmc_model_generate): the greedy
  * id of each sequence is read from (and reset in) d_keys. */
 int lmc_advance_launch(unsigned long long *d_keys, int *d_next, int *d_tok, int *d_pos, int *d_step,

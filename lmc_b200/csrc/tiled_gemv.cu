@@ -76,8 +76,6 @@ __device__ __forceinline__ void imma_k16(int (&d)[4], uint32_t a0, uint32_t a1, 
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
-__device__ __forceinline__ int ubyte(uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xFFu); }
-__device__ __forceinline__ int sbyte(uint32_t w, int i) { return (int)(int8_t)((w >> (8 * i)) & 0xFFu); }
 
 // ---------------------------------------------------------------------------
 // repack kernels (upload time)

@@ -45,6 +45,7 @@ struct lmc_model {
     size_t ws_bytes;
     int *d_tok, *d_pos, *d_next, *d_step, *d_prompt, *d_ids;
     unsigned long long *d_keys; /* per sequence greedy-pick key of the step */
+    int *d_attn_cnt;            /* attention split arrival counters [batch][kv heads] */
     int *h_stage; /* pinned: tokens, positions, next ids */
     int prompt_cap, ids_cap;
     cudaStream_t stream;
@@ -410,6 +411,11 @@ static int alloc_state(lmc_model *m) {
     TRY(dev_alloc((void **)&m->h, 4 * B * 2 * F)); /* gate | up rows */
     TRY(dev_alloc((void **)&m->h2, 4 * B * F));
     TRY(dev_alloc((void **)&m->d_keys, 8 * B));
+    {   /* LMC_ATTN_FUSED=0: merge the attention splits in a separate kernel
+         * instead of in the last split CTA (same result, one launch more) */
+        const char *f = getenv("LMC_ATTN_FUSED");
+        if (!(f && f[0] == '0')) TRY(dev_alloc((void **)&m->d_attn_cnt, 4 * B * (size_t)m->hkvl));
+    }
     TRY(dev_alloc((void **)&m->logits, 4 * B * V));
     m->ws_bytes = lmc_attention_workspace_bytes((int)B, c->n_heads, c->head_dim, c->seq_len);
     TRY(dev_alloc(&m->ws, m->ws_bytes));
@@ -513,7 +519,7 @@ int lmc_model_free(lmc_model *m) {
     lmc_qtensor_free(m->lm_head);
     void *ps[] = {m->wpe, m->lnf_w, m->lnf_b, m->rmsf, m->rope_cos, m->rope_sin, m->kc, m->vc, m->x, m->xn, m->qkv,
                   m->att, m->h, m->h2, m->logits, m->ws, m->d_tok, m->d_pos, m->d_next, m->d_step, m->d_prompt, m->d_ids,
-                  m->d_keys};
+                  m->d_keys, m->d_attn_cnt};
     for (size_t i = 0; i < sizeof ps / sizeof ps[0]; i++) if (ps[i]) cudaFree(ps[i]);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -574,7 +580,7 @@ static int step(lmc_model *m, int B) {
             TRY(norm_matmul(m, w->qkv, LMC_PRO_LAYERNORM, w->ln1_w, w->ln1_b, 1e-5f, w->qkv_b, m->qkv, 3 * D, B,
                             LMC_EPI_NONE, NULL));
             TRY(lmc_attention_launch(m->att, D, m->qkv, 3 * D, m->qkv + D, m->qkv + 2 * D, 3 * D, kc, vc, m->kv_dtype,
-                                     m->d_pos, B, H, H, Dh, S, m->ws, m->ws_bytes, s));
+                                     m->d_pos, B, H, H, Dh, S, m->ws, m->ws_bytes, m->d_attn_cnt, s));
             TRY(lmc_matmul(w->proj, m->att, D, w->proj_b, m->x, D, B, LMC_EPI_ACCUM, s));
             TRY(norm_matmul(m, w->fc, LMC_PRO_LAYERNORM, w->ln2_w, w->ln2_b, 1e-5f, w->fc_b, m->h, F, B, LMC_EPI_GELU,
                             NULL));
@@ -602,7 +608,8 @@ static int step(lmc_model *m, int B) {
             }
             /* RoPE on q and the new K row happens inside the attention kernel */
             TRY(lmc_attention_rope_launch(m->att, QD, q, ld ? ld : QD, k, v, ld ? ld : KVD, kc, vc, m->kv_dtype,
-                                          m->d_pos, B, H, Hkv, Dh, S, m->ws, m->ws_bytes, m->rope_cos, m->rope_sin, s));
+                                          m->d_pos, B, H, Hkv, Dh, S, m->ws, m->ws_bytes, m->rope_cos, m->rope_sin,
+                                          m->d_attn_cnt, s));
             TRY(lmc_matmul(w->o, m->att, QD, NULL, m->x, D, B, rp, s));
             TRY(tp_sum_x(m, B));
             if (w->gateup_cat && (lmc_qtensor_has_tiled(w->down) || (B > 8 && w->down->gemm_wscale > 0.0f))) {
