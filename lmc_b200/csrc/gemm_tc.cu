@@ -132,12 +132,26 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-__device__ __forceinline__ void epi_store(const GArgs &a, int n, int m, float v) {
+// Stores output (token n, row m) and returns its greedy-pick key.
+__device__ __forceinline__ unsigned long long epi_store(const GArgs &a, int n, int m, float v) {
     if (a.bias) v += a.bias[m];
     if (a.epi & LMC_EPI_GELU) v = lmc_gelu_f(v);
     float *o = a.y + (size_t)n * a.ldy + m;
     *o = (a.epi & LMC_EPI_ACCUM) ? *o + v : v;
-    if (a.keys) atomicMax(a.keys + n, lmc_argmax_key(v, m + a.key_base));
+    return lmc_argmax_key(v, m + a.key_base);
+}
+// Warp-collective epilogue of column n (warp-uniform) for row m (per lane):
+// store, then one atomic per warp for the greedy key of the column (the
+// 64-bit maximum as two 32-bit warp reductions).
+__device__ __forceinline__ void epi_col(const GArgs &a, int n, int m, float v) {
+    unsigned long long k = 0ull;
+    if (n < a.N && m < a.M) k = epi_store(a, n, m, v);
+    if (a.keys && n < a.N) {
+        const unsigned hi = (unsigned)(k >> 32), lo = (unsigned)k;
+        const unsigned mh = __reduce_max_sync(0xffffffffu, hi);
+        const unsigned ml = __reduce_max_sync(0xffffffffu, hi == mh ? lo : 0u);
+        if ((threadIdx.x & 31) == 0 && (mh | ml)) atomicMax(a.keys + n, ((unsigned long long)mh << 32) | ml);
+    }
 }
 
 // Accumulator (TMEM lanes = tile rows, columns = tokens) -> Y.  Warp w reads
@@ -162,7 +176,7 @@ __device__ __forceinline__ void gemm_epilogue(const GArgs &a, uint32_t tmem, int
 #pragma unroll
             for (int i = 0; i < 16; i++) {
                 const int n = n0 + c0 + i;
-                if (n < a.N && m < a.M) epi_store(a, n, m, v[i] * (wi * a.xinv[n]));
+                epi_col(a, n, m, v[i] * (wi * (n < a.N ? a.xinv[n] : 0.0f)));
             }
         }
         return;
@@ -192,7 +206,7 @@ __device__ __forceinline__ void gemm_epilogue(const GArgs &a, uint32_t tmem, int
     if (rank == 0)
         for (int c = cbeg; c < cend; c++) {
             const int n = n0 + c;
-            if (n < a.N && m < a.M) epi_store(a, n, m, red[c * BM + row] * (wi * a.xinv[n]));
+            epi_col(a, n, m, red[c * BM + row] * (wi * (n < a.N ? a.xinv[n] : 0.0f)));
         }
 }
 
@@ -600,7 +614,7 @@ __global__ void __launch_bounds__(TTHR, 1) k_gemm_tiled(GArgs a) {
 #pragma unroll
         for (int c = 0; c < BN / 2; c++) {
             const int n = n0 + cb + c;
-            if (n < a.N && m < a.M) epi_store(a, n, m, acc[c] * a.xinv[n]);
+            epi_col(a, n, m, acc[c] * (n < a.N ? a.xinv[n] : 0.0f));
         }
         return;
     }
@@ -623,10 +637,10 @@ __global__ void __launch_bounds__(TTHR, 1) k_gemm_tiled(GArgs a) {
     cl_arrive();
     cl_wait();  // every slot written
     for (int e = tid; e < W * BM; e += TTHR) {
-        const int cc = e / BM, r = e % BM, n = n0 + rank * W + cc, mm = m0 + r;
+        const int cc = e / BM, r = e % BM, n = n0 + rank * W + cc, mm = m0 + r;  // cc is warp-uniform
         float v = 0.0f;
         for (int src = 0; src < a.CL; src++) v += buf[((size_t)src * W + cc) * BM + r];
-        if (n < a.N && mm < a.M) epi_store(a, n, mm, v * a.xinv[n]);
+        epi_col(a, n, mm, v * (n < a.N ? a.xinv[n] : 0.0f));
     }
 }
 
@@ -812,8 +826,28 @@ extern "C" int lmc_gemm_prepare(lmc_qtensor *t) {
     return LMC_OK;
 }
 
+static int clusters_fit(int cl, size_t smem, const void *fn, int nthr);
 static int clusters_for(int cl, size_t smem, const void *fn, int nthr) {
     if (cl == 1) return lmc_sm_count();
+    static struct {
+        const void *fn;
+        size_t smem;
+        int cl, n;
+    } memo[64];
+    static int n_memo = 0;
+    for (int i = 0; i < n_memo; i++)
+        if (memo[i].fn == fn && memo[i].smem == smem && memo[i].cl == cl) return memo[i].n;
+    const int n = clusters_fit(cl, smem, fn, nthr);
+    if (n_memo < 64) {
+        memo[n_memo].fn = fn;
+        memo[n_memo].smem = smem;
+        memo[n_memo].cl = cl;
+        memo[n_memo++].n = n;
+    }
+    return n;
+}
+// clusters of cl CTAs that fit on the GPU at once
+static int clusters_fit(int cl, size_t smem, const void *fn, int nthr) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cl);
     cfg.blockDim = dim3(nthr);
@@ -901,10 +935,22 @@ extern "C" int lmc_gemm_launch(const lmc_qtensor *t, const float *d_x, int ldx, 
     }
     const int NTL = (N + a.BN - 1) / a.BN, tiles = a.MT * NTL;
     LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    // split K over a cluster until the tiles cover the SMs (each CTA keeps >= 2 k-blocks)
+    // split K over a cluster of cl CTAs: the cl with the least estimated
+    // time, waves x (k-blocks per CTA + one k-block for the cluster
+    // reduction), where a wave is as many tiles as clusters of that size fit
+    // on the GPU at once (each CTA keeps >= min_kb k-blocks)
     int cl = 1;
-    while (cl < 8 && tiles * cl * 2 <= lmc_sm_count() * (fast ? 2 : 1) && a.nkb >= 2 * min_kb * cl) cl *= 2;
-    while (cl > 1 && clusters_for(cl, smem, fn, nthr) < 1) cl /= 2;
+    long long best = -1;
+    for (int c = 1; c <= 8; c *= 2) {
+        if (c > 1 && a.nkb < min_kb * c) break;
+        const int fit = clusters_for(c, smem, fn, nthr);
+        if (fit < 1) break;
+        const long long waves = (tiles + fit - 1) / fit, cost = waves * ((a.nkb + c - 1) / c + (c > 1 ? 1 : 0));
+        if (best < 0 || cost < best) {
+            best = cost;
+            cl = c;
+        }
+    }
     a.CL = cl;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(tiles * cl);

@@ -577,13 +577,28 @@ __device__ __forceinline__ void flush(const Part<NT> &p, float *acc_rt, const fl
     }
 }
 
-__device__ __forceinline__ void epilogue(const TArgs &a, int b, int row, float v) {
-    if (row >= a.M || b >= a.nb) return;
+// Stores output (b, row) and returns its greedy-pick key (0 when out of range).
+__device__ __forceinline__ unsigned long long epilogue(const TArgs &a, int b, int row, float v) {
+    if (row >= a.M || b >= a.nb) return 0ull;
     if (a.bias) v += a.bias[row];
     if (a.epi & LMC_EPI_GELU) v = lmc_gelu_f(v);
     float *o = a.y + (size_t)b * a.ldy + row;
     *o = (a.epi & LMC_EPI_ACCUM) ? *o + v : v;
-    if (a.keys) atomicMax(a.keys + b, lmc_argmax_key(v, row + a.key_base));
+    return lmc_argmax_key(v, row + a.key_base);
+}
+// Outputs e = lane + 32 j of a row tile (e < 16 nb: batch row e / 16, tile row
+// e % 16); best[j] keeps the largest key this lane has seen for batch row
+// 2 j + lane / 16.
+__device__ __forceinline__ void epilogue_tile(const TArgs &a, int row0, const float *ar, int lane,
+                                              unsigned long long (&best)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int e = lane + 32 * j;
+        if (e < 16 * a.nb) {
+            const unsigned long long k = epilogue(a, e >> 4, row0 + (e & 15), ar[e]);
+            best[j] = k > best[j] ? k : best[j];
+        }
+    }
 }
 
 // Byte i of w, zero-extended / sign-extended (one PRMT each).
@@ -895,29 +910,46 @@ __global__ void __launch_bounds__(NTHR, 2) k_gemv_tiled(TArgs a) {
     if (a.CL > 1) cluster_wait();  // every accumulator of the cluster is zero
     // Row tiles of this CTA: finish the ones it holds whole, push the ones
     // that started in an earlier CTA into that CTA's accumulator.
-    const int nv = 16 * a.nb;
+    unsigned long long best[4] = {0ull, 0ull, 0ull, 0ull};
     const int rt_last = cu1 > cu0 ? (cu1 - 1) / KB : rt0 - 1;
     for (int T = rt0 + wid; T <= rt_last; T += WARPS) {
         const float *ar = acc + (T - rt0) * NB * 16;
         const int f0 = T * KB, f1 = f0 + KB;
         if (f0 >= cu0) {
-            if (f1 <= cu1)
-                for (int e = lane; e < nv; e += 32) epilogue(a, e >> 4, (t0 + T) * 16 + (e & 15), ar[e]);
+            if (f1 <= cu1) epilogue_tile(a, (t0 + T) * 16, ar, lane, best);
             continue;
         }
         const int owner = (int)(((long long)(f0 + 1) * a.CL - 1) / Uc);
         const int orow0 = (int)((long long)owner * Uc / a.CL) / KB;
         const uint32_t dst = smem_u32(acc + (T - orow0) * NB * 16);
-        for (int e = lane; e < nv; e += 32) red_cluster_add(dst + 4 * e, (uint32_t)owner, ar[e]);
+        for (int e = lane; e < 16 * a.nb; e += 32) red_cluster_add(dst + 4 * e, (uint32_t)owner, ar[e]);
     }
     const bool own_shared = cu1 > cu0 && rt_last * KB >= cu0 && (rt_last + 1) * KB > cu1;
     if (a.CL > 1) {
         cluster_arrive();  // phase 2: pushes done
         cluster_wait();
     }
-    if (own_shared && wid == 0) {  // the tile this CTA owns and later CTAs added to
-        const float *ar = acc + (rt_last - rt0) * NB * 16;
-        for (int e = lane; e < nv; e += 32) epilogue(a, e >> 4, (t0 + rt_last) * 16 + (e & 15), ar[e]);
+    if (own_shared && wid == 0)  // the tile this CTA owns and later CTAs added to
+        epilogue_tile(a, (t0 + rt_last) * 16, acc + (rt_last - rt0) * NB * 16, lane, best);
+    if (a.keys) {  // greedy keys: half-warp maxima, then one atomic per CTA and batch row
+        // [WARPS][8] over the x fragments, dead once every unit is done
+        auto kbest = reinterpret_cast<unsigned long long(*)[8]>(smem);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            unsigned long long k = best[j];
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) {
+                const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, off);
+                k = o > k ? o : k;
+            }
+            if ((lane & 15) == 0) kbest[wid][2 * j + (lane >> 4)] = k;
+        }
+        __syncthreads();
+        if ((int)threadIdx.x < a.nb) {
+            unsigned long long k = 0ull;
+            for (int w = 0; w < WARPS; w++) k = kbest[w][threadIdx.x] > k ? kbest[w][threadIdx.x] : k;
+            if (k) atomicMax(a.keys + threadIdx.x, k);
+        }
     }
 }
 
