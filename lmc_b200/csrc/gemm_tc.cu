@@ -31,6 +31,7 @@
 
 #include <algorithm>
 #include <math.h>
+#include <type_traits>
 #include <string.h>
 
 namespace {
@@ -52,8 +53,7 @@ struct GArgs {
     int BN, MT, CL, nkb;
     const uint8_t *wt;  // tiled copy (16-row x 256-column units), or NULL
     int RT, KBU;        // row tiles and unit columns of the tiled copy
-    const __half *xsh, *xsl;  // [N][K/32] 32-column sums of the scaled x, x 2^-5, hi / lo
-    int K32;
+    const uint8_t *xs;  // Q4_K fast path: 32-column sums of the scaled x (x 2^-5) as MMA tiles, see k_gemm_prep_x
     int Npad;  // fast path: x tiles are [K/64][Npad][64], pre-swizzled
 };
 
@@ -88,10 +88,14 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
 // both K-major, N/8 at bit 17, M/16 at bit 24.
 __device__ __forceinline__ uint32_t idesc(int n) { return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24); }
 
+// D (+)= A B.  The accumulate flag is an immediate in one of two forms: a
+// predicate set per MMA made the issue loop about three times slower than
+// the MMA itself.
 __device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
-    asm volatile(
-        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem),
-        "l"(a), "l"(b), "r"(id), "r"(acc));
+    if (acc)
+        asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;" ::"r"(tmem), "l"(a), "l"(b), "r"(id));
+    else
+        asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 0;" ::"r"(tmem), "l"(a), "l"(b), "r"(id));
 }
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
@@ -108,6 +112,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+// 32 lanes x 16 columns of 32-bit TMEM words; the caller waits (tcgen05.wait::ld)
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
 }
 __device__ __forceinline__ uint32_t ctarank() {
     uint32_t r;
@@ -139,6 +151,63 @@ __device__ __forceinline__ unsigned long long epi_store(const GArgs &a, int n, i
     float *o = a.y + (size_t)n * a.ldy + m;
     *o = (a.epi & LMC_EPI_ACCUM) ? *o + v : v;
     return lmc_argmax_key(v, m + a.key_base);
+}
+// Warp-collective epilogue of NC consecutive columns nc0.. (warp-uniform)
+// for row m (per lane), v[c] the unscaled sums: every load (activation
+// scales, bias, old Y) is issued before the first store.
+template <int NC>
+__device__ __forceinline__ void epi_cols(const GArgs &a, int nc0, int m, const float (&v)[NC]) {
+    const bool mok = m < a.M;
+    const float bm = (a.bias && mok) ? __ldg(a.bias + m) : 0.0f;
+    float xi[NC], old[NC];
+#pragma unroll
+    for (int c = 0; c < NC; c++) {
+        const int n = nc0 + c;
+        xi[c] = n < a.N ? __ldg(a.xinv + n) : 0.0f;
+        old[c] = (a.epi & LMC_EPI_ACCUM) && n < a.N && mok ? a.y[(size_t)n * a.ldy + m] : 0.0f;
+    }
+#pragma unroll
+    for (int c = 0; c < NC; c++) {
+        const int n = nc0 + c;
+        float r = v[c] * xi[c] + bm;
+        if (a.epi & LMC_EPI_GELU) r = lmc_gelu_f(r);
+        if (n < a.N && mok) a.y[(size_t)n * a.ldy + m] = (a.epi & LMC_EPI_ACCUM) ? old[c] + r : r;
+        if (a.keys && n < a.N) {
+            const unsigned long long k = n < a.N && mok ? lmc_argmax_key(r, m + a.key_base) : 0ull;
+            const unsigned hi = (unsigned)(k >> 32), lo = (unsigned)k;
+            const unsigned mh = __reduce_max_sync(0xffffffffu, hi);
+            const unsigned ml = __reduce_max_sync(0xffffffffu, hi == mh ? lo : 0u);
+            if ((threadIdx.x & 31) == 0 && (mh | ml)) atomicMax(a.keys + n, ((unsigned long long)mh << 32) | ml);
+        }
+    }
+}
+// Same for the columns nc0 + 4 k, 4 k < lim, k < 8.
+__device__ __forceinline__ void epi_strided(const GArgs &a, int nc0, int lim, int m, const float (&v)[8]) {
+    const bool mok = m < a.M;
+    const float bm = (a.bias && mok) ? __ldg(a.bias + m) : 0.0f;
+    float xi[8], old[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int n = nc0 + 4 * k;
+        const bool nok = 4 * k < lim && n < a.N;
+        xi[k] = nok ? __ldg(a.xinv + n) : 0.0f;
+        old[k] = (a.epi & LMC_EPI_ACCUM) && nok && mok ? a.y[(size_t)n * a.ldy + m] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        if (4 * k >= lim) break;
+        const int n = nc0 + 4 * k;
+        float r = v[k] * xi[k] + bm;
+        if (a.epi & LMC_EPI_GELU) r = lmc_gelu_f(r);
+        if (n < a.N && mok) a.y[(size_t)n * a.ldy + m] = (a.epi & LMC_EPI_ACCUM) ? old[k] + r : r;
+        if (a.keys && n < a.N) {
+            const unsigned long long kk = mok ? lmc_argmax_key(r, m + a.key_base) : 0ull;
+            const unsigned hi = (unsigned)(kk >> 32), lo = (unsigned)kk;
+            const unsigned mh = __reduce_max_sync(0xffffffffu, hi);
+            const unsigned ml = __reduce_max_sync(0xffffffffu, hi == mh ? lo : 0u);
+            if ((threadIdx.x & 31) == 0 && (mh | ml)) atomicMax(a.keys + n, ((unsigned long long)mh << 32) | ml);
+        }
+    }
 }
 // Warp-collective epilogue of column n (warp-uniform) for row m (per lane):
 // store, then one atomic per warp for the greedy key of the column (the
@@ -282,11 +351,14 @@ __global__ void __launch_bounds__(GTHR, 1) k_gemm_tc(GArgs a) {
         __syncthreads();
         if (tid == 0) {
             tc_fence_after();
+            // 16 fp16 = 32 bytes per K step = 2 in the descriptors' address field
+            const uint64_t ad = sdesc(su32(A)), bh = sdesc(su32(Bh)), bl = sdesc(su32(Bl));
+            mma_f16(tmem, ad, bh, id, it > 0 ? 1u : 0u);
+            mma_f16(tmem, ad, bl, id, 1u);
 #pragma unroll
-            for (int j = 0; j < BK / 16; j++) {  // 16 fp16 = 32 bytes per K step
-                const uint64_t ad = sdesc(su32(A) + 32 * j);
-                mma_f16(tmem, ad, sdesc(su32(Bh) + 32 * j), id, (it > 0 || j > 0) ? 1u : 0u);
-                mma_f16(tmem, ad, sdesc(su32(Bl) + 32 * j), id, 1u);
+            for (int j = 1; j < BK / 16; j++) {
+                mma_f16(tmem, ad + 2 * j, bh + 2 * j, id, 1u);
+                mma_f16(tmem, ad + 2 * j, bl + 2 * j, id, 1u);
             }
             mma_commit(su32(&bars[s]));
         }
@@ -310,25 +382,18 @@ __global__ void __launch_bounds__(GTHR, 1) k_gemm_tc(GArgs a) {
 // group in the order the extraction yields, so the activations are stored
 // with the same column permutation (see perm_pos) and no shuffles are needed.
 // ---------------------------------------------------------------------------
-constexpr int TTHR = 256;
 __host__ __device__ constexpr int tunit_bytes(int qt) { return qt == 4 ? 2304 : qt == 6 ? 3360 : 4352; }
 
 __device__ __forceinline__ __half2 u2h(uint32_t v) { return *reinterpret_cast<const __half2 *>(&v); }
 __device__ __forceinline__ uint32_t h2u(__half2 v) { return *reinterpret_cast<const uint32_t *>(&v); }
 __device__ __forceinline__ int tcode_word(int n, int t) { return ((n >> 2) * 32 + t) * 4 + (n & 3); }
-
-// 8 nibble codes (bytes 0-3: low and high nibbles) -> 8 fp16 integers q * sc
-// (exact, <= 945), in the order (b0.lo, b2.lo, b1.lo, b3.lo, b0.hi, b2.hi,
-// b1.hi, b3.hi)
-__device__ __forceinline__ uint4 cvt_nib(uint32_t P, __half2 sc) {
-    const __half2 k = __float2half2_rn(1024.0f);
-    uint4 r;
-    r.x = h2u(__hmul2(__hsub2(u2h((P & 0x000F000Fu) | 0x64006400u), k), sc));
-    r.y = h2u(__hmul2(__hsub2(u2h(((P >> 8) & 0x000F000Fu) | 0x64006400u), k), sc));
-    r.z = h2u(__hmul2(__hsub2(u2h(((P >> 4) & 0x000F000Fu) | 0x64006400u), k), sc));
-    r.w = h2u(__hmul2(__hsub2(u2h(((P >> 12) & 0x000F000Fu) | 0x64006400u), k), sc));
-    return r;
+template <int J> __device__ __forceinline__ uint32_t pick4h(const uint4 &v) {
+    return J == 0 ? v.x : J == 1 ? v.y : J == 2 ? v.z : v.w;
 }
+
+// Nibble order of the converted codes: 8 nibble codes (bytes 0-3, low and
+// high nibbles) give the fp16 values in the order (b0.lo, b2.lo, b1.lo,
+// b3.lo, b0.hi, b2.hi, b1.hi, b3.hi)
 // 4 byte codes -> 4 fp16 (q - OFF) * s, order (b0, b2, b1, b3); OFF = 32 for
 // Q6_K codes 0..63, 128 for int8 codes stored with the sign bit flipped
 template <int OFF> __device__ __forceinline__ uint2 cvt_byte(uint32_t q, __half2 s) {
@@ -362,33 +427,49 @@ __device__ __forceinline__ void q4k_scale(const uint4 &H, int j, int &sc, int &m
     }
 }
 
-// Warp u: rows 16u + g and 16u + g + 8 of the A tile for k-block h of its unit.
-//   Q4_K: A = q * sc (exact); on h == 0 also the row's 8 mins (exact) into the
-//         mins tile and (d, dmin) into dsc: the block's value is
-//         d * sum(q sc x) - dmin * sum_j m_j X_j.
-//   Q6_K: A = sc * (q - 32) (exact up to 2048 in magnitude, nearest-even
-//         above); dsc = (d, 0).
-//   Q8_0: A = fp16(q * d * ws) (one rounding); dsc = (1/ws, 0).
+// 8 nibble codes -> 8 fp16 q * sc (order above), one fused multiply-add per
+// pair: (1024 + q) sc - 1024 sc is exact (the result q sc <= 945 and
+// 1024 sc <= 64512 are fp16 integers, the product is not rounded).
+__device__ __forceinline__ uint4 cvt_nib_fma(uint32_t P, __half2 sc, __half2 nsc) {
+    uint4 r;
+    r.x = h2u(__hfma2(u2h((P & 0x000F000Fu) | 0x64006400u), sc, nsc));
+    r.y = h2u(__hfma2(u2h(((P >> 8) & 0x000F000Fu) | 0x64006400u), sc, nsc));
+    r.z = h2u(__hfma2(u2h(((P >> 4) & 0x000F000Fu) | 0x64006400u), sc, nsc));
+    r.w = h2u(__hfma2(u2h(((P >> 12) & 0x000F000Fu) | 0x64006400u), sc, nsc));
+    return r;
+}
+
+// Per unit column state of one converter warp of the warp-specialised
+// kernel: the 16-byte headers of its rows r0 = 16u + g and r1 = r0 + 8
+// (Q4_K d, dmin, scales; Q6_K the 16 int8 scales; Q8_0 the 8 fp16 block
+// scales) and, for Q4_K, the scale multipliers of its four k-blocks.
+struct ConvUnit {
+    uint4 H0, H1;
+    __half2 a0[4], a1[4];
+};
 template <int QT>
-__device__ __forceinline__ void build_a(uint8_t *A, const uint8_t *U, int u, int h, int lane, float ws, float2 *dsc,
-                                        uint8_t *Mt) {
+__device__ __forceinline__ void conv_unit(ConvUnit &cu, const uint8_t *U, int part, int lane) {
+    const int g = lane >> 2;
+    cu.H0 = *reinterpret_cast<const uint4 *>(U + 16 * g);
+    cu.H1 = *reinterpret_cast<const uint4 *>(U + 16 * g + 128);
+    if (QT == 4)
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+            int sc0, m0, sc1, m1;
+            q4k_scale(cu.H0, 2 * h + part, sc0, m0);
+            q4k_scale(cu.H1, 2 * h + part, sc1, m1);
+            cu.a0[h] = __float2half2_rn((float)sc0);
+            cu.a1[h] = __float2half2_rn((float)sc1);
+        }
+}
+// Block scales (and the Q4_K mins rows) of the unit column: part-0 warps.
+template <int QT>
+__device__ __forceinline__ void conv_unit_side(const ConvUnit &cu, const uint8_t *U, int u, int lane, float ws, float2 *dsc,
+                                               uint8_t *Mt) {
     const int g = lane >> 2, c = lane & 3, r0 = 16 * u + g, r1 = r0 + 8;
     if (QT == 4) {
-        const uint4 H0 = *reinterpret_cast<const uint4 *>(U + 16 * g);
-        const uint4 H1 = *reinterpret_cast<const uint4 *>(U + 16 * g + 128);
-        const uint32_t *cw = reinterpret_cast<const uint32_t *>(U + 256);
-#pragma unroll
-        for (int jj = 0; jj < 2; jj++) {
-            const int j = 2 * h + jj;
-            int sc0, m0, sc1, m1;
-            q4k_scale(H0, j, sc0, m0);
-            q4k_scale(H1, j, sc1, m1);
-            const uint32_t P = cw[tcode_word(2 * j, lane)], Q = cw[tcode_word(2 * j + 1, lane)];
-            put_chunk(A, r0, 4 * jj + c, cvt_nib(P, __float2half2_rn((float)sc0)));
-            put_chunk(A, r1, 4 * jj + c, cvt_nib(Q, __float2half2_rn((float)sc1)));
-        }
-        if (h == 0 && c < 2) {  // lanes c = 0 / 1: the mins rows of r0 / r1
-            const uint4 H = c == 0 ? H0 : H1;
+        if (c < 2) {  // lanes c = 0 / 1: the mins rows of r0 / r1
+            const uint4 H = c == 0 ? cu.H0 : cu.H1;
             const int r = c == 0 ? r0 : r1;
             int sc, mn[8];
 #pragma unroll
@@ -403,51 +484,57 @@ __device__ __forceinline__ void build_a(uint8_t *A, const uint8_t *U, int u, int
             dsc[r] = __half22float2(u2h(H.x));  // (d, dmin)
         }
     } else if (QT == 6) {
-        const uint4 S0 = *reinterpret_cast<const uint4 *>(U + 16 * g);
-        const uint4 S1 = *reinterpret_cast<const uint4 *>(U + 16 * g + 128);
-        const uint32_t *lw = reinterpret_cast<const uint32_t *>(U + 288), *hw = reinterpret_cast<const uint32_t *>(U + 288 + 2048);
-        const uint32_t w0 = h == 0 ? S0.x : h == 1 ? S0.y : h == 2 ? S0.z : S0.w;  // scales of chunks 4h..4h+3
-        const uint32_t w1 = h == 0 ? S1.x : h == 1 ? S1.y : h == 2 ? S1.z : S1.w;
-#pragma unroll
-        for (int jp2 = 0; jp2 < 2; jp2++) {
-            const int j = 4 * h + 2 * jp2;  // even chunk; j + 1 odd
-            const uint32_t P0 = lw[tcode_word(j, lane)], P1 = lw[tcode_word(j + 1, lane)];
-            const uint32_t H = hw[tcode_word(j >> 1, lane)];
-            const uint32_t a0 = (P0 & LO4C) | ((H << 4) & 0x30303030u), a1 = (P1 & LO4C) | (H & 0x30303030u);
-            const uint32_t b0 = ((P0 >> 4) & LO4C) | ((H << 2) & 0x30303030u), b1 = ((P1 >> 4) & LO4C) | ((H >> 2) & 0x30303030u);
-            const int e0 = 2 * jp2, e1 = e0 + 1;
-            const __half2 sg0 = __float2half2_rn((float)(int8_t)((w0 >> (8 * e0)) & 0xFF));
-            const __half2 sg1 = __float2half2_rn((float)(int8_t)((w0 >> (8 * e1)) & 0xFF));
-            const __half2 sh0 = __float2half2_rn((float)(int8_t)((w1 >> (8 * e0)) & 0xFF));
-            const __half2 sh1 = __float2half2_rn((float)(int8_t)((w1 >> (8 * e1)) & 0xFF));
-            const uint2 x0 = cvt_byte<32>(a0, sg0), x1 = cvt_byte<32>(a1, sg1);
-            const uint2 y0 = cvt_byte<32>(b0, sh0), y1 = cvt_byte<32>(b1, sh1);
-            put_chunk(A, r0, 4 * jp2 + c, make_uint4(x0.x, x0.y, x1.x, x1.y));
-            put_chunk(A, r1, 4 * jp2 + c, make_uint4(y0.x, y0.y, y1.x, y1.y));
-        }
-        if (h == 0 && c == 0) {
+        if (c == 0) {
             dsc[r0] = make_float2(__half2float(*reinterpret_cast<const __half *>(U + 256 + 2 * g)), 0.0f);
             dsc[r1] = make_float2(__half2float(*reinterpret_cast<const __half *>(U + 256 + 2 * g + 16)), 0.0f);
         }
+    } else if (c == 0) {
+        dsc[r0] = dsc[r1] = make_float2(1.0f / ws, 0.0f);
+    }
+}
+// k-block H of the unit column, K half `part`, rows r0 / r1 of the A tile:
+//   Q4_K: A = q * sc (exact); Q6_K: A = sc * (q - 32) (exact up to 2048 in
+//   magnitude, nearest-even above); Q8_0: A = fp16(q * d * ws) (one rounding).
+// The block scales enter at readout (dsc): Q4_K d * sum(q sc x) - dmin *
+// sum_j m_j X_j, Q6_K d, Q8_0 1 / ws.
+template <int QT, int H>
+__device__ __forceinline__ void conv_step(uint8_t *A, const uint8_t *U, const ConvUnit &cu, int u, int part, int lane, float ws) {
+    const int g = lane >> 2, c = lane & 3, r0 = 16 * u + g, r1 = r0 + 8;
+    if (QT == 4) {
+        const uint32_t *cw = reinterpret_cast<const uint32_t *>(U + 256);
+        const int j = 2 * H + part;
+        const uint32_t P = cw[tcode_word(2 * j, lane)], Q = cw[tcode_word(2 * j + 1, lane)];
+        const __half2 m1024 = __float2half2_rn(-1024.0f);
+        put_chunk(A, r0, 4 * part + c, cvt_nib_fma(P, cu.a0[H], __hmul2(cu.a0[H], m1024)));
+        put_chunk(A, r1, 4 * part + c, cvt_nib_fma(Q, cu.a1[H], __hmul2(cu.a1[H], m1024)));
+    } else if (QT == 6) {
+        const uint32_t *lw = reinterpret_cast<const uint32_t *>(U + 288), *hw = reinterpret_cast<const uint32_t *>(U + 288 + 2048);
+        const uint32_t w0 = pick4h<H>(cu.H0), w1 = pick4h<H>(cu.H1);  // scales of chunks 4H..4H+3
+        const int j = 4 * H + 2 * part;                                   // even chunk; j + 1 odd
+        const uint32_t P0 = lw[tcode_word(j, lane)], P1 = lw[tcode_word(j + 1, lane)];
+        const uint32_t Hb = hw[tcode_word(j >> 1, lane)];
+        const uint32_t a0 = (P0 & LO4C) | ((Hb << 4) & 0x30303030u), a1 = (P1 & LO4C) | (Hb & 0x30303030u);
+        const uint32_t b0 = ((P0 >> 4) & LO4C) | ((Hb << 2) & 0x30303030u), b1 = ((P1 >> 4) & LO4C) | ((Hb >> 2) & 0x30303030u);
+        const int e0 = 2 * part, e1 = e0 + 1;
+        const __half2 sg0 = __float2half2_rn((float)(int8_t)((w0 >> (8 * e0)) & 0xFF));
+        const __half2 sg1 = __float2half2_rn((float)(int8_t)((w0 >> (8 * e1)) & 0xFF));
+        const __half2 sh0 = __float2half2_rn((float)(int8_t)((w1 >> (8 * e0)) & 0xFF));
+        const __half2 sh1 = __float2half2_rn((float)(int8_t)((w1 >> (8 * e1)) & 0xFF));
+        const uint2 x0 = cvt_byte<32>(a0, sg0), x1 = cvt_byte<32>(a1, sg1);
+        const uint2 y0 = cvt_byte<32>(b0, sh0), y1 = cvt_byte<32>(b1, sh1);
+        put_chunk(A, r0, 4 * part + c, make_uint4(x0.x, x0.y, x1.x, x1.y));
+        put_chunk(A, r1, 4 * part + c, make_uint4(y0.x, y0.y, y1.x, y1.y));
     } else {
-        const uint4 H0 = *reinterpret_cast<const uint4 *>(U + 16 * g);
-        const uint4 H1 = *reinterpret_cast<const uint4 *>(U + 16 * g + 128);
         const uint4 *cw = reinterpret_cast<const uint4 *>(U + 256);
-#pragma unroll
-        for (int jj = 0; jj < 2; jj++) {
-            const int j = 2 * h + jj, jw = j >> 1;
-            const uint4 Aw = cw[j * 32 + lane];
-            const uint32_t hw0 = jw == 0 ? H0.x : jw == 1 ? H0.y : jw == 2 ? H0.z : H0.w;
-            const uint32_t hw1 = jw == 0 ? H1.x : jw == 1 ? H1.y : jw == 2 ? H1.z : H1.w;
-            const float2 f0 = __half22float2(u2h(hw0)), f1 = __half22float2(u2h(hw1));
-            const __half2 s0 = __float2half2_rn(((j & 1) ? f0.y : f0.x) * ws);
-            const __half2 s1 = __float2half2_rn(((j & 1) ? f1.y : f1.x) * ws);
-            const uint2 x0 = cvt_byte<128>(Aw.x ^ 0x80808080u, s0), x1 = cvt_byte<128>(Aw.z ^ 0x80808080u, s0);
-            const uint2 y0 = cvt_byte<128>(Aw.y ^ 0x80808080u, s1), y1 = cvt_byte<128>(Aw.w ^ 0x80808080u, s1);
-            put_chunk(A, r0, 4 * jj + c, make_uint4(x0.x, x0.y, x1.x, x1.y));
-            put_chunk(A, r1, 4 * jj + c, make_uint4(y0.x, y0.y, y1.x, y1.y));
-        }
-        if (h == 0 && c == 0) dsc[r0] = dsc[r1] = make_float2(1.0f / ws, 0.0f);
+        const int j = 2 * H + part;  // block j of each row; its scale is half (j & 1) of header word H
+        const uint4 Aw = cw[j * 32 + lane];
+        const float2 f0 = __half22float2(u2h(pick4h<H>(cu.H0))), f1 = __half22float2(u2h(pick4h<H>(cu.H1)));
+        const __half2 s0 = __float2half2_rn((part ? f0.y : f0.x) * ws);
+        const __half2 s1 = __float2half2_rn((part ? f1.y : f1.x) * ws);
+        const uint2 x0 = cvt_byte<128>(Aw.x ^ 0x80808080u, s0), x1 = cvt_byte<128>(Aw.z ^ 0x80808080u, s0);
+        const uint2 y0 = cvt_byte<128>(Aw.y ^ 0x80808080u, s1), y1 = cvt_byte<128>(Aw.w ^ 0x80808080u, s1);
+        put_chunk(A, r0, 4 * part + c, make_uint4(x0.x, x0.y, x1.x, x1.y));
+        put_chunk(A, r1, 4 * part + c, make_uint4(y0.x, y0.y, y1.x, y1.y));
     }
 }
 
@@ -458,46 +545,90 @@ __device__ __forceinline__ void bulk_copy(uint32_t bar, void *dst, const void *s
                  : "memory");
 }
 
-// Block accumulators -> registers: acc[c] += d * main - 32 dmin * mins.  The
-// MMAs run with N = 2 BN (hi rows then lo rows of x), so main and mins are
-// column c plus column c + BN; the sums of x enter the mins MMA x 2^-5.
-template <int QT, int BN>
-__device__ __forceinline__ void block_readout(float (&acc)[BN / 2], uint32_t tmain, uint32_t tmins, float2 dd) {
+// Accumulators of one unit column -> registers, NC columns (multiple of 8)
+// of one TMEM lane quarter in steps of 8: acc[c] += d * main - 32 dmin * mins.
+// The MMAs run with N = 2 BN (hi rows then lo rows of x), so main and mins
+// are column c plus column c + BN; the sums of x enter the mins MMA x 2^-5.
+template <int QT, int BN, int NC>
+__device__ __forceinline__ void block_readout_n(float (&acc)[NC], uint32_t tmain, uint32_t tmins, float2 dd) {
+    static_assert(NC == 16, "one x16 load per accumulator part");
+    uint32_t v[16], vl[16], mv[16], ml[16];
+    tmem_ld16_nowait(tmain, v);  // every load in flight, one wait
+    tmem_ld16_nowait(tmain + BN, vl);
+    if (QT == 4) {
+        tmem_ld16_nowait(tmins, mv);
+        tmem_ld16_nowait(tmins + BN, ml);
+    }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int c0 = 0; c0 < BN / 2; c0 += 16) {
-        float v[16], vl[16];
-        tmem_ld16(tmain + c0, v);
-        tmem_ld16(tmain + BN + c0, vl);
-        if (QT == 4) {
-            float mv[16], ml[16];
-            tmem_ld16(tmins + c0, mv);
-            tmem_ld16(tmins + BN + c0, ml);
-#pragma unroll
-            for (int i = 0; i < 16; i++) acc[c0 + i] += dd.x * (v[i] + vl[i]) - (32.0f * dd.y) * (mv[i] + ml[i]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 16; i++) acc[c0 + i] += dd.x * (v[i] + vl[i]);
-        }
+    for (int i = 0; i < 16; i++) {
+        const float main = __uint_as_float(v[i]) + __uint_as_float(vl[i]);
+        if (QT == 4)
+            acc[i] += dd.x * main - (32.0f * dd.y) * (__uint_as_float(mv[i]) + __uint_as_float(ml[i]));
+        else
+            acc[i] += dd.x * main;
     }
 }
 
-// smem: [2 A stages: 16 KB] [4 B stages: Bh BN*128 | Bl BN*128 (arrive pre-swizzled)]
-//       [2 mins stages: M 4 KB | Sh BN*32 | Sl BN*32] (Q4_K)
-//       [2 raw stages: 8 units] [dsc: 2 x 128 float2]
-//       [bars: raw full 0,1; MMA done 0,1; B full 0..3] [tmem slot]
-// TMEM: 8 BN columns: block parity p -> main (2 BN) at 4 BN p, mins (2 BN) at 4 BN p + 2 BN.
-template <int QT, int BN>
-__global__ void __launch_bounds__(TTHR, 1) k_gemm_tiled(GArgs a) {
+// Fast path for the tiled Q4_K / Q6_K / Q8_0 copies: one CTA per 128-row x
+// 64-token output tile (and K range of its cluster rank), warp-specialised,
+// every hand-off an mbarrier:
+//   warp 16 (producer, one lane): bulk copies of the weight units (8 per unit
+//           column: 128 rows x 256 K) into R raw stages, of the activation
+//           tiles (hi | lo, 64 K) into SB stages and, for Q4_K, of the
+//           32-column sums tile with each unit column; L2 prefetch one unit
+//           column further ahead.  Weights go out before the wait on the
+//           previous kernel (they do not depend on it).
+//   warp 17 (MMA, one lane): per 64-K step four tcgen05.mma (M 128, N 128 =
+//           hi rows then lo rows, K 16) into the unit column's accumulator
+//           (two in TMEM, alternating), plus the Q4_K mins MMA on the first
+//           step; commits free the A and activation stages (and, with the
+//           mins MMA, the raw stage) and mark the accumulator full.
+//   warps 0-15: warp w converts rows 16u..16u+15 (u = w % 8), K half w / 8,
+//           of each 64-K step into the A stage (exact integer * scale fp16,
+//           conv_step), then, one step into the next unit column, reads its
+//           16 columns (w / 4) of TMEM lane quarter w % 4 out of the previous
+//           accumulator with the per-row block scales and frees it.
+// After the last unit column: epilogue (direct, or a reduce-scatter over the
+// cluster when K is split).
+constexpr int WS_CONV = 16, WS_THREADS = 32 * (WS_CONV + 2);
+template <int QT> struct WsCfg {
+    static constexpr int R = QT == 8 ? 2 : 3, SA = 4, SB = 4;
+    static constexpr int UNIT = tunit_bytes(QT), RAWB = 8 * UNIT;
+    static constexpr int ABYTES = BM * 128, BBYTES = 2 * 64 * 128, MBYTES = QT == 4 ? 8192 : 0;
+    static constexpr int A_OFF = 0, B_OFF = A_OFF + SA * ABYTES, R_OFF = B_OFF + SB * BBYTES;
+    static constexpr int M_OFF = R_OFF + R * RAWB, D_OFF = M_OFF + R * MBYTES, BAR_OFF = D_OFF + 4 * BM * 8;
+    static constexpr int NBARS = 2 * R + 2 * SB + 2 * SA + 5;
+    static constexpr int SLOT_OFF = BAR_OFF + NBARS * 8, TOTAL = SLOT_OFF + 16;
+};
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void l2_prefetch(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void converters_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * WS_CONV) : "memory"); }
+
+template <int QT>
+__global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
+    static_assert(BM * 4 == 32 * WS_CONV, "the reduce-scatter tail maps 4 columns x 128 rows onto the converters");
+    using C = WsCfg<QT>;
+    constexpr int BN = 64, R = C::R, SA = C::SA, SB = C::SB, UNIT = C::UNIT;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    constexpr int UNIT = tunit_bytes(QT), AST = BM * 128, BST = 2 * BN * 128;
-    constexpr int NST = QT == 4 ? 4096 + 2 * BN * 32 : 0;
-    uint8_t *Bring = smem + 2 * AST;
-    uint8_t *mins = Bring + 4 * BST;
-    uint8_t *raw = mins + 2 * NST;
-    float2 *dsc = reinterpret_cast<float2 *>(raw + 2 * 8 * UNIT);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(dsc + 2 * BM);
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 8);
+    uint8_t *As = smem + C::A_OFF, *Bs = smem + C::B_OFF, *raw = smem + C::R_OFF, *mins = smem + C::M_OFF;
+    float2 *dsc = reinterpret_cast<float2 *>(smem + C::D_OFF);  // [4][BM] (d, dmin) per unit column
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *raw_full = bars, *raw_empty = bars + R, *b_full = bars + 2 * R, *b_empty = b_full + SB;
+    uint64_t *a_full = b_empty + SB, *a_empty = a_full + SA, *acc_full = a_empty + SA, *acc_empty = acc_full + 2;
+    uint64_t *mma_done = acc_empty + 2;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + C::SLOT_OFF);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rank = a.CL > 1 ? (int)ctarank() : 0;
     const int tile = a.CL > 1 ? (int)clusterid() : (int)blockIdx.x;
@@ -505,12 +636,29 @@ __global__ void __launch_bounds__(TTHR, 1) k_gemm_tiled(GArgs a) {
     const int kb0 = (int)((long long)rank * a.nkb / a.CL), kb1 = (int)((long long)(rank + 1) * a.nkb / a.CL);
     const int nu = kb1 - kb0;            // unit columns of this CTA
     const int nut = min(8, a.RT - rt0);  // unit rows present in this tile
+    const int nit = 4 * nu;              // 64-K steps
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tslot)), "r"(8 * BN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    if (tid == 0) {
-        for (int i = 0; i < 8; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&bars[i])));
+    if (tid == 32) {
+        for (int s = 0; s < R; s++) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], WS_CONV + (QT == 4 ? 1 : 0));  // converter warps (+ the mins MMA's commit)
+        }
+        for (int s = 0; s < SB; s++) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
+        }
+        for (int s = 0; s < SA; s++) {
+            mbar_init(&a_full[s], WS_CONV);
+            mbar_init(&a_empty[s], 1);
+        }
+        for (int p = 0; p < 2; p++) {
+            mbar_init(&acc_full[p], 1);
+            mbar_init(&acc_empty[p], WS_CONV);
+        }
+        mbar_init(mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     tc_fence_before();
@@ -518,104 +666,155 @@ __global__ void __launch_bounds__(TTHR, 1) k_gemm_tiled(GArgs a) {
     tc_fence_after();
     const uint32_t tmem = *tslot;
     pdl_launch_dependents();
-    const int nit = 4 * (kb1 - kb0);
-    auto issue_b = [&](int j) {  // activation tile of iteration j (k-block 4 kb0 + j, this n-tile): hi and lo
-        const uint32_t bar = su32(&bars[4 + (j & 3)]);
-        uint8_t *dst = Bring + (j & 3) * BST;
-        const size_t off = ((size_t)(4 * kb0 + j) * a.Npad + n0) * BK;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)BST) : "memory");
-        bulk_copy(bar, dst, a.xh + off, BN * 128);
-        bulk_copy(bar, dst + BN * 128, a.xl + off, BN * 128);
-    };
-    auto issue_raw = [&](int i) {  // unit column kb0 + i into raw stage i & 1 (weights only)
-        const uint32_t bar = su32(&bars[i & 1]);
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)(nut * UNIT))
-                     : "memory");
-        for (int u = 0; u < nut; u++)
-            bulk_copy(bar, raw + (i & 1) * 8 * UNIT + u * UNIT,
-                      a.wt + ((size_t)(rt0 + u) * a.KBU + kb0 + i) * UNIT, UNIT);
-    };
-    if (tid == 0)
-        for (int i = 0; i < 2 && i < nu; i++) issue_raw(i);
-    pdl_wait();  // X (prepared by the previous kernel), bias and Y are ready
-    if (tid == 0)
-        for (int j = 0; j < 2 && j < nit; j++) issue_b(j);
-    const uint32_t id = idesc(2 * BN);  // N = 2 BN: the hi tile rows then the lo tile rows
-    // readout geometry: TMEM lane quarter (warp % 4), column half (warp / 4)
-    const int q = warp & 3, cb = (warp >> 2) * (BN / 2), row = 32 * q + lane;
-    const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + cb;
-    float acc[BN / 2];
+    constexpr int NC = BN / 4;  // accumulator columns per converter warp
+    const int q = warp & 3, cb = (warp >> 2) * NC, row = 32 * q + lane;
+    float acc[NC];
 #pragma unroll
-    for (int i = 0; i < BN / 2; i++) acc[i] = 0.0f;
+    for (int i = 0; i < NC; i++) acc[i] = 0.0f;
     bool ok = true;
-    int it = 0;
-    for (int i = 0; i < nu; i++) {
-        const uint8_t *R = raw + (i & 1) * 8 * UNIT;
-        const int p = i & 1;
-        uint8_t *Mt = mins + p * NST, *Sh = Mt + 4096, *Sl = Sh + BN * 32;
-        if (ok) ok = bar_wait(su32(&bars[i & 1]), (uint32_t)((i >> 1) & 1));
-        for (int h = 0; h < 4; h++, it++) {
-            const int s = it & 1;
-            uint8_t *A = smem + s * AST, *Bh = Bring + (it & 3) * BST;
-            if (it >= 2 && ok) ok = bar_wait(su32(&bars[2 + s]), (uint32_t)(((it - 2) >> 1) & 1));
-            // B stage (it + 2) & 3 was last read by the MMAs of it - 2 (done): prefetch
-            if (tid == 0 && it + 2 < nit) issue_b(it + 2);
-            if (h == 1 && i > 0) {  // the previous block's MMAs are done (waited above): read it out
-                const int pp = (i - 1) & 1;
-                block_readout<QT, BN>(acc, tq + 4 * BN * pp, tq + 4 * BN * pp + 2 * BN, dsc[pp * BM + row]);
-            }
-            if (warp < nut) build_a<QT>(A, R + warp * UNIT, warp, h, lane, a.wscale, dsc + p * BM, Mt);
-            if (QT == 4 && h == 0)  // sub-block sums of x (x 2^-5), hi and lo, K = 8 (+ 8 zero)
-                for (int e = tid; e < BN * 2; e += TTHR) {
-                    const int r = e >> 1, kc = e & 1, n = n0 + r;
-                    uint4 hv = make_uint4(0u, 0u, 0u, 0u), lv = hv;
-                    if (kc == 0 && n < a.N) {
-                        const size_t off = (size_t)n * a.K32 + (size_t)(kb0 + i) * 8;
-                        hv = __ldg(reinterpret_cast<const uint4 *>(a.xsh + off));
-                        lv = __ldg(reinterpret_cast<const uint4 *>(a.xsl + off));
-                    }
-                    put_core(Sh, r, kc, hv);
-                    put_core(Sl, r, kc, lv);
+    if (warp == WS_CONV) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const size_t xs_tile = ((size_t)(a.Npad / 64)) * 4096;  // bytes per unit column of the sums tiles
+            auto weights = [&](int i) {  // unit column i: expect its bytes, copy its 8 weight units
+                uint64_t *bar = &raw_full[i % R];
+                mbar_expect(bar, (uint32_t)(nut * UNIT + (QT == 4 ? 4096 : 0)));
+                for (int u = 0; u < nut; u++)
+                    bulk_copy(su32(bar), raw + (i % R) * C::RAWB + u * UNIT,
+                              a.wt + ((size_t)(rt0 + u) * a.KBU + kb0 + i) * UNIT, UNIT);
+                if (i + R < nu)
+                    for (int u = 0; u < nut; u++)
+                        l2_prefetch(a.wt + ((size_t)(rt0 + u) * a.KBU + kb0 + i + R) * UNIT, UNIT);
+            };
+            auto sums = [&](int i) {  // Q4_K: the unit column's sums tile (hi | lo rows of this token tile)
+                if (QT == 4)
+                    bulk_copy(su32(&raw_full[i % R]), mins + (i % R) * C::MBYTES + 4096,
+                              a.xs + (size_t)(kb0 + i) * xs_tile + (size_t)(n0 / 64) * 4096, 4096);
+            };
+            auto acts = [&](int j) {  // 64-K step j: activation tile, hi then lo
+                uint64_t *bar = &b_full[j % SB];
+                uint8_t *dst = Bs + (j % SB) * C::BBYTES;
+                const size_t off = ((size_t)(4 * kb0 + j) * a.Npad + n0) * BK;
+                mbar_expect(bar, (uint32_t)C::BBYTES);
+                bulk_copy(su32(bar), dst, a.xh + off, BN * 128);
+                bulk_copy(su32(bar), dst + BN * 128, a.xl + off, BN * 128);
+            };
+            const int npre = min(R, nu);
+            for (int i = 0; i < npre; i++) weights(i);
+            pdl_wait();  // activations and sums are written by the previous kernel
+            for (int i = 0; i < npre; i++) sums(i);
+            int nb_issued = min(SB, nit), nu_issued = npre;
+            for (int j = 0; j < nb_issued; j++) acts(j);
+            for (int it = 0; it < nit && ok; it++) {
+                if (it + SB < nit) {  // stage of step it is free once its MMAs are done
+                    ok = bar_wait(su32(&b_empty[it % SB]), (uint32_t)((it / SB) & 1));
+                    if (!ok) break;
+                    acts(it + SB);
+                    nb_issued = it + SB + 1;
                 }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            tc_fence_before();
-            __syncthreads();
-            if (tid == 0) {
-                if (ok) ok = bar_wait(su32(&bars[4 + (it & 3)]), (uint32_t)((it >> 2) & 1));  // B tile landed
-                tc_fence_after();
-                const uint32_t tmain = tmem + 4 * BN * p;
-#pragma unroll
-                for (int j = 0; j < BK / 16; j++)  // Bh and Bl are one 2 BN-row tile
-                    mma_f16(tmain, sdesc(su32(A) + 32 * j), sdesc(su32(Bh) + 32 * j), id, (h > 0 || j > 0) ? 1u : 0u);
-                if (QT == 4 && h == 0)  // Sh and Sl are one 2 BN-row tile
-                    mma_f16(tmain + 2 * BN, sdesc_plain(su32(Mt)), sdesc_plain(su32(Sh)), id, 0u);
-                mma_commit(su32(&bars[2 + s]));
+                if ((it & 3) == 3 && (it >> 2) + R < nu) {  // unit column it / 4 consumed: refill its stage
+                    const int i = it >> 2;
+                    ok = bar_wait(su32(&raw_empty[i % R]), (uint32_t)((i / R) & 1));
+                    if (!ok) break;
+                    weights(i + R);
+                    sums(i + R);
+                    nu_issued = i + R + 1;
+                }
             }
+            // every copy issued has landed before the CTA can exit (bounded;
+            // immediate when the consumers saw them)
+            for (int i = max(0, nu_issued - R); i < nu_issued; i++)
+                (void)bar_wait(su32(&raw_full[i % R]), (uint32_t)((i / R) & 1));
+            for (int j = max(0, nb_issued - SB); j < nb_issued; j++)
+                (void)bar_wait(su32(&b_full[j % SB]), (uint32_t)((j / SB) & 1));
         }
-        // every warp has converted this raw stage (the barrier above): refill it
-        if (tid == 0 && i + 2 < nu) issue_raw(i + 2);
-    }
-    if (it > 0 && ok) ok = bar_wait(su32(&bars[2 + ((it - 1) & 1)]), (uint32_t)(((it - 1) >> 1) & 1));
-    if (!ok && tid == 0) {  // bounded drain of the copies still in flight
-        for (int i = max(0, nu - 2); i < nu; i++) (void)bar_wait(su32(&bars[i & 1]), (uint32_t)((i >> 1) & 1));
-        for (int j = max(0, nit - 4); j < nit; j++) (void)bar_wait(su32(&bars[4 + (j & 3)]), (uint32_t)((j >> 2) & 1));
-    }
-    tc_fence_after();
-    if (nu > 0) {
-        const int pp = (nu - 1) & 1;
-        block_readout<QT, BN>(acc, tq + 4 * BN * pp, tq + 4 * BN * pp + 2 * BN, dsc[pp * BM + row]);
+        __syncwarp();
+    } else if (warp == WS_CONV + 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t id = idesc(2 * BN);  // N = 2 BN: hi tile rows then lo tile rows
+            for (int it = 0; it < nit; it++) {
+                const int i = it >> 2, h = it & 3, p = i & 1;
+                if (ok) ok = bar_wait(su32(&a_full[it % SA]), (uint32_t)((it / SA) & 1));
+                if (ok) ok = bar_wait(su32(&b_full[it % SB]), (uint32_t)((it / SB) & 1));
+                if (ok && h == 0 && i >= 2) ok = bar_wait(su32(&acc_empty[p]), (uint32_t)(((i - 2) >> 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+                // 16 fp16 = 32 bytes per K step = 2 in the descriptors' address field
+                const uint64_t ad = sdesc(su32(As + (it % SA) * C::ABYTES)), bd = sdesc(su32(Bs + (it % SB) * C::BBYTES));
+                const uint32_t tmain = tmem + 4 * BN * p;
+                mma_f16(tmain, ad, bd, id, h > 0 ? 1u : 0u);
+#pragma unroll
+                for (int j = 1; j < BK / 16; j++) mma_f16(tmain, ad + 2 * j, bd + 2 * j, id, 1u);
+                if (QT == 4 && h == 0) {
+                    const uint32_t Mt = su32(mins + (i % R) * C::MBYTES);
+                    mma_f16(tmain + 2 * BN, sdesc_plain(Mt), sdesc_plain(Mt + 4096), id, 0u);
+                }
+                mma_commit(su32(&a_empty[it % SA]));
+                mma_commit(su32(&b_empty[it % SB]));
+                if (QT == 4 && h == 0) mma_commit(su32(&raw_empty[i % R]));
+                if (h == 3) mma_commit(su32(&acc_full[p]));
+            }
+            mma_commit(su32(mma_done));  // every MMA issued above is complete once this arrives
+            (void)bar_wait(su32(mma_done), 0u);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- converters / accumulator readout ----------------
+        const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + cb;
+        auto readout = [&](int iu) {
+            converters_sync();  // the block scales of unit column iu (every warp's rows) are in dsc
+            const int p = iu & 1;
+            if (ok) ok = bar_wait(su32(&acc_full[p]), (uint32_t)((iu >> 1) & 1));
+            tc_fence_after();
+            if (ok) block_readout_n<QT, BN, NC>(acc, tq + 4 * BN * p, tq + 4 * BN * p + 2 * BN, dsc[(iu & 3) * BM + row]);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[p]);
+        };
+        const int u = warp & 7, part = warp >> 3;
+        const bool has = u < nut;
+        ConvUnit cu;
+        for (int i = 0; i < nu; i++) {
+            const int s = i % R;
+            if (ok) ok = bar_wait(su32(&raw_full[s]), (uint32_t)((i / R) & 1));
+            const uint8_t *U = raw + s * C::RAWB + u * UNIT;
+            if (ok && has) conv_unit<QT>(cu, U, part, lane);
+            // step H of unit column i (64-K step it = 4 i + H)
+            auto step = [&](auto Hc) {
+                constexpr int H = decltype(Hc)::value;
+                const int it = 4 * i + H;
+                if (it >= SA && ok) ok = bar_wait(su32(&a_empty[it % SA]), (uint32_t)(((it - SA) / SA) & 1));
+                if (ok && has) {
+                    // the mins stage and the dsc slot are free: their last readers (the MMAs of
+                    // unit column i - R, the readout of unit column i - 4) are done
+                    if (H == 0 && part == 0)
+                        conv_unit_side<QT>(cu, U, u, lane, a.wscale, dsc + (i & 3) * BM, mins + s * C::MBYTES);
+                    conv_step<QT, H>(As + (it % SA) * C::ABYTES, U, cu, u, part, lane, a.wscale);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[it % SA]);
+                // previous unit column: its last MMAs were issued about three steps ago,
+                // and the MMAs of the next unit column need its accumulator back
+                if (H == 2 && i > 0) readout(i - 1);
+            };
+            step(std::integral_constant<int, 0>());
+            step(std::integral_constant<int, 1>());
+            step(std::integral_constant<int, 2>());
+            step(std::integral_constant<int, 3>());
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[s]);
+        }
+        if (nu > 0) readout(nu - 1);
     }
     tc_fence_before();
-    __syncthreads();
+    __syncthreads();  // MMAs complete, TMEM read
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(8 * BN));
-    // epilogue from registers (cluster split: partials added in the leader's shared memory)
+    pdl_wait();  // bias, Y and the activation scales are ready
     const int m = m0 + row;
     if (a.CL == 1) {
-#pragma unroll
-        for (int c = 0; c < BN / 2; c++) {
-            const int n = n0 + cb + c;
-            epi_col(a, n, m, acc[c] * (n < a.N ? a.xinv[n] : 0.0f));
-        }
+        if (warp < WS_CONV) epi_cols<NC>(a, n0 + cb, m, acc);
         return;
     }
     // reduce-scatter over the cluster: rank o finishes columns [o W, (o + 1) W),
@@ -623,32 +822,50 @@ __global__ void __launch_bounds__(TTHR, 1) k_gemm_tiled(GArgs a) {
     // buffer slot [source rank][column][row] (plain remote stores), then each
     // rank sums its CL slots
     const int W = BN / a.CL;
-    float *buf = reinterpret_cast<float *>(smem);  // [CL][W][128] over the idle stages
+    float *buf = reinterpret_cast<float *>(smem);  // [CL][W][128] over the idle A stages
     cl_arrive();
     cl_wait();  // every rank is done with its stages
+    if (warp < WS_CONV)
 #pragma unroll
-    for (int c = 0; c < BN / 2; c++) {
-        const int col = cb + c, o = col / W;
-        const uint32_t la = su32(&buf[((size_t)rank * W + (col - o * W)) * BM + row]);
-        uint32_t ra;
-        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"((uint32_t)o));
-        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(acc[c]) : "memory");
-    }
+        for (int c = 0; c < NC; c++) {
+            const int col = cb + c, o = col / W;
+            const uint32_t la = su32(&buf[((size_t)rank * W + (col - o * W)) * BM + row]);
+            uint32_t ra;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"((uint32_t)o));
+            asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(acc[c]) : "memory");
+        }
     cl_arrive();
     cl_wait();  // every slot written
-    for (int e = tid; e < W * BM; e += TTHR) {
-        const int cc = e / BM, r = e % BM, n = n0 + rank * W + cc, mm = m0 + r;  // cc is warp-uniform
-        float v = 0.0f;
-        for (int src = 0; src < a.CL; src++) v += buf[((size_t)src * W + cc) * BM + r];
-        epi_col(a, n, mm, v * (n < a.N ? a.xinv[n] : 0.0f));
+    // this rank's W columns x 128 rows over the converter threads: row
+    // tid % 128, columns tid / 128 + 4 k (warp-uniform), k < W / 4 <= 8
+    if (warp < WS_CONV) {
+        const int r = tid & (BM - 1), c0 = tid >> 7;
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            v[k] = 0.0f;
+            if (c0 + 4 * k < W)
+                for (int src = 0; src < a.CL; src++) v[k] += buf[((size_t)src * W + c0 + 4 * k) * BM + r];
+        }
+        epi_strided(a, n0 + rank * W + c0, W - c0, m0 + r, v);
     }
 }
 
 // Position of column src (within its 64-column block) in the fast path's
-// order: the order cvt_nib / cvt_byte produce (see build_a).
+// order: the order cvt_nib_fma / cvt_byte produce (see conv_step).
 __device__ __forceinline__ int perm_pos(int src) {
     const int w = src & 31, i = w & 3, slot = (w & 16 ? 4 : 0) + (i == 1 ? 2 : i == 2 ? 1 : i);
     return 8 * (4 * (src >> 5) + ((w & 15) >> 2)) + slot;
+}
+
+// Byte offset of the sum of 32-column chunk j of token row n in the Q4_K
+// sums tiles: per unit column (256 K) and 64-token tile one 4 KB tile of
+// 128 rows (hi sums of the 64 tokens, then lo) x 16 K, K-major without
+// swizzle (8-row x 16-byte core matrices; K columns 8-15 stay zero), the
+// B operand of the mins MMA.
+__device__ __forceinline__ size_t sums_offset(int n, int j, int Npad) {
+    const int r = n & 63, kb = j >> 3, sub = j & 7;
+    return ((size_t)kb * (Npad / 64) + (n >> 6)) * 4096 + (r >> 3) * 256 + (r & 7) * 16 + sub * 2;
 }
 
 // Activation prep: one CTA per token row n.  The row (SwiGLU: silu(x) * x2)
@@ -660,7 +877,7 @@ __device__ __forceinline__ int perm_pos(int src) {
 __global__ void __launch_bounds__(256) k_gemm_prep_x(const float *__restrict__ x, int ldx, int K, int pro,
                                                      const float *__restrict__ pw, const float *__restrict__ pb,
                                                      const float *__restrict__ x2, float eps, __half *xh, __half *xl,
-                                                     float *xinv, int perm, __half *xsh, __half *xsl, int N, int Npad) {
+                                                     float *xinv, int perm, uint8_t *xs, int N, int Npad) {
     extern __shared__ float row[];  // [K]
     __shared__ float red[32];
     pdl_launch_dependents();
@@ -672,6 +889,12 @@ __global__ void __launch_bounds__(256) k_gemm_prep_x(const float *__restrict__ x
             xh[o] = __float2half_rn(0.0f);
             xl[o] = __float2half_rn(0.0f);
         }
+        if (xs)
+            for (int j = tid; j < K / 32; j += blockDim.x) {
+                uint8_t *p = xs + sums_offset(n, j, Npad);
+                *reinterpret_cast<__half *>(p) = __float2half_rn(0.0f);
+                *reinterpret_cast<__half *>(p + 2048) = __float2half_rn(0.0f);
+            }
         return;
     }
     const float *xr = x + (size_t)n * ldx, *x2r = pro == LMC_PRO_SWIGLU ? x2 + (size_t)n * ldx : nullptr;
@@ -723,12 +946,13 @@ __global__ void __launch_bounds__(256) k_gemm_prep_x(const float *__restrict__ x
         }
         xh[o] = h;
         xl[o] = __float2half_rn(v - __half2float(h));
-        if (xsh) {
+        if (xs) {
             const float t = warp_sum(v) * (1.0f / 32.0f);
             if ((tid & 31) == 0) {
                 const __half th = __float2half_rn(t);
-                xsh[(size_t)n * (K / 32) + k / 32] = th;
-                xsl[(size_t)n * (K / 32) + k / 32] = __float2half_rn(t - __half2float(th));
+                uint8_t *p = xs + sums_offset(n, k >> 5, Npad);
+                *reinterpret_cast<__half *>(p) = th;
+                *reinterpret_cast<__half *>(p + 2048) = __float2half_rn(t - __half2float(th));
             }
         }
     }
@@ -755,7 +979,8 @@ __global__ void k_absmax(const uint8_t *__restrict__ w, size_t n_groups, unsigne
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-static __half *g_xh = NULL, *g_xl = NULL, *g_xsh = NULL, *g_xsl = NULL;
+static __half *g_xh = NULL, *g_xl = NULL;
+static uint8_t *g_xs = NULL;
 static float *g_xinv = NULL;
 static size_t g_x_cap = 0;  // elements of xh / xl
 static int g_xinv_cap = 0;
@@ -769,9 +994,8 @@ extern "C" int lmc_gemm_reserve(int N, int K, cudaStream_t s) {
         return lmc_set_error(LMC_ERR_INVALID, "gemm: workspace must be reserved before stream capture");
     if (g_xh) cudaFree(g_xh);
     if (g_xl) cudaFree(g_xl);
-    if (g_xsh) cudaFree(g_xsh);
-    if (g_xsl) cudaFree(g_xsl);
-    g_xsh = g_xsl = NULL;
+    if (g_xs) cudaFree(g_xs);
+    g_xs = NULL;
     if (g_xinv) cudaFree(g_xinv);
     g_xh = g_xl = NULL;
     g_xinv = NULL;
@@ -779,8 +1003,9 @@ extern "C" int lmc_gemm_reserve(int N, int K, cudaStream_t s) {
     g_xinv_cap = 0;
     LMC_CUDA_TRY(cudaMalloc(&g_xh, need * sizeof(__half)));
     LMC_CUDA_TRY(cudaMalloc(&g_xl, need * sizeof(__half)));
-    LMC_CUDA_TRY(cudaMalloc(&g_xsh, (need / 32 + 8) * sizeof(__half)));
-    LMC_CUDA_TRY(cudaMalloc(&g_xsl, (need / 32 + 8) * sizeof(__half)));
+    // sums tiles: K N / 4 bytes; K columns 8-15 of every tile stay zero
+    LMC_CUDA_TRY(cudaMalloc(&g_xs, need / 4 + 4096));
+    LMC_CUDA_TRY(cudaMemset(g_xs, 0, need / 4 + 4096));
     LMC_CUDA_TRY(cudaMalloc(&g_xinv, (size_t)N * sizeof(float)));
     g_x_cap = need;
     g_xinv_cap = N;
@@ -880,8 +1105,7 @@ extern "C" int lmc_gemm_launch(const lmc_qtensor *t, const float *d_x, int ldx, 
     LMC_LAUNCH("gemm prep", k_gemm_prep_x, Npad, 256, (size_t)K * 4, s, d_x, ldx, K, ex ? ex->pro : LMC_PRO_NONE,
                ex ? ex->w : (const float *)NULL, ex ? ex->b : (const float *)NULL, ex ? ex->x2 : (const float *)NULL,
                ex ? ex->eps : 0.0f, g_xh, g_xl, g_xinv, fast ? 1 : 0,
-               fast && t->type == LMC_TYPE_Q4_K ? g_xsh : (__half *)NULL,
-               fast && t->type == LMC_TYPE_Q4_K ? g_xsl : (__half *)NULL, N, Npad);
+               fast && t->type == LMC_TYPE_Q4_K ? g_xs : (uint8_t *)NULL, N, Npad);
     GArgs a = {};
     a.w = (const uint8_t *)t->blocks;
     a.M = M;
@@ -902,9 +1126,7 @@ extern "C" int lmc_gemm_launch(const lmc_qtensor *t, const float *d_x, int ldx, 
     a.wt = (const uint8_t *)t->tiled;
     a.RT = t->tiled_rows / 16;
     a.KBU = K / 256;
-    a.xsh = g_xsh;
-    a.xsl = g_xsl;
-    a.K32 = K / 32;
+    a.xs = g_xs;
     a.Npad = Npad;
     const void *fn = NULL;
     size_t smem;
@@ -913,11 +1135,9 @@ extern "C" int lmc_gemm_launch(const lmc_qtensor *t, const float *d_x, int ldx, 
         const int qt = t->type == LMC_TYPE_Q4_K ? 4 : t->type == LMC_TYPE_Q6_K ? 6 : 8;
         a.BN = 64;
         a.nkb = K / 256;
-        smem = 2 * (size_t)BM * 128 + 4 * (size_t)(2 * a.BN * 128) + (qt == 4 ? 2 * (size_t)(4096 + 2 * a.BN * 32) : 0) +
-               2 * 8 * (size_t)tunit_bytes(qt) + 2 * BM * 8 + 128 + 1024;
-        fn = qt == 4 ? (const void *)k_gemm_tiled<4, 64> : qt == 6 ? (const void *)k_gemm_tiled<6, 64>
-                                                                 : (const void *)k_gemm_tiled<8, 64>;
-        nthr = TTHR;
+        smem = (qt == 4 ? WsCfg<4>::TOTAL : qt == 6 ? WsCfg<6>::TOTAL : WsCfg<8>::TOTAL) + 1024;
+        fn = qt == 4 ? (const void *)k_gemm_ws<4> : qt == 6 ? (const void *)k_gemm_ws<6> : (const void *)k_gemm_ws<8>;
+        nthr = WS_THREADS;
         min_kb = 1;
     } else {
         a.BN = N <= 64 ? 64 : N <= 128 ? 128 : 256;
