@@ -598,7 +598,8 @@ template <int QT> struct WsCfg {
     static constexpr int ABYTES = BM * 128, BBYTES = 2 * 64 * 128, MBYTES = QT == 4 ? 8192 : 0;
     static constexpr int A_OFF = 0, B_OFF = A_OFF + SA * ABYTES, R_OFF = B_OFF + SB * BBYTES;
     static constexpr int M_OFF = R_OFF + R * RAWB, D_OFF = M_OFF + R * MBYTES, BAR_OFF = D_OFF + 4 * BM * 8;
-    static constexpr int NBARS = 2 * R + 2 * SB + 2 * SA + 5;
+    static_assert(SA == SB, "one full / empty barrier pair per stage (A tile and activation tile)");
+    static constexpr int NBARS = 2 * R + 2 * SA + 5;
     static constexpr int SLOT_OFF = BAR_OFF + NBARS * 8, TOTAL = SLOT_OFF + 16;
 };
 __device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
@@ -625,8 +626,11 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
     uint8_t *As = smem + C::A_OFF, *Bs = smem + C::B_OFF, *raw = smem + C::R_OFF, *mins = smem + C::M_OFF;
     float2 *dsc = reinterpret_cast<float2 *>(smem + C::D_OFF);  // [4][BM] (d, dmin) per unit column
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
-    uint64_t *raw_full = bars, *raw_empty = bars + R, *b_full = bars + 2 * R, *b_empty = b_full + SB;
-    uint64_t *a_full = b_empty + SB, *a_empty = a_full + SA, *acc_full = a_empty + SA, *acc_empty = acc_full + 2;
+    // full[s]: the converter warps' A tile and the producer's activation tile
+    // (its expect-tx arrival) of the step in stage s; empty[s]: that step's MMAs
+    // are done (one commit), both tiles may be refilled
+    uint64_t *raw_full = bars, *raw_empty = bars + R, *full = bars + 2 * R, *empty = full + SA;
+    uint64_t *acc_full = empty + SA, *acc_empty = acc_full + 2;
     uint64_t *mma_done = acc_empty + 2;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + C::SLOT_OFF);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -646,13 +650,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
             mbar_init(&raw_full[s], 1);
             mbar_init(&raw_empty[s], WS_CONV + (QT == 4 ? 1 : 0));  // converter warps (+ the mins MMA's commit)
         }
-        for (int s = 0; s < SB; s++) {
-            mbar_init(&b_full[s], 1);
-            mbar_init(&b_empty[s], 1);
-        }
         for (int s = 0; s < SA; s++) {
-            mbar_init(&a_full[s], WS_CONV);
-            mbar_init(&a_empty[s], 1);
+            mbar_init(&full[s], WS_CONV + 1);
+            mbar_init(&empty[s], 1);
         }
         for (int p = 0; p < 2; p++) {
             mbar_init(&acc_full[p], 1);
@@ -692,7 +692,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
                               a.xs + (size_t)(kb0 + i) * xs_tile + (size_t)(n0 / 64) * 4096, 4096);
             };
             auto acts = [&](int j) {  // 64-K step j: activation tile, hi then lo
-                uint64_t *bar = &b_full[j % SB];
+                uint64_t *bar = &full[j % SB];
                 uint8_t *dst = Bs + (j % SB) * C::BBYTES;
                 const size_t off = ((size_t)(4 * kb0 + j) * a.Npad + n0) * BK;
                 mbar_expect(bar, (uint32_t)C::BBYTES);
@@ -707,7 +707,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
             for (int j = 0; j < nb_issued; j++) acts(j);
             for (int it = 0; it < nit && ok; it++) {
                 if (it + SB < nit) {  // stage of step it is free once its MMAs are done
-                    ok = bar_wait(su32(&b_empty[it % SB]), (uint32_t)((it / SB) & 1));
+                    ok = bar_wait(su32(&empty[it % SB]), (uint32_t)((it / SB) & 1));
                     if (!ok) break;
                     acts(it + SB);
                     nb_issued = it + SB + 1;
@@ -726,22 +726,24 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
             for (int i = max(0, nu_issued - R); i < nu_issued; i++)
                 (void)bar_wait(su32(&raw_full[i % R]), (uint32_t)((i / R) & 1));
             for (int j = max(0, nb_issued - SB); j < nb_issued; j++)
-                (void)bar_wait(su32(&b_full[j % SB]), (uint32_t)((j / SB) & 1));
+                (void)bar_wait(su32(&full[j % SB]), (uint32_t)((j / SB) & 1));
         }
         __syncwarp();
     } else if (warp == WS_CONV + 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t id = idesc(2 * BN);  // N = 2 BN: hi tile rows then lo tile rows
+            // stage s: the base descriptors plus s stages in 16-byte units (the address field)
+            const uint64_t adesc0 = sdesc(su32(As)), bdesc0 = sdesc(su32(Bs));
             for (int it = 0; it < nit; it++) {
                 const int i = it >> 2, h = it & 3, p = i & 1;
-                if (ok) ok = bar_wait(su32(&a_full[it % SA]), (uint32_t)((it / SA) & 1));
-                if (ok) ok = bar_wait(su32(&b_full[it % SB]), (uint32_t)((it / SB) & 1));
+                if (ok) ok = bar_wait(su32(&full[it % SA]), (uint32_t)((it / SA) & 1));
                 if (ok && h == 0 && i >= 2) ok = bar_wait(su32(&acc_empty[p]), (uint32_t)(((i - 2) >> 1) & 1));
                 if (!ok) break;
                 tc_fence_after();
                 // 16 fp16 = 32 bytes per K step = 2 in the descriptors' address field
-                const uint64_t ad = sdesc(su32(As + (it % SA) * C::ABYTES)), bd = sdesc(su32(Bs + (it % SB) * C::BBYTES));
+                const uint64_t ad = adesc0 + (uint64_t)((it % SA) * (C::ABYTES >> 4)),
+                               bd = bdesc0 + (uint64_t)((it % SA) * (C::BBYTES >> 4));
                 const uint32_t tmain = tmem + 4 * BN * p;
                 mma_f16(tmain, ad, bd, id, h > 0 ? 1u : 0u);
 #pragma unroll
@@ -750,8 +752,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
                     const uint32_t Mt = su32(mins + (i % R) * C::MBYTES);
                     mma_f16(tmain + 2 * BN, sdesc_plain(Mt), sdesc_plain(Mt + 4096), id, 0u);
                 }
-                mma_commit(su32(&a_empty[it % SA]));
-                mma_commit(su32(&b_empty[it % SB]));
+                mma_commit(su32(&empty[it % SA]));
                 if (QT == 4 && h == 0) mma_commit(su32(&raw_empty[i % R]));
                 if (h == 3) mma_commit(su32(&acc_full[p]));
             }
@@ -784,7 +785,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
             auto step = [&](auto Hc) {
                 constexpr int H = decltype(Hc)::value;
                 const int it = 4 * i + H;
-                if (it >= SA && ok) ok = bar_wait(su32(&a_empty[it % SA]), (uint32_t)(((it - SA) / SA) & 1));
+                if (it >= SA && ok) ok = bar_wait(su32(&empty[it % SA]), (uint32_t)(((it - SA) / SA) & 1));
                 if (ok && has) {
                     // the mins stage and the dsc slot are free: their last readers (the MMAs of
                     // unit column i - R, the readout of unit column i - 4) are done
@@ -794,7 +795,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&a_full[it % SA]);
+                if (lane == 0) mbar_arrive(&full[it % SA]);
                 // previous unit column: its last MMAs were issued about three steps ago,
                 // and the MMAs of the next unit column need its accumulator back
                 if (H == 2 && i > 0) readout(i - 1);
