@@ -598,8 +598,9 @@ template <int QT> struct WsCfg {
     static constexpr int ABYTES = BM * 128, BBYTES = 2 * 64 * 128, MBYTES = QT == 4 ? 8192 : 0;
     static constexpr int A_OFF = 0, B_OFF = A_OFF + SA * ABYTES, R_OFF = B_OFF + SB * BBYTES;
     static constexpr int M_OFF = R_OFF + R * RAWB, D_OFF = M_OFF + R * MBYTES, BAR_OFF = D_OFF + 4 * BM * 8;
-    static_assert(SA == SB, "one full / empty barrier pair per stage (A tile and activation tile)");
-    static constexpr int NBARS = 2 * R + 2 * SA + 5;
+    static_assert(SA == SB && SA == 4, "hand-offs by pairs of stages (128 K): two pair slots");
+    static constexpr int PS = SA / 2;
+    static constexpr int NBARS = 2 * R + 2 * PS + 5;
     static constexpr int SLOT_OFF = BAR_OFF + NBARS * 8, TOTAL = SLOT_OFF + 16;
 };
 __device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
@@ -620,17 +621,19 @@ template <int QT>
 __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
     static_assert(BM * 4 == 32 * WS_CONV, "the reduce-scatter tail maps 4 columns x 128 rows onto the converters");
     using C = WsCfg<QT>;
-    constexpr int BN = 64, R = C::R, SA = C::SA, SB = C::SB, UNIT = C::UNIT;
+    constexpr int BN = 64, R = C::R, UNIT = C::UNIT;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *As = smem + C::A_OFF, *Bs = smem + C::B_OFF, *raw = smem + C::R_OFF, *mins = smem + C::M_OFF;
     float2 *dsc = reinterpret_cast<float2 *>(smem + C::D_OFF);  // [4][BM] (d, dmin) per unit column
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
-    // full[s]: the converter warps' A tile and the producer's activation tile
-    // (its expect-tx arrival) of the step in stage s; empty[s]: that step's MMAs
-    // are done (one commit), both tiles may be refilled
-    uint64_t *raw_full = bars, *raw_empty = bars + R, *full = bars + 2 * R, *empty = full + SA;
-    uint64_t *acc_full = empty + SA, *acc_empty = acc_full + 2;
+    // Hand-offs are by pairs of 64-K steps (128 K, stages 2 ps and 2 ps + 1 of
+    // pair slot ps): full[ps] = the converter warps' A tiles and the producer's
+    // activation tiles (its expect-tx arrival) of the pair; empty[ps] = the
+    // pair's MMAs are done (one commit), all four tiles may be refilled.
+    constexpr int PS = C::PS;
+    uint64_t *raw_full = bars, *raw_empty = bars + R, *full = bars + 2 * R, *empty = full + PS;
+    uint64_t *acc_full = empty + PS, *acc_empty = acc_full + 2;
     uint64_t *mma_done = acc_empty + 2;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + C::SLOT_OFF);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -640,7 +643,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
     const int kb0 = (int)((long long)rank * a.nkb / a.CL), kb1 = (int)((long long)(rank + 1) * a.nkb / a.CL);
     const int nu = kb1 - kb0;            // unit columns of this CTA
     const int nut = min(8, a.RT - rt0);  // unit rows present in this tile
-    const int nit = 4 * nu;              // 64-K steps
+    const int nq = 2 * nu;               // 128-K hand-offs (pairs of 64-K steps)
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tslot)), "r"(8 * BN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -650,7 +653,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
             mbar_init(&raw_full[s], 1);
             mbar_init(&raw_empty[s], WS_CONV + (QT == 4 ? 1 : 0));  // converter warps (+ the mins MMA's commit)
         }
-        for (int s = 0; s < SA; s++) {
+        for (int s = 0; s < PS; s++) {
             mbar_init(&full[s], WS_CONV + 1);
             mbar_init(&empty[s], 1);
         }
@@ -691,29 +694,32 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
                     bulk_copy(su32(&raw_full[i % R]), mins + (i % R) * C::MBYTES + 4096,
                               a.xs + (size_t)(kb0 + i) * xs_tile + (size_t)(n0 / 64) * 4096, 4096);
             };
-            auto acts = [&](int j) {  // 64-K step j: activation tile, hi then lo
-                uint64_t *bar = &full[j % SB];
-                uint8_t *dst = Bs + (j % SB) * C::BBYTES;
-                const size_t off = ((size_t)(4 * kb0 + j) * a.Npad + n0) * BK;
-                mbar_expect(bar, (uint32_t)C::BBYTES);
-                bulk_copy(su32(bar), dst, a.xh + off, BN * 128);
-                bulk_copy(su32(bar), dst + BN * 128, a.xl + off, BN * 128);
+            auto acts = [&](int q) {  // pair q: activation tiles (hi then lo) of steps 2 q, 2 q + 1
+                uint64_t *bar = &full[q % PS];
+                mbar_expect(bar, (uint32_t)(2 * C::BBYTES));
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    uint8_t *dst = Bs + (2 * (q % PS) + e) * C::BBYTES;
+                    const size_t off = ((size_t)(4 * kb0 + 2 * q + e) * a.Npad + n0) * BK;
+                    bulk_copy(su32(bar), dst, a.xh + off, BN * 128);
+                    bulk_copy(su32(bar), dst + BN * 128, a.xl + off, BN * 128);
+                }
             };
             const int npre = min(R, nu);
             for (int i = 0; i < npre; i++) weights(i);
             pdl_wait();  // activations and sums are written by the previous kernel
             for (int i = 0; i < npre; i++) sums(i);
-            int nb_issued = min(SB, nit), nu_issued = npre;
-            for (int j = 0; j < nb_issued; j++) acts(j);
-            for (int it = 0; it < nit && ok; it++) {
-                if (it + SB < nit) {  // stage of step it is free once its MMAs are done
-                    ok = bar_wait(su32(&empty[it % SB]), (uint32_t)((it / SB) & 1));
+            int nq_issued = min(PS, nq), nu_issued = npre;
+            for (int q = 0; q < nq_issued; q++) acts(q);
+            for (int q = 0; q < nq && ok; q++) {
+                if (q + PS < nq) {  // the pair slot of q is free once its MMAs are done
+                    ok = bar_wait(su32(&empty[q % PS]), (uint32_t)((q / PS) & 1));
                     if (!ok) break;
-                    acts(it + SB);
-                    nb_issued = it + SB + 1;
+                    acts(q + PS);
+                    nq_issued = q + PS + 1;
                 }
-                if ((it & 3) == 3 && (it >> 2) + R < nu) {  // unit column it / 4 consumed: refill its stage
-                    const int i = it >> 2;
+                if ((q & 1) == 1 && (q >> 1) + R < nu) {  // unit column q / 2 consumed: refill its stage
+                    const int i = q >> 1;
                     ok = bar_wait(su32(&raw_empty[i % R]), (uint32_t)((i / R) & 1));
                     if (!ok) break;
                     weights(i + R);
@@ -725,8 +731,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
             // immediate when the consumers saw them)
             for (int i = max(0, nu_issued - R); i < nu_issued; i++)
                 (void)bar_wait(su32(&raw_full[i % R]), (uint32_t)((i / R) & 1));
-            for (int j = max(0, nb_issued - SB); j < nb_issued; j++)
-                (void)bar_wait(su32(&full[j % SB]), (uint32_t)((j / SB) & 1));
+            for (int q = max(0, nq_issued - PS); q < nq_issued; q++)
+                (void)bar_wait(su32(&full[q % PS]), (uint32_t)((q / PS) & 1));
         }
         __syncwarp();
     } else if (warp == WS_CONV + 1) {
@@ -735,26 +741,29 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
             const uint32_t id = idesc(2 * BN);  // N = 2 BN: hi tile rows then lo tile rows
             // stage s: the base descriptors plus s stages in 16-byte units (the address field)
             const uint64_t adesc0 = sdesc(su32(As)), bdesc0 = sdesc(su32(Bs));
-            for (int it = 0; it < nit; it++) {
-                const int i = it >> 2, h = it & 3, p = i & 1;
-                if (ok) ok = bar_wait(su32(&full[it % SA]), (uint32_t)((it / SA) & 1));
-                if (ok && h == 0 && i >= 2) ok = bar_wait(su32(&acc_empty[p]), (uint32_t)(((i - 2) >> 1) & 1));
+            for (int q = 0; q < nq; q++) {
+                const int i = q >> 1, h2 = q & 1, p = i & 1;
+                if (ok) ok = bar_wait(su32(&full[q % PS]), (uint32_t)((q / PS) & 1));
+                if (ok && h2 == 0 && i >= 2) ok = bar_wait(su32(&acc_empty[p]), (uint32_t)(((i - 2) >> 1) & 1));
                 if (!ok) break;
                 tc_fence_after();
-                // 16 fp16 = 32 bytes per K step = 2 in the descriptors' address field
-                const uint64_t ad = adesc0 + (uint64_t)((it % SA) * (C::ABYTES >> 4)),
-                               bd = bdesc0 + (uint64_t)((it % SA) * (C::BBYTES >> 4));
                 const uint32_t tmain = tmem + 4 * BN * p;
-                mma_f16(tmain, ad, bd, id, h > 0 ? 1u : 0u);
 #pragma unroll
-                for (int j = 1; j < BK / 16; j++) mma_f16(tmain, ad + 2 * j, bd + 2 * j, id, 1u);
-                if (QT == 4 && h == 0) {
+                for (int e = 0; e < 2; e++) {
+                    // 16 fp16 = 32 bytes per K step = 2 in the descriptors' address field
+                    const int st = 2 * (q % PS) + e;
+                    const uint64_t ad = adesc0 + (uint64_t)(st * (C::ABYTES >> 4)), bd = bdesc0 + (uint64_t)(st * (C::BBYTES >> 4));
+                    mma_f16(tmain, ad, bd, id, (h2 > 0 || e > 0) ? 1u : 0u);
+#pragma unroll
+                    for (int j = 1; j < BK / 16; j++) mma_f16(tmain, ad + 2 * j, bd + 2 * j, id, 1u);
+                }
+                if (QT == 4 && h2 == 0) {
                     const uint32_t Mt = su32(mins + (i % R) * C::MBYTES);
                     mma_f16(tmain + 2 * BN, sdesc_plain(Mt), sdesc_plain(Mt + 4096), id, 0u);
                 }
-                mma_commit(su32(&empty[it % SA]));
-                if (QT == 4 && h == 0) mma_commit(su32(&raw_empty[i % R]));
-                if (h == 3) mma_commit(su32(&acc_full[p]));
+                mma_commit(su32(&empty[q % PS]));
+                if (QT == 4 && h2 == 0) mma_commit(su32(&raw_empty[i % R]));
+                if (h2 == 1) mma_commit(su32(&acc_full[p]));
             }
             mma_commit(su32(mma_done));  // every MMA issued above is complete once this arrives
             (void)bar_wait(su32(mma_done), 0u);
@@ -781,31 +790,31 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
             if (ok) ok = bar_wait(su32(&raw_full[s]), (uint32_t)((i / R) & 1));
             const uint8_t *U = raw + s * C::RAWB + u * UNIT;
             if (ok && has) conv_unit<QT>(cu, U, part, lane);
-            // step H of unit column i (64-K step it = 4 i + H)
-            auto step = [&](auto Hc) {
-                constexpr int H = decltype(Hc)::value;
-                const int it = 4 * i + H;
-                if (it >= SA && ok) ok = bar_wait(su32(&empty[it % SA]), (uint32_t)(((it - SA) / SA) & 1));
+            // pair P of unit column i (hand-off q = 2 i + P: 64-K steps 2 P, 2 P + 1)
+            auto pair = [&](auto Pc) {
+                constexpr int P = decltype(Pc)::value;
+                const int q = 2 * i + P;
+                if (q >= PS && ok) ok = bar_wait(su32(&empty[q % PS]), (uint32_t)(((q - PS) / PS) & 1));
                 if (ok && has) {
                     // the mins stage and the dsc slot are free: their last readers (the MMAs of
                     // unit column i - R, the readout of unit column i - 4) are done
-                    if (H == 0 && part == 0)
+                    if (P == 0 && part == 0)
                         conv_unit_side<QT>(cu, U, u, lane, a.wscale, dsc + (i & 3) * BM, mins + s * C::MBYTES);
-                    conv_step<QT, H>(As + (it % SA) * C::ABYTES, U, cu, u, part, lane, a.wscale);
+                    conv_step<QT, 2 * P>(As + (2 * (q % PS)) * C::ABYTES, U, cu, u, part, lane, a.wscale);
+                    conv_step<QT, 2 * P + 1>(As + (2 * (q % PS) + 1) * C::ABYTES, U, cu, u, part, lane, a.wscale);
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full[it % SA]);
-                // previous unit column: its last MMAs were issued about three steps ago,
-                // and the MMAs of the next unit column need its accumulator back
-                if (H == 2 && i > 0) readout(i - 1);
+                if (lane == 0) mbar_arrive(&full[q % PS]);
             };
-            step(std::integral_constant<int, 0>());
-            step(std::integral_constant<int, 1>());
-            step(std::integral_constant<int, 2>());
-            step(std::integral_constant<int, 3>());
+            pair(std::integral_constant<int, 0>());
+            pair(std::integral_constant<int, 1>());
             __syncwarp();
             if (lane == 0) mbar_arrive(&raw_empty[s]);
+            // previous unit column: its MMAs are done (this unit column's second
+            // pair waited for them) and the next unit column's MMAs need its
+            // accumulator back
+            if (i > 0) readout(i - 1);
         }
         if (nu > 0) readout(nu - 1);
     }
