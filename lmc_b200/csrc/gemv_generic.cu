@@ -59,14 +59,93 @@ k_gemv_generic(const uint8_t *__restrict__ W, int M, int K, const float *__restr
     }
 }
 
+// Rows made of whole 8-weight groups (K % 8 == 0) with 16-byte aligned
+// activation rows: the batch width is a template parameter (no per-weight
+// predicates) and each group's 8 activations come as two float4 loads.
+template <int T, int NB>
+__global__ void __launch_bounds__(GEN_WARPS * 32)
+k_gemv_generic_g8(const uint8_t *__restrict__ W, int M, int K, const float *__restrict__ x, int ldx,
+                  const float *__restrict__ bias, float *__restrict__ y, int ldy, int nb, int epi) {
+    using F = lmcq::Fmt<T>;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int m = blockIdx.x * GEN_WARPS + (threadIdx.x >> 5);
+    if (m >= M) return;
+    const int ng = K >> 3;
+    const size_t g0 = (size_t)m * ng;
+    float acc[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) acc[b] = 0.0f;
+    for (int gi = lane; gi < ng; gi += 32) {
+        const size_t e = (g0 + gi) << 3;
+        float w[8];
+        lmcq::decode8<T>(W + (e / F::BE) * F::BB, (int)(e % F::BE), w);
+        const float *xk = x + (gi << 3);
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            if (b < nb) {  // uniform across the warp
+                const float4 u = __ldg(reinterpret_cast<const float4 *>(xk + (size_t)b * ldx));
+                const float4 v = __ldg(reinterpret_cast<const float4 *>(xk + (size_t)b * ldx + 4));
+                float a = acc[b];
+                a = fmaf(w[0], u.x, a);
+                a = fmaf(w[1], u.y, a);
+                a = fmaf(w[2], u.z, a);
+                a = fmaf(w[3], u.w, a);
+                a = fmaf(w[4], v.x, a);
+                a = fmaf(w[5], v.y, a);
+                a = fmaf(w[6], v.z, a);
+                a = fmaf(w[7], v.w, a);
+                acc[b] = a;
+            }
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        if (b >= nb) break;
+        float v = warp_sum(acc[b]);
+        if (lane == 0) {
+            if (bias) v += bias[m];
+            if (epi & LMC_EPI_GELU) v = lmc_gelu_f(v);
+            float *o = y + (size_t)b * ldy + m;
+            *o = (epi & LMC_EPI_ACCUM) ? *o + v : v;
+        }
+    }
+}
+
 extern "C" int lmc_gemv_generic_launch(uint32_t type, const void *d_blocks, int M, int K, const float *d_x,
                                        int ldx, const float *d_bias, float *d_y, int ldy, int batch, int epi,
                                        cudaStream_t s) {
     const unsigned grid = lmc_cdiv((size_t)M, GEN_WARPS);
+    const bool g8 = K % 8 == 0 && ldx % 4 == 0 && ((uintptr_t)d_x & 15) == 0;
     for (int b0 = 0; b0 < batch; b0 += GEN_MAXB) {
         const int nb = std::min(GEN_MAXB, batch - b0);
         const float *xb = d_x + (size_t)b0 * ldx;
         float *yb = d_y + (size_t)b0 * ldy;
+        if (g8) {
+            switch (type) {
+#define CASE(T)                                                                                                  \
+    case T:                                                                                                      \
+        if (nb == 1)                                                                                             \
+            LMC_LAUNCH("gemv_generic", (k_gemv_generic_g8<T, 1>), grid, GEN_WARPS * 32, 0, s,                    \
+                       (const uint8_t *)d_blocks, M, K, xb, ldx, d_bias, yb, ldy, nb, epi);                      \
+        else if (nb == 2)                                                                                        \
+            LMC_LAUNCH("gemv_generic", (k_gemv_generic_g8<T, 2>), grid, GEN_WARPS * 32, 0, s,                    \
+                       (const uint8_t *)d_blocks, M, K, xb, ldx, d_bias, yb, ldy, nb, epi);                      \
+        else if (nb <= 4)                                                                                        \
+            LMC_LAUNCH("gemv_generic", (k_gemv_generic_g8<T, 4>), grid, GEN_WARPS * 32, 0, s,                    \
+                       (const uint8_t *)d_blocks, M, K, xb, ldx, d_bias, yb, ldy, nb, epi);                      \
+        else                                                                                                     \
+            LMC_LAUNCH("gemv_generic", (k_gemv_generic_g8<T, 8>), grid, GEN_WARPS * 32, 0, s,                    \
+                       (const uint8_t *)d_blocks, M, K, xb, ldx, d_bias, yb, ldy, nb, epi);                      \
+        break;
+                LMC_FOR_EACH_TYPE(CASE)
+#undef CASE
+            default:
+                return lmc_set_error(LMC_ERR_UNSUPPORTED, "matmul: type %u", type);
+            }
+            continue;
+        }
         switch (type) {
 #define CASE(T)                                                                                       \
     case T:                                                                                           \
