@@ -106,15 +106,40 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
 
 // One non-empty split: append the new K/V row when it falls here, scores,
 // softmax statistics and the unnormalised accumulator (or the final output
-// when there is one split).
+// when there is one split).  Query heads go in groups of up to 8:
+//   scores: lane = position (32 per warp and pass), the K row read as 16- or
+//     32-byte vectors, q broadcast from shared memory, the 8 dot products in
+//     registers (sequential over d as src/ops.c:145-149), no shuffles;
+//   out = sum_t p_t v_t: warp w takes positions t = w (mod 4), lane holds
+//     dims lane + 32 i of every head of the group, so each V element is
+//     loaded once; the 4 warps' partials are added in shared memory.
+template <typename KV> __device__ __forceinline__ void kv_ld8(const KV *p, float (&v)[8]);
+// (plain loads: the row at `pos` was written by this CTA earlier in the launch)
+template <> __device__ __forceinline__ void kv_ld8<float>(const float *p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4 *>(p), b = *(reinterpret_cast<const float4 *>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <> __device__ __forceinline__ void kv_ld8<__half>(const __half *p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(p);
+    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float2 f = __half22float2(h[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+}
+constexpr int ATT_GROUP = 8;  // query heads per pass
+
 template <typename KV>
 __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp, int kh, int b, int pos, int t0, int t1,
                                            float *wsb, size_t hstride) {
     const int G = a.H / a.Hkv, Dh = a.Dh, CH = a.CH;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = ATT_THREADS / 32;
-    float *qs = sm;               // [G][Dh]
-    float *sc = sm + G * Dh;      // [G][CH]
-    float *ml = sc + G * CH;      // [G][2]
+    float *qs = sm;                 // [G][Dh]
+    float *sc = sm + G * Dh;        // [G][CH]
+    float *ml = sc + G * CH;        // [G][2]
+    float *red = ml + 2 * G;        // [nw][ATT_GROUP][Dh]
     KV *kc = reinterpret_cast<KV *>(a.k_cache) + ((size_t)b * a.Hkv + kh) * a.S * Dh;
     KV *vc = reinterpret_cast<KV *>(a.v_cache) + ((size_t)b * a.Hkv + kh) * a.S * Dh;
     const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (Dh / 2) : nullptr;
@@ -149,25 +174,45 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
         qs[gq * Dh + 2 * d] = q0;
         qs[gq * Dh + 2 * d + 1] = q1;
     }
-    __syncthreads();
+    __syncthreads();  // the new row (read back below) and q are in place
     const float scale = 1.0f / sqrtf((float)Dh);
-    const int per_lane = Dh / 32;
-    for (int t = t0 + warp; t < t1; t += nw) {
-        float kv[8];
+    const int n = t1 - t0;
+    for (int g0 = 0; g0 < G; g0 += ATT_GROUP) {
+        const int gn = min(ATT_GROUP, G - g0);
+        for (int tb = warp * 32; tb < n; tb += nw * 32) {
+            const int tl = tb + lane;
+            if (tl >= n) continue;
+            const KV *kr = kc + (size_t)(t0 + tl) * Dh;
+            float sg[ATT_GROUP];
 #pragma unroll
-        for (int i = 0; i < 8; i++)
-            if (i < per_lane) kv[i] = kv_ld<KV>(kc + (size_t)t * Dh + lane + 32 * i);
-        for (int g = 0; g < G; g++) {
-            float dot = 0.0f;
+            for (int g = 0; g < ATT_GROUP; g++) sg[g] = 0.0f;
+            for (int d0 = 0; d0 < Dh; d0 += 8) {
+                float kv[8];
+                kv_ld8<KV>(kr + d0, kv);
 #pragma unroll
-            for (int i = 0; i < 8; i++)
-                if (i < per_lane) dot = fmaf(qs[g * Dh + lane + 32 * i], kv[i], dot);
-            dot = warp_sum(dot);
-            if (lane == 0) sc[g * CH + (t - t0)] = dot * scale;
+                for (int g = 0; g < ATT_GROUP; g++) {
+                    if (g < gn) {
+                        const float4 qa = *reinterpret_cast<const float4 *>(qs + (g0 + g) * Dh + d0);
+                        const float4 qc = *reinterpret_cast<const float4 *>(qs + (g0 + g) * Dh + d0 + 4);
+                        float t = sg[g];
+                        t = fmaf(qa.x, kv[0], t);
+                        t = fmaf(qa.y, kv[1], t);
+                        t = fmaf(qa.z, kv[2], t);
+                        t = fmaf(qa.w, kv[3], t);
+                        t = fmaf(qc.x, kv[4], t);
+                        t = fmaf(qc.y, kv[5], t);
+                        t = fmaf(qc.z, kv[6], t);
+                        t = fmaf(qc.w, kv[7], t);
+                        sg[g] = t;
+                    }
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < ATT_GROUP; g++)
+                if (g < gn) sc[(g0 + g) * CH + tl] = sg[g] * scale;
         }
     }
     __syncthreads();
-    const int n = t1 - t0;
     for (int g = warp; g < G; g += nw) {
         float m = -INFINITY;
         for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[g * CH + t]);
@@ -182,17 +227,48 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
         if (lane == 0) { ml[2 * g] = m; ml[2 * g + 1] = l; }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < G * Dh; i += ATT_THREADS) {
-        const int g = i / Dh, d = i % Dh;
-        float acc = 0.0f;
-        const float *p = sc + g * CH;
-        for (int t = 0; t < n; t++) acc = fmaf(p[t], kv_ld<KV>(vc + (size_t)(t0 + t) * Dh + d), acc);
-        if (a.nsplit == 1) {
-            a.out[(size_t)b * a.ldo + ((size_t)kh * G + g) * Dh + d] = acc / ml[2 * g + 1];
-        } else {
-            wsb[g * hstride + d] = acc;
-            if (d == 0) { wsb[g * hstride + Dh] = ml[2 * g]; wsb[g * hstride + Dh + 1] = ml[2 * g + 1]; }
+    const int dpl = Dh / 32;  // dims per lane (<= 8)
+    for (int g0 = 0; g0 < G; g0 += ATT_GROUP) {
+        const int gn = min(ATT_GROUP, G - g0);
+        float acc[ATT_GROUP][8];
+#pragma unroll
+        for (int g = 0; g < ATT_GROUP; g++)
+#pragma unroll
+            for (int i = 0; i < 8; i++) acc[g][i] = 0.0f;
+        for (int t = warp; t < n; t += nw) {
+            const KV *vr = vc + (size_t)(t0 + t) * Dh + lane;
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = i < dpl ? kv_ld<KV>(vr + 32 * i) : 0.0f;
+#pragma unroll
+            for (int g = 0; g < ATT_GROUP; g++) {
+                if (g < gn) {
+                    const float pt = sc[(g0 + g) * CH + t];
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+                        if (i < dpl) acc[g][i] = fmaf(pt, v[i], acc[g][i]);
+                }
+            }
         }
+#pragma unroll
+        for (int g = 0; g < ATT_GROUP; g++)
+            if (g < gn)
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+                    if (i < dpl) red[(warp * ATT_GROUP + g) * Dh + lane + 32 * i] = acc[g][i];
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < gn * Dh; idx += ATT_THREADS) {
+            const int gl = idx / Dh, d = idx % Dh, g = g0 + gl;
+            float s = 0.0f;
+            for (int w = 0; w < nw; w++) s += red[(w * ATT_GROUP + gl) * Dh + d];
+            if (a.nsplit == 1) {
+                a.out[(size_t)b * a.ldo + ((size_t)kh * G + g) * Dh + d] = s / ml[2 * g + 1];
+            } else {
+                wsb[g * hstride + d] = s;
+                if (d == 0) { wsb[g * hstride + Dh] = ml[2 * g]; wsb[g * hstride + Dh + 1] = ml[2 * g + 1]; }
+            }
+        }
+        __syncthreads();  // red is reused by the next group
     }
 }
 
@@ -263,7 +339,7 @@ extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, in
         return lmc_set_error(LMC_ERR_INVALID, "attention: workspace %zu bytes < %zu needed", ws_bytes, need);
     a.ws = (float *)d_ws;
     const int G = H / Hkv;
-    const size_t smem = (size_t)(G * Dh + G * a.CH + 2 * G) * sizeof(float);
+    const size_t smem = (size_t)(G * Dh + G * a.CH + 2 * G + (ATT_THREADS / 32) * ATT_GROUP * Dh) * sizeof(float);
     if (smem > 200 * 1024) return lmc_set_error(LMC_ERR_UNSUPPORTED, "attention: group too large");
     dim3 grid(a.nsplit, Hkv, batch);
     if (kv_dtype == LMC_KV_F32) {

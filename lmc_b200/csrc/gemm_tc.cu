@@ -31,12 +31,11 @@
 
 #include <algorithm>
 #include <math.h>
-#include <type_traits>
 #include <string.h>
 
 namespace {
 
-constexpr int BM = 128, BK = 64, GTHR = 128;
+constexpr int BM = 128, BK = 64, GTHR = 256;
 constexpr uint32_t LO4C = 0x0F0F0F0Fu;
 
 struct GArgs {
@@ -310,15 +309,16 @@ __global__ void __launch_bounds__(GTHR, 1) k_gemm_tc(GArgs a) {
     pdl_launch_dependents();
     pdl_wait();  // X (prepared by the previous kernel), bias and Y are ready
     const uint32_t id = idesc(BN);
-    const int m = m0 + tid;
     bool ok = true;
     for (int it = 0; it < nit; it++) {
         const int s = it & 1, kb = kb0 + it;
         uint8_t *A = smem + s * stage_bytes, *Bh = A + BM * 128, *Bl = Bh + BN * 128;
         if (it >= 2 && ok) ok = bar_wait(su32(&bars[s]), (uint32_t)(((it - 2) >> 1) & 1));  // stage free
-        // A: this thread's row, 64 weights -> 8 swizzled 16-byte chunks
+        // A: 128 rows x 8 groups of 8 weights -> swizzled 16-byte chunks; the 8
+        // lanes of a row take its 8 consecutive groups (neighbouring bytes)
 #pragma unroll 2
-        for (int c = 0; c < 8; c++) {
+        for (int q0 = 0; q0 < BM * 8 / GTHR; q0++) {
+            const int idx = tid + q0 * GTHR, r = idx >> 3, c = idx & 7, m = m0 + r;
             float v[8];
             if (m < a.M) {
                 const size_t e = (size_t)m * a.K + (size_t)kb * BK + 8 * c;
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(GTHR, 1) k_gemm_tc(GArgs a) {
             q.y = pack_h2(v[2] * a.wscale, v[3] * a.wscale);
             q.z = pack_h2(v[4] * a.wscale, v[5] * a.wscale);
             q.w = pack_h2(v[6] * a.wscale, v[7] * a.wscale);
-            *reinterpret_cast<uint4 *>(A + tid * 128 + ((c ^ (tid & 7)) << 4)) = q;
+            *reinterpret_cast<uint4 *>(A + r * 128 + ((c ^ (r & 7)) << 4)) = q;
         }
         // B: BN token rows x 8 chunks, hi and lo
         for (int i = tid; i < BN * 8; i += GTHR) {
@@ -387,9 +387,6 @@ __host__ __device__ constexpr int tunit_bytes(int qt) { return qt == 4 ? 2304 : 
 __device__ __forceinline__ __half2 u2h(uint32_t v) { return *reinterpret_cast<const __half2 *>(&v); }
 __device__ __forceinline__ uint32_t h2u(__half2 v) { return *reinterpret_cast<const uint32_t *>(&v); }
 __device__ __forceinline__ int tcode_word(int n, int t) { return ((n >> 2) * 32 + t) * 4 + (n & 3); }
-template <int J> __device__ __forceinline__ uint32_t pick4h(const uint4 &v) {
-    return J == 0 ? v.x : J == 1 ? v.y : J == 2 ? v.z : v.w;
-}
 
 // Nibble order of the converted codes: 8 nibble codes (bytes 0-3, low and
 // high nibbles) give the fp16 values in the order (b0.lo, b2.lo, b1.lo,
@@ -445,22 +442,24 @@ __device__ __forceinline__ uint4 cvt_nib_fma(uint32_t P, __half2 sc, __half2 nsc
 // scales) and, for Q4_K, the scale multipliers of its four k-blocks.
 struct ConvUnit {
     uint4 H0, H1;
-    __half2 a0[4], a1[4];
+    uint32_t s0, s1;  // Q4_K: byte h = the 6-bit scale of sub-block 2 h + part, rows r0 / r1
 };
 template <int QT>
 __device__ __forceinline__ void conv_unit(ConvUnit &cu, const uint8_t *U, int part, int lane) {
     const int g = lane >> 2;
     cu.H0 = *reinterpret_cast<const uint4 *>(U + 16 * g);
     cu.H1 = *reinterpret_cast<const uint4 *>(U + 16 * g + 128);
-    if (QT == 4)
+    if (QT == 4) {
+        cu.s0 = cu.s1 = 0u;
 #pragma unroll
         for (int h = 0; h < 4; h++) {
             int sc0, m0, sc1, m1;
             q4k_scale(cu.H0, 2 * h + part, sc0, m0);
             q4k_scale(cu.H1, 2 * h + part, sc1, m1);
-            cu.a0[h] = __float2half2_rn((float)sc0);
-            cu.a1[h] = __float2half2_rn((float)sc1);
+            cu.s0 |= (uint32_t)sc0 << (8 * h);
+            cu.s1 |= (uint32_t)sc1 << (8 * h);
         }
+    }
 }
 // Block scales (and the Q4_K mins rows) of the unit column: part-0 warps.
 template <int QT>
@@ -497,19 +496,22 @@ __device__ __forceinline__ void conv_unit_side(const ConvUnit &cu, const uint8_t
 //   magnitude, nearest-even above); Q8_0: A = fp16(q * d * ws) (one rounding).
 // The block scales enter at readout (dsc): Q4_K d * sum(q sc x) - dmin *
 // sum_j m_j X_j, Q6_K d, Q8_0 1 / ws.
-template <int QT, int H>
-__device__ __forceinline__ void conv_step(uint8_t *A, const uint8_t *U, const ConvUnit &cu, int u, int part, int lane, float ws) {
+__device__ __forceinline__ uint32_t pick4r(const uint4 &v, int j) { return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w; }
+template <int QT>
+__device__ __forceinline__ void conv_step(uint8_t *A, const uint8_t *U, const ConvUnit &cu, int u, int part, int lane, float ws,
+                                          int H) {
     const int g = lane >> 2, c = lane & 3, r0 = 16 * u + g, r1 = r0 + 8;
     if (QT == 4) {
         const uint32_t *cw = reinterpret_cast<const uint32_t *>(U + 256);
         const int j = 2 * H + part;
         const uint32_t P = cw[tcode_word(2 * j, lane)], Q = cw[tcode_word(2 * j + 1, lane)];
         const __half2 m1024 = __float2half2_rn(-1024.0f);
-        put_chunk(A, r0, 4 * part + c, cvt_nib_fma(P, cu.a0[H], __hmul2(cu.a0[H], m1024)));
-        put_chunk(A, r1, 4 * part + c, cvt_nib_fma(Q, cu.a1[H], __hmul2(cu.a1[H], m1024)));
+        const __half2 s0 = __float2half2_rn((float)((cu.s0 >> (8 * H)) & 0xFFu)), s1 = __float2half2_rn((float)((cu.s1 >> (8 * H)) & 0xFFu));
+        put_chunk(A, r0, 4 * part + c, cvt_nib_fma(P, s0, __hmul2(s0, m1024)));
+        put_chunk(A, r1, 4 * part + c, cvt_nib_fma(Q, s1, __hmul2(s1, m1024)));
     } else if (QT == 6) {
         const uint32_t *lw = reinterpret_cast<const uint32_t *>(U + 288), *hw = reinterpret_cast<const uint32_t *>(U + 288 + 2048);
-        const uint32_t w0 = pick4h<H>(cu.H0), w1 = pick4h<H>(cu.H1);  // scales of chunks 4H..4H+3
+        const uint32_t w0 = pick4r(cu.H0, H), w1 = pick4r(cu.H1, H);  // scales of chunks 4H..4H+3
         const int j = 4 * H + 2 * part;                                   // even chunk; j + 1 odd
         const uint32_t P0 = lw[tcode_word(j, lane)], P1 = lw[tcode_word(j + 1, lane)];
         const uint32_t Hb = hw[tcode_word(j >> 1, lane)];
@@ -528,7 +530,7 @@ __device__ __forceinline__ void conv_step(uint8_t *A, const uint8_t *U, const Co
         const uint4 *cw = reinterpret_cast<const uint4 *>(U + 256);
         const int j = 2 * H + part;  // block j of each row; its scale is half (j & 1) of header word H
         const uint4 Aw = cw[j * 32 + lane];
-        const float2 f0 = __half22float2(u2h(pick4h<H>(cu.H0))), f1 = __half22float2(u2h(pick4h<H>(cu.H1)));
+        const float2 f0 = __half22float2(u2h(pick4r(cu.H0, H))), f1 = __half22float2(u2h(pick4r(cu.H1, H)));
         const __half2 s0 = __float2half2_rn((part ? f0.y : f0.x) * ws);
         const __half2 s1 = __float2half2_rn((part ? f1.y : f1.x) * ws);
         const uint2 x0 = cvt_byte<128>(Aw.x ^ 0x80808080u, s0), x1 = cvt_byte<128>(Aw.z ^ 0x80808080u, s0);
@@ -790,9 +792,10 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
             if (ok) ok = bar_wait(su32(&raw_full[s]), (uint32_t)((i / R) & 1));
             const uint8_t *U = raw + s * C::RAWB + u * UNIT;
             if (ok && has) conv_unit<QT>(cu, U, part, lane);
-            // pair P of unit column i (hand-off q = 2 i + P: 64-K steps 2 P, 2 P + 1)
-            auto pair = [&](auto Pc) {
-                constexpr int P = decltype(Pc)::value;
+            // pair P of unit column i (hand-off q = 2 i + P: 64-K steps 2 P, 2 P + 1);
+            // one copy of the loop body (the instruction cache is shared by 18 warps)
+#pragma unroll 1
+            for (int P = 0; P < 2; P++) {
                 const int q = 2 * i + P;
                 if (q >= PS && ok) ok = bar_wait(su32(&empty[q % PS]), (uint32_t)(((q - PS) / PS) & 1));
                 if (ok && has) {
@@ -800,15 +803,14 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_gemm_ws(GArgs a) {
                     // unit column i - R, the readout of unit column i - 4) are done
                     if (P == 0 && part == 0)
                         conv_unit_side<QT>(cu, U, u, lane, a.wscale, dsc + (i & 3) * BM, mins + s * C::MBYTES);
-                    conv_step<QT, 2 * P>(As + (2 * (q % PS)) * C::ABYTES, U, cu, u, part, lane, a.wscale);
-                    conv_step<QT, 2 * P + 1>(As + (2 * (q % PS) + 1) * C::ABYTES, U, cu, u, part, lane, a.wscale);
+#pragma unroll 1
+                    for (int e = 0; e < 2; e++)
+                        conv_step<QT>(As + (2 * (q % PS) + e) * C::ABYTES, U, cu, u, part, lane, a.wscale, 2 * P + e);
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[q % PS]);
-            };
-            pair(std::integral_constant<int, 0>());
-            pair(std::integral_constant<int, 1>());
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&raw_empty[s]);
             // previous unit column: its MMAs are done (this unit column's second
