@@ -42,11 +42,12 @@ struct AttnArgs {
     int *cnt;  // [batch][Hkv] arrival counters, zero between launches, or NULL (separate combine kernel)
 };
 
-template <typename KV>
+template <typename KV, int DH>
 __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp, int kh, int b, int pos, int t0, int t1,
                                            float *wsb, size_t hstride);
 
-template <typename KV>
+// DH: the head size when it is 64 or 128 (compile-time register layout), 0 for any other
+template <typename KV, int DH>
 __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
     extern __shared__ float sm[];
     const int sp = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -66,7 +67,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
             }
         return;
     }
-    split_body<KV>(a, sm, sp, kh, b, pos, t0, t1, wsb, hstride);
+    split_body<KV, DH>(a, sm, sp, kh, b, pos, t0, t1, wsb, hstride);
     if (!a.cnt || a.nsplit == 1) return;
     // the last of the splits that hold positions (0..pos) to arrive merges
     // them (as k_attn_combine); empty splits took no part
@@ -107,20 +108,26 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
 // One non-empty split: append the new K/V row when it falls here, scores,
 // softmax statistics and the unnormalised accumulator (or the final output
 // when there is one split).  Query heads go in groups of up to 8:
-//   scores: lane = position (32 per warp and pass), the K row read as 16- or
-//     32-byte vectors, q broadcast from shared memory, the 8 dot products in
-//     registers (sequential over d as src/ops.c:145-149), no shuffles;
-//   out = sum_t p_t v_t: warp w takes positions t = w (mod 4), lane holds
-//     dims lane + 32 i of every head of the group, so each V element is
-//     loaded once; the 4 warps' partials are added in shared memory.
-template <typename KV> __device__ __forceinline__ void kv_ld8(const KV *p, float (&v)[8]);
-// (plain loads: the row at `pos` was written by this CTA earlier in the launch)
-template <> __device__ __forceinline__ void kv_ld8<float>(const float *p, float (&v)[8]) {
-    const float4 a = *reinterpret_cast<const float4 *>(p), b = *(reinterpret_cast<const float4 *>(p) + 1);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+//   scores: lane = position (32 per warp and pass), the K row read as 16-byte
+//     vectors all issued before the first use (up to 256 bytes at a time, so
+//     one memory latency per row instead of one per 8 elements), q broadcast
+//     from shared memory, the 8 dot products in registers (sequential over d
+//     as src/ops.c:145-149), no shuffles;
+//   out = sum_t p_t v_t: warp w takes positions t = w (mod 4), four of them
+//     per batch with every load issued first; lane holds dims lane + 32 i of
+//     every head of the group, so each V element is loaded once; the 4 warps'
+//     partials are added in shared memory.
+// Chunk c (8 elements) of a block of raw 16-byte K words -> 8 floats.  The
+// words come from plain loads: the row at `pos` was written by this CTA
+// earlier in the launch.
+template <typename KV, int NV> __device__ __forceinline__ void kv_chunk(const uint4 (&raw)[NV], int c, float (&v)[8]);
+template <int NV> __device__ __forceinline__ void kv_chunk_f32(const uint4 (&raw)[NV], int c, float (&v)[8]) {
+    const uint4 x = raw[2 * c], y = raw[2 * c + 1];
+    v[0] = __uint_as_float(x.x); v[1] = __uint_as_float(x.y); v[2] = __uint_as_float(x.z); v[3] = __uint_as_float(x.w);
+    v[4] = __uint_as_float(y.x); v[5] = __uint_as_float(y.y); v[6] = __uint_as_float(y.z); v[7] = __uint_as_float(y.w);
 }
-template <> __device__ __forceinline__ void kv_ld8<__half>(const __half *p, float (&v)[8]) {
-    const uint4 u = *reinterpret_cast<const uint4 *>(p);
+template <int NV> __device__ __forceinline__ void kv_chunk_f16(const uint4 (&raw)[NV], int c, float (&v)[8]) {
+    const uint4 u = raw[c];
     const __half2 *h = reinterpret_cast<const __half2 *>(&u);
 #pragma unroll
     for (int i = 0; i < 4; i++) {
@@ -131,10 +138,14 @@ template <> __device__ __forceinline__ void kv_ld8<__half>(const __half *p, floa
 }
 constexpr int ATT_GROUP = 8;  // query heads per pass
 
-template <typename KV>
+template <typename KV, int DH>
 __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp, int kh, int b, int pos, int t0, int t1,
                                            float *wsb, size_t hstride) {
-    const int G = a.H / a.Hkv, Dh = a.Dh, CH = a.CH;
+    const int G = a.H / a.Hkv, Dh = DH ? DH : a.Dh, CH = a.CH;
+    constexpr int ESZ = (int)sizeof(KV);
+    constexpr int RB = DH ? (DH * ESZ < 256 ? DH * ESZ : 256) : 128;  // K bytes per load block
+    constexpr int NV = RB / 16, NC = RB / (8 * ESZ);                  // 16-byte words, 8-element chunks
+    constexpr int DPLC = DH ? DH / 32 : 8;                            // dims per lane (bound)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = ATT_THREADS / 32;
     float *qs = sm;                 // [G][Dh]
     float *sc = sm + G * Dh;        // [G][CH]
@@ -186,9 +197,19 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
             float sg[ATT_GROUP];
 #pragma unroll
             for (int g = 0; g < ATT_GROUP; g++) sg[g] = 0.0f;
-            for (int d0 = 0; d0 < Dh; d0 += 8) {
+            const int rowb = Dh * ESZ;
+            for (int ob = 0; ob < rowb; ob += RB) {
+                uint4 raw[NV];
+#pragma unroll
+                for (int i = 0; i < NV; i++)
+                    if (ob + 16 * i < rowb) raw[i] = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(kr) + ob + 16 * i);
+#pragma unroll
+                for (int c = 0; c < NC; c++) {
+                const int d0 = ob / ESZ + 8 * c;
+                if (d0 >= Dh) break;
                 float kv[8];
-                kv_ld8<KV>(kr + d0, kv);
+                if (ESZ == 4) kv_chunk_f32<NV>(raw, c, kv);
+                else kv_chunk_f16<NV>(raw, c, kv);
 #pragma unroll
                 for (int g = 0; g < ATT_GROUP; g++) {
                     if (g < gn) {
@@ -205,6 +226,7 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
                         t = fmaf(qc.w, kv[7], t);
                         sg[g] = t;
                     }
+                }
                 }
             }
 #pragma unroll
@@ -230,23 +252,33 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
     const int dpl = Dh / 32;  // dims per lane (<= 8)
     for (int g0 = 0; g0 < G; g0 += ATT_GROUP) {
         const int gn = min(ATT_GROUP, G - g0);
-        float acc[ATT_GROUP][8];
+        float acc[ATT_GROUP][DPLC];
 #pragma unroll
         for (int g = 0; g < ATT_GROUP; g++)
 #pragma unroll
-            for (int i = 0; i < 8; i++) acc[g][i] = 0.0f;
-        for (int t = warp; t < n; t += nw) {
-            const KV *vr = vc + (size_t)(t0 + t) * Dh + lane;
-            float v[8];
+            for (int i = 0; i < DPLC; i++) acc[g][i] = 0.0f;
+        constexpr int U = 4;  // positions per batch of loads
+        for (int t = warp; t < n; t += U * nw) {
+            float v[U][DPLC];
 #pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = i < dpl ? kv_ld<KV>(vr + 32 * i) : 0.0f;
+            for (int uu = 0; uu < U; uu++) {
+                const int tt = t + uu * nw;
+                const KV *vr = vc + (size_t)(t0 + tt) * Dh + lane;
 #pragma unroll
-            for (int g = 0; g < ATT_GROUP; g++) {
-                if (g < gn) {
-                    const float pt = sc[(g0 + g) * CH + t];
+                for (int i = 0; i < DPLC; i++) v[uu][i] = (tt < n && i < dpl) ? kv_ld<KV>(vr + 32 * i) : 0.0f;
+            }
 #pragma unroll
-                    for (int i = 0; i < 8; i++)
-                        if (i < dpl) acc[g][i] = fmaf(pt, v[i], acc[g][i]);
+            for (int uu = 0; uu < U; uu++) {
+                const int tt = t + uu * nw;
+                if (tt >= n) break;
+#pragma unroll
+                for (int g = 0; g < ATT_GROUP; g++) {
+                    if (g < gn) {
+                        const float pt = sc[(g0 + g) * CH + tt];
+#pragma unroll
+                        for (int i = 0; i < DPLC; i++)
+                            if (i < dpl) acc[g][i] = fmaf(pt, v[uu][i], acc[g][i]);
+                    }
                 }
             }
         }
@@ -254,7 +286,7 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
         for (int g = 0; g < ATT_GROUP; g++)
             if (g < gn)
 #pragma unroll
-                for (int i = 0; i < 8; i++)
+                for (int i = 0; i < DPLC; i++)
                     if (i < dpl) red[(warp * ATT_GROUP + g) * Dh + lane + 32 * i] = acc[g][i];
         __syncthreads();
         for (int idx = threadIdx.x; idx < gn * Dh; idx += ATT_THREADS) {
@@ -343,13 +375,13 @@ extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, in
     if (smem > 200 * 1024) return lmc_set_error(LMC_ERR_UNSUPPORTED, "attention: group too large");
     dim3 grid(a.nsplit, Hkv, batch);
     if (kv_dtype == LMC_KV_F32) {
-        if (smem > 48 * 1024)
-            LMC_CUDA_TRY(cudaFuncSetAttribute(k_attn_split<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        LMC_LAUNCH("attention", k_attn_split<float>, grid, ATT_THREADS, smem, s, a);
+        void (*fn)(AttnArgs) = Dh == 64 ? k_attn_split<float, 64> : Dh == 128 ? k_attn_split<float, 128> : k_attn_split<float, 0>;
+        if (smem > 48 * 1024) LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        LMC_LAUNCH("attention", fn, grid, ATT_THREADS, smem, s, a);
     } else {
-        if (smem > 48 * 1024)
-            LMC_CUDA_TRY(cudaFuncSetAttribute(k_attn_split<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        LMC_LAUNCH("attention", k_attn_split<__half>, grid, ATT_THREADS, smem, s, a);
+        void (*fn)(AttnArgs) = Dh == 64 ? k_attn_split<__half, 64> : Dh == 128 ? k_attn_split<__half, 128> : k_attn_split<__half, 0>;
+        if (smem > 48 * 1024) LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        LMC_LAUNCH("attention", fn, grid, ATT_THREADS, smem, s, a);
     }
     if (a.nsplit > 1 && !d_cnt) {
         LMC_LAUNCH("attention combine", k_attn_combine, dim3(H, batch), Dh, 0, s, a);
