@@ -326,16 +326,26 @@ __global__ void k_attn_combine(AttnArgs a) {
     }
 }
 
-static void attn_plan(int S, int *CH, int *nsplit) {
+// Split length: 64 positions, longer while the context would need more than
+// ATT_MAX_SPLITS splits.  When the splits are merged in the launch (`fine`:
+// arrival counters given) and there are few (sequence, head) pairs (bh =
+// batch x heads, a batch-1 decode), shorter, down to 16 positions and
+// ATT_MAX_SPLITS_FEW splits, so that more CTAs stream the cache at once (a
+// separate merge kernel over that many splits costs more than it saves).
+#define ATT_MAX_SPLITS_FEW 64
+static void attn_plan(int S, int bh, bool fine, int *CH, int *nsplit) {
     int ch = 64;
     while ((S + ch - 1) / ch > ATT_MAX_SPLITS) ch *= 2;
+    while (fine && ch > 16 && (long long)bh * ((S + ch - 1) / ch) < 2048 &&
+           (S + ch / 2 - 1) / (ch / 2) <= ATT_MAX_SPLITS_FEW)
+        ch /= 2;
     *CH = ch;
     *nsplit = (S + ch - 1) / ch;
 }
 
 extern "C" size_t lmc_attention_workspace_bytes(int batch, int H, int Dh, int S) {
     int CH, ns;
-    attn_plan(S, &CH, &ns);
+    attn_plan(S, batch * H, true, &CH, &ns);  // the larger of the two plans
     return ns > 1 ? (size_t)batch * H * ns * (Dh + 2) * sizeof(float) : 0;
 }
 
@@ -365,8 +375,8 @@ extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, in
     a.ldo = ldo; a.ldq = ldq; a.ldkv = ldkv;
     a.rope_cos = rope_cos; a.rope_sin = rope_sin;
     a.cnt = d_cnt;
-    attn_plan(S, &a.CH, &a.nsplit);
-    const size_t need = lmc_attention_workspace_bytes(batch, H, Dh, S);
+    attn_plan(S, batch * H, d_cnt != NULL, &a.CH, &a.nsplit);
+    const size_t need = a.nsplit > 1 ? (size_t)batch * H * a.nsplit * (Dh + 2) * sizeof(float) : 0;  // this launch's plan
     if (need > ws_bytes || (need && !d_ws))
         return lmc_set_error(LMC_ERR_INVALID, "attention: workspace %zu bytes < %zu needed", ws_bytes, need);
     a.ws = (float *)d_ws;

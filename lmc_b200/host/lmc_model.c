@@ -417,7 +417,13 @@ static int alloc_state(lmc_model *m) {
         if (!(f && f[0] == '0')) TRY(dev_alloc((void **)&m->d_attn_cnt, 4 * B * (size_t)m->hkvl));
     }
     TRY(dev_alloc((void **)&m->logits, 4 * B * V));
-    m->ws_bytes = lmc_attention_workspace_bytes((int)B, c->n_heads, c->head_dim, c->seq_len);
+    /* attention split scratch: the split count depends on batch x heads, and a
+     * step may run any batch up to B with this rank's heads */
+    m->ws_bytes = 0;
+    for (int b = 1; b <= (int)B; b++) {
+        const size_t need = lmc_attention_workspace_bytes(b, m->hl, c->head_dim, c->seq_len);
+        if (need > m->ws_bytes) m->ws_bytes = need;
+    }
     TRY(dev_alloc(&m->ws, m->ws_bytes));
     TRY(dev_alloc((void **)&m->d_tok, 4 * B));
     TRY(dev_alloc((void **)&m->d_pos, 4 * B));
