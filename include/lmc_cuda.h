@@ -198,6 +198,12 @@ int lmc_model_load(const char *gguf_path, int max_batch, int kv_dtype, lmc_model
 int lmc_nccl_unique_id(void *nccl_id_128);
 int lmc_model_load_tp(const char *gguf_path, int max_batch, int kv_dtype, int tp_rank, int tp_size,
                       const void *nccl_id_128, lmc_model **out);
+/* lmc_model_load / lmc_model_load_tp with max_rows >= max_batch rows per
+ * step: the prompt chunk length of lmc_model_prefill (the KV cache still
+ * holds max_batch sequences; activations are sized for max_rows rows).
+ * tp_size 1 (nccl_id NULL) loads the whole model. */
+int lmc_model_load_ex(const char *gguf_path, int max_batch, int max_rows, int kv_dtype, int tp_rank, int tp_size,
+                      const void *nccl_id_128, lmc_model **out);
 int lmc_model_shard(const lmc_model *m, int *tp_rank, int *tp_size, int *vocab_begin, int *vocab_rows);
 int lmc_model_get_config(const lmc_model *m, lmc_model_config *cfg);
 int lmc_model_free(lmc_model *m);
@@ -207,6 +213,18 @@ int lmc_model_free(lmc_model *m);
  * not NULL, the batch x vocab logits. */
 int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int batch,
                       float *h_logits, int *h_next);
+/* Batched prefill of one sequence's prompt: the n tokens h_tokens at
+ * positions start_pos .. start_pos + n - 1 of sequence `seq` run as the rows
+ * of one step, max_rows positions at a time (the projections become GEMMs
+ * over the chunk; each row attends to positions <= its own, including the
+ * chunk's earlier rows).  Replaces LMc's token-by-token prompt feed
+ * (src/lmc.c:109-112), which is what lmc_model_generate does: the KV cache of
+ * `seq` and the logits of the last position come out the same (within
+ * floating-point rounding).  Writes the next greedy id to h_next and, when
+ * h_logits is not NULL, the last position's logits (vocab rows of this
+ * rank).  Continue with lmc_model_forward at position start_pos + n. */
+int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int start_pos, float *h_logits,
+                      int *h_next);
 /* The generate() loop of src/lmc.c:108-132 without tokenizer or EOS, run
  * entirely on the device: the n_prompt prompt tokens of each sequence are
  * fed one position at a time, then n_new greedy steps; h_out_ids receives

@@ -40,6 +40,12 @@ struct AttnArgs {
     // the new K row here, or NULL
     const float *rope_cos, *rope_sin;
     int *cnt;  // [batch][Hkv] arrival counters, zero between launches, or NULL (separate combine kernel)
+    // Row -> cache sequence (NULL: row b uses sequence b).  Rows may share a
+    // sequence (a prompt chunk of one sequence, one position per row); their
+    // K/V rows are then appended by k_kv_append before this launch and
+    // `append` is 0, so every row sees the rows of earlier positions.
+    const int *seq;
+    int append;
 };
 
 template <typename KV, int DH>
@@ -151,11 +157,12 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
     float *sc = sm + G * Dh;        // [G][CH]
     float *ml = sc + G * CH;        // [G][2]
     float *red = ml + 2 * G;        // [nw][ATT_GROUP][Dh]
-    KV *kc = reinterpret_cast<KV *>(a.k_cache) + ((size_t)b * a.Hkv + kh) * a.S * Dh;
-    KV *vc = reinterpret_cast<KV *>(a.v_cache) + ((size_t)b * a.Hkv + kh) * a.S * Dh;
+    const size_t cs = a.seq ? (size_t)a.seq[b] : (size_t)b;  // cache sequence of this row
+    KV *kc = reinterpret_cast<KV *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * Dh;
+    KV *vc = reinterpret_cast<KV *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * Dh;
     const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (Dh / 2) : nullptr;
     const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (Dh / 2) : nullptr;
-    if (pos >= t0 && pos < t1) {  // append this step's K/V row (K rotated first when RoPE applies)
+    if (a.append && pos >= t0 && pos < t1) {  // append this step's K/V row (K rotated first when RoPE applies)
         const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
         const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
         for (int d = threadIdx.x; d < Dh / 2; d += ATT_THREADS) {
@@ -304,6 +311,38 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
     }
 }
 
+// K/V append for rows that share a cache sequence: row b's new K (rotated
+// when RoPE applies) and V rows go to position pos[b] of sequence seq[b],
+// before the attention launch reads them.  One CTA per (kv head, row).
+template <typename KV>
+__global__ void k_kv_append(AttnArgs a) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int kh = blockIdx.x, b = blockIdx.y, Dh = a.Dh;
+    const int pos = a.pos[b];
+    if (pos < 0 || pos >= a.S) return;
+    const size_t cs = (size_t)a.seq[b];
+    KV *kc = reinterpret_cast<KV *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * Dh + (size_t)pos * Dh;
+    KV *vc = reinterpret_cast<KV *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * Dh + (size_t)pos * Dh;
+    const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
+    const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
+    const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (Dh / 2) : nullptr;
+    const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (Dh / 2) : nullptr;
+    for (int d = threadIdx.x; d < Dh / 2; d += blockDim.x) {
+        float k0 = kn[2 * d], k1 = kn[2 * d + 1];
+        if (rc) {
+            const float c = rc[d], sn = rs[d];
+            const float r0 = k0 * c - k1 * sn, r1 = k0 * sn + k1 * c;
+            k0 = r0;
+            k1 = r1;
+        }
+        kc[2 * d] = kv_cvt<KV>(k0);
+        kc[2 * d + 1] = kv_cvt<KV>(k1);
+        vc[2 * d] = kv_cvt<KV>(vn[2 * d]);
+        vc[2 * d + 1] = kv_cvt<KV>(vn[2 * d + 1]);
+    }
+}
+
 // Merge the splits of one (sequence, query head): rescale each split's sum
 // and accumulator to the global maximum.
 __global__ void k_attn_combine(AttnArgs a) {
@@ -362,6 +401,15 @@ extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, in
                                          const int *d_pos, int batch, int H, int Hkv, int Dh, int S, void *d_ws,
                                          size_t ws_bytes, const float *rope_cos, const float *rope_sin, int *d_cnt,
                                          cudaStream_t s) {
+    return lmc_attention_rows_launch(out, ldo, q, ldq, k_new, v_new, ldkv, k_cache, v_cache, kv_dtype, d_pos, NULL,
+                                     batch, H, Hkv, Dh, S, d_ws, ws_bytes, rope_cos, rope_sin, d_cnt, s);
+}
+
+extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, int ldq, const float *k_new,
+                                         const float *v_new, int ldkv, void *k_cache, void *v_cache, int kv_dtype,
+                                         const int *d_pos, const int *d_seq, int batch, int H, int Hkv, int Dh, int S,
+                                         void *d_ws, size_t ws_bytes, const float *rope_cos, const float *rope_sin,
+                                         int *d_cnt, cudaStream_t s) {
     if (!out || !q || !k_new || !v_new || !k_cache || !v_cache || !d_pos)
         return lmc_set_error(LMC_ERR_INVALID, "attention: null pointer");
     if (batch <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh % 32 || Dh > 256 || S <= 0)
@@ -375,6 +423,8 @@ extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, in
     a.ldo = ldo; a.ldq = ldq; a.ldkv = ldkv;
     a.rope_cos = rope_cos; a.rope_sin = rope_sin;
     a.cnt = d_cnt;
+    a.seq = d_seq;
+    a.append = d_seq ? 0 : 1;
     attn_plan(S, batch * H, d_cnt != NULL, &a.CH, &a.nsplit);
     const size_t need = a.nsplit > 1 ? (size_t)batch * H * a.nsplit * (Dh + 2) * sizeof(float) : 0;  // this launch's plan
     if (need > ws_bytes || (need && !d_ws))
@@ -384,6 +434,10 @@ extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, in
     const size_t smem = (size_t)(G * Dh + G * a.CH + 2 * G + (ATT_THREADS / 32) * ATT_GROUP * Dh) * sizeof(float);
     if (smem > 200 * 1024) return lmc_set_error(LMC_ERR_UNSUPPORTED, "attention: group too large");
     dim3 grid(a.nsplit, Hkv, batch);
+    if (d_seq) {  // rows share cache sequences: append every row's K/V first
+        if (kv_dtype == LMC_KV_F32) LMC_LAUNCH("kv append", k_kv_append<float>, dim3(Hkv, batch), 64, 0, s, a);
+        else LMC_LAUNCH("kv append", k_kv_append<__half>, dim3(Hkv, batch), 64, 0, s, a);
+    }
     if (kv_dtype == LMC_KV_F32) {
         void (*fn)(AttnArgs) = Dh == 64 ? k_attn_split<float, 64> : Dh == 128 ? k_attn_split<float, 128> : k_attn_split<float, 0>;
         if (smem > 48 * 1024) LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -88,6 +88,14 @@ int lmc_attention_rope_launch(float *out, int ldo, const float *q, int ldq, cons
                               int ldkv, void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, int batch, int H,
                               int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes, const float *rope_cos,
                               const float *rope_sin, int *d_cnt, cudaStream_t s);
+/* As lmc_attention_rope_launch, with d_seq[b] the cache sequence of row b
+ * (NULL: row b uses sequence b).  Rows may share a sequence (a prompt chunk,
+ * one position per row): their K/V rows are appended by a separate kernel
+ * first, so row b attends to every row of the chunk at positions <= pos[b]. */
+int lmc_attention_rows_launch(float *out, int ldo, const float *q, int ldq, const float *k_new, const float *v_new,
+                              int ldkv, void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, const int *d_seq,
+                              int batch, int H, int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes,
+                              const float *rope_cos, const float *rope_sin, int *d_cnt, cudaStream_t s);
 /* Generation bookkeeping after one step (see lmc_model_generate): the greedy
  * id of each sequence is read from (and reset in) d_keys. */
 int lmc_advance_launch(unsigned long long *d_keys, int *d_next, int *d_tok, int *d_pos, int *d_step,

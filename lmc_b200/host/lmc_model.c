@@ -35,6 +35,10 @@ typedef struct {
 struct lmc_model {
     lmc_model_config cfg;
     int max_batch, kv_dtype;
+    /* rows per step (>= max_batch): a prompt chunk of one sequence runs one
+     * position per row (lmc_model_prefill); d_seq[row] = its cache sequence */
+    int max_rows, prefill, prefill_head; /* prefill_head: this chunk is the prompt's last */
+    int *d_seq;
     lmc_qtensor *wte, *lm_head;
     float *wpe, *lnf_w, *lnf_b, *rmsf, *rope_cos, *rope_sin;
     Layer *layers;
@@ -398,10 +402,12 @@ static int build_rope(lmc_model *m) {
 
 static int alloc_state(lmc_model *m) {
     const lmc_model_config *c = &m->cfg;
-    const size_t B = (size_t)m->max_batch, D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size;
+    /* KV cache: max_batch sequences; everything per row: max_rows rows */
+    const size_t NS = (size_t)m->max_batch, B = (size_t)m->max_rows, D = c->embed_dim, F = c->ffn_dim,
+                 V = c->vocab_size;
     const size_t QD = (size_t)c->n_heads * c->head_dim, KV = (size_t)c->n_kv_heads * c->head_dim;
     const size_t esz = m->kv_dtype == LMC_KV_F16 ? 2 : 4;
-    m->kv_layer_elems = B * (size_t)m->hkvl * c->head_dim * (size_t)c->seq_len;  /* this rank's kv heads */
+    m->kv_layer_elems = NS * (size_t)m->hkvl * c->head_dim * (size_t)c->seq_len;  /* this rank's kv heads */
     TRY(dev_alloc(&m->kc, esz * m->kv_layer_elems * c->n_layers));
     TRY(dev_alloc(&m->vc, esz * m->kv_layer_elems * c->n_layers));
     TRY(dev_alloc((void **)&m->x, 4 * B * D));
@@ -427,6 +433,7 @@ static int alloc_state(lmc_model *m) {
     TRY(dev_alloc(&m->ws, m->ws_bytes));
     TRY(dev_alloc((void **)&m->d_tok, 4 * B));
     TRY(dev_alloc((void **)&m->d_pos, 4 * B));
+    TRY(dev_alloc((void **)&m->d_seq, 4 * B));
     TRY(dev_alloc((void **)&m->d_next, 4 * B));
     TRY(dev_alloc((void **)&m->d_step, 16));
     CUTRY(cudaMallocHost((void **)&m->h_stage, 3 * sizeof(int) * B));
@@ -448,8 +455,8 @@ int lmc_nccl_unique_id(void *id) {
     return LMC_OK;
 }
 
-static int model_load(const char *path, int max_batch, int kv_dtype, int tp_rank, int tp_size, const void *nccl_id,
-                      lmc_model **out) {
+static int model_load(const char *path, int max_batch, int max_rows, int kv_dtype, int tp_rank, int tp_size,
+                      const void *nccl_id, lmc_model **out) {
     if (!path || !out || max_batch <= 0) return lmc_set_error(LMC_ERR_INVALID, "model_load: args");
     if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16) return lmc_set_error(LMC_ERR_INVALID, "model_load: kv dtype");
     if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size || (tp_size > 1 && !nccl_id))
@@ -458,6 +465,7 @@ static int model_load(const char *path, int max_batch, int kv_dtype, int tp_rank
     lmc_model *m = (lmc_model *)calloc(1, sizeof(lmc_model));
     if (!m) return lmc_set_error(LMC_ERR_OOM, "model struct");
     m->max_batch = max_batch;
+    m->max_rows = max_rows > max_batch ? max_rows : max_batch;
     m->kv_dtype = kv_dtype;
     m->tp_rank = tp_rank;
     m->tp_size = tp_size;
@@ -481,12 +489,17 @@ static int model_load(const char *path, int max_batch, int kv_dtype, int tp_rank
 }
 
 int lmc_model_load(const char *path, int max_batch, int kv_dtype, lmc_model **out) {
-    return model_load(path, max_batch, kv_dtype, 0, 1, NULL, out);
+    return model_load(path, max_batch, max_batch, kv_dtype, 0, 1, NULL, out);
+}
+
+int lmc_model_load_ex(const char *path, int max_batch, int max_rows, int kv_dtype, int tp_rank, int tp_size,
+                      const void *nccl_id, lmc_model **out) {
+    return model_load(path, max_batch, max_rows, kv_dtype, tp_rank, tp_size, nccl_id, out);
 }
 
 int lmc_model_load_tp(const char *path, int max_batch, int kv_dtype, int tp_rank, int tp_size, const void *nccl_id,
                       lmc_model **out) {
-    return model_load(path, max_batch, kv_dtype, tp_rank, tp_size, nccl_id, out);
+    return model_load(path, max_batch, max_batch, kv_dtype, tp_rank, tp_size, nccl_id, out);
 }
 
 int lmc_model_shard(const lmc_model *m, int *tp_rank, int *tp_size, int *vocab_begin, int *vocab_rows) {
@@ -525,7 +538,7 @@ int lmc_model_free(lmc_model *m) {
     lmc_qtensor_free(m->lm_head);
     void *ps[] = {m->wpe, m->lnf_w, m->lnf_b, m->rmsf, m->rope_cos, m->rope_sin, m->kc, m->vc, m->x, m->xn, m->qkv,
                   m->att, m->h, m->h2, m->logits, m->ws, m->d_tok, m->d_pos, m->d_next, m->d_step, m->d_prompt, m->d_ids,
-                  m->d_keys, m->d_attn_cnt};
+                  m->d_keys, m->d_attn_cnt, m->d_seq};
     for (size_t i = 0; i < sizeof ps / sizeof ps[0]; i++) if (ps[i]) cudaFree(ps[i]);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -540,20 +553,25 @@ int lmc_model_free(lmc_model *m) {
 /* x -> norm -> W, as one tensor-core launch with the norm as its prologue
  * when W has the tiled layout (batch <= 8: the GEMV) or the batched GEMM
  * applies (batch > 8), else a norm kernel and a plain matmul. */
-static int norm_matmul(lmc_model *m, const lmc_qtensor *W, int pro, const float *nw, const float *nb, float eps,
-                       const float *bias, float *y, int ldy, int B, int epi, unsigned long long *keys) {
+static int norm_matmul_in(lmc_model *m, const float *xin, const lmc_qtensor *W, int pro, const float *nw,
+                          const float *nb, float eps, const float *bias, float *y, int ldy, int B, int epi,
+                          unsigned long long *keys) {
     const int D = m->cfg.embed_dim;
     cudaStream_t s = m->stream;
     if ((B > 8 && W->gemm_wscale > 0.0f) || (lmc_qtensor_has_tiled(W) && (keys == NULL || B <= 8))) {
         lmc_gemv_extra ex = {pro, nw, nb, NULL, eps, keys, keys ? m->v0 : 0};
-        return lmc_tiled_gemv_ex(W, m->x, D, bias, y, ldy, B, epi, &ex, s);
+        return lmc_tiled_gemv_ex(W, xin, D, bias, y, ldy, B, epi, &ex, s);
     }
     if (keys && m->v0) return lmc_set_error(LMC_ERR_UNSUPPORTED, "sharded lm_head needs the tensor-core layout");
-    if (pro == LMC_PRO_LAYERNORM) TRY(lmc_layer_norm(m->xn, m->x, nw, nb, D, B, s));
-    else TRY(lmc_rms_norm(m->xn, m->x, nw, D, B, eps, s));
+    if (pro == LMC_PRO_LAYERNORM) TRY(lmc_layer_norm(m->xn, xin, nw, nb, D, B, s));
+    else TRY(lmc_rms_norm(m->xn, xin, nw, D, B, eps, s));
     TRY(lmc_matmul(W, m->xn, D, bias, y, ldy, B, epi, s));
     if (keys) TRY(lmc_argmax_keys_launch(y, W->rows, B, keys, s));
     return LMC_OK;
+}
+static int norm_matmul(lmc_model *m, const lmc_qtensor *W, int pro, const float *nw, const float *nb, float eps,
+                       const float *bias, float *y, int ldy, int B, int epi, unsigned long long *keys) {
+    return norm_matmul_in(m, m->x, W, pro, nw, nb, eps, bias, y, ldy, B, epi, keys);
 }
 
 /* Sum of the ranks' partial x (tensor parallel): rank 0 added its partial to
@@ -585,8 +603,9 @@ static int step(lmc_model *m, int B) {
         if (c->arch == 1) { /* src/ops.c:182-206 */
             TRY(norm_matmul(m, w->qkv, LMC_PRO_LAYERNORM, w->ln1_w, w->ln1_b, 1e-5f, w->qkv_b, m->qkv, 3 * D, B,
                             LMC_EPI_NONE, NULL));
-            TRY(lmc_attention_launch(m->att, D, m->qkv, 3 * D, m->qkv + D, m->qkv + 2 * D, 3 * D, kc, vc, m->kv_dtype,
-                                     m->d_pos, B, H, H, Dh, S, m->ws, m->ws_bytes, m->d_attn_cnt, s));
+            TRY(lmc_attention_rows_launch(m->att, D, m->qkv, 3 * D, m->qkv + D, m->qkv + 2 * D, 3 * D, kc, vc,
+                                          m->kv_dtype, m->d_pos, m->prefill ? m->d_seq : NULL, B, H, H, Dh, S, m->ws,
+                                          m->ws_bytes, NULL, NULL, m->d_attn_cnt, s));
             TRY(lmc_matmul(w->proj, m->att, D, w->proj_b, m->x, D, B, LMC_EPI_ACCUM, s));
             TRY(norm_matmul(m, w->fc, LMC_PRO_LAYERNORM, w->ln2_w, w->ln2_b, 1e-5f, w->fc_b, m->h, F, B, LMC_EPI_GELU,
                             NULL));
@@ -613,9 +632,9 @@ static int step(lmc_model *m, int B) {
                 ld = 0;
             }
             /* RoPE on q and the new K row happens inside the attention kernel */
-            TRY(lmc_attention_rope_launch(m->att, QD, q, ld ? ld : QD, k, v, ld ? ld : KVD, kc, vc, m->kv_dtype,
-                                          m->d_pos, B, H, Hkv, Dh, S, m->ws, m->ws_bytes, m->rope_cos, m->rope_sin,
-                                          m->d_attn_cnt, s));
+            TRY(lmc_attention_rows_launch(m->att, QD, q, ld ? ld : QD, k, v, ld ? ld : KVD, kc, vc, m->kv_dtype,
+                                          m->d_pos, m->prefill ? m->d_seq : NULL, B, H, Hkv, Dh, S, m->ws,
+                                          m->ws_bytes, m->rope_cos, m->rope_sin, m->d_attn_cnt, s));
             TRY(lmc_matmul(w->o, m->att, QD, NULL, m->x, D, B, rp, s));
             TRY(tp_sum_x(m, B));
             if (w->gateup_cat && (lmc_qtensor_has_tiled(w->down) || (B > 8 && w->down->gemm_wscale > 0.0f))) {
@@ -633,14 +652,19 @@ static int step(lmc_model *m, int B) {
             TRY(tp_sum_x(m, B));
         }
     }
+    /* a prompt needs the logits of its last row only (the next token): the
+     * head runs for the last chunk's last row and not at all for the others */
+    if (m->prefill && !m->prefill_head) return LMC_OK;
+    const float *xl = m->prefill ? m->x + (size_t)(B - 1) * D : m->x;
+    const int BL = m->prefill ? 1 : B;
     if (c->arch == 1)
-        TRY(norm_matmul(m, m->lm_head, LMC_PRO_LAYERNORM, m->lnf_w, m->lnf_b, 1e-5f, NULL, m->logits, V, B,
-                        LMC_EPI_NONE, m->d_keys));
+        TRY(norm_matmul_in(m, xl, m->lm_head, LMC_PRO_LAYERNORM, m->lnf_w, m->lnf_b, 1e-5f, NULL, m->logits, V, BL,
+                           LMC_EPI_NONE, m->d_keys));
     else
-        TRY(norm_matmul(m, m->lm_head, LMC_PRO_RMSNORM, m->rmsf, NULL, c->norm_eps, NULL, m->logits, m->vl, B,
-                        LMC_EPI_NONE, m->d_keys));
+        TRY(norm_matmul_in(m, xl, m->lm_head, LMC_PRO_RMSNORM, m->rmsf, NULL, c->norm_eps, NULL, m->logits, m->vl, BL,
+                           LMC_EPI_NONE, m->d_keys));
     if (m->tp_size > 1) { /* greedy pick over the vocabulary shards: max of the 64-bit keys */
-        ncclResult_t r = ncclAllReduce(m->d_keys, m->d_keys, (size_t)B, ncclUint64, ncclMax, m->comm, m->stream);
+        ncclResult_t r = ncclAllReduce(m->d_keys, m->d_keys, (size_t)BL, ncclUint64, ncclMax, m->comm, m->stream);
         if (r != ncclSuccess) return lmc_set_error(LMC_ERR_CUDA, "ncclAllReduce(keys): %s", ncclGetErrorString(r));
     }
     return LMC_OK;
@@ -667,6 +691,44 @@ int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B
     CUTRY(cudaMemcpyAsync(m->h_stage + 2 * B, m->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, m->stream));
     CUTRY(cudaStreamSynchronize(m->stream));
     if (h_next) memcpy(h_next, m->h_stage + 2 * B, sizeof(int) * B);
+    return LMC_OK;
+}
+
+int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int start_pos, float *h_logits, int *h_next) {
+    if (!m || !h_tokens || n <= 0 || seq < 0 || seq >= m->max_batch || start_pos < 0 ||
+        start_pos + n > m->cfg.seq_len)
+        return lmc_set_error(LMC_ERR_INVALID, "model_prefill: sequence %d (of %d), positions %d + %d (context %d)", seq,
+                             m ? m->max_batch : 0, start_pos, n, m ? m->cfg.seq_len : 0);
+    for (int i = 0; i < n; i++)
+        if (h_tokens[i] < 0 || h_tokens[i] >= m->cfg.vocab_size)
+            return lmc_set_error(LMC_ERR_INVALID, "model_prefill: token %d outside [0, %d)", h_tokens[i], m->cfg.vocab_size);
+    cudaStream_t s = m->stream;
+    const int R = m->max_rows;
+    int rc = LMC_OK;
+    for (int i0 = 0; i0 < n && !rc; i0 += R) {
+        const int c = n - i0 < R ? n - i0 : R;
+        for (int r = 0; r < c; r++) {
+            m->h_stage[r] = h_tokens[i0 + r];
+            m->h_stage[R + r] = start_pos + i0 + r;
+            m->h_stage[2 * R + r] = seq;
+        }
+        CUTRY(cudaMemcpyAsync(m->d_tok, m->h_stage, sizeof(int) * c, cudaMemcpyHostToDevice, s));
+        CUTRY(cudaMemcpyAsync(m->d_pos, m->h_stage + R, sizeof(int) * c, cudaMemcpyHostToDevice, s));
+        CUTRY(cudaMemcpyAsync(m->d_seq, m->h_stage + 2 * R, sizeof(int) * c, cudaMemcpyHostToDevice, s));
+        m->prefill = 1;
+        m->prefill_head = i0 + c == n;
+        if (m->prefill_head) CUTRY(cudaMemsetAsync(m->d_keys, 0, sizeof(unsigned long long), s));
+        rc = step(m, c);
+        m->prefill = m->prefill_head = 0;
+        /* the staging buffer is rewritten for the next chunk */
+        if (!rc && cudaStreamSynchronize(s) != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "model_prefill: sync");
+    }
+    if (rc) return rc;
+    TRY(lmc_keys_to_ids_launch(m->d_keys, m->d_next, 1, s));
+    if (h_logits) CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * m->vl, cudaMemcpyDeviceToHost, s));
+    CUTRY(cudaMemcpyAsync(m->h_stage, m->d_next, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CUTRY(cudaStreamSynchronize(s));
+    if (h_next) *h_next = m->h_stage[0];
     return LMC_OK;
 }
 

@@ -45,6 +45,8 @@ SIGNATURES = {
     "lmc_model_load": ([_c.c_char_p, _i, _i, _c.POINTER(_vp)], _i),
     "lmc_nccl_unique_id": ([_vp], _i),
     "lmc_model_load_tp": ([_c.c_char_p, _i, _i, _i, _i, _vp, _c.POINTER(_vp)], _i),
+    "lmc_model_load_ex": ([_c.c_char_p, _i, _i, _i, _i, _i, _vp, _c.POINTER(_vp)], _i),
+    "lmc_model_prefill": ([_vp, _i, _ip, _i, _i, _vp, _ip], _i),
     "lmc_model_shard": ([_vp, _ip, _ip, _ip, _ip], _i),
     "lmc_model_get_config": ([_vp, _vp], _i),
     "lmc_model_free": ([_vp], _i),
@@ -149,11 +151,17 @@ def nccl_unique_id():
 class Model:
     """A GGUF model loaded onto the device (lmc_model_load), or one
     tensor-parallel shard of it when tp = (rank, size, nccl_id) is given
-    (lmc_model_load_tp; every rank of the group constructs its shard)."""
+    (lmc_model_load_tp; every rank of the group constructs its shard).
+    max_rows > max_batch: rows per step for prefill() chunks (lmc_model_load_ex)."""
 
-    def __init__(self, path, max_batch=1, kv_dtype=KV_F32, tp=None):
+    def __init__(self, path, max_batch=1, kv_dtype=KV_F32, tp=None, max_rows=None):
         h = _vp()
-        if tp is None:
+        if max_rows is not None and max_rows > max_batch:
+            rank, size, nid = tp if tp is not None else (0, 1, None)
+            idbuf = ctypes.create_string_buffer(bytes(nid), 128) if nid is not None else None
+            call("lmc_model_load_ex", path.encode(), max_batch, max_rows, kv_dtype, rank, size,
+                 ctypes.cast(idbuf, _vp) if idbuf is not None else None, ctypes.byref(h))
+        elif tp is None:
             call("lmc_model_load", path.encode(), max_batch, kv_dtype, ctypes.byref(h))
         else:
             rank, size, nid = tp
@@ -178,6 +186,17 @@ class Model:
         call("lmc_model_forward", self.h, tokens.ctypes.data_as(_ip), positions.ctypes.data_as(_ip), B,
              None if logits is None else logits.ctypes.data, nxt.ctypes.data_as(_ip))
         return logits, nxt
+
+    def prefill(self, seq, tokens, start_pos=0, want_logits=True):
+        """Batched prefill of sequence `seq` (lmc_model_prefill): tokens at
+        positions start_pos.. -> (last position's logits or None, next id)."""
+        import numpy as np
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(self.vocab_rows, np.float32) if want_logits else None
+        nxt = np.empty(1, np.int32)
+        call("lmc_model_prefill", self.h, seq, tokens.ctypes.data_as(_ip), tokens.size, start_pos,
+             None if logits is None else logits.ctypes.data, nxt.ctypes.data_as(_ip))
+        return logits, int(nxt[0])
 
     def generate(self, prompt, n_new, use_graph=True):
         """prompt: [B][n_prompt] token ids -> [B][n_new] greedy ids."""

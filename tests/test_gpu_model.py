@@ -109,3 +109,35 @@ def test_batched_gemm_path_matches_oracle(cuda, orc, model_dir, kind, kw):
     got = m2.generate(prompts, n_new, use_graph=True)
     for b in range(B):
         assert got[b].tolist() == want_ids[b]
+
+
+@pytest.mark.parametrize("kind,kw", [
+    ("gpt2", dict(L=2, D=256, H=4, S=128, V=1000, seed=5)),
+    ("llama", dict(L=2, D=256, H=8, Hkv=2, F=512, S=128, V=1000, seed=5)),
+])
+@pytest.mark.parametrize("kvd", [rt.KV_F32, rt.KV_F16])
+def test_prefill_matches_oracle(cuda, orc, model_dir, kind, kw, kvd):
+    """Batched prefill (lmc_model_prefill): a 21-token prompt of sequence 1 in
+    chunks of 16 and 5 rows (the first through the tensor-core GEMM) gives
+    the oracle's last-position logits and next id, and greedy decoding then
+    continues with the oracle's ids from the cache the prefill wrote."""
+    path = tiny(kind, model_dir, **kw)
+    prompt = np.random.default_rng(3).integers(0, kw["V"], 21).astype(np.int32)
+    om = orc.model(path)
+    lg = None
+    for pos, t in enumerate(prompt):
+        lg = om.forward(int(t), pos)
+    tol = 1e-3 if kvd == rt.KV_F32 else 5e-3
+    m = rt.Model(path, max_batch=2, kv_dtype=kvd, max_rows=16)
+    got, nxt = m.prefill(1, prompt)
+    assert rel_err(got, lg) < tol
+    assert nxt == orc.argmax(lg) == int(np.argmax(got))
+    pos, ids, want = len(prompt), [], []
+    for _ in range(8):
+        want.append(orc.argmax(lg))
+        lg = om.forward(want[-1], pos)
+        _, n2 = m.forward([0, nxt], [0, pos])  # sequence 0 is idle (any token at position 0)
+        ids.append(nxt)
+        nxt = int(n2[1])
+        pos += 1
+    assert ids == want
