@@ -51,7 +51,7 @@ def model_file(name, directory):
     return synth.cached_model(kind, directory, **kw)
 
 
-def run(name, batch, n_prompt, n_gen, kv, directory, tp=False):
+def run(name, batch, n_prompt, n_gen, kv, directory, tp=False, prefill_rows=0):
     import torch
     dist, rank, world, dev = None, 0, 1, 0
     if tp:
@@ -72,9 +72,9 @@ def run(name, batch, n_prompt, n_gen, kv, directory, tp=False):
     if dist:
         from lmc_b200 import tp as tpm
         nid = tpm.exchange_id(dist, rt.nccl_unique_id)
-        m = rt.Model(path, max_batch=batch, kv_dtype=kvd, tp=(rank, world, nid))
+        m = rt.Model(path, max_batch=batch, kv_dtype=kvd, tp=(rank, world, nid), max_rows=prefill_rows or None)
     else:
-        m = rt.Model(path, max_batch=batch, kv_dtype=kvd)
+        m = rt.Model(path, max_batch=batch, kv_dtype=kvd, max_rows=prefill_rows or None)
     rng = np.random.default_rng(0)
     prompts = rng.integers(0, m.cfg.vocab_size, (batch, n_prompt)).astype(np.int32)
 
@@ -93,6 +93,23 @@ def run(name, batch, n_prompt, n_gen, kv, directory, tp=False):
             dt = float(t.item())
         return dt
 
+    def timed_prefill():  # every sequence's prompt, chunks of prefill_rows positions
+        for rep in range(2):  # the first pass warms up (GEMM workspace, lazy module loads)
+            torch.cuda.synchronize()
+            if dist:
+                dist.barrier()
+            t0 = time.perf_counter()
+            for b in range(batch):
+                m.prefill(b, prompts[b], 0, want_logits=False)
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+        if dist:
+            t = torch.tensor([dt])
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+        return dt
+
+    t_prefill = timed_prefill() if prefill_rows else None
     t_feed = timed(1)        # n_prompt steps
     t_all = timed(n_gen)     # n_prompt + n_gen - 1 steps
     t_dec = max(t_all - t_feed, 1e-9)
@@ -101,6 +118,9 @@ def run(name, batch, n_prompt, n_gen, kv, directory, tp=False):
            "ms_per_step_prompt": 1e3 * t_feed / n_prompt, "ms_per_step_decode": 1e3 * t_dec / max(n_gen - 1, 1),
            "graph_kernels_per_step": m.graph_kernels(), "weights_bytes": os.path.getsize(path),
            "tensor_parallel": world}
+    if t_prefill:
+        res.update({"prefill_rows": prefill_rows, "prefill_tok_s": batch * n_prompt / t_prefill,
+                    "prefill_ms": 1e3 * t_prefill})
     m.close()
     if dist:
         dist.barrier()
@@ -117,8 +137,10 @@ def main():
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
     ap.add_argument("--dir", default=os.environ.get("LMC_BENCH_DIR", "/tmp/lmc_models"))
     ap.add_argument("--tp", action="store_true", help="tensor parallel over the torchrun ranks")
+    ap.add_argument("--prefill-rows", type=int, default=0,
+                    help="also time batched prefill (lmc_model_prefill) in chunks of this many positions")
     a = ap.parse_args()
-    r = run(a.model, a.batch, a.prompt, a.gen, a.kv, a.dir, tp=a.tp)
+    r = run(a.model, a.batch, a.prompt, a.gen, a.kv, a.dir, tp=a.tp, prefill_rows=a.prefill_rows)
     if r is not None:
         print(json.dumps(r), flush=True)
 
