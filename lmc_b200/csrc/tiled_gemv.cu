@@ -1032,8 +1032,9 @@ static int clusters_per_gpu(int cl) {
     return n > 0 ? n : -1;
 }
 
-// Cluster shape (fewest units for the busiest CTA; ties go to more CTAs,
-// then to smaller clusters), fragment width and ring depth for one launch.
+// Cluster shape (fewest rounds of units for the busiest CTA, a split
+// charged for its cluster synchronisation; ties go to more CTAs, then to
+// smaller clusters), fragment width and ring depth for one launch.
 static int plan_for(uint32_t type, int rows_tiled, int cols, int nb, Plan *P) {
     const int QT = qt_of(type), KB = cols / 256, RT = rows_tiled / 16;
     const int NT = nb <= 2 ? 1 : nb <= 4 ? 2 : 4;
@@ -1065,9 +1066,12 @@ static int plan_for(uint32_t type, int rows_tiled, int cols, int nb, Plan *P) {
                 }
             }
         if (!stages) continue;
-        // lower is better: the busiest CTA's units, plus about one unit for the
-        // two cluster barriers of a split, minus a little per CTA engaged
-        const long long score = (per_cta + (cl > 1 ? 1 : 0)) * 4096 - (long long)NC * cl * 8 + cl;
+        // lower is better: rounds of units per warp of the busiest CTA (a
+        // round ~0.3 us), plus ~5 rounds for a split's cluster barriers and
+        // distributed-shared-memory pushes (measured 1.5-2.5 us), minus a
+        // little per CTA engaged
+        const long long rounds = (per_cta + WARPS - 1) / WARPS;
+        const long long score = (rounds + (cl > 1 ? 5 : 0)) * 4096 - (long long)NC * cl * 8 + cl;
         if (best < 0 || score < best) {
             best = score;
             bestp = Plan{NT, XL, cl, NC, maxrt, stages, smem};
