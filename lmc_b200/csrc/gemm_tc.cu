@@ -893,6 +893,11 @@ __global__ void __launch_bounds__(256) k_gemm_prep_x(const float *__restrict__ x
     extern __shared__ float row[];  // [K]
     __shared__ float red[32];
     pdl_launch_dependents();
+    if (pw)  // norm weights and bias do not depend on the previous kernel: into L1 meanwhile
+        for (int k = threadIdx.x * 32; k < K; k += blockDim.x * 32) {
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(pw + k));
+            if (pb) asm volatile("prefetch.global.L1 [%0];" ::"l"(pb + k));
+        }
     pdl_wait();
     const int n = blockIdx.x, tid = threadIdx.x;
     if (n >= N) {  // fast-path padding rows: zero tiles

@@ -505,6 +505,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     return false;
 }
 
+// Pull one 128-byte line into this SM's L1 (a hint; no value is returned).
+__device__ __forceinline__ void prefetch_l1(const void *p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+
 // cluster helpers (distributed shared memory)
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
@@ -858,6 +861,11 @@ __global__ void __launch_bounds__(NTHR, 2) k_gemv_tiled(TArgs a) {
     float *acc = reinterpret_cast<float *>(smem + L.acc_off());
     for (int i = threadIdx.x; i < a.maxrt * NB * 16; i += NTHR) acc[i] = 0.0f;
     if (a.CL > 1) cluster_arrive();  // this CTA's accumulator is zero (phase 1)
+    if (a.pro == LMC_PRO_LAYERNORM || a.pro == LMC_PRO_RMSNORM)  // norm weights: independent of the previous kernel
+        for (int k = threadIdx.x * 32; k < a.KB * 256; k += NTHR * 32) {
+            prefetch_l1(a.pw + k);
+            if (a.pb) prefetch_l1(a.pb + k);
+        }
     pdl_wait();
     build_x<NT, QT>(smem, L, a);
     __syncthreads();
