@@ -229,7 +229,10 @@ int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int sta
  * entirely on the device: the n_prompt prompt tokens of each sequence are
  * fed one position at a time, then n_new greedy steps; h_out_ids receives
  * batch x n_new ids.  With use_graph = 1 every step is one CUDA-graph
- * launch and the host does not wait between steps. */
+ * launch and the host does not wait between steps.  A model loaded with
+ * more rows than sequences (lmc_model_load_ex) prefills all but the last
+ * prompt token of each sequence in chunks first (lmc_model_prefill) and
+ * starts the step loop at the last prompt position: the same ids. */
 int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int batch,
                        int n_new, int use_graph, int *h_out_ids);
 /* Runs `n` more steps of the last lmc_model_generate (replaying its CUDA

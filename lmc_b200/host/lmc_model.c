@@ -694,14 +694,9 @@ int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B
     return LMC_OK;
 }
 
-int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int start_pos, float *h_logits, int *h_next) {
-    if (!m || !h_tokens || n <= 0 || seq < 0 || seq >= m->max_batch || start_pos < 0 ||
-        start_pos + n > m->cfg.seq_len)
-        return lmc_set_error(LMC_ERR_INVALID, "model_prefill: sequence %d (of %d), positions %d + %d (context %d)", seq,
-                             m ? m->max_batch : 0, start_pos, n, m ? m->cfg.seq_len : 0);
-    for (int i = 0; i < n; i++)
-        if (h_tokens[i] < 0 || h_tokens[i] >= m->cfg.vocab_size)
-            return lmc_set_error(LMC_ERR_INVALID, "model_prefill: token %d outside [0, %d)", h_tokens[i], m->cfg.vocab_size);
+/* Prompt chunks of sequence `seq` (validated by the caller); `head`: run the
+ * lm_head for the last position (its greedy key in d_keys[0]). */
+static int prefill_chunks(lmc_model *m, int seq, const int *h_tokens, int n, int start_pos, int head) {
     cudaStream_t s = m->stream;
     const int R = m->max_rows;
     int rc = LMC_OK;
@@ -716,14 +711,26 @@ int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int sta
         CUTRY(cudaMemcpyAsync(m->d_pos, m->h_stage + R, sizeof(int) * c, cudaMemcpyHostToDevice, s));
         CUTRY(cudaMemcpyAsync(m->d_seq, m->h_stage + 2 * R, sizeof(int) * c, cudaMemcpyHostToDevice, s));
         m->prefill = 1;
-        m->prefill_head = i0 + c == n;
+        m->prefill_head = head && i0 + c == n;
         if (m->prefill_head) CUTRY(cudaMemsetAsync(m->d_keys, 0, sizeof(unsigned long long), s));
         rc = step(m, c);
         m->prefill = m->prefill_head = 0;
         /* the staging buffer is rewritten for the next chunk */
         if (!rc && cudaStreamSynchronize(s) != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "model_prefill: sync");
     }
-    if (rc) return rc;
+    return rc;
+}
+
+int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int start_pos, float *h_logits, int *h_next) {
+    if (!m || !h_tokens || n <= 0 || seq < 0 || seq >= m->max_batch || start_pos < 0 ||
+        start_pos + n > m->cfg.seq_len)
+        return lmc_set_error(LMC_ERR_INVALID, "model_prefill: sequence %d (of %d), positions %d + %d (context %d)", seq,
+                             m ? m->max_batch : 0, start_pos, n, m ? m->cfg.seq_len : 0);
+    for (int i = 0; i < n; i++)
+        if (h_tokens[i] < 0 || h_tokens[i] >= m->cfg.vocab_size)
+            return lmc_set_error(LMC_ERR_INVALID, "model_prefill: token %d outside [0, %d)", h_tokens[i], m->cfg.vocab_size);
+    cudaStream_t s = m->stream;
+    TRY(prefill_chunks(m, seq, h_tokens, n, start_pos, 1));
     TRY(lmc_keys_to_ids_launch(m->d_keys, m->d_next, 1, s));
     if (h_logits) CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * m->vl, cudaMemcpyDeviceToHost, s));
     CUTRY(cudaMemcpyAsync(m->h_stage, m->d_next, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -773,12 +780,19 @@ int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, i
     const char *ng = getenv("LMC_NO_GRAPH");
     if (ng && ng[0] == '1') use_graph = 0;
     cudaStream_t s = m->stream;
+    /* With more rows per step than sequences (lmc_model_load_ex) every prompt
+     * but its last token goes through batched prefill; the step loop then
+     * starts at the last prompt position (same ids: the cache holds the same
+     * rows either way). */
+    const int p0 = m->max_rows > m->max_batch && n_prompt > 1 ? n_prompt - 1 : 0;
+    for (int b = 0; b < B && p0; b++) TRY(prefill_chunks(m, b, h_prompt + (size_t)b * n_prompt, p0, 0, 0));
     CUTRY(cudaMemcpyAsync(m->d_prompt, h_prompt, sizeof(int) * (size_t)B * n_prompt, cudaMemcpyHostToDevice, s));
-    for (int b = 0; b < B; b++) { m->h_stage[b] = h_prompt[(size_t)b * n_prompt]; m->h_stage[B + b] = 0; }
+    for (int b = 0; b < B; b++) { m->h_stage[b] = h_prompt[(size_t)b * n_prompt + p0]; m->h_stage[B + b] = p0; }
     CUTRY(cudaMemcpyAsync(m->d_tok, m->h_stage, sizeof(int) * B, cudaMemcpyHostToDevice, s));
     CUTRY(cudaMemcpyAsync(m->d_pos, m->h_stage + B, sizeof(int) * B, cudaMemcpyHostToDevice, s));
-    CUTRY(cudaMemsetAsync(m->d_step, 0, sizeof(int), s));
-    const int steps = n_prompt + n_new - 1;
+    m->h_stage[2 * B] = p0;
+    CUTRY(cudaMemcpyAsync(m->d_step, m->h_stage + 2 * B, sizeof(int), cudaMemcpyHostToDevice, s));
+    const int steps = n_prompt + n_new - 1 - p0;
     if (use_graph) {
         if (m->gexec && (m->g_batch != B || m->g_nprompt != n_prompt || m->g_nnew != n_new)) {
             cudaGraphExecDestroy(m->gexec);

@@ -141,3 +141,33 @@ def test_prefill_matches_oracle(cuda, orc, model_dir, kind, kw, kvd):
         nxt = int(n2[1])
         pos += 1
     assert ids == want
+
+
+@pytest.mark.parametrize("kind,kw", [
+    ("gpt2", dict(L=2, D=256, H=4, S=128, V=1000, seed=6)),
+    ("llama", dict(L=2, D=256, H=8, Hkv=2, F=512, S=128, V=1000, seed=6)),
+])
+def test_generate_with_prefill_matches_oracle(cuda, orc, model_dir, kind, kw):
+    """lmc_model_generate on a model with more rows per step than sequences
+    prefills the prompts in chunks and then runs the step graph from the last
+    prompt position: the oracle's greedy ids for both sequences."""
+    path = tiny(kind, model_dir, **kw)
+    rng = np.random.default_rng(7)
+    prompts = rng.integers(0, kw["V"], (2, 21)).astype(np.int32)
+    want = []
+    for p in prompts:
+        om = orc.model(path)
+        lg = None
+        for pos, t in enumerate(p):
+            lg = om.forward(int(t), pos)
+        ids, pos = [], len(p)
+        for _ in range(16):
+            ids.append(orc.argmax(lg))
+            lg = om.forward(ids[-1], pos)
+            pos += 1
+        want.append(ids)
+    m = rt.Model(path, max_batch=2, max_rows=16)
+    got = m.generate(prompts, 16, use_graph=True)
+    assert got.tolist() == want
+    got2 = m.generate(prompts, 16, use_graph=False)
+    assert got2.tolist() == want
