@@ -51,9 +51,13 @@ struct AttnArgs {
 template <typename KV, int DH>
 __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp, int kh, int b, int pos, int t0, int t1,
                                            float *wsb, size_t hstride);
+template <int DH>
+__device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int kh, int b, int pos, int t0, int t1,
+                                              float *wsb, size_t hstride);
 
-// DH: the head size when it is 64 or 128 (compile-time register layout), 0 for any other
-template <typename KV, int DH>
+// DH: the head size when it is 64 or 128 (compile-time register layout), 0 for any other.
+// TC: the tensor-core body (fp16 cache, DH 64 / 128, at most 8 query heads per kv head).
+template <typename KV, int DH, bool TC>
 __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
     extern __shared__ float sm[];
     const int sp = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -73,7 +77,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
             }
         return;
     }
-    split_body<KV, DH>(a, sm, sp, kh, b, pos, t0, t1, wsb, hstride);
+    if constexpr (TC) split_body_tc<DH>(a, sm, kh, b, pos, t0, t1, wsb, hstride);
+    else split_body<KV, DH>(a, sm, sp, kh, b, pos, t0, t1, wsb, hstride);
     if (!a.cnt || a.nsplit == 1) return;
     // the last of the splits that hold positions (0..pos) to arrive merges
     // them (as k_attn_combine); empty splits took no part
@@ -311,6 +316,185 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
     }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core split body (fp16 cache).  The group's G <= 8 query heads are
+// the rows of mma.sync m16n8k16 tiles (rows G..15 zero):
+//   scores: A = q (fp16 hi + lo parts, two MMAs, so the product carries q to
+//     ~22 bits; K is exact in fp16), B = 8 cached positions x 16 dims read
+//     straight from the cache, one 16-byte load per lane and 32 dims (the k
+//     index is permuted within each 32 dims, identically in A and B);
+//   out = P V: A = the probabilities e^(s - m) (hi + lo), B = V rows staged in
+//     shared memory (padded rows) and read transposed with ldmatrix; each
+//     warp owns DH / 32 of the 8-dim column tiles, so no cross-warp sum.
+// Same statistics and outputs as split_body; fp32 accumulation throughout.
+__device__ __forceinline__ void hmma16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void split_h2(float x, float y, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(x, y);
+    const float2 f = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x - f.x, y - f.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+// Dim of logical k (0..15) of slice ks (within its 32-dim pair kp = ks / 2)
+// for lane group tig: the 16-byte load of dims 32 kp + 8 tig .. + 7 feeds
+// b0 / b1 of slices 2 kp and 2 kp + 1.
+__device__ __forceinline__ int qk_dim(int ks, int tig, int e, bool second) {
+    return 32 * (ks >> 1) + 8 * tig + 4 * (ks & 1) + (second ? 2 : 0) + e;
+}
+
+template <int DH>
+__device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int kh, int b, int pos, int t0, int t1,
+                                              float *wsb, size_t hstride) {
+    constexpr int KS = DH / 16, VSTR = DH + 8;  // k slices; V staging row stride (halves, conflict-free ldmatrix)
+    const int G = a.H / a.Hkv, CH = a.CH;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = ATT_THREADS / 32;
+    const int g = lane >> 2, tig = lane & 3;
+    float *qs = sm;            // [G][DH]
+    float *sc = sm + G * DH;   // [G][CH16]
+    const int CH16 = (CH + 15) & ~15;
+    float *ml = sc + G * CH16;  // [G][2]
+    __half *vt = reinterpret_cast<__half *>(sm + ((G * DH + G * CH16 + 2 * G + 3) & ~3));  // [CH16][VSTR], 16-byte aligned
+    const size_t cs = a.seq ? (size_t)a.seq[b] : (size_t)b;
+    __half *kc = reinterpret_cast<__half *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * DH;
+    __half *vc = reinterpret_cast<__half *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * DH;
+    const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (DH / 2) : nullptr;
+    const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (DH / 2) : nullptr;
+    if (a.append && pos >= t0 && pos < t1) {  // append this step's K/V row (K rotated first when RoPE applies)
+        const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * DH;
+        const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * DH;
+        for (int d = threadIdx.x; d < DH / 2; d += ATT_THREADS) {
+            float k0 = kn[2 * d], k1 = kn[2 * d + 1];
+            if (rc) {
+                const float c = rc[d], sn = rs[d];
+                const float r0 = k0 * c - k1 * sn, r1 = k0 * sn + k1 * c;
+                k0 = r0;
+                k1 = r1;
+            }
+            kc[(size_t)pos * DH + 2 * d] = __float2half_rn(k0);
+            kc[(size_t)pos * DH + 2 * d + 1] = __float2half_rn(k1);
+            vc[(size_t)pos * DH + 2 * d] = __float2half_rn(vn[2 * d]);
+            vc[(size_t)pos * DH + 2 * d + 1] = __float2half_rn(vn[2 * d + 1]);
+        }
+    }
+    const float *qb = a.q + (size_t)b * a.ldq + (size_t)kh * G * DH;
+    for (int i = threadIdx.x; i < G * DH / 2; i += ATT_THREADS) {  // q pairs (rotated when RoPE applies)
+        const int gq = i / (DH / 2), d = i % (DH / 2);
+        float q0 = qb[gq * DH + 2 * d], q1 = qb[gq * DH + 2 * d + 1];
+        if (rc) {
+            const float c = rc[d], sn = rs[d];
+            const float r0 = q0 * c - q1 * sn, r1 = q0 * sn + q1 * c;
+            q0 = r0;
+            q1 = r1;
+        }
+        qs[gq * DH + 2 * d] = q0;
+        qs[gq * DH + 2 * d + 1] = q1;
+    }
+    __syncthreads();  // the new row (read back below) and q are in place
+    const int n = t1 - t0, n16 = (n + 15) & ~15;
+    // stage V rows [t0, t0 + n) (zero rows up to n16), 16 bytes per thread and step
+    for (int i = threadIdx.x; i < n16 * (DH / 8); i += ATT_THREADS) {
+        const int r = i / (DH / 8), c8 = i % (DH / 8);
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < n) v = *reinterpret_cast<const uint4 *>(vc + (size_t)(t0 + r) * DH + 8 * c8);
+        *reinterpret_cast<uint4 *>(vt + r * VSTR + 8 * c8) = v;
+    }
+    // q fragments: row g (query head g of the group), hi and lo
+    uint32_t qa0h[KS], qa0l[KS], qa2h[KS], qa2l[KS];
+#pragma unroll
+    for (int ks = 0; ks < KS; ks++) {
+        float x0 = 0.f, x1 = 0.f, y0 = 0.f, y1 = 0.f;
+        if (g < G) {
+            const float *qr = qs + g * DH;
+            x0 = qr[qk_dim(ks, tig, 0, false)], x1 = qr[qk_dim(ks, tig, 1, false)];
+            y0 = qr[qk_dim(ks, tig, 0, true)], y1 = qr[qk_dim(ks, tig, 1, true)];
+        }
+        split_h2(x0, x1, qa0h[ks], qa0l[ks]);
+        split_h2(y0, y1, qa2h[ks], qa2l[ks]);
+    }
+    const float scale = 1.0f / sqrtf((float)DH);
+    for (int j = warp; 8 * j < n; j += nw) {  // 8-position tiles
+        const int p = 8 * j + g;               // this lane's B column (position within the split)
+        const __half *kr = kc + (size_t)(t0 + p) * DH + 8 * tig;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kp = 0; kp < KS / 2; kp++) {
+            uint4 kv = make_uint4(0u, 0u, 0u, 0u);
+            if (p < n) kv = *reinterpret_cast<const uint4 *>(kr + 32 * kp);
+            hmma16816(d, qa0h[2 * kp], qa2h[2 * kp], kv.x, kv.y);
+            hmma16816(d, qa0l[2 * kp], qa2l[2 * kp], kv.x, kv.y);
+            hmma16816(d, qa0h[2 * kp + 1], qa2h[2 * kp + 1], kv.z, kv.w);
+            hmma16816(d, qa0l[2 * kp + 1], qa2l[2 * kp + 1], kv.z, kv.w);
+        }
+        // d[0], d[1]: head g at positions 8 j + 2 tig, + 1 (rows 8-15 are padding)
+        const int c0 = 8 * j + 2 * tig;
+        if (g < G) {
+            if (c0 < n) sc[g * CH16 + c0] = d[0] * scale;
+            if (c0 + 1 < n) sc[g * CH16 + c0 + 1] = d[1] * scale;
+        }
+    }
+    __syncthreads();
+    for (int gg = warp; gg < G; gg += nw) {
+        float m = -INFINITY;
+        for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[gg * CH16 + t]);
+        m = warp_max(m);
+        float l = 0.0f;
+        for (int t = lane; t < n16; t += 32) {
+            const float e = t < n ? expf(sc[gg * CH16 + t] - m) : 0.0f;
+            sc[gg * CH16 + t] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) { ml[2 * gg] = m; ml[2 * gg + 1] = l; }
+    }
+    __syncthreads();
+    // out = P V: warp w owns the 8-dim column tiles w, w + nw, ...
+    constexpr int NTW = DH / 8 / (ATT_THREADS / 32);
+    float o[NTW][4];
+#pragma unroll
+    for (int i = 0; i < NTW; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    const uint32_t vbase = (uint32_t)__cvta_generic_to_shared(vt);
+    for (int kk = 0; kk < n16; kk += 16) {
+        float x0 = 0.f, x1 = 0.f, y0 = 0.f, y1 = 0.f;
+        if (g < G) {
+            const float *pr = sc + g * CH16 + kk;
+            x0 = pr[2 * tig], x1 = pr[2 * tig + 1], y0 = pr[8 + 2 * tig], y1 = pr[8 + 2 * tig + 1];
+        }
+        uint32_t pa0h, pa0l, pa2h, pa2l;
+        split_h2(x0, x1, pa0h, pa0l);
+        split_h2(y0, y1, pa2h, pa2l);
+#pragma unroll
+        for (int i = 0; i < NTW; i++) {
+            const int nt = warp + i * nw;
+            // lanes 0-15 address rows kk + lane of the 16 x 8 V tile (column block nt)
+            const uint32_t addr = vbase + (uint32_t)(((kk + (lane & 15)) * VSTR + 8 * nt) * 2);
+            uint32_t b0, b1;
+            asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(addr));
+            hmma16816(o[i], pa0h, pa2h, b0, b1);
+            hmma16816(o[i], pa0l, pa2l, b0, b1);
+        }
+    }
+    if (g < G) {
+#pragma unroll
+        for (int i = 0; i < NTW; i++) {
+            const int d = 8 * (warp + i * nw) + 2 * tig;
+            if (a.nsplit == 1) {
+                const float inv = 1.0f / ml[2 * g + 1];
+                float *op = a.out + (size_t)b * a.ldo + ((size_t)kh * G + g) * DH + d;
+                op[0] = o[i][0] * inv;
+                op[1] = o[i][1] * inv;
+            } else {
+                wsb[g * hstride + d] = o[i][0];
+                wsb[g * hstride + d + 1] = o[i][1];
+                if (d == 0) { wsb[g * hstride + DH] = ml[2 * g]; wsb[g * hstride + DH + 1] = ml[2 * g + 1]; }
+            }
+        }
+    }
+}
+
 // K/V append for rows that share a cache sequence: row b's new K (rotated
 // when RoPE applies) and V rows go to position pos[b] of sequence seq[b],
 // before the attention launch reads them.  One CTA per (kv head, row).
@@ -431,7 +615,13 @@ extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, in
         return lmc_set_error(LMC_ERR_INVALID, "attention: workspace %zu bytes < %zu needed", ws_bytes, need);
     a.ws = (float *)d_ws;
     const int G = H / Hkv;
-    const size_t smem = (size_t)(G * Dh + G * a.CH + 2 * G + (ATT_THREADS / 32) * ATT_GROUP * Dh) * sizeof(float);
+    // tensor-core body: fp16 cache, head 64 / 128, 1-8 query heads per kv head
+    // (LMC_ATTN_TC=0 selects the CUDA-core body; both give the same result)
+    const char *tce = getenv("LMC_ATTN_TC");
+    const bool tc = kv_dtype == LMC_KV_F16 && (Dh == 64 || Dh == 128) && G <= 8 && !(tce && tce[0] == '0');
+    const int CH16 = (a.CH + 15) & ~15;
+    const size_t smem = tc ? (size_t)(G * Dh + G * CH16 + 2 * G + 2) * sizeof(float) + 16 + (size_t)CH16 * (Dh + 8) * 2
+                           : (size_t)(G * Dh + G * a.CH + 2 * G + (ATT_THREADS / 32) * ATT_GROUP * Dh) * sizeof(float);
     if (smem > 200 * 1024) return lmc_set_error(LMC_ERR_UNSUPPORTED, "attention: group too large");
     dim3 grid(a.nsplit, Hkv, batch);
     if (d_seq) {  // rows share cache sequences: append every row's K/V first
@@ -439,11 +629,14 @@ extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, in
         else LMC_LAUNCH("kv append", k_kv_append<__half>, dim3(Hkv, batch), 64, 0, s, a);
     }
     if (kv_dtype == LMC_KV_F32) {
-        void (*fn)(AttnArgs) = Dh == 64 ? k_attn_split<float, 64> : Dh == 128 ? k_attn_split<float, 128> : k_attn_split<float, 0>;
+        void (*fn)(AttnArgs) = Dh == 64 ? k_attn_split<float, 64, false> : Dh == 128 ? k_attn_split<float, 128, false>
+                                                                      : k_attn_split<float, 0, false>;
         if (smem > 48 * 1024) LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         LMC_LAUNCH("attention", fn, grid, ATT_THREADS, smem, s, a);
     } else {
-        void (*fn)(AttnArgs) = Dh == 64 ? k_attn_split<__half, 64> : Dh == 128 ? k_attn_split<__half, 128> : k_attn_split<__half, 0>;
+        void (*fn)(AttnArgs) = tc ? (Dh == 64 ? k_attn_split<__half, 64, true> : k_attn_split<__half, 128, true>)
+                                  : Dh == 64 ? k_attn_split<__half, 64, false> : Dh == 128 ? k_attn_split<__half, 128, false>
+                                                                                  : k_attn_split<__half, 0, false>;
         if (smem > 48 * 1024) LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         LMC_LAUNCH("attention", fn, grid, ATT_THREADS, smem, s, a);
     }
