@@ -395,13 +395,16 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
     }
     __syncthreads();  // the new row (read back below) and q are in place
     const int n = t1 - t0, n16 = (n + 15) & ~15;
-    // stage V rows [t0, t0 + n) (zero rows up to n16), 16 bytes per thread and step
+    // stage V rows [t0, t0 + n) (zero rows up to n16) by asynchronous 16-byte
+    // copies: they land while the scores are computed (waited before the output)
     for (int i = threadIdx.x; i < n16 * (DH / 8); i += ATT_THREADS) {
         const int r = i / (DH / 8), c8 = i % (DH / 8);
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (r < n) v = *reinterpret_cast<const uint4 *>(vc + (size_t)(t0 + r) * DH + 8 * c8);
-        *reinterpret_cast<uint4 *>(vt + r * VSTR + 8 * c8) = v;
+        const __half *src = vc + (size_t)(t0 + (r < n ? r : 0)) * DH + 8 * c8;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(vt + r * VSTR + 8 * c8)),
+                     "l"(src), "r"(r < n ? 16 : 0)
+                     : "memory");
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     // q fragments: row g (query head g of the group), hi and lo
     uint32_t qa0h[KS], qa0l[KS], qa2h[KS], qa2l[KS];
 #pragma unroll
@@ -416,24 +419,35 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
         split_h2(y0, y1, qa2h[ks], qa2l[ks]);
     }
     const float scale = 1.0f / sqrtf((float)DH);
-    for (int j = warp; 8 * j < n; j += nw) {  // 8-position tiles
-        const int p = 8 * j + g;               // this lane's B column (position within the split)
-        const __half *kr = kc + (size_t)(t0 + p) * DH + 8 * tig;
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
+    constexpr int TB = DH == 128 ? 2 : 4;  // tiles per warp whose K loads are issued together
+    for (int j0 = warp; 8 * j0 < n; j0 += TB * nw) {  // 8-position tiles j0, j0 + nw, ...
+        uint4 kv[TB][KS / 2];
 #pragma unroll
-        for (int kp = 0; kp < KS / 2; kp++) {
-            uint4 kv = make_uint4(0u, 0u, 0u, 0u);
-            if (p < n) kv = *reinterpret_cast<const uint4 *>(kr + 32 * kp);
-            hmma16816(d, qa0h[2 * kp], qa2h[2 * kp], kv.x, kv.y);
-            hmma16816(d, qa0l[2 * kp], qa2l[2 * kp], kv.x, kv.y);
-            hmma16816(d, qa0h[2 * kp + 1], qa2h[2 * kp + 1], kv.z, kv.w);
-            hmma16816(d, qa0l[2 * kp + 1], qa2l[2 * kp + 1], kv.z, kv.w);
+        for (int u = 0; u < TB; u++) {
+            const int p = 8 * (j0 + u * nw) + g;  // this lane's B column (position within the split)
+            const __half *kr = kc + (size_t)(t0 + (p < n ? p : 0)) * DH + 8 * tig;
+#pragma unroll
+            for (int kp = 0; kp < KS / 2; kp++)
+                kv[u][kp] = p < n ? *reinterpret_cast<const uint4 *>(kr + 32 * kp) : make_uint4(0u, 0u, 0u, 0u);
         }
-        // d[0], d[1]: head g at positions 8 j + 2 tig, + 1 (rows 8-15 are padding)
-        const int c0 = 8 * j + 2 * tig;
-        if (g < G) {
-            if (c0 < n) sc[g * CH16 + c0] = d[0] * scale;
-            if (c0 + 1 < n) sc[g * CH16 + c0 + 1] = d[1] * scale;
+#pragma unroll
+        for (int u = 0; u < TB; u++) {
+            const int j = j0 + u * nw;
+            if (8 * j >= n) break;
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kp = 0; kp < KS / 2; kp++) {
+                hmma16816(d, qa0h[2 * kp], qa2h[2 * kp], kv[u][kp].x, kv[u][kp].y);
+                hmma16816(d, qa0l[2 * kp], qa2l[2 * kp], kv[u][kp].x, kv[u][kp].y);
+                hmma16816(d, qa0h[2 * kp + 1], qa2h[2 * kp + 1], kv[u][kp].z, kv[u][kp].w);
+                hmma16816(d, qa0l[2 * kp + 1], qa2l[2 * kp + 1], kv[u][kp].z, kv[u][kp].w);
+            }
+            // d[0], d[1]: head g at positions 8 j + 2 tig, + 1 (rows 8-15 are padding)
+            const int c0 = 8 * j + 2 * tig;
+            if (g < G) {
+                if (c0 < n) sc[g * CH16 + c0] = d[0] * scale;
+                if (c0 + 1 < n) sc[g * CH16 + c0 + 1] = d[1] * scale;
+            }
         }
     }
     __syncthreads();
@@ -450,7 +464,8 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
         l = warp_sum(l);
         if (lane == 0) { ml[2 * gg] = m; ml[2 * gg + 1] = l; }
     }
-    __syncthreads();
+    asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's V copies landed
+    __syncthreads();                                   // and every thread's
     // out = P V: warp w owns the 8-dim column tiles w, w + nw, ...
     constexpr int NTW = DH / 8 / (ATT_THREADS / 32);
     float o[NTW][4];
