@@ -235,7 +235,12 @@ def test_argmax_first_max(cuda, orc):
 @pytest.mark.parametrize("H,Hkv,Dh,S,pos,kvd", [
     (12, 12, 64, 1024, 0, rt.KV_F32), (12, 12, 64, 1024, 135, rt.KV_F32),
     (32, 4, 64, 2048, 700, rt.KV_F32), (32, 8, 128, 4096, 1500, rt.KV_F32),
-    (32, 4, 64, 2048, 511, rt.KV_F16), (8, 8, 64, 64, 63, rt.KV_F32)])
+    (32, 4, 64, 2048, 511, rt.KV_F16), (8, 8, 64, 64, 63, rt.KV_F32),
+    # fp16 caches: the tensor-core body (head 64/128, 1-8 query heads per kv
+    # head, short and long contexts) and the CUDA-core body (16 query heads
+    # per kv head; head 96)
+    (32, 8, 128, 4096, 1500, rt.KV_F16), (12, 12, 64, 1024, 135, rt.KV_F16), (32, 4, 64, 2048, 14, rt.KV_F16),
+    (32, 2, 64, 512, 300, rt.KV_F16), (6, 2, 96, 256, 200, rt.KV_F16), (6, 2, 96, 256, 200, rt.KV_F32)])
 def test_attention(cuda, orc, H, Hkv, Dh, S, pos, kvd):
     rng = np.random.default_rng(pos + H)
     B = 2
