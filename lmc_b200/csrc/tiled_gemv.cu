@@ -58,6 +58,8 @@ constexpr int NTHR = WARPS * 32;
 constexpr int SMEM_PAIR = 112 * 1024;      // two such CTAs fit on one SM
 constexpr int SMEM_LIMIT = 200 * 1024;     // one CTA per SM
 constexpr int RING_TARGET = 80 * 1024;     // bulk-copy bytes in flight per CTA
+// activation tasks a thread holds in registers in the long-row variant
+__host__ __device__ constexpr int rx_tasks(int QT) { return QT == 6 ? 16 : 7; }
 constexpr long long PF_BYTES = 40ll << 20;  // L2 prefetch ahead of the rings, per launch
 constexpr uint32_t LO4 = 0x0F0F0F0Fu;
 
@@ -230,6 +232,13 @@ template <int NT, int QT> struct Smem {
     __device__ __host__ size_t total() const { return bar_off() + (size_t)WARPS * stages * 8; }
 };
 
+// silu(x) = x / (1 + e^-x) from the fast exponential and divide intrinsics
+// (a few ulp, far inside the GEMV's 1e-3 bound).  With the full-precision
+// expf and IEEE division the SwiGLU prologue cost the 8B model's decode step
+// 8% at one sequence and 18% at four.  For x < -87 the divisor passes 2^126
+// and the result is 0 (the exact value is below 1e-35 in magnitude).
+__device__ __forceinline__ float silu_short(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 // The activation a GEMV multiplies, after its prologue op:
 //   LMC_PRO_NONE     x
 //   LMC_PRO_LAYERNORM (x - mean) * rstd * w + b      (src/ops.c:47-59)
@@ -250,8 +259,8 @@ struct XView {
         if (pro == LMC_PRO_NONE) return v;
         if (pro == LMC_PRO_SWIGLU) {
             const float4 u = __ldg(reinterpret_cast<const float4 *>(x2 + (size_t)bi * ldx + k));
-            return make_float4(lmc_silu_f(v.x) * u.x, lmc_silu_f(v.y) * u.y, lmc_silu_f(v.z) * u.z,
-                               lmc_silu_f(v.w) * u.w);
+            return make_float4(silu_short(v.x) * u.x, silu_short(v.y) * u.y, silu_short(v.z) * u.z,
+                               silu_short(v.w) * u.w);
         }
         const float4 ww = __ldg(reinterpret_cast<const float4 *>(w + k));
         if (pro == LMC_PRO_RMSNORM) {
@@ -290,7 +299,7 @@ __device__ __forceinline__ void cta_reduce(float (&v)[N], float *red) {
 // Each task (chunk q, batch row b, c) handles the 8 (k32) or 4 (k16) columns
 // of lane column c and writes all three limbs; the 4 tasks of a chunk are
 // adjacent lanes, so the chunk's integer sum is a 2-step shuffle.
-template <int NT, int QT>
+template <int NT, int QT, bool RX>
 __device__ __forceinline__ void build_x(uint8_t *smem, const Smem<NT, QT> &L, const TArgs &a) {
     constexpr int NB = 2 * NT, CH = Smem<NT, QT>::CH, SPAN = QT == 6 ? 16 : 32;
     float *scl = reinterpret_cast<float *>(smem + L.sc_off());
@@ -368,8 +377,31 @@ __device__ __forceinline__ void build_x(uint8_t *smem, const Smem<NT, QT> &L, co
     float m[NB];
 #pragma unroll
     for (int b = 0; b < NB; b++) m[b] = 0.0f;
+    // RX (long rows of one batch row, more than two tasks a thread): every
+    // task of this thread stays in registers, all its loads in flight at
+    // once, and pass 2 reads them back instead of going to L2 again.  The
+    // host picks RX only when nb == 1 and ntask <= rx_tasks(QT) * NTHR.
+    constexpr int MT = RX ? rx_tasks(QT) : 1;
+    const bool regs = RX && nb == 1 && ntask <= MT * NTHR;
+    float cv[MT][TV];
+    if (RX && regs) {
+#pragma unroll
+        for (int jt = 0; jt < MT; jt++) {
+            const int t = tid + jt * NTHR;
+            if (t < ntask) {
+                load_task(t, 0, cv[jt]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < TV; i++) cv[jt][i] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int jt = 0; jt < MT; jt++)
+#pragma unroll
+            for (int i = 0; i < TV; i++) m[0] = fmaxf(m[0], fabsf(cv[jt][i]));
+    }
 #pragma unroll 2
-    for (int t = tid; t < ntask; t += NTHR) {
+    for (int t = regs ? ntask : tid; t < ntask; t += NTHR) {
 #pragma unroll
         for (int b = 0; b < NB; b++)
             if (b < nb) {
@@ -397,21 +429,9 @@ __device__ __forceinline__ void build_x(uint8_t *smem, const Smem<NT, QT> &L, co
     }
     // pass 2: limbs into the fragments, integer chunk sums (rows >= nb are zero)
     int *xs = reinterpret_cast<int *>(smem + L.xs_off());
-    for (int t = tid; t < ntask; t += NTHR) {
+    auto quant_task = [&](int t, int b, const float (&v)[TV]) {
         const int c = t & 3, q = t >> 2;
-#pragma unroll
-        for (int b = 0; b < NB; b++) {
-            float v[TV];
-#pragma unroll
-            for (int i = 0; i < TV; i++) v[i] = 0.0f;
-            if (b < nb) {
-                if (NT == 1 && t == tid) {
-#pragma unroll
-                    for (int i = 0; i < TV; i++) v[i] = c0[b < NC0 ? b : 0][i];
-                } else {
-                    load_task(t, b, v);
-                }
-            }
+        {
             uint32_t r[2][3] = {{0u, 0u, 0u}, {0u, 0u, 0u}};
             int isum = 0;
 #pragma unroll
@@ -438,6 +458,38 @@ __device__ __forceinline__ void build_x(uint8_t *smem, const Smem<NT, QT> &L, co
                 isum += __shfl_xor_sync(0xffffffffu, isum, 1);
                 isum += __shfl_xor_sync(0xffffffffu, isum, 2);
                 if (c == 0) xs[(size_t)q * NB + b] = isum;
+            }
+        }
+    };
+    if (RX && regs) {  // task counts are multiples of 32: warps stay uniform (shuffles above)
+        float z[TV];
+#pragma unroll
+        for (int i = 0; i < TV; i++) z[i] = 0.0f;
+#pragma unroll
+        for (int jt = 0; jt < MT; jt++) {
+            const int t = tid + jt * NTHR;
+            if (t < ntask) {
+                quant_task(t, 0, cv[jt]);
+#pragma unroll
+                for (int b = 1; b < NB; b++) quant_task(t, b, z);
+            }
+        }
+    } else {
+        for (int t = tid; t < ntask; t += NTHR) {
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                float v[TV];
+#pragma unroll
+                for (int i = 0; i < TV; i++) v[i] = 0.0f;
+                if (b < nb) {
+                    if (NT == 1 && t == tid) {
+#pragma unroll
+                        for (int i = 0; i < TV; i++) v[i] = c0[b < NC0 ? b : 0][i];
+                    } else {
+                        load_task(t, b, v);
+                    }
+                }
+                quant_task(t, b, v);
             }
         }
     }
@@ -827,7 +879,7 @@ __device__ __forceinline__ void refill(bool leader, uint64_t *bar, void *dst, co
 // adds each finished row tile into the CTA accumulator.  Then every row tile
 // is completed by the CTA holding its first unit: partial tiles of the other
 // CTAs are added into it through distributed shared memory.
-template <int NT, int QT>
+template <int NT, int QT, bool RX>
 __global__ void __launch_bounds__(NTHR, 2) k_gemv_tiled(TArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NB = 2 * NT, UNIT = unit_bytes(QT);
@@ -867,7 +919,7 @@ __global__ void __launch_bounds__(NTHR, 2) k_gemv_tiled(TArgs a) {
             if (a.pb) prefetch_l1(a.pb + k);
         }
     pdl_wait();
-    build_x<NT, QT>(smem, L, a);
+    build_x<NT, QT, RX>(smem, L, a);
     __syncthreads();
     const float *inv = reinterpret_cast<const float *>(smem + L.sc_off()) + 8;
     const int XS = a.XL * XSTR;                         // bytes per (kb, nt) fragment block
@@ -993,8 +1045,13 @@ static int qt_of(uint32_t type) { return type == LMC_TYPE_Q4_K ? 4 : type == LMC
     case 82: return F(2, 8);                                              \
     default: return F(4, 8);                                              \
     }
-#define LMC_KERNEL_PTR(n, q) (const void *)k_gemv_tiled<n, q>
-static const void *kernel_for(int NT, int QT) { LMC_TILED_SWITCH(NT, QT, LMC_KERNEL_PTR) }
+#define LMC_KERNEL_PTR(n, q) (const void *)k_gemv_tiled<n, q, false>
+static const void *kernel_for(int NT, int QT, bool rx = false) {
+    if (rx && NT == 1) return QT == 4 ? (const void *)k_gemv_tiled<1, 4, true>
+                              : QT == 6 ? (const void *)k_gemv_tiled<1, 6, true>
+                                        : (const void *)k_gemv_tiled<1, 8, true>;
+    LMC_TILED_SWITCH(NT, QT, LMC_KERNEL_PTR)
+}
 static size_t smem_for(int NT, int QT, int KB, int XL, int maxrt, int stages) {
 #define LMC_SMEM_TOTAL(n, q) Smem<n, q>{KB, XL, maxrt, stages}.total()
     LMC_TILED_SWITCH(NT, QT, LMC_SMEM_TOTAL)
@@ -1113,7 +1170,15 @@ extern "C" int lmc_tiled_build(lmc_qtensor *t) {
 }
 
 static int launch_plan(const lmc_qtensor *t, TArgs a, const Plan &P, cudaStream_t s) {
-    const void *fn = kernel_for(P.NT, qt_of(t->type));
+    // one batch row whose activation tasks (32 per 256 columns, 64 for Q6_K)
+    // come to more than two a thread: the register-held activation variant.
+    // Not behind a SwiGLU prologue: there the unrolled gate arithmetic of all
+    // tasks made decode steps slower (the 8B model by 6% at K = 14336,
+    // TinyLlama by 7% at K = 5632) than the rolled loop.
+    const int QT = qt_of(t->type), ntask = a.KB * (QT == 6 ? 64 : 32);
+    const bool rx = P.NT == 1 && a.nb == 1 && ntask > 2 * NTHR && ntask <= rx_tasks(QT) * NTHR &&
+                    a.pro != LMC_PRO_SWIGLU;
+    const void *fn = kernel_for(P.NT, QT, rx);
     // dynamic shared-memory limit per kernel: only ever raised (lowering it
     // under a launch already queued on another stream is not allowed)
     static thread_local struct { const void *fn; size_t max_smem; } attr[16];

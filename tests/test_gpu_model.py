@@ -58,6 +58,20 @@ def test_tiny_generate_matches_oracle(cuda, orc, model_dir, kind, kw):
     assert got2[0].tolist() == ids
 
 
+def test_llama_long_rows_logits(cuda, orc, model_dir):
+    """A one-layer LLaMA whose Q6_K head (K = 2304, RMS prologue fused) takes
+    the GEMV's register-held activation variant, and whose Q4_K down
+    projection (K = 4608) takes the SwiGLU prologue with the short silu."""
+    path = tiny("llama", model_dir, L=1, D=2304, H=18, Hkv=6, F=4608, S=64, V=512, seed=4)
+    om = orc.model(path)
+    m = rt.Model(path, max_batch=1)
+    for pos, t in enumerate([3, 500, 77, 1]):
+        want = om.forward(t, pos)
+        got, nxt = m.forward([t], [pos])
+        assert rel_err(got[0], want) < 1e-3
+        assert nxt[0] == int(np.argmax(got[0]))
+
+
 def test_gpt2_small_greedy_32(cuda, model_dir):
     """GPT-2 Small shape (12 x 768, V 50257, Q4_K + Q6_K): 8-token prompt,
     32 greedy ids identical to LMc's compiled model_forward."""
