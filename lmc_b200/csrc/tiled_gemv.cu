@@ -377,7 +377,7 @@ __device__ __forceinline__ void build_x(uint8_t *smem, const Smem<NT, QT> &L, co
     float m[NB];
 #pragma unroll
     for (int b = 0; b < NB; b++) m[b] = 0.0f;
-    // RX (long rows of one batch row, more than two tasks a thread): every
+    // RX (long rows of one batch row, more than four tasks a thread): every
     // task of this thread stays in registers, all its loads in flight at
     // once, and pass 2 reads them back instead of going to L2 again.  The
     // host picks RX only when nb == 1 and ntask <= rx_tasks(QT) * NTHR.
@@ -1171,12 +1171,13 @@ extern "C" int lmc_tiled_build(lmc_qtensor *t) {
 
 static int launch_plan(const lmc_qtensor *t, TArgs a, const Plan &P, cudaStream_t s) {
     // one batch row whose activation tasks (32 per 256 columns, 64 for Q6_K)
-    // come to more than two a thread: the register-held activation variant.
-    // Not behind a SwiGLU prologue: there the unrolled gate arithmetic of all
-    // tasks made decode steps slower (the 8B model by 6% at K = 14336,
-    // TinyLlama by 7% at K = 5632) than the rolled loop.
+    // come to more than four a thread: the register-held activation variant
+    // (at three and four tasks a thread, Q6_K K = 3072 and 4096, it was the
+    // slower one).  Not behind a SwiGLU prologue: there the unrolled gate
+    // arithmetic of all tasks made decode steps slower (the 8B model by 6% at
+    // K = 14336, TinyLlama by 7% at K = 5632) than the rolled loop.
     const int QT = qt_of(t->type), ntask = a.KB * (QT == 6 ? 64 : 32);
-    const bool rx = P.NT == 1 && a.nb == 1 && ntask > 2 * NTHR && ntask <= rx_tasks(QT) * NTHR &&
+    const bool rx = P.NT == 1 && a.nb == 1 && ntask > 4 * NTHR && ntask <= rx_tasks(QT) * NTHR &&
                     a.pro != LMC_PRO_SWIGLU;
     const void *fn = kernel_for(P.NT, QT, rx);
     // dynamic shared-memory limit per kernel: only ever raised (lowering it

@@ -59,10 +59,10 @@ def test_tiny_generate_matches_oracle(cuda, orc, model_dir, kind, kw):
 
 
 def test_llama_long_rows_logits(cuda, orc, model_dir):
-    """A one-layer LLaMA whose Q6_K head (K = 2304, RMS prologue fused) takes
+    """A one-layer LLaMA whose Q6_K head (K = 4352, RMS prologue fused) takes
     the GEMV's register-held activation variant, and whose Q4_K down
     projection (K = 4608) takes the SwiGLU prologue with the short silu."""
-    path = tiny("llama", model_dir, L=1, D=2304, H=18, Hkv=6, F=4608, S=64, V=512, seed=4)
+    path = tiny("llama", model_dir, L=1, D=4352, H=34, Hkv=17, F=4608, S=64, V=512, seed=4)
     om = orc.model(path)
     m = rt.Model(path, max_batch=1)
     for pos, t in enumerate([3, 500, 77, 1]):
