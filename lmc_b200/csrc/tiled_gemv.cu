@@ -58,7 +58,8 @@ constexpr int NTHR = WARPS * 32;
 constexpr int SMEM_PAIR = 112 * 1024;      // two such CTAs fit on one SM
 constexpr int SMEM_LIMIT = 200 * 1024;     // one CTA per SM
 constexpr int RING_TARGET = 80 * 1024;     // bulk-copy bytes in flight per CTA
-// activation tasks a thread holds in registers in the long-row variant
+// activation tasks a thread holds in registers in the longest-row variant
+// (a shorter one holds 4)
 __host__ __device__ constexpr int rx_tasks(int QT) { return QT == 6 ? 16 : 7; }
 constexpr long long PF_BYTES = 40ll << 20;  // L2 prefetch ahead of the rings, per launch
 constexpr uint32_t LO4 = 0x0F0F0F0Fu;
@@ -299,7 +300,7 @@ __device__ __forceinline__ void cta_reduce(float (&v)[N], float *red) {
 // Each task (chunk q, batch row b, c) handles the 8 (k32) or 4 (k16) columns
 // of lane column c and writes all three limbs; the 4 tasks of a chunk are
 // adjacent lanes, so the chunk's integer sum is a 2-step shuffle.
-template <int NT, int QT, bool RX>
+template <int NT, int QT, int RX>
 __device__ __forceinline__ void build_x(uint8_t *smem, const Smem<NT, QT> &L, const TArgs &a) {
     constexpr int NB = 2 * NT, CH = Smem<NT, QT>::CH, SPAN = QT == 6 ? 16 : 32;
     float *scl = reinterpret_cast<float *>(smem + L.sc_off());
@@ -377,14 +378,15 @@ __device__ __forceinline__ void build_x(uint8_t *smem, const Smem<NT, QT> &L, co
     float m[NB];
 #pragma unroll
     for (int b = 0; b < NB; b++) m[b] = 0.0f;
-    // RX (long rows of one batch row, more than four tasks a thread): every
-    // task of this thread stays in registers, all its loads in flight at
-    // once, and pass 2 reads them back instead of going to L2 again.  The
-    // host picks RX only when nb == 1 and ntask <= rx_tasks(QT) * NTHR.
-    constexpr int MT = RX ? rx_tasks(QT) : 1;
-    const bool regs = RX && nb == 1 && ntask <= MT * NTHR;
+    // RX > 0 (rows of one batch row with more than two tasks a thread):
+    // every task of this thread, up to RX of them, stays in registers, all
+    // its loads in flight at once, and pass 2 reads them back instead of
+    // going to L2 again.  The host picks RX = 4 for three or four tasks a
+    // thread and RX = rx_tasks(QT) above that, only when nb == 1.
+    constexpr int MT = RX > 0 ? RX : 1;
+    const bool regs = RX > 0 && nb == 1 && ntask <= MT * NTHR;
     float cv[MT][TV];
-    if (RX && regs) {
+    if (RX > 0 && regs) {
 #pragma unroll
         for (int jt = 0; jt < MT; jt++) {
             const int t = tid + jt * NTHR;
@@ -461,7 +463,7 @@ __device__ __forceinline__ void build_x(uint8_t *smem, const Smem<NT, QT> &L, co
             }
         }
     };
-    if (RX && regs) {  // task counts are multiples of 32: warps stay uniform (shuffles above)
+    if (RX > 0 && regs) {  // task counts are multiples of 32: warps stay uniform (shuffles above)
         float z[TV];
 #pragma unroll
         for (int i = 0; i < TV; i++) z[i] = 0.0f;
@@ -879,7 +881,7 @@ __device__ __forceinline__ void refill(bool leader, uint64_t *bar, void *dst, co
 // adds each finished row tile into the CTA accumulator.  Then every row tile
 // is completed by the CTA holding its first unit: partial tiles of the other
 // CTAs are added into it through distributed shared memory.
-template <int NT, int QT, bool RX>
+template <int NT, int QT, int RX>
 __global__ void __launch_bounds__(NTHR, 2) k_gemv_tiled(TArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NB = 2 * NT, UNIT = unit_bytes(QT);
@@ -1045,11 +1047,14 @@ static int qt_of(uint32_t type) { return type == LMC_TYPE_Q4_K ? 4 : type == LMC
     case 82: return F(2, 8);                                              \
     default: return F(4, 8);                                              \
     }
-#define LMC_KERNEL_PTR(n, q) (const void *)k_gemv_tiled<n, q, false>
-static const void *kernel_for(int NT, int QT, bool rx = false) {
-    if (rx && NT == 1) return QT == 4 ? (const void *)k_gemv_tiled<1, 4, true>
-                              : QT == 6 ? (const void *)k_gemv_tiled<1, 6, true>
-                                        : (const void *)k_gemv_tiled<1, 8, true>;
+#define LMC_KERNEL_PTR(n, q) (const void *)k_gemv_tiled<n, q, 0>
+static const void *kernel_for(int NT, int QT, int rx = 0) {
+    if (rx == 4 && NT == 1) return QT == 4 ? (const void *)k_gemv_tiled<1, 4, 4>
+                                   : QT == 6 ? (const void *)k_gemv_tiled<1, 6, 4>
+                                             : (const void *)k_gemv_tiled<1, 8, 4>;
+    if (rx > 4 && NT == 1) return QT == 4 ? (const void *)k_gemv_tiled<1, 4, rx_tasks(4)>
+                                  : QT == 6 ? (const void *)k_gemv_tiled<1, 6, rx_tasks(6)>
+                                            : (const void *)k_gemv_tiled<1, 8, rx_tasks(8)>;
     LMC_TILED_SWITCH(NT, QT, LMC_KERNEL_PTR)
 }
 static size_t smem_for(int NT, int QT, int KB, int XL, int maxrt, int stages) {
@@ -1171,14 +1176,17 @@ extern "C" int lmc_tiled_build(lmc_qtensor *t) {
 
 static int launch_plan(const lmc_qtensor *t, TArgs a, const Plan &P, cudaStream_t s) {
     // one batch row whose activation tasks (32 per 256 columns, 64 for Q6_K)
-    // come to more than four a thread: the register-held activation variant
-    // (at three and four tasks a thread, Q6_K K = 3072 and 4096, it was the
-    // slower one).  Not behind a SwiGLU prologue: there the unrolled gate
-    // arithmetic of all tasks made decode steps slower (the 8B model by 6% at
-    // K = 14336, TinyLlama by 7% at K = 5632) than the rolled loop.
+    // come to more than two a thread: the register-held activation variant,
+    // sized to the tasks (four slots, else the longest rows' rx_tasks; the
+    // longest variant's unrolled code made three or four tasks slower than
+    // the rolled loop).  Not behind a SwiGLU prologue: there the unrolled
+    // gate arithmetic of all tasks made decode steps slower (the 8B model by
+    // 6% at K = 14336, TinyLlama by 7% at K = 5632) than the rolled loop.
     const int QT = qt_of(t->type), ntask = a.KB * (QT == 6 ? 64 : 32);
-    const bool rx = P.NT == 1 && a.nb == 1 && ntask > 4 * NTHR && ntask <= rx_tasks(QT) * NTHR &&
-                    a.pro != LMC_PRO_SWIGLU;
+    const int tpt = (ntask + NTHR - 1) / NTHR;
+    const int rx = P.NT == 1 && a.nb == 1 && tpt > 2 && a.pro != LMC_PRO_SWIGLU
+                       ? (tpt <= 4 ? 4 : tpt <= rx_tasks(QT) ? rx_tasks(QT) : 0)
+                       : 0;
     const void *fn = kernel_for(P.NT, QT, rx);
     // dynamic shared-memory limit per kernel: only ever raised (lowering it
     // under a launch already queued on another stream is not allowed)

@@ -101,14 +101,17 @@ def test_gemv(cuda, orc, t, M, K, B):
 # Shapes of the tensor-core path (Q4_K / Q6_K / Q8_0, cols % 256 == 0) that
 # exercise its work split: long rows (K = 14336), ragged row count, many row
 # tiles per cluster, and batch widths 2 and 5 (two rows per fragment, and an
-# odd row in the last fragment).  At batch 1 the rows of more than four
-# activation tasks a thread (K > 8192, Q6_K K > 4096) take the register-held
-# activation variant, up to its limits (K = 14336; Q6_K K = 16384; Q6_K
-# K = 4352 gives some threads five tasks and the others four), and Q4_K
-# K = 16384 the default one again.
+# odd row in the last fragment).  At batch 1 the rows of more than two
+# activation tasks a thread (K > 4096, Q6_K K > 2048) take a register-held
+# activation variant: four slots for three or four tasks (Q6_K K = 3072,
+# Q8_0 K = 5120 with some threads at three tasks and the others at two), the
+# longest one up to its limits (K = 14336; Q6_K K = 16384; Q6_K K = 4352
+# gives some threads five tasks and the others four), and Q4_K K = 16384
+# the default one again.
 TILED_CASES = [(synth.Q4_K, 4096, 14336), (synth.Q6_K, 50257, 768), (synth.Q8_0, 2048, 4096),
                (synth.Q4_K, 14336, 2048), (synth.Q8_0, 520, 768), (synth.Q8_0, 1024, 14336),
-               (synth.Q6_K, 1040, 16384), (synth.Q6_K, 2048, 4352), (synth.Q4_K, 512, 16384)]
+               (synth.Q6_K, 1040, 16384), (synth.Q6_K, 2048, 4352), (synth.Q4_K, 512, 16384),
+               (synth.Q6_K, 768, 3072), (synth.Q8_0, 600, 5120)]
 
 
 @pytest.mark.parametrize("t,M,K", TILED_CASES, ids=lambda v: str(v))
