@@ -7,7 +7,7 @@ every host.  The GPU path and the CPU reference read the same files.
 
 Block geometry and type IDs follow LMc src/quant.h:27-99.  The quantizers are
 plain per-block absmax / min-max quantizers (LMc ships none: it only reads
-GGUF files); parity is always judged on the dequantized bytes, so their
+GGUF files); parity is always checked on the dequantized bytes, so their
 quality only matters for keeping activations in a sane range.
 """
 import os

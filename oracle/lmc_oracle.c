@@ -1,10 +1,10 @@
 /* lmc_oracle.c - CPU restatement of LMc's quantized-weight hot path.
  *
- * TEST INFRASTRUCTURE ONLY (the checker, never the product): see
+ * TEST INFRASTRUCTURE ONLY (the oracle, never the product): see
  * lmc_oracle.h.  Compiled with -ffp-contract=off and without -ffast-math so
  * every float operation happens in the order written, which is the order LMc
  * writes them in quant.c.  Parity with LMc's own compiled sources is pinned
- * by tests/test_oracle_vs_ref.py and the fixtures in tests/golden/.
+ * by tests/test_oracle.py and the fixtures in tests/golden/.
  */
 #include "lmc_oracle.h"
 

@@ -1,6 +1,6 @@
 /* lmc_oracle.h - CPU restatement of LMc's quantized-weight hot path.
  *
- * TEST INFRASTRUCTURE ONLY.  This is the checker the CUDA path is compared
+ * TEST INFRASTRUCTURE ONLY.  This is the oracle the CUDA path is compared
  * against; it is never linked into, called by or shipped with the product
  * library (lmc_b200/liblmc_b200.so).  Only tests/, __graft_entry__.smoke()
  * and bench.py's cpu_baseline leg use it.
@@ -9,7 +9,7 @@
  * per function).  Parity of this restatement is pinned against LMc's own
  * sources, compiled from source into oracle/_ref/ by oracle/Makefile, on
  * seeded random blocks for all 13 block formats plus F16/F32, on single ops,
- * and on whole-model logits (tests/test_oracle_vs_ref.py), and against the
+ * and on whole-model logits (tests/test_oracle.py), and against the
  * committed golden fixtures in tests/golden/ (made by
  * tests/golden/make_golden.py from the same compiled LMc sources).
  */

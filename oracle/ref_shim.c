@@ -1,7 +1,7 @@
 /* ref_shim.c - ctypes-friendly entry points around LMc's own compiled
  * sources (nile-agi/LMc src/*.c, built from where they lie by
- * oracle/Makefile into oracle/_ref/).  TEST INFRASTRUCTURE ONLY: the
- * checker and the CPU baseline, never the product.
+ * oracle/Makefile into oracle/_ref/).  TEST INFRASTRUCTURE ONLY: a
+ * parity reference and the CPU baseline, never the product.
  *
  * LMc's lmc.c (CLI, tokenizer, sampling) is not linked; this file takes its
  * place as the driver.  Greedy selection restates lmc.c:45-47 (strict '>'),
