@@ -99,3 +99,51 @@ def test_matmul_vs_lmc(orc, ref):
         x = rng.normal(0, 1, K).astype(np.float32)
         b = rng.normal(0, 1, M).astype(np.float32)
         assert rel_err(orc.matmul_vec(w, x, b), ref.matmul_vec(w, x, b)) < 1e-5
+
+
+def test_norms_softmax_vs_lmc(orc, ref):
+    """LayerNorm, RMSNorm and softmax of the oracle against LMc's compiled
+    ops.c / ops_llama.c on random rows of the model widths and on edge rows:
+    one element, a constant row (zero variance: rstd = 1/sqrt(eps)), zeros,
+    and large magnitudes."""
+    rng = np.random.default_rng(11)
+    rows = [rng.normal(0, s, n).astype(np.float32) for n, s in ((768, 1.0), (2048, 3.0), (4096, 0.1), (100, 50.0))]
+    rows += [np.array([2.5], np.float32), np.full(256, 7.0, np.float32), np.zeros(64, np.float32),
+             rng.normal(0, 1e4, 512).astype(np.float32)]
+    for x in rows:
+        w = rng.normal(1, 0.1, x.size).astype(np.float32)
+        b = rng.normal(0, 0.1, x.size).astype(np.float32)
+        assert rel_err(orc.layer_norm(x, w, b), ref.layer_norm(x, w, b)) < 1e-5
+        if np.any(x):
+            assert rel_err(orc.rms_norm(x, w, 1e-5), ref.rms_norm(x, w, 1e-5)) < 1e-5
+        else:
+            assert np.array_equal(orc.rms_norm(x, w, 1e-5), ref.rms_norm(x, w, 1e-5))
+        assert rel_err(orc.softmax(x), ref.softmax(x)) < 1e-5
+
+
+@pytest.mark.parametrize("kind,kw", [
+    ("gpt2", dict(L=2, D=256, H=4, S=64, V=700, seed=21)),
+    ("llama", dict(L=2, D=256, H=8, Hkv=2, F=512, S=64, V=700, seed=21)),
+])
+def test_model_vs_lmc_random(orc, ref, tmp_path, kind, kw):
+    """A freshly generated model (not a fixture): the oracle's teacher-forced
+    logits match LMc's compiled model_forward within 1e-5 and its greedy ids
+    match LMc's generate loop."""
+    path = str(tmp_path / f"{kind}.gguf")
+    (synth.make_gpt2 if kind == "gpt2" else synth.make_llama)(path, **kw)
+    prompt = np.random.default_rng(3).integers(0, kw["V"], 6).astype(np.int32)
+    ref.load(path)
+    want_ids, _, _ = ref.generate(prompt, 12)
+    ref.load(path)
+    m = orc.model(path)
+    lg = None
+    for pos, t in enumerate(prompt):
+        lg = m.forward(int(t), pos)
+        assert rel_err(lg, ref.forward(int(t), pos)) < 1e-5
+    ids, pos = [], len(prompt)
+    for _ in range(12):
+        ids.append(orc.argmax(lg))
+        lg = m.forward(ids[-1], pos)
+        pos += 1
+    m.close()
+    assert ids == want_ids.tolist()
