@@ -65,3 +65,60 @@ def test_model_load_errors_are_status_codes(tmp_path):
     assert L.lmc_model_load(str(tmp_path / "missing.gguf").encode(), 1, 0, ctypes.byref(h)) == -5
     assert b"cannot open" in L.lmc_last_error()
     assert L.lmc_model_load(b"x", 0, 0, ctypes.byref(h)) == -1
+
+
+def _load_status(path, tp_rank=0, tp_size=1):
+    h = ctypes.c_void_p()
+    nid = ctypes.create_string_buffer(128)
+    rc = rt.lib().lmc_model_load_ex(str(path).encode(), 1, 1, 0, tp_rank, tp_size,
+                                    ctypes.cast(nid, ctypes.c_void_p) if tp_size > 1 else None, ctypes.byref(h))
+    return rc, rt.lib().lmc_last_error()
+
+
+def test_model_load_rejects_malformed_gguf(tmp_path):
+    """Malformed GGUF headers are reported as status codes with a message
+    (the header is parsed before anything is uploaded, so no GPU is needed):
+    bad magic, unknown version, truncated metadata, truncated tensor table,
+    missing block/head/width keys, heads not a multiple of kv heads."""
+    import struct
+    from lmc_b200 import synth
+    good = synth.make_llama(str(tmp_path / "ok.gguf"), L=1, D=64, H=4, Hkv=2, F=128, S=16, V=64, seed=1)
+    raw = open(good, "rb").read()
+
+    def case(name, data):
+        p = tmp_path / name
+        p.write_bytes(data)
+        return _load_status(p)
+
+    rc, msg = case("magic.gguf", b"GGUX" + raw[4:])
+    assert rc == -5 and b"not a GGUF v1-3 file" in msg
+    rc, msg = case("ver.gguf", raw[:4] + struct.pack("<I", 7) + raw[8:])
+    assert rc == -5 and b"not a GGUF v1-3 file" in msg
+    rc, msg = case("meta.gguf", raw[:60])
+    assert rc == -5 and b"truncated metadata" in msg
+    # header only: metadata intact, the tensor table cut in its first entry
+    hdr_end = raw.index(b"token_embd.weight") + 8
+    rc, msg = case("table.gguf", raw[:hdr_end])
+    assert rc == -5 and b"truncated tensor table" in msg
+    p = synth.write_gguf(str(tmp_path / "nokeys.gguf"), "llama", {"llama.block_count": 1}, {}, [])
+    rc, msg = _load_status(p)
+    assert rc == -5 and b"missing L/H/D metadata" in msg
+    p = synth.write_gguf(str(tmp_path / "kv.gguf"), "llama",
+                         {"llama.block_count": 1, "llama.attention.head_count": 6, "llama.embedding_length": 96,
+                          "llama.attention.head_count_kv": 4}, {}, [])
+    rc, msg = _load_status(p)
+    assert rc == -5 and b"not a multiple of kv heads" in msg
+
+
+def test_model_load_rejects_unshardable_tensor_parallel(tmp_path):
+    """Tensor parallel is for LLaMA models whose heads, kv heads and ffn rows
+    divide by the group size; other requests fail before any upload."""
+    from lmc_b200 import synth
+    g = synth.make_gpt2(str(tmp_path / "g.gguf"), L=1, D=64, H=4, S=16, V=64, seed=1)
+    rc, msg = _load_status(g, 0, 2)
+    assert rc == -2 and b"LLaMA models only" in msg
+    p = synth.make_llama(str(tmp_path / "l.gguf"), L=1, D=96, H=6, Hkv=3, F=192, S=16, V=64, seed=1)
+    rc, msg = _load_status(p, 0, 2)
+    assert rc == -2 and b"not divisible by 2" in msg
+    rc, msg = _load_status(p, 2, 2)
+    assert rc == -1 and b"shard 2 of 2" in msg
