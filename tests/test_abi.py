@@ -122,3 +122,33 @@ def test_model_load_rejects_unshardable_tensor_parallel(tmp_path):
     assert rc == -2 and b"not divisible by 2" in msg
     rc, msg = _load_status(p, 2, 2)
     assert rc == -1 and b"shard 2 of 2" in msg
+
+
+def test_entry_points_validate_arguments_first():
+    """Every entry point checks its arguments before it touches the device:
+    null pointers, sizes that are not whole blocks, empty shapes and
+    oversized requests come back as LMC_ERR_INVALID with a message, the way
+    LMc's LMC_FATAL checks fire before any work."""
+    L = rt.lib()
+    p = ctypes.c_void_p(256)  # never dereferenced: the checks fail first
+    calls = [
+        ("lmc_dequant", (12, None, 256, None, None), b"null"),
+        ("lmc_dequant", (12, p, 300, p, None), b"not a multiple of 256"),
+        ("lmc_qtensor_upload", (12, 0, 256, None, 0, None), b"args"),
+        ("lmc_layer_norm", (None, None, None, None, 768, 1, None), b"args"),
+        ("lmc_rms_norm", (None, None, None, 768, 1, 1e-5, None), b"args"),
+        ("lmc_softmax", (None, 10, 1, None), b"args"),
+        ("lmc_argmax", (None, 10, 1, None, None), b"args"),
+        ("lmc_gelu", (None, 10, None), b"null"),
+        ("lmc_model_forward", (None, None, None, 1, None, None), b"args"),
+        ("lmc_model_generate", (None, None, 1, 1, 1, 0, None), b"args"),
+        ("lmc_model_prefill", (None, 0, None, 1, 0, None, None), b"sequence"),
+        # 64 sequences x 32 heads x 128 dims over 32768 positions: the
+        # split-context scratch exceeds the fixed array
+        ("lmc_attention_decode_noalloc", (p, p, p, p, p, p, 0, p, 64, 32, 8, 128, 32768, None), b"attention_noalloc"),
+    ]
+    for name, args, word in calls:
+        rc = getattr(L, name)(*args)
+        assert rc == -1, (name, rc)
+        assert word in L.lmc_last_error(), (name, L.lmc_last_error())
+    assert L.lmc_model_free(None) == 0 and L.lmc_qtensor_free(None) == 0
