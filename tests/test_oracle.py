@@ -147,3 +147,25 @@ def test_model_vs_lmc_random(orc, ref, tmp_path, kind, kw):
         pos += 1
     m.close()
     assert ids == want_ids.tolist()
+
+
+@pytest.mark.parametrize("H,Hkv,Dh,S,pos", [(12, 12, 64, 32, 0), (12, 12, 64, 32, 31), (32, 4, 64, 128, 100),
+                                            (32, 8, 128, 64, 40), (6, 2, 16, 8, 5)])
+def test_attention_vs_float64(orc, H, Hkv, Dh, S, pos):
+    """The oracle's attention read against a float64 statement of LMc's
+    (ops.c:128-178, ops_llama.c:88-134): scores q.k / sqrt(Dh) over positions
+    0..pos, softmax, weighted V; query head h reads kv head h / (H / Hkv)
+    (the code's division, not the modulo its header comment names)."""
+    rng = np.random.default_rng(H * 1000 + pos)
+    q = rng.normal(0, 1, H * Dh).astype(np.float32)
+    kc = rng.normal(0, 1, (Hkv, S, Dh)).astype(np.float32)
+    vc = rng.normal(0, 1, (Hkv, S, Dh)).astype(np.float32)
+    got = orc.attention(q, kc, vc, H, Hkv, Dh, S, pos).reshape(H, Dh)
+    G = H // Hkv
+    for h in range(H):
+        k = kc[h // G, :pos + 1].astype(np.float64)
+        v = vc[h // G, :pos + 1].astype(np.float64)
+        s = k @ q[h * Dh:(h + 1) * Dh].astype(np.float64) / np.sqrt(Dh)
+        p = np.exp(s - s.max())
+        want = (p / p.sum()) @ v
+        assert rel_err(got[h], want) < 1e-5, h
