@@ -169,3 +169,28 @@ def test_attention_vs_float64(orc, H, Hkv, Dh, S, pos):
         p = np.exp(s - s.max())
         want = (p / p.sum()) @ v
         assert rel_err(got[h], want) < 1e-5, h
+
+
+def test_rope_and_activations_vs_float64(orc):
+    """RoPE table (models.c:101-117: angle = pos / theta^(2d/Dh)), the pair
+    rotation (ops_llama.c:39-48) and GELU / SiLU (ops.c:20-29) of the oracle
+    against float64 statements of the same formulas."""
+    S, Dh, theta = 300, 128, 10000.0
+    c, s = orc.rope_cache(S, Dh, theta)
+    pos = np.arange(S, dtype=np.float64)[:, None]
+    d = np.arange(Dh // 2, dtype=np.float64)[None, :]
+    ang = pos / np.power(theta, 2.0 * d / Dh)
+    # float32 angles of up to ~300 rad: the table matches to float32 angle rounding
+    assert np.max(np.abs(c - np.cos(ang))) < 2e-4 and np.max(np.abs(s - np.sin(ang))) < 2e-4
+    rng = np.random.default_rng(2)
+    v = rng.normal(0, 1, Dh).astype(np.float32)
+    got = orc.rope_apply(v, c[123], s[123])
+    x0, x1 = v[0::2].astype(np.float64), v[1::2].astype(np.float64)
+    cc, ss = c[123].astype(np.float64), s[123].astype(np.float64)
+    want = np.empty(Dh)
+    want[0::2], want[1::2] = x0 * cc - x1 * ss, x0 * ss + x1 * cc
+    assert np.max(np.abs(got - want)) < 1e-5
+    x = np.linspace(-20, 20, 401).astype(np.float32)
+    xd = x.astype(np.float64)
+    assert np.allclose(orc.gelu(x), xd / (1 + np.exp(-1.702 * xd)), rtol=1e-5, atol=1e-6)
+    assert np.allclose(orc.silu(x), xd / (1 + np.exp(-xd)), rtol=1e-5, atol=1e-6)
