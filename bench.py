@@ -1,19 +1,30 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 hot path: GPT-2 Small decode tokens/s.
+"""Benchmark of the B200 hot path.
 
-Workload (the decode configuration the headline metric is quoted on): a
-GPT-2 Small-shaped model (12 layers x 768, 12 heads, vocab 50257, context
-1024; attention/MLP weights Q4_K, ffn_down and output Q6_K, fp32 norms and
-biases) with seeded synthetic N(0, 0.02) weights, an 8-token random prompt,
-batch 1, fp32 head-major KV cache.  One step = one greedy decode token
-(embedding, 12 blocks, final norm, lm_head GEMV, device argmax), replayed as
-one CUDA graph.  The weights (86.7 MB) fit in the 126 MB L2, so L2 is flushed
-(256 MB write) before every timed step: every step streams its weights from
-HBM.
+Default workload (the headline line): GPT-2 Small decode tokens/s.  A GPT-2
+Small-shaped model (12 layers x 768, 12 heads, vocab 50257, context 1024;
+attention/MLP weights Q4_K, ffn_down and output Q6_K, fp32 norms and biases)
+with seeded synthetic N(0, 0.02) weights, an 8-token random prompt, batch 1,
+fp32 head-major KV cache.  One step = one greedy decode token (embedding, 12
+blocks, final norm, lm_head GEMV, device argmax) replayed as one CUDA graph;
+on one GPU the step is one persistent kernel.  The weights (86.7 MB) fit in the
+126 MB L2, so L2 is flushed (256 MB write) before every timed step, in the
+device-timed loop and in the end-to-end loop alike: every step streams its
+weights from HBM.  The line also carries the Q4_K 3072x768 GEMV (the other
+half of the metric) with LMc's matmul_vec time on the same weights beside it.
 
 GPT-2 Small does not shard: with --gpus N each rank decodes its own replica
 (weak scaling, no collective on the data path); value = all ranks' tokens /
 the slowest rank's time.
+
+Other workloads (--workload), one JSON line each (sweep: one per case):
+  gemv       one GEMV (--type/--rows/--cols/--batch; default Q4_K 3072x768 B=1)
+  sweep      the format sweep: Q4_0 Q5_1 Q8_0 Q3_K Q5_K Q6_K IQ4_XS at 6400x1600
+             and 1600x6400, batch 1 / 8 / 64 / 512
+  tinyllama  TinyLlama-1.1B shape, --batch sequences, --prompt / --gen tokens
+  llama8b    Llama-8B shape; under torchrun with --tp, tensor parallel over the ranks
+Model weights for tinyllama / llama8b are random blocks of the named formats
+(the same bytes per weight as quantized weights, written in seconds).
 
 --impl reference times LMc's own C sources (oracle/_ref, built from source
 with its `make omp` flags) on this host's cores: rank 0 only.
@@ -21,7 +32,6 @@ with its `make omp` flags) on this host's cores: rank 0 only.
 import argparse
 import json
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -34,9 +44,11 @@ sys.path.insert(0, ROOT)
 METRIC = "Q4_K GEMV HBM GB/s vs ~8 TB/s; GPT-2/TinyLlama decode tok/s at 1/2/4/8 GPU"
 UNIT = "tokens/s"
 N_PROMPT = 8
+GPT2 = dict(L=12, D=768, H=12, S=1024, V=50257, F=3072)
 WORKLOAD = ("gpt2-small decode: 12L x 768 (12 heads), vocab 50257, ctx 1024; Q4_K attn/MLP, Q6_K ffn_down+output, "
             "fp32 norms/biases; 8-token prompt, batch 1 per GPU, greedy, fp32 KV")
-L2_NOTE = "L2 flushed (256 MB write) before every timed step"
+L2_NOTE = "L2 flushed (256 MB write) before every timed step (device-timed and end-to-end loops)"
+CPU_REPS = 5  # repetitions of the LMc baseline; the median is reported
 
 
 def env_int(k, d):
@@ -55,6 +67,17 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def step_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu capture of it
+    (profiles/traffic.json: {kernel: {"bytes": ..., "source": ...}}), or None."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get(kernel)
+    except (OSError, ValueError):
+        return None
+
+
 def model_path(rank, barrier):
     from lmc_b200 import synth
     d = os.environ.get("LMC_BENCH_CACHE", "/tmp/lmc_bench_models")
@@ -70,10 +93,20 @@ def prompt_ids():
     return np.random.default_rng(0).integers(0, 50257, N_PROMPT).astype(np.int32)
 
 
-# DRAM bytes (read + write) of one lm_head-shape GEMV launch, from the ncu
-# capture summarised in profiles/gemv_q6k_50257x768.md (same kernel and shape
-# as the roofline line below).
-LM_HEAD_DRAM_BYTES = 31747584
+def gpt2_step_bytes(ctx_positions):
+    """Algorithmic bytes of one GPT-2 Small decode step: every weight once
+    (Q4_K 0.5625 B/weight, Q6_K 0.8203, fp32 norms and biases), the embedding
+    row, and the fp32 K and V rows of the `ctx_positions` cached positions."""
+    from lmc_b200 import synth
+    g = GPT2
+    D, F, L, V, S = g["D"], g["F"], g["L"], g["V"], g["S"]
+    q4 = lambda r, c: synth.tensor_bytes(synth.Q4_K, r * c)
+    q6 = lambda r, c: synth.tensor_bytes(synth.Q6_K, r * c)
+    layer = q4(3 * D, D) + q4(D, D) + q4(F, D) + q6(D, F) + 4 * (4 * D + 3 * D + D + F + D)
+    head = q6(V, D) + 4 * 2 * D
+    embed = synth.tensor_bytes(synth.Q6_K, 256) * ((D + 255) // 256) + 4 * D
+    kv = 2 * L * D * 4 * ctx_positions
+    return L * layer + head + embed + kv
 
 
 class Clocks:
@@ -140,21 +173,42 @@ class Clocks:
 # ---------------------------------------------------------------------------
 # CPU side: LMc's own sources (oracle/_ref), timed on this host's cores
 # ---------------------------------------------------------------------------
-def cpu_reference(path, n_decode, warmup=1):
-    """Greedy decode with LMc's model_forward on all host threads; returns
-    (tokens/s of the decode part, threads, sample description)."""
+def cpu_reference(path, n_decode, reps=CPU_REPS):
+    """Greedy decode with LMc's model_forward on all host threads: one
+    untimed warm-up run, then `reps` runs of the 8-token prompt and n_decode
+    decode tokens; returns the median decode and prompt-feed tokens/s."""
     from oracle import Ref
     ref = Ref()
     threads = os.cpu_count() or 1
     ref.set_threads(threads)
     ref.load(path)
     p = prompt_ids()
-    if warmup:
-        ref.generate(p, 2)
-    ids, tp, td = ref.generate(p, n_decode + 1)  # n_decode forwards after the prompt
-    rate = n_decode / td
-    return rate, threads, (f"LMc model_forward (oracle/_ref, make-omp flags, {os.path.basename(ref.path)}), "
-                           f"{N_PROMPT}-token prompt then {n_decode} greedy decode tokens, wall clock")
+    ref.generate(p, 2)
+    dec, feed = [], []
+    for _ in range(reps):
+        _, tp, td = ref.generate(p, n_decode + 1)  # n_decode forwards after the prompt
+        dec.append(n_decode / td)
+        feed.append(len(p) / tp)
+    sample = (f"LMc model_forward (oracle/_ref, make-omp flags, {os.path.basename(ref.path)}), "
+              f"{N_PROMPT}-token prompt then {n_decode} greedy decode tokens, median of {reps} runs after a warm-up, "
+              f"wall clock; prompt fed token by token (timed apart)")
+    return float(np.median(dec)), float(np.median(feed)), threads, sample
+
+
+def cpu_matmul_c1(reps=200):
+    """LMc's matmul_vec on the dequantized C1 weights (Q4_K 3072x768, the
+    same seeded blocks as the GPU measurement), all host threads: seconds per
+    call (median of 5 timings of `reps` calls)."""
+    from lmc_b200 import synth
+    from oracle import Ref
+    ref = Ref()
+    ref.set_threads(os.cpu_count() or 1)
+    M, K = 3072, 768
+    blk = synth.random_blocks(synth.Q4_K, M * K, seed=0)
+    w = ref.dequant(synth.Q4_K, blk, M * K).reshape(M, K)
+    x = np.random.default_rng(0).normal(0, 1, K).astype(np.float32)
+    ref.time_matmul(w, x, 20)
+    return float(np.median([ref.time_matmul(w, x, reps) / reps for _ in range(5)]))
 
 
 def run_reference(args, rank, world):
@@ -162,8 +216,7 @@ def run_reference(args, rank, world):
         return
     path = model_path(0, lambda: None)
     n_dec = max(args.steps, 8)
-    from oracle import Ref  # noqa: F401  (fails loudly if the reference build is missing)
-    rate, threads, sample = cpu_reference(path, n_dec, warmup=args.warmup)
+    rate, feed, threads, sample = cpu_reference(path, n_dec)
     line = {"metric": METRIC, "value": round(rate, 3), "unit": UNIT, "n_gpus": world, "steps": n_dec,
             "warmup": args.warmup, "ms_per_step": round(1000.0 / rate, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -171,16 +224,17 @@ def run_reference(args, rank, world):
             "config": {"workload": WORKLOAD, "parallelism": "replicas", "global_batch": 1,
                        "seq_len": 1024, "l2": "n/a (CPU)"},
             "cpu_baseline": {"value": round(rate, 3), "unit": UNIT, "cores": threads, "kind": "reference",
-                             "sample": sample},
+                             "sample": sample, "prompt_feed_tok_s": round(feed, 3)},
             "e2e": {"value": round(rate, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
-# GPU side
+# GPU side: GPT-2 Small decode (the headline)
 # ---------------------------------------------------------------------------
-def run_lmc(args, rank, world, local_rank, dist):
+def run_gpt2(args, rank, world, local_rank, dist):
     import torch
+    from lmc_b200 import microbench
     from lmc_b200 import runtime as rt
     from lmc_b200 import synth
 
@@ -191,10 +245,11 @@ def run_lmc(args, rank, world, local_rank, dist):
     m = rt.Model(path, max_batch=1)
     p = prompt_ids()
     K, W = args.steps, args.warmup
-    if N_PROMPT + W + K + 2 > m.cfg.seq_len:
+    if N_PROMPT + W + 2 * K + 2 > m.cfg.seq_len:
         raise SystemExit(f"steps + warmup exceed the context of {m.cfg.seq_len}")
-    # prefill + W warm-up decode steps; captures the step graph
+    # prompt + W warm-up decode steps; captures the step graph
     m.generate(p[None], max(W, 1), use_graph=True)
+    pos_start = N_PROMPT + max(W, 1) - 1  # position of the first timed step
     sh = m.replay(0)
     s = torch.cuda.ExternalStream(sh)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
@@ -217,52 +272,203 @@ def run_lmc(args, rank, world, local_rank, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
     value = world * K / (total_ms * 1e-3)
-    launches = m.graph_kernels() * K
+    kernels_per_step = m.graph_kernels()
+    launches = kernels_per_step * K
 
     # end to end: the per-token public call (model_forward drop-in) with the
-    # token/position copied from host memory and the greedy id read back
-    pos0 = N_PROMPT + W + K + 1
+    # token/position copied from host memory and the greedy id read back;
+    # L2 flushed before each call (outside the timed interval), like the
+    # device-timed loop
+    pos0 = pos_start + K + 1
     n_e2e = min(K, m.cfg.seq_len - pos0 - 1)
     tok = np.array([int(p[0])], np.int32)
-    torch.cuda.synchronize()
+    e2e_s = 0.0
     barrier()
-    t0 = time.perf_counter()
     for i in range(n_e2e):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
         _, nxt = m.forward(tok, np.array([pos0 + i], np.int32), want_logits=False)
+        e2e_s += time.perf_counter() - t0
         tok = nxt
-    e2e_s = time.perf_counter() - t0
     if dist:
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     e2e = world * n_e2e / e2e_s
 
-    from lmc_b200 import microbench
-    # the dominant kernel of the step: the largest GEMV (lm_head shape)
-    r = microbench.run(torch, synth.Q6_K, 50257, 768, 1, iters=60)
-    gbs, gemv_ms, alg, tiled = r["gbs"], r["ms"], r["bytes"], r["tiled"]
+    # C1: the single Q4_K 3072x768 GEMV (rotated copies > 2x L2)
+    c1 = microbench.run(torch, synth.Q4_K, 3072, 768, 1, iters=200, seed=0)
     peak, peak_kind = measured_peaks()
     cpu = None
+    ref_c1 = None
     if rank == 0:
-        rate, threads, sample = cpu_reference(path, 16, warmup=1)
-        cpu = {"value": round(rate, 3), "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample}
+        rate, feed, threads, sample = cpu_reference(path, 32)
+        cpu = {"value": round(rate, 3), "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample,
+               "prompt_feed_tok_s": round(feed, 3)}
+        ref_c1 = cpu_matmul_c1()
     if rank == 0:
+        # the dominant kernel: the persistent step kernel (one launch per
+        # token) when the step is one kernel, else the step as a whole
+        ctx_mean = pos_start + (K + 1) / 2.0
+        alg = gpt2_step_bytes(ctx_mean)
+        step_ms_avg = total_ms / K
+        gbs = alg / (step_ms_avg * 1e-3) / 1e9
+        kname = "k_step" if kernels_per_step == 1 else None
+        tr = step_traffic(kname) if kname else None
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
-                "warmup": W, "ms_per_step": round(total_ms / K, 4), "higher_is_better": True, "scaling": "weak",
+                "warmup": W, "ms_per_step": round(step_ms_avg, 4), "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": WORKLOAD, "l2": L2_NOTE, "parallelism": f"replicas x{world}",
                            "global_batch": world, "seq_len": 1024, "prompt": N_PROMPT},
                 "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
                 "gpu_launches": launches,
-                "roofline": {"bound": "hbm", "kernel": "gemv " + ("tiled tensor-core" if tiled else "generic") +
-                             " Q6_K 50257x768 (lm_head shape), rotated copies > 2x L2",
-                             "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                             "frac": round(gbs / peak, 4), "peak_kind": peak_kind + " (hbm_gbs, burst)",
-                             "traffic": LM_HEAD_DRAM_BYTES, "traffic_source": "profiles/gemv_q6k_50257x768.md",
-                             "algorithmic_bytes": alg, "avg_launch_ms": round(gemv_ms, 5)},
+                "roofline": {"bound": "hbm",
+                             "kernel": ("persistent decode step k_step (one launch per token)" if kname else
+                                        f"decode step ({kernels_per_step} launches)"),
+                             "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                             "peak_kind": peak_kind + " (hbm_gbs, burst)",
+                             "traffic": tr["bytes"] if tr else None,
+                             "traffic_source": tr["source"] if tr else None,
+                             "algorithmic_bytes": int(alg), "avg_launch_ms": round(step_ms_avg, 5)},
+                "gemv_c1": {"kernel": "tiled tensor-core GEMV Q4_K 3072x768, batch 1, rotated copies > 2x L2",
+                            "us": round(c1["ms"] * 1e3, 3), "gbs": round(c1["gbs"], 1),
+                            "frac": round(c1["gbs"] / peak, 4), "algorithmic_bytes": c1["bytes"],
+                            "reference_matmul_vec_us": round(ref_c1 * 1e6, 2) if ref_c1 else None},
                 "cpu_baseline": cpu,
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
+    m.close()
+
+
+# ---------------------------------------------------------------------------
+# other workloads
+# ---------------------------------------------------------------------------
+SWEEP_TYPES = ["Q4_0", "Q5_1", "Q8_0", "Q3_K", "Q5_K", "Q6_K", "IQ4_XS"]
+SWEEP_SHAPES = ["6400x1600", "1600x6400"]
+SWEEP_BATCHES = [1, 8, 64, 512]
+MODELS = {
+    # TinyLlama-1.1B architecture: 22 x 2048, FFN 5632, 32 / 4 heads, vocab 32000
+    "tinyllama": dict(kind="llama", L=22, D=2048, H=32, Hkv=4, F=5632, S=2048, V=32000),
+    # Llama-style 8B shape: 32 x 4096, FFN 14336, 32 / 8 heads, vocab 128256, ctx 4096
+    "llama8b": dict(kind="llama", L=32, D=4096, H=32, Hkv=8, F=14336, S=4096, V=128256),
+}
+
+
+def kernel_family(qtype, cols, batch):
+    from lmc_b200 import synth
+    tiled = qtype in (synth.Q4_K, synth.Q6_K, synth.Q8_0) and cols % 256 == 0
+    if batch > 8:
+        return "tcgen05 gemm (tiled fast path)" if tiled else "tcgen05 gemm (generic decoders)"
+    return "tensor-core gemv (tiled)" if tiled else "generic gemv"
+
+
+def run_gemv(args):
+    import torch
+    from lmc_b200 import microbench as mb
+    from lmc_b200 import runtime as rt
+    from lmc_b200 import synth
+    torch.cuda.set_device(0)
+    rt.init(0)
+    names = {v: k for k, v in synth.NAMES.items()}
+    peak, kind = measured_peaks()
+    cases = []
+    if args.workload == "sweep":
+        for tn in SWEEP_TYPES:
+            for shp in SWEEP_SHAPES:
+                for b in SWEEP_BATCHES:
+                    cases.append((tn, shp, b))
+    else:
+        cases.append((args.type, f"{args.rows}x{args.cols}", args.batch))
+    for tn, shp, b in cases:
+        t = names[tn]
+        rows, cols = (int(v) for v in shp.split("x"))
+        r = mb.run(torch, t, rows, cols, b, iters=max(args.steps, 20), seed=0)
+        fl = 2.0 * rows * cols * b / (r["ms"] * 1e-3) / 1e12
+        print(json.dumps({"metric": "GEMV/GEMM throughput", "workload": "gemv", "type": tn, "rows": rows,
+                          "cols": cols, "batch": b, "kernel": kernel_family(t, cols, b),
+                          "us": round(r["ms"] * 1e3, 3), "gbs": round(r["gbs"], 1),
+                          "hbm_frac": round(r["gbs"] / peak, 4), "tflops": round(fl, 2),
+                          "algorithmic_bytes": r["bytes"], "peak_kind": kind,
+                          "l2": "rotated weight copies > 2x L2, graph of back-to-back launches"}), flush=True)
+
+
+def run_model(args, rank, world, local_rank, dist):
+    """Prompt feed + greedy decode through lmc_model_generate (one graph
+    launch per step for the whole batch); with --tp every rank holds its
+    tensor-parallel shard and the times are the maximum over the ranks."""
+    import torch
+    from lmc_b200 import runtime as rt
+    from lmc_b200 import synth
+    kw = dict(MODELS[args.workload])
+    kind = kw.pop("kind")
+    kw["blocks"] = "random"
+    d = os.environ.get("LMC_BENCH_CACHE", "/tmp/lmc_bench_models")
+    torch.cuda.set_device(local_rank)
+    rt.init(local_rank)
+    path = synth.cached_model(kind, d, **kw) if rank == 0 else None
+    if dist:
+        obj = [path]
+        dist.broadcast_object_list(obj, src=0)
+        path = obj[0]
+    kvd = rt.KV_F16 if args.kv == "f16" else rt.KV_F32
+    B = args.batch
+    rows = args.prefill_rows or None
+    if dist and world > 1:
+        from lmc_b200 import tp as tpm
+        nid = tpm.exchange_id(dist, rt.nccl_unique_id)
+        m = rt.Model(path, max_batch=B, kv_dtype=kvd, tp=(rank, world, nid), max_rows=rows)
+    else:
+        m = rt.Model(path, max_batch=B, kv_dtype=kvd, max_rows=rows)
+    prompts = np.random.default_rng(0).integers(0, m.cfg.vocab_size, (B, args.prompt)).astype(np.int32)
+
+    def slowest(dt):
+        if dist:
+            t = torch.tensor([dt], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+        return dt
+
+    def timed(n_new):
+        m.generate(prompts, n_new)  # captures this shape's step graph
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        m.generate(prompts, n_new)
+        torch.cuda.synchronize()
+        return slowest(time.perf_counter() - t0)
+
+    t_prefill = None
+    if rows:
+        for _ in range(2):  # the first pass warms up
+            torch.cuda.synchronize()
+            if dist:
+                dist.barrier()
+            t0 = time.perf_counter()
+            for b in range(B):
+                m.prefill(b, prompts[b], 0, want_logits=False)
+            torch.cuda.synchronize()
+            t_prefill = slowest(time.perf_counter() - t0)
+    t_feed = timed(1)
+    t_all = timed(args.gen)
+    t_dec = max(t_all - t_feed, 1e-9)
+    if rank == 0:
+        wbytes = os.path.getsize(path)
+        dec = B * (args.gen - 1) / t_dec
+        step_s = t_dec / max(args.gen - 1, 1)
+        peak, kind_p = measured_peaks()
+        res = {"metric": METRIC, "workload": args.workload, "value": round(dec, 2), "unit": UNIT,
+               "n_gpus": world, "batch": B, "prompt": args.prompt, "gen": args.gen, "kv": args.kv,
+               "prompt_feed_tok_s": round(B * args.prompt / t_feed, 2),
+               "ms_per_step_decode": round(1e3 * step_s, 4),
+               "graph_kernels_per_step": m.graph_kernels(), "weights_bytes": wbytes,
+               "weights_hbm_frac_per_rank": round(wbytes / world / step_s / 1e9 / peak, 4),
+               "tensor_parallel": world, "data": "synthetic (random blocks of the named formats)",
+               "timing": "host clock around synchronised generate runs (second of two)", "peak_kind": kind_p}
+        if t_prefill:
+            res.update({"prefill_rows": rows, "prefill_tok_s": round(B * args.prompt / t_prefill, 2)})
+        print(json.dumps(res), flush=True)
     m.close()
 
 
@@ -272,6 +478,16 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["lmc", "reference"], default="lmc")
+    ap.add_argument("--workload", choices=["gpt2", "gemv", "sweep", "tinyllama", "llama8b"], default="gpt2")
+    ap.add_argument("--type", default="Q4_K")
+    ap.add_argument("--rows", type=int, default=3072)
+    ap.add_argument("--cols", type=int, default=768)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--gen", type=int, default=64)
+    ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
+    ap.add_argument("--prefill-rows", type=int, default=0)
+    ap.add_argument("--tp", action="store_true", help="tensor parallel over the torchrun ranks (llama8b)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -279,7 +495,17 @@ def main():
     rank = env_int("RANK", 0)
     local_rank = env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
-        run_reference(args, rank, world)
+        if args.workload == "gpt2":
+            run_reference(args, rank, world)
+        elif rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the gpt2 workload only"}))
+        return
+    if args.workload in ("gemv", "sweep") or (args.workload != "gpt2" and world > 1 and not args.tp):
+        if rank == 0:  # single-GPU workloads: rank 0 alone
+            if args.workload in ("gemv", "sweep"):
+                run_gemv(args)
+            else:
+                run_model(args, 0, 1, local_rank, None)
         return
     dist = None
     if world > 1:
@@ -291,7 +517,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_lmc(args, rank, world, local_rank, dist)
+        if args.workload == "gpt2":
+            run_gpt2(args, rank, world, local_rank, dist)
+        else:
+            run_model(args, rank, world, local_rank, dist if args.tp else None)
     finally:
         if dist:
             dist.destroy_process_group()

@@ -90,6 +90,8 @@ int lmc_qtensor_upload(uint32_t type, int rows, int cols, const void *h_blocks,
 int lmc_qtensor_free(lmc_qtensor *t);
 /* Device pointer to the raw GGUF block stream (read-only view). */
 const void *lmc_qtensor_blocks(const lmc_qtensor *t);
+/* Type and shape of a qtensor (any output pointer may be NULL). */
+int lmc_qtensor_shape(const lmc_qtensor *t, uint32_t *type, int *rows, int *cols);
 /* 1 when the tensor-core GEMV layout was built for this tensor. */
 int lmc_qtensor_has_tiled(const lmc_qtensor *t);
 
@@ -112,6 +114,21 @@ int lmc_matmul_blocks(uint32_t type, const void *d_blocks, int rows, int cols,
                       const float *d_x, int ldx, const float *d_bias, float *d_y,
                       int ldy, int batch, int epilogue, void *stream);
 
+/* ---- device buffers ------------------------------------------------------------
+ * Plain device memory for callers without CUDA headers (the ops.h drop-in
+ * layer keeps its scratch and KV-cache mirrors in these).  No counterpart in
+ * LMc, whose buffers are host arrays (src/models.c:122-164).  lmc_copy
+ * direction: LMC_H2D, LMC_D2H or LMC_D2D; it is ordered on `stream` and
+ * returns once the copy is enqueued (host memory must stay valid until
+ * lmc_stream_sync). */
+#define LMC_H2D 0
+#define LMC_D2H 1
+#define LMC_D2D 2
+int lmc_buffer_alloc(size_t bytes, void **d_out);
+int lmc_buffer_free(void *d);
+int lmc_copy(void *dst, const void *src, size_t bytes, int direction, void *stream);
+int lmc_stream_sync(void *stream);
+
 /* ---- small ops kept on the device --------------------------------------------
  * Each processes `rows` independent rows. */
 /* layer_norm (src/ops.c:47-59), eps fixed at 1e-5 as in LMc. */
@@ -132,6 +149,19 @@ int lmc_rope_apply(float *d_vec, const float *d_cos_row, const float *d_sin_row,
                    int head_dim, int n_heads, void *stream);
 /* Greedy pick (src/lmc.c:45-47): first index of the maximum of each row. */
 int lmc_argmax(const float *d_x, int n, int rows, int *d_idx, void *stream);
+/* Top-p (nucleus) sampling with temperature, sample_top_p (src/lmc.c:42-59),
+ * for `rows` rows of n logits (read only; LMc scales its logits in place):
+ * below temperature 1e-6 the greedy pick, else softmax(logits / temperature),
+ * the shortest run of the most probable tokens whose probability reaches
+ * top_p, and a draw r from the row's xorshift64 state d_rng[row]
+ * (src/lmc.c:31-33, advanced once per draw) picks the first token of that
+ * run, in descending order, whose running probability passes r.  Tokens of
+ * exactly equal probability are taken in index order (LMc leaves their order
+ * to qsort).  d_idx[row] receives the token. */
+int lmc_sample_top_p(const float *d_logits, int n, int rows, float temperature, float top_p,
+                     unsigned long long *d_rng, int *d_idx, void *stream);
+/* The xorshift64 state LMc's rng_seed makes from a seed (src/lmc.c:30-31). */
+unsigned long long lmc_rng_seed(unsigned long long seed);
 
 /* ---- K4: attention over the head-major KV cache -------------------------------
  * Replaces the cache write and per-head read of attention_forward
@@ -162,9 +192,11 @@ int lmc_attention_decode(float *d_out, const float *d_q, const float *d_k_new,
  * library until exit); shapes whose lmc_attention_workspace_bytes exceed it
  * are rejected with LMC_ERR_INVALID.  The first call on each device looks up
  * the array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture.  The call allocates nothing.  All calls on a
- * device share the one array, which keeps the last call's contents: calls
- * that may overlap on the GPU (different streams without ordering) race. */
+ * before any stream capture; the address is kept for the life of the
+ * process, so cudaDeviceReset after that first call is not supported.  The
+ * call allocates nothing.  All calls on a device share the one array, which
+ * keeps the last call's contents: calls that may overlap on the GPU
+ * (different streams without ordering) race. */
 int lmc_attention_decode_noalloc(float *d_out, const float *d_q, const float *d_k_new,
                                  const float *d_v_new, void *d_k_cache, void *d_v_cache,
                                  int kv_dtype, const int *d_pos, int batch, int H, int Hkv,
@@ -235,6 +267,16 @@ int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int sta
  * starts the step loop at the last prompt position: the same ids. */
 int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int batch,
                        int n_new, int use_graph, int *h_out_ids);
+/* lmc_model_generate with LMc's top-p sampling (src/lmc.c:42-59,123)
+ * instead of the greedy pick: each generated token is drawn on the device by
+ * lmc_sample_top_p from the step's logits (temperature below 1e-6: greedy).
+ * Sequence b draws from its own xorshift64 stream, seeded as LMc seeds its
+ * one stream (src/lmc.c:30-31) with seed + b, so sequence 0 with `seed`
+ * follows LMc's stream; the prompt steps draw nothing.  Needs the whole
+ * vocabulary on this GPU (not a tensor-parallel shard). */
+int lmc_model_generate_sample(lmc_model *m, const int *h_prompt, int n_prompt, int batch, int n_new,
+                              float temperature, float top_p, unsigned long long seed, int use_graph,
+                              int *h_out_ids);
 /* Runs `n` more steps of the last lmc_model_generate (replaying its CUDA
  * graph, or launching the kernels directly when it ran without one),
  * continuing from the current device-side positions (a timing helper:
@@ -246,6 +288,38 @@ int lmc_model_graph_kernels(const lmc_model *m);
 /* Device-side buffers of the model, for callers that drive steps themselves:
  * which = 0 logits [max_batch][V] fp32. */
 void *lmc_model_device_buffer(lmc_model *m, int which);
+/* The model's weights on the device, by LMc's names (LayerWeights and
+ * ModelWeights, src/models.h:79-150), for callers that run single ops on them
+ * (the ops.h drop-in layer, include/lmc_ops.h, resolves LMc's weight
+ * pointers through these).  No counterpart in LMc, whose weights are fp32
+ * host arrays.  Matrices are qtensors; vectors are device fp32 arrays of
+ * *len floats.  `layer` is ignored for the whole-model tensors.  NULL when
+ * the model has no such tensor (the other architecture's, or out of range). */
+#define LMC_W_TOKEN_EMBD 0  /* wte            [V][D]    */
+#define LMC_W_OUTPUT     1  /* lm_head        [V][D]    */
+#define LMC_W_QKV        2  /* GPT-2 qkv      [3D][D]   */
+#define LMC_W_ATTN_OUT   3  /* attn_proj / o  [D][H Dh] */
+#define LMC_W_FFN_UP     4  /* GPT-2 fc / LLaMA up [F][D] */
+#define LMC_W_FFN_DOWN   5  /* fc2 / down     [D][F]    */
+#define LMC_W_Q          6  /* LLaMA q        [H Dh][D] */
+#define LMC_W_K          7  /* LLaMA k        [Hkv Dh][D] */
+#define LMC_W_V          8  /* LLaMA v        [Hkv Dh][D] */
+#define LMC_W_GATE       9  /* LLaMA gate     [F][D]    */
+const lmc_qtensor *lmc_model_matrix(const lmc_model *m, int layer, int which);
+#define LMC_V_POS_EMBD      0  /* GPT-2 wpe [S][D] */
+#define LMC_V_OUTPUT_NORM   1  /* ln_f weight / rms_f weight */
+#define LMC_V_OUTPUT_NORM_B 2  /* ln_f bias */
+#define LMC_V_ATTN_NORM     3  /* ln1 weight / rms_attn weight */
+#define LMC_V_ATTN_NORM_B   4  /* ln1 bias */
+#define LMC_V_FFN_NORM      5  /* ln2 weight / rms_ffn weight */
+#define LMC_V_FFN_NORM_B    6  /* ln2 bias */
+#define LMC_V_QKV_B         7
+#define LMC_V_ATTN_OUT_B    8
+#define LMC_V_FFN_UP_B      9
+#define LMC_V_FFN_DOWN_B   10
+#define LMC_V_ROPE_COS     11  /* LLaMA [S][Dh/2] (src/models.c:101-117) */
+#define LMC_V_ROPE_SIN     12
+const float *lmc_model_vector(const lmc_model *m, int layer, int which, int *len);
 
 #ifdef __cplusplus
 }

@@ -168,6 +168,41 @@ extern "C" int lmc_qtensor_free(lmc_qtensor *t) {
 }
 
 extern "C" const void *lmc_qtensor_blocks(const lmc_qtensor *t) { return t ? t->blocks : NULL; }
+extern "C" int lmc_qtensor_shape(const lmc_qtensor *t, uint32_t *type, int *rows, int *cols) {
+    if (!t) return lmc_set_error(LMC_ERR_INVALID, "qtensor_shape: null");
+    if (type) *type = t->type;
+    if (rows) *rows = t->rows;
+    if (cols) *cols = t->cols;
+    return LMC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// device buffers for callers without CUDA headers
+// ---------------------------------------------------------------------------
+extern "C" int lmc_buffer_alloc(size_t bytes, void **d_out) {
+    if (!d_out) return lmc_set_error(LMC_ERR_INVALID, "buffer_alloc: null");
+    *d_out = NULL;
+    cudaError_t e = cudaMalloc(d_out, bytes ? bytes : 16);
+    if (e != cudaSuccess) return lmc_set_error(LMC_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    return LMC_OK;
+}
+extern "C" int lmc_buffer_free(void *d) {
+    if (d) LMC_CUDA_TRY(cudaFree(d));
+    return LMC_OK;
+}
+extern "C" int lmc_copy(void *dst, const void *src, size_t bytes, int dir, void *stream) {
+    if ((!dst || !src) && bytes) return lmc_set_error(LMC_ERR_INVALID, "copy: null pointer");
+    if (dir < LMC_H2D || dir > LMC_D2D) return lmc_set_error(LMC_ERR_INVALID, "copy: direction %d", dir);
+    if (!bytes) return LMC_OK;
+    const cudaMemcpyKind k = dir == LMC_H2D ? cudaMemcpyHostToDevice
+                             : dir == LMC_D2H ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+    LMC_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, k, lmc_stream(stream)));
+    return LMC_OK;
+}
+extern "C" int lmc_stream_sync(void *stream) {
+    LMC_CUDA_TRY(cudaStreamSynchronize(lmc_stream(stream)));
+    return LMC_OK;
+}
 extern "C" int lmc_qtensor_has_tiled(const lmc_qtensor *t) { return t && t->tiled ? 1 : 0; }
 
 // ---------------------------------------------------------------------------

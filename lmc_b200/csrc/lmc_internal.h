@@ -97,9 +97,80 @@ int lmc_attention_rows_launch(float *out, int ldo, const float *q, int ldq, cons
                               int batch, int H, int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes,
                               const float *rope_cos, const float *rope_sin, int *d_cnt, cudaStream_t s);
 /* Generation bookkeeping after one step (see lmc_model_generate): the greedy
- * id of each sequence is read from (and reset in) d_keys. */
+ * id of each sequence is read from (and reset in) d_keys, or, with
+ * from_next, the pick is the one already in d_next (a sampler wrote it; the
+ * keys are still reset). */
 int lmc_advance_launch(unsigned long long *d_keys, int *d_next, int *d_tok, int *d_pos, int *d_step,
-                       const int *d_prompt, int n_prompt, int *d_ids, int n_new, int batch, cudaStream_t s);
+                       const int *d_prompt, int n_prompt, int *d_ids, int n_new, int batch, int from_next,
+                       cudaStream_t s);
+/* lmc_sample_top_p on rows of ld floats (ld must equal n) on stream s; with
+ * d_step, only in steps whose pick is a generated token (step + 1 >= n_prompt). */
+int lmc_sample_launch(const float *d_logits, int n, int ld, int rows, float temperature, float top_p,
+                      unsigned long long *d_rng, int *d_idx, const int *d_step, int n_prompt, cudaStream_t s);
+/* Split plan of the decode attention (attention.cu): positions per split
+ * and split count for context S and bh = batch x heads; fine = the splits
+ * are merged inside the launch (arrival counters). */
+void lmc_attn_plan(int S, int bh, int fine, int *CH, int *nsplit);
+
+/* ---- persistent decode step (step_kernel.cu) -------------------------------
+ * A whole decode step as ONE cooperative launch: every CTA walks the same list
+ * of ops (embedding, tensor-core GEMVs with their prologue/epilogue, attention,
+ * greedy bookkeeping) and the CTAs meet at a grid-wide barrier (a counter in
+ * device memory, bounded wait) after each op instead of at a kernel boundary.
+ * While a CTA waits, the weights of its share of the next GEMV are already
+ * being copied into its shared memory. */
+#define LMC_OP_EMBED 1   /* x[b] = wte[tok[b]] (+ wpe[pos[b]])                     */
+#define LMC_OP_GEMV 2    /* tiled qtensor, batch <= 2, prologue + epilogue of ex      */
+#define LMC_OP_ATTN 3    /* decode attention, K/V append, optional RoPE, merge      */
+#define LMC_OP_KEYS 4    /* next[b] = greedy key index, keys reset (model_forward)  */
+#define LMC_OP_ADVANCE 5 /* the generate() bookkeeping of lmc_advance_launch         */
+#define LMC_OP_SAMPLE 6  /* top-p draw per row into next (lmc_sample_launch)      */
+typedef struct {
+    int kind, batch;
+    /* GEMV */
+    const struct lmc_qtensor *w;
+    const float *x, *bias;
+    float *y;
+    int ldx, ldy, epi;
+    lmc_gemv_extra ex;
+    /* ATTN */
+    float *out;
+    const float *q, *k_new, *v_new;
+    int ldo, ldq, ldkv;
+    void *k_cache, *v_cache;
+    int kv_dtype, H, Hkv, Dh, S;
+    const float *rope_cos, *rope_sin;
+    void *ws;
+    size_t ws_bytes;
+    int *cnt;
+    /* EMBED (tok, pos), ATTN (pos), KEYS / ADVANCE */
+    uint32_t wte_type;
+    const void *wte;
+    const float *wpe;
+    int D, V;
+    int *tok, *pos;
+    unsigned long long *keys;
+    int *next, *step, *ids;
+    const int *prompt;
+    int n_prompt, n_new;
+    /* SAMPLE (logits in y, V, rng, next, step, n_prompt); ADVANCE: from_next */
+    float temperature, top_p;
+    unsigned long long *rng;
+    int from_next;
+} lmc_step_op;
+typedef struct lmc_step_prog lmc_step_prog;
+/* LMC_ERR_UNSUPPORTED when an op cannot run inside the persistent kernel
+ * (the caller then launches the step kernel by kernel). */
+int lmc_step_prog_build(const lmc_step_op *ops, int n, lmc_step_prog **out);
+int lmc_step_prog_launch(const lmc_step_prog *p, cudaStream_t s);
+void lmc_step_prog_free(lmc_step_prog *p);
+/* LMC_OK, or LMC_ERR_TIMEOUT once after a persistent step gave up a bounded
+ * wait (its barrier state is then reset for the next launch). */
+int lmc_step_status(void);
+/* Wait limit of the bounded device waits of the GEMV rings and of the
+ * persistent step's barriers (nanoseconds; 0 restores the default). */
+int lmc_tiled_set_wait_limit(long long ns);
+int lmc_step_set_wait_limit(long long ns);
 
 #ifdef __cplusplus
 }

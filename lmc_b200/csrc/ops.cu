@@ -306,12 +306,12 @@ extern "C" int lmc_keys_to_ids_launch(unsigned long long *d_keys, int *d_next, i
 // pick is read from the step's argmax key, which is reset for the next step.
 __global__ void k_advance(unsigned long long *__restrict__ keys, int *__restrict__ next, int *__restrict__ tok,
                           int *__restrict__ pos, int *__restrict__ step_p, const int *__restrict__ prompt, int n_prompt,
-                          int *__restrict__ ids, int n_new, int batch) {
+                          int *__restrict__ ids, int n_new, int batch, int from_next) {
     pdl_wait();
     pdl_launch_dependents();
     const int step = *step_p;
     for (int b = threadIdx.x; b < batch; b += blockDim.x) {
-        const int nx = lmc_key_index(keys[b]);
+        const int nx = from_next ? next[b] : lmc_key_index(keys[b]);
         keys[b] = 0ull;
         next[b] = nx;
         if (step + 1 < n_prompt) {
@@ -328,9 +328,9 @@ __global__ void k_advance(unsigned long long *__restrict__ keys, int *__restrict
 }
 
 extern "C" int lmc_advance_launch(unsigned long long *d_keys, int *d_next, int *d_tok, int *d_pos, int *d_step,
-                                  const int *d_prompt, int n_prompt, int *d_ids, int n_new, int batch,
+                                  const int *d_prompt, int n_prompt, int *d_ids, int n_new, int batch, int from_next,
                                   cudaStream_t s) {
     LMC_LAUNCH("advance", k_advance, 1, 256, 0, s, d_keys, d_next, d_tok, d_pos, d_step, d_prompt, n_prompt, d_ids,
-               n_new, batch);
+               n_new, batch, from_next);
     return LMC_OK;
 }

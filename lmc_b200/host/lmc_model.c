@@ -62,6 +62,22 @@ struct lmc_model {
      * its heads, and lm_head rows [v0, v0 + vl). */
     int tp_rank, tp_size, hl, hkvl, fl, vl, v0;
     ncclComm_t comm;
+    /* the step as one persistent launch (lmc_step_prog), built on first use:
+     * per batch size for lmc_model_forward, and one for the generate loop
+     * (with the arguments it was built for); no_persist: it cannot be built */
+    lmc_step_prog *pfwd[3], *pgen;
+    int no_persist[3], gen_persist_failed;
+    int pg_batch, pg_nprompt, pg_nnew, pg_smp;
+    float pg_t, pg_p;
+    /* top-p sampling in the generate loop (lmc_model_generate_sample):
+     * smp = 1 while such a loop runs; one xorshift64 state per sequence */
+    int smp;
+    float smp_t, smp_p;
+    unsigned long long *d_rng;
+    int g_smp;
+    float g_t, g_p;
+    const int *pg_prompt;
+    const int *pg_ids;
 };
 
 #define TRY(expr)                     \
@@ -436,6 +452,7 @@ static int alloc_state(lmc_model *m) {
     TRY(dev_alloc((void **)&m->d_seq, 4 * B));
     TRY(dev_alloc((void **)&m->d_next, 4 * B));
     TRY(dev_alloc((void **)&m->d_step, 16));
+    TRY(dev_alloc((void **)&m->d_rng, 8 * B));
     CUTRY(cudaMallocHost((void **)&m->h_stage, 3 * sizeof(int) * B));
     CUTRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     if (B > 8) { /* the batched GEMM's activation workspace, sized before any graph capture */
@@ -522,6 +539,8 @@ void *lmc_model_device_buffer(lmc_model *m, int which) { return m && which == 0 
 int lmc_model_free(lmc_model *m) {
     if (!m) return LMC_OK;
     if (m->gexec) cudaGraphExecDestroy(m->gexec); /* (it may hold the communicator's calls) */
+    for (int b = 0; b < 3; b++) lmc_step_prog_free(m->pfwd[b]);
+    lmc_step_prog_free(m->pgen);
     if (m->comm) ncclCommDestroy(m->comm);
     if (m->layers) {
         for (int l = 0; l < m->cfg.n_layers; l++) {
@@ -538,7 +557,7 @@ int lmc_model_free(lmc_model *m) {
     lmc_qtensor_free(m->lm_head);
     void *ps[] = {m->wpe, m->lnf_w, m->lnf_b, m->rmsf, m->rope_cos, m->rope_sin, m->kc, m->vc, m->x, m->xn, m->qkv,
                   m->att, m->h, m->h2, m->logits, m->ws, m->d_tok, m->d_pos, m->d_next, m->d_step, m->d_prompt, m->d_ids,
-                  m->d_keys, m->d_attn_cnt, m->d_seq};
+                  m->d_keys, m->d_attn_cnt, m->d_seq, m->d_rng};
     for (size_t i = 0; i < sizeof ps / sizeof ps[0]; i++) if (ps[i]) cudaFree(ps[i]);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -670,6 +689,164 @@ static int step(lmc_model *m, int B) {
     return LMC_OK;
 }
 
+/* ------------------------------------------------------------------------ */
+/* The same step as one persistent launch (step_kernel.cu)                    */
+/* ------------------------------------------------------------------------ */
+static int persist_enabled(void) {
+    /* LMC_PERSISTENT=0: launch the step kernel by kernel (same results) */
+    const char *e = getenv("LMC_PERSISTENT");
+    return !(e && e[0] == '0');
+}
+
+static lmc_step_op *add_op(lmc_step_op *ops, int *n, int kind, int B) {
+    lmc_step_op *o = &ops[(*n)++];
+    memset(o, 0, sizeof *o);
+    o->kind = kind;
+    o->batch = B;
+    return o;
+}
+static void add_gemv(lmc_step_op *ops, int *n, int B, const lmc_qtensor *w, const float *x, int ldx, const float *bias,
+                     float *y, int ldy, int epi, int pro, const float *nw, const float *nb, float eps,
+                     const float *x2) {
+    lmc_step_op *o = add_op(ops, n, LMC_OP_GEMV, B);
+    o->w = w;
+    o->x = x;
+    o->ldx = ldx;
+    o->bias = bias;
+    o->y = y;
+    o->ldy = ldy;
+    o->epi = epi;
+    o->ex.pro = pro;
+    o->ex.w = nw;
+    o->ex.b = nb;
+    o->ex.eps = eps;
+    o->ex.x2 = x2;
+}
+static void add_attn(lmc_step_op *ops, int *n, lmc_model *m, int B, float *out, int ldo, const float *q, int ldq,
+                     const float *k, const float *v, int ldkv, void *kc, void *vc, int H, int Hkv, const float *rc,
+                     const float *rs) {
+    const lmc_model_config *c = &m->cfg;
+    lmc_step_op *o = add_op(ops, n, LMC_OP_ATTN, B);
+    o->out = out;
+    o->ldo = ldo;
+    o->q = q;
+    o->ldq = ldq;
+    o->k_new = k;
+    o->v_new = v;
+    o->ldkv = ldkv;
+    o->k_cache = kc;
+    o->v_cache = vc;
+    o->kv_dtype = m->kv_dtype;
+    o->H = H;
+    o->Hkv = Hkv;
+    o->Dh = c->head_dim;
+    o->S = c->seq_len;
+    o->rope_cos = rc;
+    o->rope_sin = rs;
+    o->ws = m->ws;
+    o->ws_bytes = m->ws_bytes;
+    o->cnt = m->d_attn_cnt;
+    o->pos = m->d_pos;
+}
+
+/* step() (and the greedy pick, or with gen the generate bookkeeping) as a
+ * persistent program: the whole model on one GPU, batch <= 2, every
+ * projection on the tiled layout; else LMC_ERR_UNSUPPORTED. */
+static int build_prog(lmc_model *m, int B, int gen, int n_prompt, int n_new, lmc_step_prog **out) {
+    const lmc_model_config *c = &m->cfg;
+    *out = NULL;
+    if (!persist_enabled() || m->tp_size > 1 || B > 2 || !m->d_attn_cnt)
+        return lmc_set_error(LMC_ERR_UNSUPPORTED, "persistent step: not for this model or batch");
+    const int D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size, H = c->n_heads, Dh = c->head_dim;
+    const size_t esz = m->kv_dtype == LMC_KV_F16 ? 2 : 4;
+    lmc_step_op *ops = (lmc_step_op *)calloc((size_t)(5 * c->n_layers + 5), sizeof(lmc_step_op));
+    if (!ops) return lmc_set_error(LMC_ERR_OOM, "persistent step: host");
+    int n = 0, rc = LMC_OK;
+    lmc_step_op *e = add_op(ops, &n, LMC_OP_EMBED, B);
+    e->wte_type = m->wte->type;
+    e->wte = m->wte->blocks;
+    e->wpe = c->arch == 1 ? m->wpe : NULL;
+    e->D = D;
+    e->V = V;
+    e->S = c->seq_len;
+    e->tok = m->d_tok;
+    e->pos = m->d_pos;
+    e->y = m->x;
+    for (int l = 0; l < c->n_layers && !rc; l++) {
+        const Layer *w = &m->layers[l];
+        char *kc = (char *)m->kc + esz * m->kv_layer_elems * l, *vc = (char *)m->vc + esz * m->kv_layer_elems * l;
+        if (c->arch == 1) { /* src/ops.c:182-206 */
+            add_gemv(ops, &n, B, w->qkv, m->x, D, w->qkv_b, m->qkv, 3 * D, LMC_EPI_NONE, LMC_PRO_LAYERNORM, w->ln1_w,
+                     w->ln1_b, 1e-5f, NULL);
+            add_attn(ops, &n, m, B, m->att, D, m->qkv, 3 * D, m->qkv + D, m->qkv + 2 * D, 3 * D, kc, vc, H, H, NULL,
+                     NULL);
+            add_gemv(ops, &n, B, w->proj, m->att, D, w->proj_b, m->x, D, LMC_EPI_ACCUM, LMC_PRO_NONE, NULL, NULL, 0.0f,
+                     NULL);
+            add_gemv(ops, &n, B, w->fc, m->x, D, w->fc_b, m->h, F, LMC_EPI_GELU, LMC_PRO_LAYERNORM, w->ln2_w, w->ln2_b,
+                     1e-5f, NULL);
+            add_gemv(ops, &n, B, w->fc2, m->h, F, w->fc2_b, m->x, D, LMC_EPI_ACCUM, LMC_PRO_NONE, NULL, NULL, 0.0f,
+                     NULL);
+        } else { /* src/ops_llama.c:165-187 */
+            if (!w->qkv_cat || !w->gateup_cat) {
+                rc = lmc_set_error(LMC_ERR_UNSUPPORTED, "persistent step: q/k/v or gate/up not fused");
+                break;
+            }
+            const int QD = H * Dh, KVD = c->n_kv_heads * Dh, LQ = QD + 2 * KVD;
+            add_gemv(ops, &n, B, w->qkv_cat, m->x, D, NULL, m->qkv, LQ, LMC_EPI_NONE, LMC_PRO_RMSNORM, w->rms_attn,
+                     NULL, c->norm_eps, NULL);
+            add_attn(ops, &n, m, B, m->att, QD, m->qkv, LQ, m->qkv + QD, m->qkv + QD + KVD, LQ, kc, vc, H,
+                     c->n_kv_heads, m->rope_cos, m->rope_sin);
+            add_gemv(ops, &n, B, w->o, m->att, QD, NULL, m->x, D, LMC_EPI_ACCUM, LMC_PRO_NONE, NULL, NULL, 0.0f, NULL);
+            add_gemv(ops, &n, B, w->gateup_cat, m->x, D, NULL, m->h, 2 * F, LMC_EPI_NONE, LMC_PRO_RMSNORM, w->rms_ffn,
+                     NULL, c->norm_eps, NULL);
+            add_gemv(ops, &n, B, w->down, m->h, 2 * F, NULL, m->x, D, LMC_EPI_ACCUM, LMC_PRO_SWIGLU, NULL, NULL, 0.0f,
+                     m->h + F);
+        }
+    }
+    if (!rc) {
+        if (c->arch == 1)
+            add_gemv(ops, &n, B, m->lm_head, m->x, D, NULL, m->logits, V, LMC_EPI_NONE, LMC_PRO_LAYERNORM, m->lnf_w,
+                     m->lnf_b, 1e-5f, NULL);
+        else
+            add_gemv(ops, &n, B, m->lm_head, m->x, D, NULL, m->logits, m->vl, LMC_EPI_NONE, LMC_PRO_RMSNORM, m->rmsf,
+                     NULL, c->norm_eps, NULL);
+        ops[n - 1].ex.keys = m->d_keys;
+        ops[n - 1].ex.key_base = m->v0;
+        if (gen && m->smp) { /* the top-p draw replaces the greedy pick */
+            lmc_step_op *sp = add_op(ops, &n, LMC_OP_SAMPLE, B);
+            sp->y = m->logits;
+            sp->V = V;
+            sp->temperature = m->smp_t;
+            sp->top_p = m->smp_p;
+            sp->rng = m->d_rng;
+            sp->next = m->d_next;
+            sp->step = m->d_step;
+            sp->n_prompt = n_prompt;
+        }
+        lmc_step_op *k = add_op(ops, &n, gen ? LMC_OP_ADVANCE : LMC_OP_KEYS, B);
+        k->from_next = gen && m->smp;
+        k->keys = m->d_keys;
+        k->next = m->d_next;
+        k->tok = m->d_tok;
+        k->pos = m->d_pos;
+        k->step = m->d_step;
+        k->prompt = m->d_prompt;
+        k->ids = m->d_ids;
+        k->n_prompt = n_prompt;
+        k->n_new = n_new;
+        rc = lmc_step_prog_build(ops, n, out);
+    }
+    free(ops);
+    return rc;
+}
+
+/* The forward program for batch B, built on first use (NULL: not possible) */
+static lmc_step_prog *fwd_prog(lmc_model *m, int B) {
+    if (B > 2 || m->no_persist[B]) return NULL;
+    if (!m->pfwd[B] && build_prog(m, B, 0, 0, 0, &m->pfwd[B]) != LMC_OK) m->no_persist[B] = 1;
+    return m->pfwd[B];
+}
+
 int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B, float *h_logits, int *h_next) {
     if (!m || !h_tokens || !h_pos || B <= 0 || B > m->max_batch)
         return lmc_set_error(LMC_ERR_INVALID, "model_forward: args (batch %d, max %d)", B, m ? m->max_batch : 0);
@@ -683,8 +860,13 @@ int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B
     memcpy(m->h_stage + B, h_pos, sizeof(int) * B);
     CUTRY(cudaMemcpyAsync(m->d_tok, m->h_stage, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
     CUTRY(cudaMemcpyAsync(m->d_pos, m->h_stage + B, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
-    TRY(step(m, B));
-    TRY(lmc_keys_to_ids_launch(m->d_keys, m->d_next, B, m->stream));
+    lmc_step_prog *p = fwd_prog(m, B);
+    if (p) {
+        TRY(lmc_step_prog_launch(p, m->stream));
+    } else {
+        TRY(step(m, B));
+        TRY(lmc_keys_to_ids_launch(m->d_keys, m->d_next, B, m->stream));
+    }
     if (h_logits) /* [B][vocab rows of this rank] (the whole vocabulary without sharding) */
         CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * (size_t)B * m->vl, cudaMemcpyDeviceToHost,
                               m->stream));
@@ -741,9 +923,13 @@ int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int sta
 
 /* step + bookkeeping, the unit that is captured as one graph */
 static int gen_step(lmc_model *m, int B, int n_prompt, int n_new) {
+    if (m->pgen) return lmc_step_prog_launch(m->pgen, m->stream);
     TRY(step(m, B));
+    if (m->smp)
+        TRY(lmc_sample_launch(m->logits, m->cfg.vocab_size, m->vl, B, m->smp_t, m->smp_p, m->d_rng, m->d_next,
+                              m->d_step, n_prompt, m->stream));
     return lmc_advance_launch(m->d_keys, m->d_next, m->d_tok, m->d_pos, m->d_step, m->d_prompt, n_prompt, m->d_ids, n_new, B,
-                              m->stream);
+                              m->smp, m->stream);
 }
 
 static int ensure_gen_buffers(lmc_model *m, int B, int n_prompt, int n_new) {
@@ -764,8 +950,40 @@ static int ensure_gen_buffers(lmc_model *m, int B, int n_prompt, int n_new) {
     return LMC_OK;
 }
 
+static int generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, int n_new, int use_graph,
+                    int *h_out_ids);
+
 int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, int n_new, int use_graph,
                        int *h_out_ids) {
+    if (m) m->smp = 0;
+    return generate(m, h_prompt, n_prompt, B, n_new, use_graph, h_out_ids);
+}
+
+int lmc_model_generate_sample(lmc_model *m, const int *h_prompt, int n_prompt, int B, int n_new, float temperature,
+                              float top_p, unsigned long long seed, int use_graph, int *h_out_ids) {
+    if (!m || B <= 0 || B > m->max_batch) return lmc_set_error(LMC_ERR_INVALID, "model_generate_sample: args");
+    if (temperature != temperature || top_p != top_p)
+        return lmc_set_error(LMC_ERR_INVALID, "model_generate_sample: NaN temperature or top_p");
+    if (m->tp_size > 1)
+        return lmc_set_error(LMC_ERR_UNSUPPORTED, "model_generate_sample: the vocabulary is sharded across ranks");
+    /* sequence b draws from its own stream, seeded as LMc seeds its one
+     * stream (src/lmc.c:30-31) with seed + b */
+    unsigned long long *st = (unsigned long long *)malloc(sizeof(unsigned long long) * (size_t)B);
+    if (!st) return lmc_set_error(LMC_ERR_OOM, "model_generate_sample: host");
+    for (int b = 0; b < B; b++) st[b] = lmc_rng_seed(seed + (unsigned long long)b);
+    cudaError_t e = cudaMemcpy(m->d_rng, st, sizeof(unsigned long long) * (size_t)B, cudaMemcpyHostToDevice);
+    free(st);
+    if (e != cudaSuccess) return lmc_set_error(LMC_ERR_CUDA, "model_generate_sample: %s", cudaGetErrorString(e));
+    m->smp = 1;
+    m->smp_t = temperature;
+    m->smp_p = top_p;
+    const int rc = generate(m, h_prompt, n_prompt, B, n_new, use_graph, h_out_ids);
+    m->smp = 0;
+    return rc;
+}
+
+static int generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, int n_new, int use_graph,
+                    int *h_out_ids) {
     if (!m || !h_prompt || n_prompt <= 0 || n_new <= 0 || B <= 0 || B > m->max_batch || !h_out_ids)
         return lmc_set_error(LMC_ERR_INVALID, "model_generate: args");
     if (n_prompt + n_new - 1 > m->cfg.seq_len)
@@ -793,8 +1011,28 @@ int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, i
     m->h_stage[2 * B] = p0;
     CUTRY(cudaMemcpyAsync(m->d_step, m->h_stage + 2 * B, sizeof(int), cudaMemcpyHostToDevice, s));
     const int steps = n_prompt + n_new - 1 - p0;
+    /* the persistent program of this loop (its advance op holds the prompt
+     * and id buffers and the loop's shape) */
+    if (m->pgen && (m->pg_batch != B || m->pg_nprompt != n_prompt || m->pg_nnew != n_new ||
+                    m->pg_prompt != m->d_prompt || m->pg_ids != m->d_ids || m->pg_smp != m->smp ||
+                    (m->smp && (m->pg_t != m->smp_t || m->pg_p != m->smp_p)))) {
+        if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = NULL; }
+        lmc_step_prog_free(m->pgen);
+        m->pgen = NULL;
+    }
+    if (!m->pgen && B <= 2 && !m->gen_persist_failed) {
+        if (build_prog(m, B, 1, n_prompt, n_new, &m->pgen) == LMC_OK) {
+            m->pg_batch = B; m->pg_nprompt = n_prompt; m->pg_nnew = n_new;
+            m->pg_prompt = m->d_prompt; m->pg_ids = m->d_ids;
+            m->pg_smp = m->smp; m->pg_t = m->smp_t; m->pg_p = m->smp_p;
+            if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = NULL; }
+        } else {
+            m->gen_persist_failed = 1;
+        }
+    }
     if (use_graph) {
-        if (m->gexec && (m->g_batch != B || m->g_nprompt != n_prompt || m->g_nnew != n_new)) {
+        if (m->gexec && (m->g_batch != B || m->g_nprompt != n_prompt || m->g_nnew != n_new || m->g_smp != m->smp ||
+                         (m->smp && (m->g_t != m->smp_t || m->g_p != m->smp_p)))) {
             cudaGraphExecDestroy(m->gexec);
             m->gexec = NULL;
         }
@@ -821,11 +1059,13 @@ int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, i
             cudaGraphDestroy(g);
             if (e != cudaSuccess) return lmc_set_error(LMC_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
             m->g_batch = B; m->g_nprompt = n_prompt; m->g_nnew = n_new;
+            m->g_smp = m->smp; m->g_t = m->smp_t; m->g_p = m->smp_p;
         }
         for (int i = 0; i < steps; i++) CUTRY(cudaGraphLaunch(m->gexec, s));
     } else {
         if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = NULL; }
         m->g_batch = B; m->g_nprompt = n_prompt; m->g_nnew = n_new;
+        m->g_smp = m->smp; m->g_t = m->smp_t; m->g_p = m->smp_p;
         for (int i = 0; i < steps; i++) TRY(gen_step(m, B, n_prompt, n_new));
     }
     /* the last greedy pick needs no forward of its own: take it from the
@@ -840,12 +1080,73 @@ int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, i
  * steps continue from the current device-side position. */
 int lmc_model_replay(lmc_model *m, int n, void *stream_out) {
     if (!m || !m->g_batch) return lmc_set_error(LMC_ERR_INVALID, "model_replay: no generation to continue");
-    for (int i = 0; i < n; i++) {
-        if (m->gexec) CUTRY(cudaGraphLaunch(m->gexec, m->stream));
-        else TRY(gen_step(m, m->g_batch, m->g_nprompt, m->g_nnew));
+    m->smp = m->g_smp; /* the last generation's pick: greedy or its top-p draw */
+    m->smp_t = m->g_t;
+    m->smp_p = m->g_p;
+    int rc = LMC_OK;
+    for (int i = 0; i < n && !rc; i++) {
+        if (m->gexec) {
+            if (cudaGraphLaunch(m->gexec, m->stream) != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "graph launch");
+        } else {
+            rc = gen_step(m, m->g_batch, m->g_nprompt, m->g_nnew);
+        }
     }
+    m->smp = 0;
+    TRY(rc);
     if (stream_out) *(cudaStream_t *)stream_out = m->stream;
     return LMC_OK;
 }
 
 int lmc_model_graph_kernels(const lmc_model *m) { return m && m->gexec ? m->g_kernels : -1; }
+
+const lmc_qtensor *lmc_model_matrix(const lmc_model *m, int layer, int which) {
+    if (!m) return NULL;
+    if (which == LMC_W_TOKEN_EMBD) return m->wte;
+    if (which == LMC_W_OUTPUT) return m->lm_head;
+    if (layer < 0 || layer >= m->cfg.n_layers) return NULL;
+    const Layer *w = &m->layers[layer];
+    const int gpt2 = m->cfg.arch == 1;
+    switch (which) {
+    case LMC_W_QKV: return gpt2 ? w->qkv : NULL;
+    case LMC_W_ATTN_OUT: return gpt2 ? w->proj : w->o;
+    case LMC_W_FFN_UP: return gpt2 ? w->fc : w->up;
+    case LMC_W_FFN_DOWN: return gpt2 ? w->fc2 : w->down;
+    case LMC_W_Q: return gpt2 ? NULL : w->q;
+    case LMC_W_K: return gpt2 ? NULL : w->k;
+    case LMC_W_V: return gpt2 ? NULL : w->v;
+    case LMC_W_GATE: return gpt2 ? NULL : w->gate;
+    default: return NULL;
+    }
+}
+
+const float *lmc_model_vector(const lmc_model *m, int layer, int which, int *len) {
+    if (!m) return NULL;
+    const lmc_model_config *c = &m->cfg;
+    const int D = c->embed_dim, gpt2 = c->arch == 1;
+    const float *v = NULL;
+    int n = D;
+    switch (which) {
+    case LMC_V_POS_EMBD: v = gpt2 ? m->wpe : NULL; n = c->seq_len * D; break;
+    case LMC_V_OUTPUT_NORM: v = gpt2 ? m->lnf_w : m->rmsf; break;
+    case LMC_V_OUTPUT_NORM_B: v = gpt2 ? m->lnf_b : NULL; break;
+    case LMC_V_ROPE_COS: v = gpt2 ? NULL : m->rope_cos; n = c->seq_len * (c->head_dim / 2); break;
+    case LMC_V_ROPE_SIN: v = gpt2 ? NULL : m->rope_sin; n = c->seq_len * (c->head_dim / 2); break;
+    default: {
+        if (layer < 0 || layer >= c->n_layers) return NULL;
+        const Layer *w = &m->layers[layer];
+        switch (which) {
+        case LMC_V_ATTN_NORM: v = gpt2 ? w->ln1_w : w->rms_attn; break;
+        case LMC_V_ATTN_NORM_B: v = gpt2 ? w->ln1_b : NULL; break;
+        case LMC_V_FFN_NORM: v = gpt2 ? w->ln2_w : w->rms_ffn; break;
+        case LMC_V_FFN_NORM_B: v = gpt2 ? w->ln2_b : NULL; break;
+        case LMC_V_QKV_B: v = gpt2 ? w->qkv_b : NULL; n = 3 * D; break;
+        case LMC_V_ATTN_OUT_B: v = gpt2 ? w->proj_b : NULL; break;
+        case LMC_V_FFN_UP_B: v = gpt2 ? w->fc_b : NULL; n = c->ffn_dim; break;
+        case LMC_V_FFN_DOWN_B: v = gpt2 ? w->fc2_b : NULL; break;
+        default: return NULL;
+        }
+    }
+    }
+    if (v && len) *len = n;
+    return v;
+}

@@ -55,6 +55,16 @@ SIGNATURES = {
     "lmc_model_replay": ([_vp, _i, _vp], _i),
     "lmc_model_device_buffer": ([_vp, _i], _vp),
     "lmc_model_graph_kernels": ([_vp], _i),
+    "lmc_qtensor_shape": ([_vp, _c.POINTER(_u32), _ip, _ip], _i),
+    "lmc_buffer_alloc": ([_sz, _c.POINTER(_vp)], _i),
+    "lmc_buffer_free": ([_vp], _i),
+    "lmc_copy": ([_vp, _vp, _sz, _i, _vp], _i),
+    "lmc_stream_sync": ([_vp], _i),
+    "lmc_model_matrix": ([_vp, _i, _i], _vp),
+    "lmc_model_vector": ([_vp, _i, _i, _ip], _vp),
+    "lmc_sample_top_p": ([_vp, _i, _i, _f, _f, _vp, _vp, _vp], _i),
+    "lmc_rng_seed": ([_c.c_uint64], _c.c_uint64),
+    "lmc_model_generate_sample": ([_vp, _ip, _i, _i, _i, _f, _f, _c.c_uint64, _i, _ip], _i),
 }
 
 

@@ -43,6 +43,8 @@ class Oracle:
         L.orc_rope_cache.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float]
         L.orc_attention.argtypes = [_f32p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 5
         L.orc_argmax.argtypes = [_f32p, ctypes.c_int]
+        L.orc_sample_top_p.argtypes = [_f32p, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                       ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_double)]
         L.orc_model_load.argtypes = [ctypes.c_char_p]
         L.orc_model_load.restype = ctypes.c_void_p
         L.orc_model_free.argtypes = [ctypes.c_void_p]
@@ -116,6 +118,13 @@ class Oracle:
     def argmax(self, x):
         x = np.ascontiguousarray(x, np.float32)
         return self.lib.orc_argmax(_ptr(x, _f32p), x.size)
+
+    def sample_top_p(self, logits, temperature, top_p, state):
+        """(token, next xorshift64 state, margin of the draw to a cdf boundary)."""
+        x = np.array(logits, np.float32)
+        st, m = ctypes.c_uint64(state), ctypes.c_double()
+        tok = self.lib.orc_sample_top_p(_ptr(x, _f32p), x.size, temperature, top_p, ctypes.byref(st), ctypes.byref(m))
+        return tok, st.value, m.value
 
     def model(self, path):
         return OracleModel(self, path)
@@ -194,6 +203,8 @@ class Ref:
         L.silu.argtypes = [ctypes.c_float]
         L.silu.restype = ctypes.c_float
         L.rope_apply.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int]
+        L.refshim_sample_top_p.argtypes = [_f32p, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                           ctypes.POINTER(ctypes.c_uint64)]
         self.cfg = None
 
     def set_threads(self, n):
@@ -252,6 +263,14 @@ class Ref:
         out = np.empty(self.cfg["V"], np.float32)
         self.lib.refshim_forward(tok, pos, _ptr(out, _f32p))
         return out
+
+    def sample_top_p(self, logits, temperature, top_p, state):
+        """LMc's own sample_top_p (lmc.c:42-59) from xorshift64 state `state`:
+        (token, next state)."""
+        x = np.array(logits, np.float32)
+        st = ctypes.c_uint64(state)
+        tok = self.lib.refshim_sample_top_p(_ptr(x, _f32p), x.size, temperature, top_p, ctypes.byref(st))
+        return tok, st.value
 
     def generate(self, prompt, n_new):
         prompt = np.ascontiguousarray(prompt, np.int32)

@@ -396,6 +396,56 @@ int orc_argmax(const float *x, int n) {
     return best;
 }
 
+/* lmc.c:29-59: xorshift64 (shifts 13, 7, 17), a draw = top 53 bits / 2^53 in
+ * float; greedy below temperature 1e-6; otherwise scale, softmax, sort
+ * descending (qsort with the same comparison), nucleus = shortest prefix
+ * whose running sum reaches top_p, renormalised walk until r < cdf. */
+typedef struct { float prob; int idx; } OrcProbIdx;
+static int orc_cmp_desc(const void *a, const void *b) {
+    const OrcProbIdx *pa = (const OrcProbIdx *)a, *pb = (const OrcProbIdx *)b;
+    return (pb->prob > pa->prob) ? 1 : (pb->prob < pa->prob) ? -1 : 0;
+}
+int orc_sample_top_p(float *logits, int V, float temperature, float top_p, uint64_t *rng, double *margin) {
+    if (margin) *margin = 1.0;
+    if (temperature < 1e-6f) return orc_argmax(logits, V);
+    const float inv_temp = 1.0f / temperature;
+    for (int i = 0; i < V; i++) logits[i] *= inv_temp;
+    orc_softmax(logits, V);
+    OrcProbIdx *srt = (OrcProbIdx *)malloc(sizeof(OrcProbIdx) * (size_t)V);
+    if (!srt) return -1;
+    for (int i = 0; i < V; i++) { srt[i].prob = logits[i]; srt[i].idx = i; }
+    qsort(srt, (size_t)V, sizeof(OrcProbIdx), orc_cmp_desc);
+    float cumsum = 0.0f;
+    int nucleus = 0;
+    for (int i = 0; i < V; i++) { cumsum += srt[i].prob; nucleus = i + 1; if (cumsum >= top_p) break; }
+    float ns = 0.0f;
+    for (int i = 0; i < nucleus; i++) ns += srt[i].prob;
+    uint64_t st = *rng;
+    st ^= st << 13; st ^= st >> 7; st ^= st << 17;
+    *rng = st;
+    const float inv_ns = 1.0f / ns, r = (float)(st >> 11) / (float)(1ULL << 53);
+    float cdf = 0.0f;
+    int pick = srt[nucleus - 1].idx;
+    double m = 1.0;
+    for (int i = 0; i < nucleus; i++) {
+        cdf += srt[i].prob * inv_ns;
+        const double d = fabs((double)cdf - (double)r);
+        if (d < m) m = d;
+        if (r < cdf) { pick = srt[i].idx; break; }
+    }
+    /* the nucleus boundary: how close the running sum came to top_p */
+    double c2 = 0.0;
+    for (int i = 0; i < nucleus; i++) c2 += srt[i].prob;
+    if (fabs(c2 - top_p) < m) m = fabs(c2 - top_p);
+    if (nucleus >= 1) {
+        double c1 = c2 - srt[nucleus - 1].prob;
+        if (fabs(c1 - top_p) < m) m = fabs(c1 - top_p);
+    }
+    if (margin) *margin = m;
+    free(srt);
+    return pick;
+}
+
 /* ------------------------------------------------------------------------ */
 /* Whole model: GGUF parse (gguf.c:114-353) + forward (ops.c, ops_llama.c)    */
 /* ------------------------------------------------------------------------ */

@@ -72,6 +72,14 @@ void  orc_attention(float *out, const float *q, const float *k_cache,
 /* First index of the maximum (strict '>' scan), lmc.c:45-47. */
 int   orc_argmax(const float *x, int n);
 
+/* Top-p sampling with temperature as lmc.c:42-59 (logits scaled in place,
+ * softmax, qsort descending, nucleus, one draw of the xorshift64 state
+ * *rng as lmc.c:31-33).  Returns the token.  margin (may be NULL) receives
+ * the distance, in probability, from the draw to the nearest cdf boundary of
+ * the walk (a draw that close may land elsewhere under other rounding). */
+int   orc_sample_top_p(float *logits, int V, float temperature, float top_p,
+                       uint64_t *rng, double *margin);
+
 /* ---- whole-model restatement (gguf.c load + ops.c/ops_llama.c forward) ---- */
 typedef struct OrcModel OrcModel;
 /* Parse a GGUF v1-3 file the way LMc's load_model_gguf does

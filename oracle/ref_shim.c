@@ -135,3 +135,28 @@ double refshim_time_matmul(float *out, const float *w, const float *bias, const 
     for (int r = 0; r < reps; r++) matmul_vec(out, w, bias, in, M, K);
     return now_s() - t0;
 }
+
+/* LMc's own sample_top_p and RNG (lmc.c:29-59) are file-static in lmc.c, so
+ * lmc.c itself is compiled into this file, its main renamed out of the way.
+ * refshim_sample_top_p seeds the RNG state directly and runs LMc's function
+ * on a logits row (scaled and softmaxed in place, as LMc does); vocab_size
+ * and the sort buffer are set for the call and restored after it. */
+#define main lmc_cli_main_unused
+#include "lmc.c"
+#undef main
+
+int refshim_sample_top_p(float *logits, int V, float temperature, float top_p, uint64_t *state) {
+    const int saved_v = g_cfg.vocab_size;
+    void *saved_buf = g_act.sorted_buf;
+    void *buf = malloc((size_t)V * (sizeof(float) + sizeof(int)));
+    if (!buf) return -1;
+    g_cfg.vocab_size = V;
+    g_act.sorted_buf = buf;
+    g_rng_state = *state;
+    const int tok = sample_top_p(logits, temperature, top_p);
+    *state = g_rng_state;
+    g_cfg.vocab_size = saved_v;
+    g_act.sorted_buf = saved_buf;
+    free(buf);
+    return tok;
+}

@@ -146,6 +146,11 @@ def test_entry_points_validate_arguments_first():
         # 64 sequences x 32 heads x 128 dims over 32768 positions: the
         # split-context scratch exceeds the fixed array
         ("lmc_attention_decode_noalloc", (p, p, p, p, p, p, 0, p, 64, 32, 8, 128, 32768, None), b"attention_noalloc"),
+        # null pointers and H not a multiple of Hkv: rejected before the
+        # entry point looks up its scratch array (a CUDA call)
+        ("lmc_attention_decode_noalloc", (None, p, p, p, p, p, 0, p, 1, 32, 8, 128, 1024, None), b"null"),
+        ("lmc_attention_decode_noalloc", (p, p, p, p, p, None, 0, p, 1, 32, 8, 128, 1024, None), b"null"),
+        ("lmc_attention_decode_noalloc", (p, p, p, p, p, p, 0, p, 1, 30, 8, 128, 1024, None), b"Hkv=8"),
     ]
     for name, args, word in calls:
         rc = getattr(L, name)(*args)

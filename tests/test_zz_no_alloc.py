@@ -2,8 +2,9 @@
 cannot allocate device memory where they decode (graph capture, loops that
 must not synchronize on cudaMalloc/cudaFree, hosts owning all device
 memory).  Called through the C ABI, it must match lmc_attention_decode with
-a caller workspace, on two calls in a row (the fixed scratch array keeps the
-previous call's contents, which must not leak into the next result).
+a caller workspace and the oracle's attention read, on two calls in a row
+(the fixed scratch array keeps the previous call's contents, which must not
+leak into the next result).
 
 Kept in a file pytest collects last, so a stop-at-first-failure run has
 already run every other test."""
@@ -43,14 +44,31 @@ def _run(torch, t, H, Hkv, Dh, S, B, noalloc):
     return out.cpu().numpy(), kc.cpu().numpy()
 
 
-@pytest.mark.parametrize("H,Hkv,Dh,S,pos,B", [(12, 12, 64, 1024, 700, 2), (32, 8, 128, 4096, 3000, 1)])
-def test_noalloc_matches_workspace_entry(cuda, H, Hkv, Dh, S, pos, B):
-    for call, seed in enumerate((11, 12)):  # two calls in a row, different data
-        t = _case(cuda, seed, H, Hkv, Dh, S, pos - 37 * call, B)
+# The second call's position lies several context splits below the first's,
+# so the splits the first call filled are empty in the second: leftovers of
+# the first call in the shared array must not reach the second result.
+@pytest.mark.parametrize("H,Hkv,Dh,S,pos,pos2,B",
+                         [(12, 12, 64, 1024, 700, 90, 2), (32, 8, 128, 4096, 3000, 200, 1)])
+def test_noalloc_matches_workspace_entry(cuda, orc, H, Hkv, Dh, S, pos, pos2, B):
+    for call, (seed, p) in enumerate(((11, pos), (12, pos2))):  # two calls in a row, different data
+        t = _case(cuda, seed, H, Hkv, Dh, S, p, B)
         want, kc_want = _run(cuda, t, H, Hkv, Dh, S, B, noalloc=False)
         got, kc_got = _run(cuda, t, H, Hkv, Dh, S, B, noalloc=True)
         assert rel_err(got, want) < 1e-5, f"call {call}"
         assert np.array_equal(kc_got, kc_want)
+        # and the oracle's attention read over the cache the call wrote
+        for b in range(B):
+            ref = orc.attention(t["q"][b].cpu().numpy(), kc_got[b], _vc_after(t, b), H, Hkv, Dh, S, p - b)
+            assert rel_err(got[b], ref) < 1e-5, f"call {call} row {b} vs oracle"
+
+
+def _vc_after(t, b):
+    """The V cache of row b after the call: the new V row at its position."""
+    vc = t["vc"][b].cpu().numpy().copy()
+    pos = int(t["pos"][b].item())
+    Hkv, Dh = vc.shape[0], vc.shape[2]
+    vc[:, pos, :] = t["vn"][b].cpu().numpy().reshape(Hkv, Dh)
+    return vc
 
 
 def test_noalloc_rejects_oversized_shape(cuda):
