@@ -157,6 +157,11 @@ typedef struct {
     float temperature, top_p;
     unsigned long long *rng;
     int from_next;
+    /* norm statistics passed from the op that writes x to the norm that reads
+     * it: slot number + 1 (0 = none).  stats_out on EMBED and on GEMVs that
+     * add into the residual; stats_in on GEMVs with a LayerNorm/RMSNorm
+     * prologue (which then skip their own statistics passes). */
+    int stats_in, stats_out;
 } lmc_step_op;
 typedef struct lmc_step_prog lmc_step_prog;
 /* LMC_ERR_UNSUPPORTED when an op cannot run inside the persistent kernel

@@ -33,6 +33,8 @@
 #include "sample.cuh"
 #include "tiled_gemv.cuh"
 
+#include <stdlib.h>
+
 #include <mutex>
 #include <vector>
 
@@ -46,6 +48,14 @@ struct EmbedArgs {
     const int *tok, *pos;
     int D, V, S, type;
     float *out;
+    double *stats_out;  // {sum x, sum x^2} per row for the norm that reads x, or NULL
+};
+// The K/V rows an attention op will read (positions 0..pos-1 of every
+// sequence and kv head): asked of L2 by the GEMV op before it.
+struct KvPf {
+    const uint8_t *kc, *vc;
+    const int *pos;
+    int Hkv, S, row_bytes, nb;
 };
 struct AdvArgs {
     unsigned long long *keys;
@@ -66,24 +76,37 @@ struct alignas(16) DOp {
     int kind, sync, nb;
     int qt;           // GEMV: 4 / 6 / 8
     int next_gemv;    // index of the next GEMV op (its ring is filled at the end of this one), -1 none
+    int nqt;          // its format
     int kv, dh;       // ATTN: 0 fp32 / 1 fp16 cache; head size 64 / 128
     int items;        // ATTN: splits x kv heads x batch
+    int kpf;          // GEMV: 1 = prefetch kp into L2 first
+    int ff;           // GEMV: 1 = the latency (fp32) form, 0 = the tensor-core form
     TArgs g;
+    TArgs ng;         // the next GEMV's arguments (its ring prefill reads them here)
+    KvPf kp;
     AttnArgs at;
     EmbedArgs e;
     AdvArgs v;
     SampArgs sm;
 };
+// Barrier arrivals go to BAR_GROUPS counters (CTA c to counter c % BAR_GROUPS),
+// each on its own 128-byte line, so the atomics do not queue on one address.
+constexpr int BAR_GROUPS = 8;
+struct alignas(128) BarCount {
+    unsigned v;
+};
 struct StepCtl {
-    unsigned count;  // barrier arrivals, never reset between launches
-    unsigned base;   // count at the start of the next launch
-    int abort;       // set when a wait ran out: every CTA leaves
-    int where;       // op index + 1 of the wait that ran out
+    BarCount cnt[BAR_GROUPS];   // arrivals, never reset between launches
+    unsigned base[BAR_GROUPS];  // each counter at the start of the next launch
+    int abort;                  // set when a wait ran out: every CTA leaves
+    int where;                  // op index + 1 of the wait that ran out
 };
 struct StepParams {
     const DOp *ops;
     int nops, first_gemv, ring_off, stages;
     StepCtl *ctl;
+    double *stats;  // norm statistics slots, zeroed again at the end of each launch
+    int stats_n;    // doubles in the slots
 };
 
 __device__ long long g_step_wait_ns = 1000000000ll;
@@ -94,36 +117,61 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     return v;
 }
 
-// Grid-wide barrier number `target` / gridDim.x: thread 0 of each CTA adds its
-// arrival (after a fence, so the CTA's writes are visible) and polls until all
-// arrived, the abort flag is set, or the wait limit passes (then it sets the
-// flag).  Returns false when the CTA must leave.
-__device__ __forceinline__ bool grid_sync(StepCtl *ctl, unsigned target, int where, int *sh_ok) {
+// Arrivals the counter of group k holds after `passed` barriers of a launch
+// that started at base[k]: CTAs c with c % BAR_GROUPS == k arrive there.
+__device__ __forceinline__ unsigned group_size(int k) {
+    return (gridDim.x + BAR_GROUPS - 1 - (unsigned)k) / BAR_GROUPS;
+}
+
+// Grid-wide barrier: thread 0 of each CTA adds its arrival to its group's
+// counter (after a fence, so the CTA's writes are visible); lanes 0..7 of
+// warp 0 poll one counter each until every group is complete, the abort flag
+// is set, or the wait limit passes (then they set the flag).  Meanwhile the
+// other warps copy the next op into `next_op` (the op list is constant).
+// Returns false when the CTA must leave.
+__device__ __forceinline__ bool grid_sync(StepCtl *ctl, const unsigned *base, unsigned passed, int where, int *sh_ok,
+                                          const DOp *next_src, DOp *next_op) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(&ctl->count, 1u);
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x < 32) {
+        if (lane == 0) {
+            __threadfence();
+            atomicAdd(&ctl->cnt[blockIdx.x % BAR_GROUPS].v, 1u);
+        }
+        const int k = lane < BAR_GROUPS ? lane : 0;
+        const unsigned target = base[k] + passed * group_size(k);
         int ok = 1;
         long long t0 = 0;
         for (unsigned it = 0;; it++) {
-            if ((int)(ld_acquire_u32(&ctl->count) - target) >= 0) break;
+            const bool mine = lane >= BAR_GROUPS || (int)(ld_acquire_u32(&ctl->cnt[k].v) - target) >= 0;
+            if (__all_sync(0xffffffffu, mine)) break;
             if ((it & 31) == 31) {
-                if (*(volatile int *)&ctl->abort) {
-                    ok = 0;
-                    break;
+                int stop = 0;
+                if (lane == 0) {
+                    if (*(volatile int *)&ctl->abort) {
+                        stop = 1;
+                    } else {
+                        const long long t = globaltimer_ns();
+                        if (!t0) t0 = t;
+                        else if (t - t0 > g_step_wait_ns) {
+                            atomicExch(&ctl->where, where + 1);
+                            atomicExch(&ctl->abort, 1);
+                            stop = 1;
+                        }
+                    }
                 }
-                const long long t = globaltimer_ns();
-                if (!t0) t0 = t;
-                else if (t - t0 > g_step_wait_ns) {
-                    atomicExch(&ctl->where, where + 1);
-                    atomicExch(&ctl->abort, 1);
+                if (__shfl_sync(0xffffffffu, stop, 0)) {
                     ok = 0;
                     break;
                 }
             }
         }
         __threadfence();
-        *sh_ok = ok;
+        if (lane == 0) *sh_ok = ok;
+    } else if (next_src) {
+        const int4 *src = reinterpret_cast<const int4 *>(next_src);
+        int4 *dst = reinterpret_cast<int4 *>(next_op);
+        for (int w = threadIdx.x - 32; w < (int)(sizeof(DOp) / 16); w += NTHR - 32) dst[w] = __ldg(src + w);
     }
     __syncthreads();
     return *sh_ok != 0;
@@ -145,11 +193,12 @@ __device__ __forceinline__ bool warp_units(const TArgs &a, int cid, int wid, int
         w0 = w1 = t0 = t1 = 0;
         return false;
     }
-    t0 = (int)((long long)cid * a.RT / a.NC);
-    t1 = (int)((long long)(cid + 1) * a.RT / a.NC);
+    // 32-bit products: cid * RT < 2^31 for every shape the host plans here
+    t0 = cid * a.RT / a.NC;
+    t1 = (cid + 1) * a.RT / a.NC;
     const int Uc = (t1 - t0) * a.KB;
-    w0 = (int)((long long)Uc * wid / WARPS);
-    w1 = (int)((long long)Uc * (wid + 1) / WARPS);
+    w0 = Uc * wid / WARPS;
+    w1 = Uc * (wid + 1) / WARPS;
     return true;
 }
 
@@ -174,28 +223,312 @@ __device__ __forceinline__ void ring_prefill(Ring &r, const TArgs &a, int qt, in
     __syncwarp();
 }
 
+// Ask L2 for the K/V rows the coming attention op reads (positions 0..pos-1
+// of each sequence and kv head; the rows were written by earlier steps), in
+// 16 KB pieces, one (sequence, kv head, K or V) range per CTA.
+__device__ __forceinline__ void kv_prefetch(const KvPf &k) {
+    if (threadIdx.x != 0) return;
+    const int items = k.nb * k.Hkv * 2;
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        const int half = it & 1, bh = it >> 1, b = bh / k.Hkv, kh = bh % k.Hkv;
+        const int pos = min(max(__ldcg(k.pos + b), 0), k.S);
+        const uint8_t *base = (half ? k.vc : k.kc) + ((size_t)b * k.Hkv + kh) * k.S * (size_t)k.row_bytes;
+        const size_t bytes = (size_t)pos * k.row_bytes;
+        for (size_t o = 0; o < bytes; o += 16384)
+            prefetch_l2(base + o, (uint32_t)min((size_t)16384, bytes - o));
+    }
+}
+
+// The outputs e = lane + 32 j (e < 16 nb: batch row e / 16, tile row e % 16)
+// of one row tile: bias (preloaded in pbias when given), GELU, residual add
+// (the old values preloaded in `pre` when given), the greedy-pick key, and
+// the sums of the final values for the norm that reads them next.
+__device__ __forceinline__ void step_epilogue_tile(const TArgs &a, int row0, const float *ar, int lane,
+                                                   unsigned long long (&best)[4], const float *pre,
+                                                   const float *pbias, double (&st)[2][2]) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int e = lane + 32 * j, b = e >> 4, row = row0 + (e & 15);
+        if (e >= 16 * a.nb || row >= a.M) continue;
+        float v = ar[e];
+        if (a.bias) v += pbias ? pbias[j] : __ldg(a.bias + row);
+        if (a.epi & LMC_EPI_GELU) v = lmc_gelu_f(v);
+        float *o = a.y + (size_t)b * a.ldy + row;
+        const float out = (a.epi & LMC_EPI_ACCUM) ? (pre ? pre[j] : __ldcg(o)) + v : v;
+        *o = out;
+        const unsigned long long k = lmc_argmax_key(v, row + a.key_base);
+        best[j] = k > best[j] ? k : best[j];
+        if (b == 0) {
+            st[0][0] += (double)out;
+            st[0][1] += (double)out * (double)out;
+        } else {
+            st[1][0] += (double)out;
+            st[1][1] += (double)out * (double)out;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// The latency GEMV.  The tensor-core GEMV quantizes x into three int8 limbs
+// per CTA (several dependent passes and CTA-wide reductions), which pays off
+// when each warp streams many units.  In a decode step most GEMVs give a warp
+// one to a few units, and that set-up is most of the op's time.  For those
+// ops x is staged once as fp32 in shared memory (its norm from the writer's
+// statistics) and each lane dots the 128 weights it holds in a unit - rows
+// g and g + 8 of the tile at the same 64 columns, in the tiled layout the
+// tensor-core GEMV reads - against it with fp32 FMAs, applies the sub-block
+// scales, and the four lanes of a row are summed by shuffles.  Results agree
+// with the tensor-core path to fp32 rounding.
+// ---------------------------------------------------------------------------
+// Byte i of w as the float 2^23 + byte (one PRMT: the byte under 0x4B0000);
+// subtracting 2^23 (or 2^23 + an offset) gives the byte exactly.
+template <int I> __device__ __forceinline__ float byte_2p23(uint32_t w) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u + I));
+}
+
+struct FAcc {
+    float v[2][2];  // [batch row][row half: g, g + 8]
+    __device__ __forceinline__ void zero() { v[0][0] = v[0][1] = v[1][0] = v[1][1] = 0.0f; }
+};
+
+// Q4_K unit: d * sum_j sc_j (sum q x) - dmin * sum_j m_j (sum x)  (src/quant.c:275-303)
+template <int NBR>
+__device__ __forceinline__ void funit_q4k(FAcc &o, const uint8_t *u, const float *xs, int K, int k0, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+    const uint4 H0 = *reinterpret_cast<const uint4 *>(u + 16 * g);
+    const uint4 H1 = *reinterpret_cast<const uint4 *>(u + 16 * g + 128);
+    const uint4 *cw = reinterpret_cast<const uint4 *>(u + 256) + lane;
+    const uint4 q0 = cw[0], q1 = cw[32], q2 = cw[64], q3 = cw[96];
+    const uint32_t qs[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
+                             q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+    // 6-bit scales / mins, four per word (src/quant.c:44-53)
+    const uint32_t sc0[2] = {H0.y & 0x3F3F3F3Fu, (H0.w & LO4) | ((H0.y >> 2) & 0x30303030u)};
+    const uint32_t sc1[2] = {H1.y & 0x3F3F3F3Fu, (H1.w & LO4) | ((H1.y >> 2) & 0x30303030u)};
+    const uint32_t mn0[2] = {H0.z & 0x3F3F3F3Fu, ((H0.w >> 4) & LO4) | ((H0.z >> 2) & 0x30303030u)};
+    const uint32_t mn1[2] = {H1.z & 0x3F3F3F3Fu, ((H1.w >> 4) & LO4) | ((H1.z >> 2) & 0x30303030u)};
+    float sg[NBR], s8[NBR], mg[NBR], m8[NBR];
+#pragma unroll
+    for (int b = 0; b < NBR; b++) sg[b] = s8[b] = mg[b] = m8[b] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        // byte i of P: code(32j + 4c + i) | code(32j + 16 + 4c + i) << 4 (row g); Q: row g + 8
+        const uint32_t P = qs[2 * j], Q = qs[2 * j + 1];
+        const uint32_t Pl = P & LO4, Ph = (P >> 4) & LO4, Ql = Q & LO4, Qh = (Q >> 4) & LO4;
+        const float ag[8] = {byte_2p23<0>(Pl), byte_2p23<1>(Pl), byte_2p23<2>(Pl), byte_2p23<3>(Pl),
+                             byte_2p23<0>(Ph), byte_2p23<1>(Ph), byte_2p23<2>(Ph), byte_2p23<3>(Ph)};
+        const float a8[8] = {byte_2p23<0>(Ql), byte_2p23<1>(Ql), byte_2p23<2>(Ql), byte_2p23<3>(Ql),
+                             byte_2p23<0>(Qh), byte_2p23<1>(Qh), byte_2p23<2>(Qh), byte_2p23<3>(Qh)};
+        const int sh = 8 * (j & 3);
+        const float scg = (float)((sc0[j >> 2] >> sh) & 63u), sc8 = (float)((sc1[j >> 2] >> sh) & 63u);
+        const float mng = (float)((mn0[j >> 2] >> sh) & 63u), mn8 = (float)((mn1[j >> 2] >> sh) & 63u);
+#pragma unroll
+        for (int b = 0; b < NBR; b++) {
+            const float4 xa = *reinterpret_cast<const float4 *>(xs + b * K + k0 + 32 * j + 4 * c);
+            const float4 xb = *reinterpret_cast<const float4 *>(xs + b * K + k0 + 32 * j + 16 + 4 * c);
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            // ag[i] - 2^23 is the code q exactly
+            float pg = 0.0f, p8 = 0.0f, X = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                pg = fmaf(ag[i] - 8388608.0f, xv[i], pg);
+                p8 = fmaf(a8[i] - 8388608.0f, xv[i], p8);
+                X += xv[i];
+            }
+            sg[b] = fmaf(scg, pg, sg[b]);
+            s8[b] = fmaf(sc8, p8, s8[b]);
+            mg[b] = fmaf(mng, X, mg[b]);
+            m8[b] = fmaf(mn8, X, m8[b]);
+        }
+    }
+    const float2 dd0 = __half22float2(*reinterpret_cast<const __half2 *>(&H0.x));  // (d, dmin)
+    const float2 dd1 = __half22float2(*reinterpret_cast<const __half2 *>(&H1.x));
+#pragma unroll
+    for (int b = 0; b < NBR; b++) {
+        o.v[b][0] += dd0.x * sg[b] - dd0.y * mg[b];
+        o.v[b][1] += dd1.x * s8[b] - dd1.y * m8[b];
+    }
+}
+
+// Q6_K unit: d * sum_chunks sc * sum (q - 32) x  (src/quant.c:386-414)
+template <int NBR>
+__device__ __forceinline__ void funit_q6k(FAcc &o, const uint8_t *u, const float *xs, int K, int k0, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+    const uint4 s0v = *reinterpret_cast<const uint4 *>(u + 16 * g);
+    const uint4 s1v = *reinterpret_cast<const uint4 *>(u + 16 * g + 128);
+    const float d0 = __half2float(*reinterpret_cast<const __half *>(u + 256 + 2 * g));
+    const float d1 = __half2float(*reinterpret_cast<const __half *>(u + 256 + 2 * g + 16));
+    const uint4 *lw = reinterpret_cast<const uint4 *>(u + 288) + lane;
+    const uint4 *hw = reinterpret_cast<const uint4 *>(u + 288 + 2048) + lane;
+    const uint4 l0 = lw[0], l1 = lw[32], l2 = lw[64], l3 = lw[96], h0 = hw[0], h1 = hw[32];
+    const uint32_t lo[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w,
+                             l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
+    const uint32_t hs[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    const uint32_t sw0[4] = {s0v.x, s0v.y, s0v.z, s0v.w}, sw1[4] = {s1v.x, s1v.y, s1v.z, s1v.w};
+    float sg[NBR], s8[NBR];
+#pragma unroll
+    for (int b = 0; b < NBR; b++) sg[b] = s8[b] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        // byte i of P: lo(g, k) | lo(g + 8, k) << 4, k = 16 j + 4 c + i; H (chunk
+        // pair j / 2): hi(g, k) | hi(g+8, k) << 2 | hi(g, k+16) << 4 | hi(g+8, k+16) << 6
+        const uint32_t P = lo[j], H = (j & 1) ? hs[j >> 1] >> 4 : hs[j >> 1];
+        const uint32_t wg = (P & LO4) | ((H << 4) & 0x30303030u);         // q, row g
+        const uint32_t w8 = ((P >> 4) & LO4) | ((H << 2) & 0x30303030u);  // q, row g + 8
+        const float vg[4] = {byte_2p23<0>(wg) - 8388640.0f, byte_2p23<1>(wg) - 8388640.0f,
+                             byte_2p23<2>(wg) - 8388640.0f, byte_2p23<3>(wg) - 8388640.0f};  // q - 32
+        const float v8[4] = {byte_2p23<0>(w8) - 8388640.0f, byte_2p23<1>(w8) - 8388640.0f,
+                             byte_2p23<2>(w8) - 8388640.0f, byte_2p23<3>(w8) - 8388640.0f};
+        const float scg = (float)(int)(int8_t)(sw0[j >> 2] >> (8 * (j & 3)));
+        const float sc8 = (float)(int)(int8_t)(sw1[j >> 2] >> (8 * (j & 3)));
+#pragma unroll
+        for (int b = 0; b < NBR; b++) {
+            const float4 x = *reinterpret_cast<const float4 *>(xs + b * K + k0 + 16 * j + 4 * c);
+            const float pg = fmaf(vg[3], x.w, fmaf(vg[2], x.z, fmaf(vg[1], x.y, vg[0] * x.x)));
+            const float p8 = fmaf(v8[3], x.w, fmaf(v8[2], x.z, fmaf(v8[1], x.y, v8[0] * x.x)));
+            sg[b] = fmaf(scg, pg, sg[b]);
+            s8[b] = fmaf(sc8, p8, s8[b]);
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < NBR; b++) {
+        o.v[b][0] += d0 * sg[b];
+        o.v[b][1] += d1 * s8[b];
+    }
+}
+
+// Q8_0 unit: sum_blocks d * sum q x  (src/quant.c:419-429)
+template <int NBR>
+__device__ __forceinline__ void funit_q80(FAcc &o, const uint8_t *u, const float *xs, int K, int k0, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+    const uint4 H0 = *reinterpret_cast<const uint4 *>(u + 16 * g);
+    const uint4 H1 = *reinterpret_cast<const uint4 *>(u + 16 * g + 128);
+    const uint32_t hw0[4] = {H0.x, H0.y, H0.z, H0.w}, hw1[4] = {H1.x, H1.y, H1.z, H1.w};
+    const uint4 *cw = reinterpret_cast<const uint4 *>(u + 256) + lane;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        // int8 codes with the sign bit flipped are the unsigned byte q + 128
+        const uint4 A = cw[32 * j];
+        const uint32_t ax = A.x ^ 0x80808080u, ay = A.y ^ 0x80808080u, az = A.z ^ 0x80808080u,
+                       aw = A.w ^ 0x80808080u;
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&hw0[j >> 1]));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&hw1[j >> 1]));
+        const float dg = (j & 1) ? f0.y : f0.x, d8 = (j & 1) ? f1.y : f1.x;
+        constexpr float B = 8388736.0f;  // 2^23 + 128
+        const float ag[8] = {byte_2p23<0>(ax) - B, byte_2p23<1>(ax) - B, byte_2p23<2>(ax) - B, byte_2p23<3>(ax) - B,
+                             byte_2p23<0>(az) - B, byte_2p23<1>(az) - B, byte_2p23<2>(az) - B, byte_2p23<3>(az) - B};
+        const float a8[8] = {byte_2p23<0>(ay) - B, byte_2p23<1>(ay) - B, byte_2p23<2>(ay) - B, byte_2p23<3>(ay) - B,
+                             byte_2p23<0>(aw) - B, byte_2p23<1>(aw) - B, byte_2p23<2>(aw) - B, byte_2p23<3>(aw) - B};
+#pragma unroll
+        for (int b = 0; b < NBR; b++) {
+            const float4 xa = *reinterpret_cast<const float4 *>(xs + b * K + k0 + 32 * j + 4 * c);
+            const float4 xb = *reinterpret_cast<const float4 *>(xs + b * K + k0 + 32 * j + 16 + 4 * c);
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            float pg = 0.0f, p8 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                pg = fmaf(ag[i], xv[i], pg);
+                p8 = fmaf(a8[i], xv[i], p8);
+            }
+            o.v[b][0] = fmaf(dg, pg, o.v[b][0]);
+            o.v[b][1] = fmaf(d8, p8, o.v[b][1]);
+        }
+    }
+}
+
+// A row tile's partial sums into the CTA accumulator acc[b][16]: the four
+// lanes of each row are added by shuffles, one shared atomic per value.
+__device__ __forceinline__ void fflush(const FAcc &o, float *acc_rt, int nb, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int b = 0; b < 2; b++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float v = o.v[b][h];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            if (c == 0 && b < nb) atomicAdd(acc_rt + b * 16 + g + 8 * h, v);
+        }
+}
+
+// x after its prologue, as fp32 rows xs[b][K] at shared-memory offset 0 (one
+// trip to L2: the norm statistics come from the op that wrote x).
+__device__ __forceinline__ void load_x_f32(float *xs, float *mr, const TArgs &a) {
+    const int K = a.KB * 256, tid = threadIdx.x;
+    float *mean = mr, *rstd = mr + 2;
+    if (a.pro == LMC_PRO_LAYERNORM || a.pro == LMC_PRO_RMSNORM) {
+        if (tid < a.nb) {
+            const double sx = __ldcg(a.stats + 2 * tid), sq = __ldcg(a.stats + 2 * tid + 1);
+            const double mu = a.pro == LMC_PRO_RMSNORM ? 0.0 : sx / (double)K;
+            const double var = fmax(sq / (double)K - mu * mu, 0.0);
+            mean[tid] = (float)mu;
+            rstd[tid] = 1.0f / sqrtf((float)var + (a.pro == LMC_PRO_RMSNORM ? a.eps : 1e-5f));
+        }
+        __syncthreads();
+    }
+    const XView<true> xv{a.x, a.x2, a.pw, a.pb, a.ldx, a.pro, mean, rstd};
+    for (int b = 0; b < a.nb; b++) {
+        int k = tid * 4;
+        for (; k + 3 * NTHR * 4 < K; k += 4 * NTHR * 4) {  // four loads in flight per thread
+            const float4 v0 = xv.at4(b, k), v1 = xv.at4(b, k + NTHR * 4), v2 = xv.at4(b, k + 2 * NTHR * 4),
+                         v3 = xv.at4(b, k + 3 * NTHR * 4);
+            *reinterpret_cast<float4 *>(xs + b * K + k) = v0;
+            *reinterpret_cast<float4 *>(xs + b * K + k + NTHR * 4) = v1;
+            *reinterpret_cast<float4 *>(xs + b * K + k + 2 * NTHR * 4) = v2;
+            *reinterpret_cast<float4 *>(xs + b * K + k + 3 * NTHR * 4) = v3;
+        }
+        for (; k < K; k += NTHR * 4) *reinterpret_cast<float4 *>(xs + b * K + k) = xv.at4(b, k);
+    }
+    __syncthreads();
+}
+
+// Shared memory of a latency-GEMV op below the ring: xs, mean/rstd, acc.
+__host__ __device__ __forceinline__ size_t fgemv_acc_off(int KB, int nb) { return (size_t)nb * KB * 256 * 4 + 16; }
+__host__ __device__ __forceinline__ size_t fgemv_smem(int KB, int nb, int maxrt) {
+    return fgemv_acc_off(KB, nb) + (size_t)maxrt * 2 * 16 * 4;
+}
+
 // One GEMV op (the body of k_gemv_tiled with clusters of one CTA): this CTA
 // owns row tiles [t0, t1) whole, so every tile is finished here.
-template <int QT>
-__device__ __forceinline__ bool gemv_op(uint8_t *smem, const TArgs &a, Ring &r, const DOp *next, StepCtl *ctl) {
+template <int QT, bool FF>
+__device__ __forceinline__ bool gemv_op(uint8_t *smem, const DOp &op, Ring &r, StepCtl *ctl) {
     constexpr int NB = 2, UNIT = unit_bytes(QT);
+    const TArgs &a = op.g;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     int w0, w1, t0, t1;
     const bool mine = warp_units(a, blockIdx.x, wid, w0, w1, t0, t1);
+    // the residual this warp's first tile adds to, loaded now (it is only
+    // needed in the epilogue) so its latency hides behind the work below
+    float pre[4] = {0.0f, 0.0f, 0.0f, 0.0f}, pbias[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const bool has_pre = mine && (a.epi & LMC_EPI_ACCUM) && wid < t1 - t0;
+    const bool has_pb = mine && a.bias && wid < t1 - t0;
+    if (has_pre || has_pb) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int e = lane + 32 * j, row = (t0 + wid) * 16 + (e & 15);
+            if (e < 16 * a.nb && row < a.M) {
+                if (has_pre) pre[j] = __ldcg(a.y + (size_t)(e >> 4) * a.ldy + row);
+                if (has_pb) pbias[j] = __ldg(a.bias + row);
+            }
+        }
+    }
     const Smem<1, QT> L{a.KB, a.XL, a.maxrt, 0};
-    float *acc = reinterpret_cast<float *>(smem + L.acc_off());
+    float *acc = reinterpret_cast<float *>(smem + (FF ? fgemv_acc_off(a.KB, a.nb) : L.acc_off()));
     bool ok = true;
     if (mine) {
         for (int i = threadIdx.x; i < a.maxrt * NB * 16; i += NTHR) acc[i] = 0.0f;
-        build_x<1, QT, 0, true>(smem, L, a);
+        if (FF) load_x_f32(reinterpret_cast<float *>(smem), reinterpret_cast<float *>(smem + fgemv_acc_off(a.KB, a.nb) - 16), a);
+        else build_x<1, QT, 0, true>(smem, L, a);
         __syncthreads();
         const float *inv = reinterpret_cast<const float *>(smem + L.sc_off()) + 8;
-        const int XS = a.XL * XSTR, KB = a.KB;
+        const int XS = a.XL * XSTR, KB = a.KB, K = KB * 256;
         const uint8_t *xbl = smem + lane * XSTR;
         const uint32_t *xml = reinterpret_cast<const uint32_t *>(smem + L.xm_off()) + lane;
+        const float *xsf = reinterpret_cast<const float *>(smem);
         const uint8_t *wbase = a.w + (size_t)t0 * KB * UNIT;
         Part<1> p;
         p.zero();
+        FAcc fa;
+        fa.zero();
         int cur = -1;
         int rt = w0 / KB, kb = w0 - rt * KB, s = r.s, i = w0;
         uint32_t parity = r.par;
@@ -207,15 +540,31 @@ __device__ __forceinline__ bool gemv_op(uint8_t *smem, const TArgs &a, Ring &r, 
             }
             r.inflight--;
             if (rt != cur) {
-                if (cur >= 0) flush<1>(p, acc + cur * NB * 16, inv, a.nb, lane);
+                if (cur >= 0) {
+                    if (FF) fflush(fa, acc + cur * NB * 16, a.nb, lane);
+                    else flush<1>(p, acc + cur * NB * 16, inv, a.nb, lane);
+                }
                 p.zero();
+                fa.zero();
                 cur = rt;
             }
             const uint8_t *u = r.slots + (size_t)s * SLOT;
-            const uint8_t *xb = xbl + kb * XS;
-            if (QT == 4) unit_q4k<1>(p, u, xb, XS, xml + kb * 32, lane);
-            else if (QT == 6) unit_q6k<1>(p, u, xb, XS, xml + kb * 32, lane);
-            else unit_q80<1>(p, u, xb, XS, lane);
+            if (FF) {
+                if (a.nb == 1) {
+                    if (QT == 4) funit_q4k<1>(fa, u, xsf, K, kb * 256, lane);
+                    else if (QT == 6) funit_q6k<1>(fa, u, xsf, K, kb * 256, lane);
+                    else funit_q80<1>(fa, u, xsf, K, kb * 256, lane);
+                } else {
+                    if (QT == 4) funit_q4k<2>(fa, u, xsf, K, kb * 256, lane);
+                    else if (QT == 6) funit_q6k<2>(fa, u, xsf, K, kb * 256, lane);
+                    else funit_q80<2>(fa, u, xsf, K, kb * 256, lane);
+                }
+            } else {
+                const uint8_t *xb = xbl + kb * XS;
+                if (QT == 4) unit_q4k<1>(p, u, xb, XS, xml + kb * 32, lane);
+                else if (QT == 6) unit_q6k<1>(p, u, xb, XS, xml + kb * 32, lane);
+                else unit_q80<1>(p, u, xb, XS, lane);
+            }
             __syncwarp();
             if (i + stages < w1) {
                 refill(lane == 0, &r.bars[s], r.slots + (size_t)s * SLOT, wbase + (size_t)(i + stages) * UNIT, UNIT,
@@ -233,18 +582,41 @@ __device__ __forceinline__ bool gemv_op(uint8_t *smem, const TArgs &a, Ring &r, 
         }
         r.s = s;
         r.par = parity;
-        if (cur >= 0 && ok) flush<1>(p, acc + cur * NB * 16, inv, a.nb, lane);
+        if (cur >= 0 && ok) {
+            if (FF) fflush(fa, acc + cur * NB * 16, a.nb, lane);
+            else flush<1>(p, acc + cur * NB * 16, inv, a.nb, lane);
+        }
     }
+    // this warp's slots are all consumed: start the next GEMV's weights - now
+    // for a warp that had no units here, after the epilogue for the others
+    // (issuing the copies is slow enough to delay the epilogue)
+    const bool late_prefill = ok && op.next_gemv >= 0 && w1 > w0;
     if (!ok) {
         atomicExch(&ctl->abort, 1);
-    } else if (next) {
-        // this warp's slots are all consumed: start the next GEMV's weights
-        ring_prefill(r, next->g, next->qt, lane, wid);
+    } else if (op.next_gemv >= 0 && !late_prefill) {
+        ring_prefill(r, op.ng, op.nqt, lane, wid);
     }
-    if (!mine) return ok;
+    if (!mine) {
+        if (op.kpf) kv_prefetch(op.kp);
+        return ok;
+    }
     __syncthreads();
     unsigned long long best[4] = {0ull, 0ull, 0ull, 0ull};
-    for (int T = wid; T < t1 - t0; T += WARPS) epilogue_tile(a, (t0 + T) * 16, acc + T * NB * 16, lane, best);
+    double st[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
+    for (int T = wid; T < t1 - t0; T += WARPS)
+        step_epilogue_tile(a, (t0 + T) * 16, acc + T * NB * 16, lane, best, T == wid && has_pre ? pre : nullptr,
+                           T == wid && has_pb ? pbias : nullptr, st);
+    if (a.stats_out) {  // sums of this CTA's outputs for the next norm: fp32 in the warp, fp64 across
+#pragma unroll
+        for (int b = 0; b < 2; b++)
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                float v = (float)st[b][q];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+                if (lane == 0 && b < a.nb && v != 0.0f) atomicAdd(a.stats_out + 2 * b + q, (double)v);
+            }
+    }
     if (a.keys) {  // greedy keys: half-warp maxima, then one atomic per CTA and batch row
         auto kbest = reinterpret_cast<unsigned long long(*)[8]>(smem);
         __syncthreads();  // the x fragments at offset 0 are dead
@@ -265,6 +637,8 @@ __device__ __forceinline__ bool gemv_op(uint8_t *smem, const TArgs &a, Ring &r, 
             if (k) atomicMax(a.keys + threadIdx.x, k);
         }
     }
+    if (late_prefill) ring_prefill(r, op.ng, op.nqt, lane, wid);
+    if (op.kpf) kv_prefetch(op.kp);
     return ok;
 }
 
@@ -288,7 +662,7 @@ __device__ __forceinline__ void attn_op(uint8_t *smem, const AttnArgs &a, int it
 }
 
 template <int T>
-__device__ __forceinline__ void embed_row(const EmbedArgs &e, int b) {
+__device__ __forceinline__ void embed_row(const EmbedArgs &e, int b, double (&st)[2]) {
     using F = lmcq::Fmt<T>;
     const int tok = __ldcg(e.tok + b), pos = e.wpe ? __ldcg(e.pos + b) : 0;
     if (tok < 0 || tok >= e.V || pos < 0 || pos >= e.S) return;  // the host validates tokens and positions
@@ -304,20 +678,40 @@ __device__ __forceinline__ void embed_row(const EmbedArgs &e, int b) {
                 float v = w[i];
                 if (e.wpe) v = v + e.wpe[(size_t)pos * e.D + k];
                 e.out[(size_t)b * e.D + k] = v;
+                st[0] += (double)v;
+                st[1] += (double)v * (double)v;
             }
         }
     }
 }
 
-__device__ __forceinline__ void embed_op(const EmbedArgs &e, int nb) {
+// One CTA per sequence row; the row's fp64 sums (for the first norm) are
+// stored, not added, so they need no zeroing.
+__device__ __forceinline__ void embed_op(const EmbedArgs &e, int nb, double *red) {
     for (int b = blockIdx.x; b < nb; b += gridDim.x) {
+        double st[2] = {0.0, 0.0};
         switch (e.type) {
-        case LMC_TYPE_Q4_K: embed_row<LMC_TYPE_Q4_K>(e, b); break;
-        case LMC_TYPE_Q6_K: embed_row<LMC_TYPE_Q6_K>(e, b); break;
-        case LMC_TYPE_Q8_0: embed_row<LMC_TYPE_Q8_0>(e, b); break;
-        case LMC_TYPE_F16: embed_row<LMC_TYPE_F16>(e, b); break;
-        default: embed_row<LMC_TYPE_F32>(e, b); break;
+        case LMC_TYPE_Q4_K: embed_row<LMC_TYPE_Q4_K>(e, b, st); break;
+        case LMC_TYPE_Q6_K: embed_row<LMC_TYPE_Q6_K>(e, b, st); break;
+        case LMC_TYPE_Q8_0: embed_row<LMC_TYPE_Q8_0>(e, b, st); break;
+        case LMC_TYPE_F16: embed_row<LMC_TYPE_F16>(e, b, st); break;
+        default: embed_row<LMC_TYPE_F32>(e, b, st); break;
         }
+        if (!e.stats_out) continue;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            double v = st[q];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if ((threadIdx.x & 31) == 0) red[2 * (threadIdx.x >> 5) + q] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x < 2) {
+            double t = 0.0;
+            for (int w = 0; w < WARPS; w++) t += red[2 * w + threadIdx.x];
+            e.stats_out[2 * b + threadIdx.x] = t;
+        }
+        __syncthreads();
     }
 }
 
@@ -356,18 +750,21 @@ __device__ __forceinline__ void sample_op(uint8_t *smem, const SampArgs &a, int 
 
 __global__ void __launch_bounds__(NTHR, 2) k_step(StepParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(16) DOp op;
+    __shared__ __align__(16) DOp ops[2];  // op i in ops[i & 1]; op i + 1 is copied in during barrier i
     __shared__ int sh_ok, sh_last;
-    __shared__ unsigned sh_base;
+    __shared__ unsigned sh_base[BAR_GROUPS];
+    __shared__ double sh_red[2 * WARPS];
     StepCtl *ctl = P.ctl;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    if (threadIdx.x == 0) {
-        sh_ok = *(volatile int *)&ctl->abort == 0;  // an earlier launch gave up: run nothing
-        sh_base = *(volatile unsigned *)&ctl->base;
+    if (threadIdx.x == 0) sh_ok = *(volatile int *)&ctl->abort == 0;  // an earlier launch gave up: run nothing
+    if (threadIdx.x < BAR_GROUPS) sh_base[threadIdx.x] = *(volatile unsigned *)&ctl->base[threadIdx.x];
+    {
+        const int4 *src = reinterpret_cast<const int4 *>(P.ops);
+        int4 *dst = reinterpret_cast<int4 *>(&ops[0]);
+        for (int w = threadIdx.x; w < (int)(sizeof(DOp) / 16); w += NTHR) dst[w] = __ldg(src + w);
     }
     __syncthreads();
     if (!sh_ok) return;
-    const unsigned base = sh_base;
     Ring r;
     r.stages = P.stages;
     r.slots = smem + P.ring_off + (size_t)wid * P.stages * SLOT;
@@ -384,19 +781,19 @@ __global__ void __launch_bounds__(NTHR, 2) k_step(StepParams P) {
     unsigned passed = 0;
     bool alive = true;
     for (int i = 0; i < P.nops && alive; i++) {
-        {  // this op's arguments into shared memory
-            const int4 *src = reinterpret_cast<const int4 *>(P.ops + i);
-            int4 *dst = reinterpret_cast<int4 *>(&op);
-            for (int w = threadIdx.x; w < (int)(sizeof(DOp) / 16); w += NTHR) dst[w] = __ldg(src + w);
-        }
-        __syncthreads();
-        const DOp *next = op.next_gemv >= 0 ? P.ops + op.next_gemv : nullptr;
+        const DOp &op = ops[i & 1];
         switch (op.kind) {
-        case LMC_OP_EMBED: embed_op(op.e, op.nb); break;
+        case LMC_OP_EMBED: embed_op(op.e, op.nb, sh_red); break;
         case LMC_OP_GEMV:
-            if (op.qt == 4) alive = gemv_op<4>(smem, op.g, r, next, ctl);
-            else if (op.qt == 6) alive = gemv_op<6>(smem, op.g, r, next, ctl);
-            else alive = gemv_op<8>(smem, op.g, r, next, ctl);
+            if (op.ff) {
+                if (op.qt == 4) alive = gemv_op<4, true>(smem, op, r, ctl);
+                else if (op.qt == 6) alive = gemv_op<6, true>(smem, op, r, ctl);
+                else alive = gemv_op<8, true>(smem, op, r, ctl);
+            } else {
+                if (op.qt == 4) alive = gemv_op<4, false>(smem, op, r, ctl);
+                else if (op.qt == 6) alive = gemv_op<6, false>(smem, op, r, ctl);
+                else alive = gemv_op<8, false>(smem, op, r, ctl);
+            }
             break;
         case LMC_OP_ATTN:
             if (op.kv == 0) {
@@ -410,15 +807,28 @@ __global__ void __launch_bounds__(NTHR, 2) k_step(StepParams P) {
         case LMC_OP_SAMPLE: sample_op(smem, op.sm, op.nb); break;
         default: advance_op(op.v, op.nb); break;
         }
-        // a ring wait that ran out in any warp of any CTA aborts the step at
-        // the next barrier (grid_sync polls the flag)
+        const DOp *nsrc = i + 1 < P.nops ? P.ops + i + 1 : nullptr;
         if (op.sync) {
+            // a ring wait that ran out in any warp of any CTA aborts the step
+            // here (grid_sync polls the flag)
             passed++;
-            alive = grid_sync(ctl, base + passed * gridDim.x, i, &sh_ok) && alive;
+            alive = grid_sync(ctl, sh_base, passed, i, &sh_ok, nsrc, &ops[(i + 1) & 1]) && alive;
+        } else {
+            __syncthreads();
+            if (nsrc) {
+                const int4 *src = reinterpret_cast<const int4 *>(nsrc);
+                int4 *dst = reinterpret_cast<int4 *>(&ops[(i + 1) & 1]);
+                for (int w = threadIdx.x; w < (int)(sizeof(DOp) / 16); w += NTHR) dst[w] = __ldg(src + w);
+            }
+            __syncthreads();
         }
-        __syncthreads();  // every warp is done with `op` before it is replaced
     }
-    if (alive && blockIdx.x == 0 && threadIdx.x == 0) ctl->base = base + passed * gridDim.x;
+    if (alive && blockIdx.x == 0) {
+        if (threadIdx.x < BAR_GROUPS) ctl->base[threadIdx.x] = sh_base[threadIdx.x] + passed * group_size(threadIdx.x);
+        // every norm has read its statistics (before the last barrier): zero
+        // the slots for the next launch
+        for (int k = threadIdx.x; k < P.stats_n; k += NTHR) P.stats[k] = 0.0;
+    }
     // after an abort: wait (bounded) for this warp's copies still in flight
     if (lane == 0 && r.inflight > 0) {
         int s = r.s;
@@ -443,7 +853,10 @@ struct lmc_step_prog {
     int nops, first_gemv, grid, stages, ring_off;
     size_t smem;
     StepCtl *ctl;
+    double *stats;
+    int stats_n;
 };
+constexpr int STATS_STRIDE = 4;  // doubles per slot: {sum, sum of squares} x 2 batch rows
 
 static std::vector<lmc_step_prog *> g_progs;  // live programs, for lmc_step_status
 static std::mutex g_progs_mu;
@@ -493,7 +906,16 @@ static size_t plan_gemv(const lmc_step_op *o, int grid, int stages, DOp *d) {
     a.pf = (int)std::min<long long>(64, PF_BYTES / ((long long)a.NC * WARPS * unit));
     d->g = a;
     d->qt = qt;
-    return gemv_smem(qt, a.KB, a.XL, a.maxrt);
+    // the latency form when a warp gets few units, x fits in shared memory as
+    // fp32, and a norm prologue has its statistics from the op that wrote x
+    // (LMC_STEP_FF=0: the tensor-core form everywhere; same results to fp32
+    // rounding)
+    const char *env = getenv("LMC_STEP_FF");
+    const long long per_warp = ((long long)(a.maxrt - 1) * a.KB + WARPS - 1) / WARPS;
+    const bool norm = a.pro == LMC_PRO_LAYERNORM || a.pro == LMC_PRO_RMSNORM;
+    d->ff = !(env && env[0] == '0') && per_warp <= 8 && (size_t)o->batch * a.KB * 1024 <= 64 * 1024 &&
+            (!norm || o->stats_in);
+    return d->ff ? fgemv_smem(a.KB, o->batch, a.maxrt) : gemv_smem(qt, a.KB, a.XL, a.maxrt);
 }
 
 static size_t plan_attn(const lmc_step_op *o, DOp *d) {
@@ -618,9 +1040,27 @@ extern "C" int lmc_step_prog_build(const lmc_step_op *ops, int n, lmc_step_prog 
     int first = -1;
     for (int i = n - 1, nxt = -1; i >= 0; i--) {
         d[i].next_gemv = nxt;
+        if (nxt >= 0) {
+            d[i].ng = d[nxt].g;
+            d[i].nqt = d[nxt].qt;
+        }
         if (d[i].kind == LMC_OP_GEMV) nxt = i;
         first = nxt;
     }
+    // the K/V rows an attention op reads are asked of L2 at the end of the
+    // GEMV two ops before it (one op before, when that is the first GEMV), so
+    // they arrive while other work runs
+    for (int i = 1; i < n; i++)
+        if (d[i].kind == LMC_OP_ATTN) {
+            const int j = i >= 2 && d[i - 2].kind == LMC_OP_GEMV ? i - 2 : d[i - 1].kind == LMC_OP_GEMV ? i - 1 : -1;
+            if (j < 0) continue;
+            const AttnArgs &at = d[i].at;
+            d[j].kpf = 1;
+            d[j].kp = KvPf{(const uint8_t *)at.k_cache, (const uint8_t *)at.v_cache, at.pos, at.Hkv, at.S,
+                           at.Dh * (d[i].kv ? 2 : 4), d[i].nb};
+        }
+    int slots = 0;
+    for (int i = 0; i < n; i++) slots = std::max(slots, std::max(ops[i].stats_in, ops[i].stats_out));
     lmc_step_prog *p = (lmc_step_prog *)calloc(1, sizeof(lmc_step_prog));
     if (!p) return lmc_set_error(LMC_ERR_OOM, "step_prog: host");
     p->nops = n;
@@ -629,8 +1069,25 @@ extern "C" int lmc_step_prog_build(const lmc_step_op *ops, int n, lmc_step_prog 
     p->stages = stages;
     p->ring_off = (int)below;
     p->smem = smem;
+    p->stats_n = slots * STATS_STRIDE;
     cudaError_t e = cudaMalloc((void **)&p->d_ops, sizeof(DOp) * n);
     if (e == cudaSuccess) e = cudaMalloc((void **)&p->ctl, sizeof(StepCtl));
+    if (e == cudaSuccess && slots) e = cudaMalloc((void **)&p->stats, sizeof(double) * p->stats_n);
+    if (e == cudaSuccess && slots) e = cudaMemset(p->stats, 0, sizeof(double) * p->stats_n);
+    if (e == cudaSuccess && slots)
+        for (int i = 0; i < n; i++) {
+            double *in = ops[i].stats_in ? p->stats + (size_t)(ops[i].stats_in - 1) * STATS_STRIDE : nullptr;
+            double *out = ops[i].stats_out ? p->stats + (size_t)(ops[i].stats_out - 1) * STATS_STRIDE : nullptr;
+            if (d[i].kind == LMC_OP_GEMV) {
+                d[i].g.stats = in;
+                d[i].g.stats_out = out;
+            } else if (d[i].kind == LMC_OP_EMBED) {
+                d[i].e.stats_out = out;
+            }
+        }
+    // the copies of the next GEMV's arguments pick up its statistics pointers
+    for (int i = 0; i < n; i++)
+        if (d[i].next_gemv >= 0) d[i].ng = d[d[i].next_gemv].g;
     if (e == cudaSuccess) e = cudaMemcpy(p->d_ops, d.data(), sizeof(DOp) * n, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(p->ctl, 0, sizeof(StepCtl));
     if (e != cudaSuccess) {
@@ -654,6 +1111,8 @@ extern "C" int lmc_step_prog_launch(const lmc_step_prog *p, cudaStream_t s) {
     P.ring_off = p->ring_off;
     P.stages = p->stages;
     P.ctl = p->ctl;
+    P.stats = p->stats;
+    P.stats_n = p->stats_n;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p->grid);
     cfg.blockDim = dim3(NTHR);
@@ -680,6 +1139,7 @@ extern "C" void lmc_step_prog_free(lmc_step_prog *p) {
         }
     if (p->d_ops) cudaFree(p->d_ops);
     if (p->ctl) cudaFree(p->ctl);
+    if (p->stats) cudaFree(p->stats);
     free(p);
 }
 
@@ -698,8 +1158,9 @@ extern "C" int lmc_step_status(void) {
         StepCtl c;
         if (cudaMemcpy(&c, p->ctl, sizeof c, cudaMemcpyDeviceToHost) != cudaSuccess)
             return lmc_set_error(LMC_ERR_CUDA, "step_status: read barrier state");
-        if (c.abort) {
+        if (c.abort) {  // the launch left its barrier counters and statistics mid-way
             cudaMemset(p->ctl, 0, sizeof(StepCtl));
+            if (p->stats) cudaMemset(p->stats, 0, sizeof(double) * p->stats_n);
             rc = lmc_set_error(LMC_ERR_TIMEOUT, "persistent step: a grid barrier wait ran out (op %d)", c.where - 1);
         }
     }

@@ -56,6 +56,11 @@ struct TArgs {
     float eps;
     unsigned long long *keys;  // non-NULL: greedy-pick key per batch row (argmax epilogue)
     int key_base;              // global index of row 0 in the keys
+    // Norm statistics of x supplied by whoever wrote x (the persistent step):
+    // per batch row {sum x, sum x^2} in fp64, or NULL (build_x computes them)
+    const double *stats;
+    // non-NULL: the epilogue adds {sum y, sum y^2} of its final outputs here
+    double *stats_out;
     int XL;      // B-fragment lanes stored per chunk: 12 per batch row (3 limbs x 4), 24 for two
     int CL;      // CTAs per cluster
     int NC;      // clusters; cluster c owns row tiles [c*RT/NC, (c+1)*RT/NC)
@@ -169,7 +174,24 @@ __device__ __forceinline__ void build_x(uint8_t *smem, const Smem<NT, QT> &L, co
     const int tid = threadIdx.x;
     const int K = a.KB * 256, nb = a.nb;
     const XView<CG> xv{a.x, a.x2, a.pw, a.pb, a.ldx, a.pro, mean, rstd};
-    if (a.pro == LMC_PRO_LAYERNORM || a.pro == LMC_PRO_RMSNORM) {  // per-row statistics
+    if ((a.pro == LMC_PRO_LAYERNORM || a.pro == LMC_PRO_RMSNORM) && a.stats) {
+        // statistics accumulated in fp64 by the ops that wrote x: mean and
+        // variance (E x^2 - mean^2; the two-pass float form of src/ops.c:52-54
+        // agrees to ~1e-7 relative), or the mean square for RMSNorm
+        if (tid < NB) {
+#pragma unroll
+            for (int b = 0; b < NB; b++)
+                if (tid == b) {
+                    const double sx = b < nb ? __ldcg(a.stats + 2 * b) : 0.0;
+                    const double sq = b < nb ? __ldcg(a.stats + 2 * b + 1) : 0.0;
+                    const double mu = a.pro == LMC_PRO_RMSNORM ? 0.0 : sx / (double)K;
+                    const double var = fmax(sq / (double)K - mu * mu, 0.0);
+                    mean[b] = (float)mu;
+                    rstd[b] = 1.0f / sqrtf((float)var + (a.pro == LMC_PRO_RMSNORM ? a.eps : 1e-5f));
+                }
+        }
+        __syncthreads();
+    } else if (a.pro == LMC_PRO_LAYERNORM || a.pro == LMC_PRO_RMSNORM) {  // per-row statistics
         float s[NB];
 #pragma unroll
         for (int b = 0; b < NB; b++) s[b] = 0.0f;

@@ -772,7 +772,12 @@ static int build_prog(lmc_model *m, int B, int gen, int n_prompt, int n_new, lmc
     e->tok = m->d_tok;
     e->pos = m->d_pos;
     e->y = m->x;
+    /* norm statistics: slot 1 = x after the embedding, 2 + 2l = x after layer
+     * l's attention output, 3 + 2l = x after layer l's FFN (see lmc_step_op) */
+    e->stats_out = 1;
     for (int l = 0; l < c->n_layers && !rc; l++) {
+        const int s_in = l == 0 ? 1 : 3 + 2 * (l - 1), s_mid = 2 + 2 * l, s_out = 3 + 2 * l;
+        const int n0 = n;
         const Layer *w = &m->layers[l];
         char *kc = (char *)m->kc + esz * m->kv_layer_elems * l, *vc = (char *)m->vc + esz * m->kv_layer_elems * l;
         if (c->arch == 1) { /* src/ops.c:182-206 */
@@ -802,6 +807,11 @@ static int build_prog(lmc_model *m, int B, int gen, int n_prompt, int n_new, lmc
             add_gemv(ops, &n, B, w->down, m->h, 2 * F, NULL, m->x, D, LMC_EPI_ACCUM, LMC_PRO_SWIGLU, NULL, NULL, 0.0f,
                      m->h + F);
         }
+        /* this layer's five ops: norm-in, attention, residual, norm-in, residual */
+        ops[n0].stats_in = s_in;
+        ops[n0 + 2].stats_out = s_mid;
+        ops[n0 + 3].stats_in = s_mid;
+        ops[n0 + 4].stats_out = s_out;
     }
     if (!rc) {
         if (c->arch == 1)
@@ -812,6 +822,7 @@ static int build_prog(lmc_model *m, int B, int gen, int n_prompt, int n_new, lmc
                      NULL, c->norm_eps, NULL);
         ops[n - 1].ex.keys = m->d_keys;
         ops[n - 1].ex.key_base = m->v0;
+        ops[n - 1].stats_in = 3 + 2 * (c->n_layers - 1);
         if (gen && m->smp) { /* the top-p draw replaces the greedy pick */
             lmc_step_op *sp = add_op(ops, &n, LMC_OP_SAMPLE, B);
             sp->y = m->logits;
