@@ -124,36 +124,32 @@ def test_device_sampler_ties_and_edges(cuda, orc):
 @pytest.mark.parametrize("use_graph", [True, False])
 def test_generate_sample_matches_oracle(cuda, orc, model_dir, kind, kw, use_graph):
     """lmc_model_generate_sample against the oracle's forward + sampler loop
-    (LMc's generate with --temp 0.8 --top-p 0.9): identical tokens up to the
-    first draw that lies within 1e-5 of a boundary (none, in practice)."""
+    (LMc's generate with --temp 0.8 --top-p 0.9): every draw that lies more
+    than 1e-5 from a cdf boundary picks the oracle's token; where a draw is
+    that close, the oracle continues from the device's token."""
     path = synth.cached_model(kind, model_dir, **kw)
     prompt = np.random.default_rng(2).integers(0, kw["V"], 6).astype(np.int32)
     T, P, seed, n_new = 0.8, 0.9, 4242, 24
-    want = []
-    for b in range(2):
-        om = orc.model(path)
-        lg = None
-        for pos, t in enumerate(prompt):
-            lg = om.forward(int(t), pos)
-        st = rt.lib().lmc_rng_seed(seed + b)
-        ids, pos = [], len(prompt)
-        for _ in range(n_new):
-            tok, st, margin = orc.sample_top_p(lg, T, P, st)
-            ids.append(tok if margin >= MARGIN else None)
-            if margin < MARGIN:
-                break
-            lg = om.forward(tok, pos)
-            pos += 1
-        want.append(ids)
     m = rt.Model(path, max_batch=2)
     out = np.empty((2, n_new), np.int32)
     p2 = np.ascontiguousarray(np.stack([prompt, prompt]))
     rt.call("lmc_model_generate_sample", m.h, p2.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), len(prompt), 2, n_new,
             T, P, seed, int(use_graph), out.ctypes.data_as(ctypes.POINTER(ctypes.c_int)))
     for b in range(2):
-        n = len(want[b]) if want[b][-1] is not None else len(want[b]) - 1
-        assert out[b, :n].tolist() == want[b][:n]
-        assert n >= 8
+        om = orc.model(path)
+        lg = None
+        for pos, t in enumerate(prompt):
+            lg = om.forward(int(t), pos)
+        st = rt.lib().lmc_rng_seed(seed + b)
+        pos, compared = len(prompt), 0
+        for i in range(n_new):
+            tok, st, margin = orc.sample_top_p(lg, T, P, st)
+            if margin >= MARGIN:
+                assert int(out[b, i]) == tok, (b, i)
+                compared += 1
+            lg = om.forward(int(out[b, i]), pos)
+            pos += 1
+        assert compared >= n_new // 2
     # temperature 0 is the greedy loop
     g = m.generate(p2, n_new, use_graph=use_graph)
     rt.call("lmc_model_generate_sample", m.h, p2.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), len(prompt), 2, n_new,
