@@ -57,6 +57,19 @@ const char *lmc_last_error(void);
  * spin-wait in the kernels has an iteration limit instead of hanging. */
 int lmc_device_status(void);
 
+/* Limit of every bounded wait inside the kernels - the bulk-copy rings of
+ * the GEMV and GEMM, the grid barriers of the persistent decode step - in
+ * nanoseconds; 0 restores the default of one second.  A wait that runs out
+ * records a timeout that lmc_device_status reports; the kernel drains its
+ * own copies and returns, and the context stays usable.  No counterpart in
+ * LMc (a CPU program has no device waits). */
+int lmc_set_wait_limit(long long ns);
+/* Self-test of that failure path: runs a device wait that nothing can
+ * complete - which = 0: a GEMV ring's mbarrier wait, 1: a persistent-step
+ * grid barrier (two CTAs) - under the current limit.  Returns LMC_ERR_TIMEOUT
+ * when the wait ran out as designed (and clears the recorded timeout). */
+int lmc_wait_selftest(int which);
+
 /* Select and initialise CUDA device `device` for the calling thread.
  * Fails with LMC_ERR_CUDA when no sm_100 device is present. */
 int lmc_init(int device);

@@ -29,6 +29,35 @@ extern "C" int lmc_pdl_enabled(void) {
     return flag;
 }
 
+extern "C" int lmc_set_wait_limit(long long ns) {
+    if (ns < 0) return lmc_set_error(LMC_ERR_INVALID, "set_wait_limit: %lld", ns);
+    int rc = lmc_tiled_set_wait_limit(ns);
+    if (!rc) rc = lmc_step_set_wait_limit(ns);
+    if (!rc) rc = lmc_gemm_set_wait_limit(ns);
+    return rc;
+}
+
+extern "C" int lmc_wait_selftest(int which) {
+    if (which != 0 && which != 1) return lmc_set_error(LMC_ERR_INVALID, "wait_selftest: %d", which);
+    int *d = NULL;
+    LMC_CUDA_TRY(cudaMalloc((void **)&d, sizeof(int)));
+    LMC_CUDA_TRY(cudaMemset(d, 0, sizeof(int)));
+    int rc;
+    if (which == 0) {
+        rc = lmc_tiled_wait_selftest(d, 0);
+        if (!rc && cudaDeviceSynchronize() != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "wait self-test sync");
+        int gave_up = 0;
+        if (!rc && cudaMemcpy(&gave_up, d, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = lmc_set_error(LMC_ERR_CUDA, "wait self-test read");
+        if (!rc) rc = lmc_device_status(); /* reports (and clears) the recorded timeout */
+        if (rc == LMC_OK && gave_up) rc = lmc_set_error(LMC_ERR_CUDA, "wait self-test: timeout not recorded");
+    } else {
+        rc = lmc_step_barrier_selftest(d, 0);
+    }
+    cudaFree(d);
+    return rc;
+}
+
 extern "C" int lmc_init(int device) {
     int n = 0;
     cudaError_t e = cudaGetDeviceCount(&n);

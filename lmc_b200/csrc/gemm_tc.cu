@@ -68,10 +68,19 @@ __device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// bounded: about one second, then the flag is set and the caller goes on
+// Limit of every bounded wait below (nanoseconds of %globaltimer).
+__device__ long long g_gemm_wait_ns = 1000000000ll;
+// bounded: about one second (g_gemm_wait_ns), then the flag is set and the caller goes on
 __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t t = 0; t < (1u << 14); t++)
+    if (bar_try(bar, parity)) return true;
+    long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
         if (bar_try(bar, parity)) return true;
+        long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > g_gemm_wait_ns) break;
+    }
     atomicExch(&g_gemm_timeout, 1);
     return false;
 }
@@ -1026,6 +1035,12 @@ extern "C" int lmc_gemm_reserve(int N, int K, cudaStream_t s) {
     LMC_CUDA_TRY(cudaMalloc(&g_xinv, (size_t)N * sizeof(float)));
     g_x_cap = need;
     g_xinv_cap = N;
+    return LMC_OK;
+}
+
+extern "C" int lmc_gemm_set_wait_limit(long long ns) {
+    const long long v = ns > 0 ? ns : 1000000000ll;
+    LMC_CUDA_TRY(cudaMemcpyToSymbol(g_gemm_wait_ns, &v, sizeof v));
     return LMC_OK;
 }
 

@@ -176,6 +176,12 @@ int lmc_step_status(void);
  * persistent step's barriers (nanoseconds; 0 restores the default). */
 int lmc_tiled_set_wait_limit(long long ns);
 int lmc_step_set_wait_limit(long long ns);
+int lmc_gemm_set_wait_limit(long long ns);
+/* Self-tests of the bounded waits: a wait on an mbarrier that nothing
+ * completes (the GEMV's wait; *d_flag = 1 when it gave up), and a grid
+ * barrier that can never complete (LMC_ERR_TIMEOUT when every CTA left). */
+int lmc_tiled_wait_selftest(int *d_flag, cudaStream_t s);
+int lmc_step_barrier_selftest(int *d_left, cudaStream_t s);
 
 #ifdef __cplusplus
 }

@@ -843,6 +843,18 @@ __global__ void __launch_bounds__(NTHR, 2) k_step(StepParams P) {
     }
 }
 
+// Failure-path self-test of the grid barrier: the counters' base is set so
+// that the first barrier can never complete (a count nothing reaches); every
+// CTA gives up after the wait limit, raises the abort flag and returns.
+__global__ void k_barrier_selftest(StepCtl *ctl, int *left) {
+    __shared__ int sh_ok;
+    __shared__ unsigned base[BAR_GROUPS];
+    if (threadIdx.x < BAR_GROUPS) base[threadIdx.x] = 0x40000000u;
+    __syncthreads();
+    const bool ok = grid_sync(ctl, base, 1, 0, &sh_ok, nullptr, nullptr);
+    if (threadIdx.x == 0 && !ok) atomicAdd(left, 1);
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -1172,4 +1184,20 @@ extern "C" int lmc_step_set_wait_limit(long long ns) {
     LMC_CUDA_TRY(cudaMemcpyToSymbol(g_step_wait_ns, &v, sizeof v));
     LMC_CUDA_TRY(cudaMemcpyToSymbol(g_wait_ns, &v, sizeof v));
     return LMC_OK;
+}
+
+extern "C" int lmc_step_barrier_selftest(int *d_left, cudaStream_t s) {
+    StepCtl *ctl = NULL;
+    LMC_CUDA_TRY(cudaMalloc((void **)&ctl, sizeof(StepCtl)));
+    cudaError_t e = cudaMemset(ctl, 0, sizeof(StepCtl));
+    if (e == cudaSuccess) {
+        void *args[2] = {&ctl, &d_left};
+        e = cudaLaunchCooperativeKernel((const void *)k_barrier_selftest, dim3(2), dim3(NTHR), args, 0, s);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    StepCtl c;
+    if (e == cudaSuccess) e = cudaMemcpy(&c, ctl, sizeof c, cudaMemcpyDeviceToHost);
+    cudaFree(ctl);
+    if (e != cudaSuccess) return lmc_set_error(LMC_ERR_CUDA, "barrier self-test: %s", cudaGetErrorString(e));
+    return c.abort ? lmc_set_error(LMC_ERR_TIMEOUT, "grid barrier wait ran out (self-test)") : LMC_OK;
 }

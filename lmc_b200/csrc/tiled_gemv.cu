@@ -320,6 +320,23 @@ extern "C" int lmc_device_status(void) {
                          v ? "bulk copy not completed" : "tensor-core MMA not completed");
 }
 
+// Failure-path self-test: one thread waits (bounded) on an mbarrier phase
+// that nothing completes, so the wait runs out, records the timeout and the
+// kernel returns normally.
+__global__ void k_wait_selftest(int *gave_up) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x) return;
+    mbar_init(&bar);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    *gave_up = mbar_wait(&bar, 0u) ? 0 : 1;
+}
+
+extern "C" int lmc_tiled_wait_selftest(int *d_flag, cudaStream_t s) {
+    k_wait_selftest<<<1, 32, 0, s>>>(d_flag);
+    LMC_LAUNCH_CHECK("wait self-test");
+    return LMC_OK;
+}
+
 extern "C" int lmc_tiled_set_wait_limit(long long ns) {
     const long long v = ns > 0 ? ns : 1000000000ll;
     LMC_CUDA_TRY(cudaMemcpyToSymbol(g_wait_ns, &v, sizeof v));

@@ -15,6 +15,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include <nccl.h>
 
@@ -467,7 +468,7 @@ int lmc_nccl_unique_id(void *id) {
     if (!id) return lmc_set_error(LMC_ERR_INVALID, "nccl_unique_id: null");
     ncclUniqueId u;
     ncclResult_t r = ncclGetUniqueId(&u);
-    if (r != ncclSuccess) return lmc_set_error(LMC_ERR_CUDA, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+    if (r != ncclSuccess) return lmc_set_error(LMC_ERR_NCCL, "ncclGetUniqueId: %s", ncclGetErrorString(r));
     memcpy(id, &u, sizeof u);
     return LMC_OK;
 }
@@ -492,7 +493,7 @@ static int model_load(const char *path, int max_batch, int max_rows, int kv_dtyp
         ncclUniqueId u;
         memcpy(&u, nccl_id, sizeof u);
         ncclResult_t r = ncclCommInitRank(&m->comm, tp_size, u, tp_rank);
-        if (r != ncclSuccess) { m->comm = NULL; rc = lmc_set_error(LMC_ERR_CUDA, "ncclCommInitRank: %s", ncclGetErrorString(r)); }
+        if (r != ncclSuccess) { m->comm = NULL; rc = lmc_set_error(LMC_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r)); }
     }
     if (!rc && cudaDeviceSynchronize() != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "load sync");
     if (rc) {
@@ -593,13 +594,52 @@ static int norm_matmul(lmc_model *m, const lmc_qtensor *W, int pro, const float 
     return norm_matmul_in(m, m->x, W, pro, nw, nb, eps, bias, y, ldy, B, epi, keys);
 }
 
+/* Waits for the model's stream.  In a tensor-parallel group a step's NCCL
+ * kernels wait for every rank, so a rank that left or failed would stall the
+ * stream for good: the wait polls the stream, checks NCCL's asynchronous
+ * error between polls, and on an error, or after LMC_NCCL_WAIT_S seconds
+ * (default 300), aborts the communicator (which ends its kernels) and
+ * returns LMC_ERR_NCCL or LMC_ERR_TIMEOUT.  The model then has no
+ * communicator and its tensor-parallel calls fail. */
+static int model_sync(lmc_model *m) {
+    if (m->tp_size <= 1 || !m->comm) {
+        CUTRY(cudaStreamSynchronize(m->stream));
+        return LMC_OK;
+    }
+    const char *e = getenv("LMC_NCCL_WAIT_S");
+    const double limit = e && atof(e) > 0 ? atof(e) : 300.0;
+    struct timespec t0, t, nap = {0, 50000};
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(m->stream);
+        if (q == cudaSuccess) return LMC_OK;
+        if (q != cudaErrorNotReady) return lmc_set_error(LMC_ERR_CUDA, "stream: %s", cudaGetErrorString(q));
+        ncclResult_t ae = ncclSuccess;
+        if (ncclCommGetAsyncError(m->comm, &ae) == ncclSuccess && ae != ncclSuccess && ae != ncclInProgress) {
+            ncclCommAbort(m->comm);
+            m->comm = NULL;
+            return lmc_set_error(LMC_ERR_NCCL, "NCCL error in a step: %s (communicator aborted)",
+                                 ncclGetErrorString(ae));
+        }
+        clock_gettime(CLOCK_MONOTONIC, &t);
+        if ((double)(t.tv_sec - t0.tv_sec) + 1e-9 * (double)(t.tv_nsec - t0.tv_nsec) > limit) {
+            ncclCommAbort(m->comm);
+            m->comm = NULL;
+            return lmc_set_error(LMC_ERR_TIMEOUT, "a step's collectives did not finish in %.0f s "
+                                 "(a rank left?); communicator aborted", limit);
+        }
+        nanosleep(&nap, NULL);
+    }
+}
+
 /* Sum of the ranks' partial x (tensor parallel): rank 0 added its partial to
  * the residual, the others wrote theirs over it, so the in-place sum is the
  * next residual on every rank. */
 static int tp_sum_x(lmc_model *m, int B) {
     if (m->tp_size <= 1) return LMC_OK;
+    if (!m->comm) return lmc_set_error(LMC_ERR_NCCL, "the tensor-parallel communicator was aborted");
     ncclResult_t r = ncclAllReduce(m->x, m->x, (size_t)B * m->cfg.embed_dim, ncclFloat32, ncclSum, m->comm, m->stream);
-    return r == ncclSuccess ? LMC_OK : lmc_set_error(LMC_ERR_CUDA, "ncclAllReduce: %s", ncclGetErrorString(r));
+    return r == ncclSuccess ? LMC_OK : lmc_set_error(LMC_ERR_NCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
 }
 
 /* One decode step for B sequences: tokens d_tok, positions d_pos -> logits
@@ -683,8 +723,9 @@ static int step(lmc_model *m, int B) {
         TRY(norm_matmul_in(m, xl, m->lm_head, LMC_PRO_RMSNORM, m->rmsf, NULL, c->norm_eps, NULL, m->logits, m->vl, BL,
                            LMC_EPI_NONE, m->d_keys));
     if (m->tp_size > 1) { /* greedy pick over the vocabulary shards: max of the 64-bit keys */
+        if (!m->comm) return lmc_set_error(LMC_ERR_NCCL, "the tensor-parallel communicator was aborted");
         ncclResult_t r = ncclAllReduce(m->d_keys, m->d_keys, (size_t)BL, ncclUint64, ncclMax, m->comm, m->stream);
-        if (r != ncclSuccess) return lmc_set_error(LMC_ERR_CUDA, "ncclAllReduce(keys): %s", ncclGetErrorString(r));
+        if (r != ncclSuccess) return lmc_set_error(LMC_ERR_NCCL, "ncclAllReduce(keys): %s", ncclGetErrorString(r));
     }
     return LMC_OK;
 }
@@ -882,7 +923,7 @@ int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B
         CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * (size_t)B * m->vl, cudaMemcpyDeviceToHost,
                               m->stream));
     CUTRY(cudaMemcpyAsync(m->h_stage + 2 * B, m->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, m->stream));
-    CUTRY(cudaStreamSynchronize(m->stream));
+    TRY(model_sync(m));
     if (h_next) memcpy(h_next, m->h_stage + 2 * B, sizeof(int) * B);
     return LMC_OK;
 }
@@ -909,7 +950,7 @@ static int prefill_chunks(lmc_model *m, int seq, const int *h_tokens, int n, int
         rc = step(m, c);
         m->prefill = m->prefill_head = 0;
         /* the staging buffer is rewritten for the next chunk */
-        if (!rc && cudaStreamSynchronize(s) != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "model_prefill: sync");
+        if (!rc) rc = model_sync(m);
     }
     return rc;
 }
@@ -927,7 +968,7 @@ int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int sta
     TRY(lmc_keys_to_ids_launch(m->d_keys, m->d_next, 1, s));
     if (h_logits) CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * m->vl, cudaMemcpyDeviceToHost, s));
     CUTRY(cudaMemcpyAsync(m->h_stage, m->d_next, sizeof(int), cudaMemcpyDeviceToHost, s));
-    CUTRY(cudaStreamSynchronize(s));
+    TRY(model_sync(m));
     if (h_next) *h_next = m->h_stage[0];
     return LMC_OK;
 }
@@ -1082,7 +1123,7 @@ static int generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, int 
     /* the last greedy pick needs no forward of its own: take it from the
      * last step's argmax (the advance kernel recorded it as well) */
     CUTRY(cudaMemcpyAsync(h_out_ids, m->d_ids, sizeof(int) * (size_t)B * n_new, cudaMemcpyDeviceToHost, s));
-    CUTRY(cudaStreamSynchronize(s));
+    TRY(model_sync(m));
     return LMC_OK;
 }
 

@@ -65,6 +65,8 @@ SIGNATURES = {
     "lmc_sample_top_p": ([_vp, _i, _i, _f, _f, _vp, _vp, _vp], _i),
     "lmc_rng_seed": ([_c.c_uint64], _c.c_uint64),
     "lmc_model_generate_sample": ([_vp, _ip, _i, _i, _i, _f, _f, _c.c_uint64, _i, _ip], _i),
+    "lmc_set_wait_limit": ([_c.c_longlong], _i),
+    "lmc_wait_selftest": ([_i], _i),
 }
 
 

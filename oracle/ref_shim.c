@@ -73,13 +73,30 @@ int refshim_dequant(uint32_t type, const uint8_t *src, float *dst, size_t n) {
 
 /* load_model (gguf.c:422) + init_kv_cache + init_activations
  * (models.c:122-164), with LMc's [INFO] chatter on stdout silenced. */
+/* LMc's own cleanup (lmc.c:320-324), so a process can load one model
+ * after another without keeping the previous arena. */
+static int g_loaded = 0;
+void refshim_free(void) {
+    if (!g_loaded) return;
+    arena_free();
+    free(g_weights.layers);
+    g_weights.layers = NULL;
+    free(g_kv_cache.k_cache);
+    free(g_kv_cache.v_cache);
+    g_kv_cache.k_cache = g_kv_cache.v_cache = NULL;
+    free_activations();
+    g_loaded = 0;
+}
+
 int refshim_load(const char *path) {
+    refshim_free();
     fflush(stdout);
     int saved = dup(1), devnull = open("/dev/null", O_WRONLY);
     if (devnull >= 0) dup2(devnull, 1);
     load_model(path);
     init_kv_cache();
     init_activations();
+    g_loaded = 1;
     fflush(stdout);
     if (saved >= 0) { dup2(saved, 1); close(saved); }
     if (devnull >= 0) close(devnull);

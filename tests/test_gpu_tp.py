@@ -74,3 +74,60 @@ def test_tp2_matches_oracle(cuda, orc, model_dir):
                 assert rel_err(lg[pos, b], want_lg[b][pos, v0:v0 + vl]) < 1e-3
             assert ids[b].tolist() == want_ids[b]
     assert res[0][1] == 0 and res[0][2] + res[1][2] == KW["V"]
+
+
+# The Llama-8B width (4096, 32 / 8 heads, FFN 14336, vocab 128256) with two
+# layers, sharded over 2, 4 and 8 GPUs: each rank's vocabulary slice of the
+# teacher-forced logits within 1e-3 of LMc's own (oracle/_ref), and the
+# group's greedy pick equal to the argmax of LMc's logits.
+W8B = dict(L=2, D=4096, H=32, Hkv=8, F=14336, S=256, V=128256, blocks="random", seed=8)
+
+
+def _rank_logits(rank, world, path, nid, toks, q):
+    try:
+        import torch
+        torch.cuda.set_device(rank)
+        rt.init(rank)
+        m = rt.Model(path, max_batch=1, tp=(rank, world, nid))
+        out = []
+        for pos, t in enumerate(toks):
+            lg, nxt = m.forward([int(t)], [pos])
+            out.append((lg[0], int(nxt[0])))
+        q.put((rank, m.vocab_begin, m.vocab_rows, out, None))
+        m.close()
+    except Exception as e:
+        q.put((rank, 0, 0, None, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_8b_width_vs_lmc(cuda, model_dir, world):
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from oracle import Ref
+    path = synth.cached_model("llama", model_dir, **W8B)
+    toks = np.random.default_rng(3).integers(0, W8B["V"], 3)
+    ref = Ref()
+    ref.load(path)
+    want = [ref.forward(int(t), pos) for pos, t in enumerate(toks)]
+    nid = rt.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_logits, args=(r, world, path, nid, toks, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=600) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+    covered = 0
+    for rank, v0, vl, out, err in res:
+        assert err is None, err
+        covered += vl
+        for pos, (lg, nxt) in enumerate(out):
+            assert rel_err(lg, want[pos][v0:v0 + vl]) < 1e-3
+            assert nxt == int(np.argmax(want[pos]))
+    assert covered == W8B["V"]
