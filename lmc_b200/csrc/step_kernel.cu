@@ -123,21 +123,26 @@ __device__ __forceinline__ unsigned group_size(int k) {
     return (gridDim.x + BAR_GROUPS - 1 - (unsigned)k) / BAR_GROUPS;
 }
 
-// Grid-wide barrier: thread 0 of each CTA adds its arrival to its group's
-// counter (after a fence, so the CTA's writes are visible); lanes 0..7 of
-// warp 0 poll one counter each until every group is complete, the abort flag
-// is set, or the wait limit passes (then they set the flag).  Meanwhile the
-// other warps copy the next op into `next_op` (the op list is constant).
-// Returns false when the CTA must leave.
-__device__ __forceinline__ bool grid_sync(StepCtl *ctl, const unsigned *base, unsigned passed, int where, int *sh_ok,
-                                          const DOp *next_src, DOp *next_op) {
+// Grid-wide barrier in two phases.  grid_arrive: once every thread of the
+// CTA is done with the op (bar.sync), thread 0 makes the CTA's writes
+// visible (fence) and adds its arrival to its group's counter.  Work that the
+// next op does not read (the next GEMV's weight copies, K/V prefetch) runs
+// between the phases.  grid_wait: lanes 0..7 of warp 0 poll one counter each
+// until every group is complete, the abort flag is set, or the wait limit
+// passes (then they set the flag); meanwhile the other warps copy the next op
+// into `next_op` (the op list is constant).  Returns false when the CTA must
+// leave.
+__device__ __forceinline__ void grid_arrive(StepCtl *ctl) {
     __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(&ctl->cnt[blockIdx.x % BAR_GROUPS].v, 1u);
+    }
+}
+__device__ __forceinline__ bool grid_wait(StepCtl *ctl, const unsigned *base, unsigned passed, int where, int *sh_ok,
+                                          const DOp *next_src, DOp *next_op) {
     const int lane = threadIdx.x & 31;
     if (threadIdx.x < 32) {
-        if (lane == 0) {
-            __threadfence();
-            atomicAdd(&ctl->cnt[blockIdx.x % BAR_GROUPS].v, 1u);
-        }
         const int k = lane < BAR_GROUPS ? lane : 0;
         const unsigned target = base[k] + passed * group_size(k);
         int ok = 1;
@@ -175,6 +180,11 @@ __device__ __forceinline__ bool grid_sync(StepCtl *ctl, const unsigned *base, un
     }
     __syncthreads();
     return *sh_ok != 0;
+}
+__device__ __forceinline__ bool grid_sync(StepCtl *ctl, const unsigned *base, unsigned passed, int where, int *sh_ok,
+                                          const DOp *next_src, DOp *next_op) {
+    grid_arrive(ctl);
+    return grid_wait(ctl, base, passed, where, sh_ok, next_src, next_op);
 }
 
 // Per-warp bulk-copy ring, carried across the GEMV ops of the step: the next
@@ -489,8 +499,12 @@ __host__ __device__ __forceinline__ size_t fgemv_smem(int KB, int nb, int maxrt)
 
 // One GEMV op (the body of k_gemv_tiled with clusters of one CTA): this CTA
 // owns row tiles [t0, t1) whole, so every tile is finished here.
+// Returns GEMV_OK when no ring wait ran out, plus GEMV_LATE when this warp
+// still has to start the next GEMV's weight copies (after the op's outputs
+// are out: the caller does it between the barrier's two phases).
+constexpr int GEMV_OK = 1, GEMV_LATE = 2;
 template <int QT, bool FF>
-__device__ __forceinline__ bool gemv_op(uint8_t *smem, const DOp &op, Ring &r, StepCtl *ctl) {
+__device__ __forceinline__ int gemv_op_impl(uint8_t *smem, const DOp &op, Ring &r, StepCtl *ctl) {
     constexpr int NB = 2, UNIT = unit_bytes(QT);
     const TArgs &a = op.g;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -596,10 +610,7 @@ __device__ __forceinline__ bool gemv_op(uint8_t *smem, const DOp &op, Ring &r, S
     } else if (op.next_gemv >= 0 && !late_prefill) {
         ring_prefill(r, op.ng, op.nqt, lane, wid);
     }
-    if (!mine) {
-        if (op.kpf) kv_prefetch(op.kp);
-        return ok;
-    }
+    if (!mine) return ok ? GEMV_OK : 0;
     __syncthreads();
     unsigned long long best[4] = {0ull, 0ull, 0ull, 0ull};
     double st[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
@@ -637,9 +648,7 @@ __device__ __forceinline__ bool gemv_op(uint8_t *smem, const DOp &op, Ring &r, S
             if (k) atomicMax(a.keys + threadIdx.x, k);
         }
     }
-    if (late_prefill) ring_prefill(r, op.ng, op.nqt, lane, wid);
-    if (op.kpf) kv_prefetch(op.kp);
-    return ok;
+    return (ok ? GEMV_OK : 0) | (late_prefill ? GEMV_LATE : 0);
 }
 
 // Attention work items (split, kv head, sequence), dealt round-robin to the
@@ -782,18 +791,20 @@ __global__ void __launch_bounds__(NTHR, 2) k_step(StepParams P) {
     bool alive = true;
     for (int i = 0; i < P.nops && alive; i++) {
         const DOp &op = ops[i & 1];
+        int gres = 0;
         switch (op.kind) {
         case LMC_OP_EMBED: embed_op(op.e, op.nb, sh_red); break;
         case LMC_OP_GEMV:
             if (op.ff) {
-                if (op.qt == 4) alive = gemv_op<4, true>(smem, op, r, ctl);
-                else if (op.qt == 6) alive = gemv_op<6, true>(smem, op, r, ctl);
-                else alive = gemv_op<8, true>(smem, op, r, ctl);
+                if (op.qt == 4) gres = gemv_op_impl<4, true>(smem, op, r, ctl);
+                else if (op.qt == 6) gres = gemv_op_impl<6, true>(smem, op, r, ctl);
+                else gres = gemv_op_impl<8, true>(smem, op, r, ctl);
             } else {
-                if (op.qt == 4) alive = gemv_op<4, false>(smem, op, r, ctl);
-                else if (op.qt == 6) alive = gemv_op<6, false>(smem, op, r, ctl);
-                else alive = gemv_op<8, false>(smem, op, r, ctl);
+                if (op.qt == 4) gres = gemv_op_impl<4, false>(smem, op, r, ctl);
+                else if (op.qt == 6) gres = gemv_op_impl<6, false>(smem, op, r, ctl);
+                else gres = gemv_op_impl<8, false>(smem, op, r, ctl);
             }
+            alive = (gres & GEMV_OK) != 0;
             break;
         case LMC_OP_ATTN:
             if (op.kv == 0) {
@@ -810,9 +821,14 @@ __global__ void __launch_bounds__(NTHR, 2) k_step(StepParams P) {
         const DOp *nsrc = i + 1 < P.nops ? P.ops + i + 1 : nullptr;
         if (op.sync) {
             // a ring wait that ran out in any warp of any CTA aborts the step
-            // here (grid_sync polls the flag)
+            // here (grid_wait polls the flag)
             passed++;
-            alive = grid_sync(ctl, sh_base, passed, i, &sh_ok, nsrc, &ops[(i + 1) & 1]) && alive;
+            grid_arrive(ctl);
+            // in the barrier's shadow: the next GEMV's first weight copies for
+            // warps that had units here, and the K/V rows of a coming attention
+            if (gres & GEMV_LATE) ring_prefill(r, op.ng, op.nqt, lane, wid);
+            if (op.kind == LMC_OP_GEMV && op.kpf) kv_prefetch(op.kp);
+            alive = grid_wait(ctl, sh_base, passed, i, &sh_ok, nsrc, &ops[(i + 1) & 1]) && alive;
         } else {
             __syncthreads();
             if (nsrc) {

@@ -81,3 +81,30 @@ def test_persistent_matches_kernel_by_kernel(cuda, model_dir, monkeypatch):
     lg2, _ = m2.forward([3], [30])
     assert a.tolist() == b.tolist()
     assert rel_err(lg1, lg2) < 1e-5
+
+
+def test_persistent_forced_on_wide_model(cuda, model_dir, monkeypatch):
+    """Models above the size where the kernel-by-kernel path is the default
+    still run the persistent step when it is asked for (LMC_PERSISTENT=1):
+    the TinyLlama width (2048, 32 / 4 heads, FFN 5632, vocab 32000), two
+    layers, tensor-core GEMVs on the long rows: the same logits and ids as
+    the kernel-by-kernel step."""
+    kw = dict(L=2, D=2048, H=32, Hkv=4, F=5632, S=256, V=32000, blocks="random", seed=13)
+    path = synth.cached_model("llama", model_dir, **kw)
+    toks = np.random.default_rng(6).integers(0, kw["V"], 5)
+    monkeypatch.setenv("LMC_PERSISTENT", "0")
+    m0 = rt.Model(path, max_batch=1)
+    want = [m0.forward([int(t)], [pos])[0][0] for pos, t in enumerate(toks)]
+    m0.close()
+    monkeypatch.setenv("LMC_PERSISTENT", "1")
+    m1 = rt.Model(path, max_batch=1)
+    for pos, t in enumerate(toks):
+        got, nxt = m1.forward([int(t)], [pos])
+        assert rel_err(got[0], want[pos]) < 1e-3
+        assert nxt[0] == int(np.argmax(want[pos]))
+    prompt = toks[:4].astype(np.int32)
+    a = m1.generate(prompt[None], 12, use_graph=True)
+    assert m1.graph_kernels() == 1
+    monkeypatch.setenv("LMC_PERSISTENT", "0")
+    m2 = rt.Model(path, max_batch=1)
+    assert m2.generate(prompt[None], 12, use_graph=True).tolist() == a.tolist()
