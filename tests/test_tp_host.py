@@ -69,3 +69,59 @@ def test_shard_plan_8_ranks_block_aligned():
         assert p["o_cols"][0] % 256 == 0 and p["o_cols"][1] % 256 == 0
         assert p["down_cols"][0] % 256 == 0 and p["down_cols"][1] % 256 == 0
     _cover([tp.shard_plan(CFG, r, 8)["vocab_rows"] for r in range(8)], CFG.vocab_size)
+
+
+def _failing_worker(rank, world, port, q, mode):
+    """Rank 1 fails on the host: it raises before the id exchange
+    ("raise"), or exits after one step without a word ("leave").  Rank 0
+    must end with an error from the process group's short timeout, not
+    hang."""
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 1 and mode == "raise":
+        q.put((rank, "raised"))
+        raise SystemExit(3)
+    t0 = time.time()
+    try:
+        tp.exchange_id(dist, lambda: os.urandom(128))
+        x = torch.ones(4)
+        dist.all_reduce(x)  # step 1: every rank takes part
+        if rank == 1:
+            _put_and_exit(q, (rank, "left"))  # leaves between steps, no collective in flight
+        time.sleep(0.5)
+        dist.all_reduce(x)  # step 2: the peer is gone
+        _put_and_exit(q, (rank, "no error"))
+    except Exception as e:  # the bounded collective ends with an error
+        _put_and_exit(q, (rank, f"error after {time.time() - t0:.1f}s: {type(e).__name__}"))
+
+
+def _put_and_exit(q, msg):
+    q.put(msg)
+    q.close()
+    q.join_thread()  # the message is in the pipe before the process ends
+    os._exit(0)
+
+
+def test_rank_failure_ends_peers_with_error():
+    import pytest
+    ctx = mp.get_context("spawn")
+    for mode in ("raise", "leave"):
+        q = ctx.Queue()
+        port = _free_port()
+        procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q, mode)) for r in range(2)]
+        for p in procs:
+            p.start()
+        res = dict(q.get(timeout=120) for _ in range(2))
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+                pytest.fail(f"{mode}: a rank hung")
+        assert res[1] in ("raised", "left")
+        assert res[0].startswith("error after"), (mode, res[0])
+        assert float(res[0].split()[2].rstrip("s:")) < 60
