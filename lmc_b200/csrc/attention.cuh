@@ -75,10 +75,12 @@ template <int NV> __device__ __forceinline__ void kv_chunk_f16(const uint4 (&raw
 constexpr int ATT_GROUP = 8;  // query heads per pass
 
 // RBMAX: K bytes loaded per block of the scores loop (registers: RBMAX / 4).
+// ch: positions per split when the caller coarsened the plan (0: a.CH);
+// single: this is the only split holding positions (the output is final).
 template <typename KV, int DH, int NTH = ATT_THREADS, int RBMAX = 256>
 __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp, int kh, int b, int pos, int t0, int t1,
-                                           float *wsb, size_t hstride) {
-    const int G = a.H / a.Hkv, Dh = DH ? DH : a.Dh, CH = a.CH;
+                                           float *wsb, size_t hstride, int ch = 0, bool single = false) {
+    const int G = a.H / a.Hkv, Dh = DH ? DH : a.Dh, CH = ch ? ch : a.CH;
     constexpr int ESZ = (int)sizeof(KV);
     constexpr int RB = DH ? (DH * ESZ < RBMAX ? DH * ESZ : RBMAX) : 128;  // K bytes per load block
     constexpr int NV = RB / 16, NC = RB / (8 * ESZ);                  // 16-byte words, 8-element chunks
@@ -231,7 +233,7 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
             const int gl = idx / Dh, d = idx % Dh, g = g0 + gl;
             float s = 0.0f;
             for (int w = 0; w < nw; w++) s += red[(w * ATT_GROUP + gl) * Dh + d];
-            if (a.nsplit == 1) {
+            if (a.nsplit == 1 || single) {
                 a.out[(size_t)b * a.ldo + ((size_t)kh * G + g) * Dh + d] = s / ml[2 * g + 1];
             } else {
                 wsb[g * hstride + d] = s;
@@ -248,9 +250,9 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
 // CTA calls this (it synchronises the CTA).
 template <int NTH>
 __device__ __forceinline__ void attn_merge_last(const AttnArgs &a, const float *wsb, size_t hstride, int kh, int b,
-                                                int pos, int *last) {
+                                                int pos, int *last, int ch = 0) {
     const int G = a.H / a.Hkv, Dh = a.Dh;
-    const int active = min(a.nsplit, pos / a.CH + 1);
+    const int active = min(a.nsplit, pos / (ch ? ch : a.CH) + 1);
     if (active == 1) {  // the only split: normalise its own accumulator
         __syncthreads();
         for (int i = threadIdx.x; i < G * Dh; i += NTH) {

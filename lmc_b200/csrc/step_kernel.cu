@@ -101,12 +101,21 @@ struct StepCtl {
     int abort;                  // set when a wait ran out: every CTA leaves
     int where;                  // op index + 1 of the wait that ran out
 };
+// A byte range asked of L2 at the start of a step: 16-byte aligned start and
+// length (the norm weights and biases of every GEMV, which are otherwise
+// first read from HBM on the critical path of their op).
+struct PfRange {
+    const void *p;
+    unsigned bytes;
+};
 struct StepParams {
     const DOp *ops;
     int nops, first_gemv, ring_off, stages;
     StepCtl *ctl;
     double *stats;  // norm statistics slots, zeroed again at the end of each launch
     int stats_n;    // doubles in the slots
+    const PfRange *pf;
+    int pf_n;
 };
 
 __device__ long long g_step_wait_ns = 1000000000ll;
@@ -124,20 +133,24 @@ __device__ __forceinline__ unsigned group_size(int k) {
 }
 
 // Grid-wide barrier in two phases.  grid_arrive: once every thread of the
-// CTA is done with the op (bar.sync), thread 0 makes the CTA's writes
-// visible (fence) and adds its arrival to its group's counter.  Work that the
+// CTA is done with the op (bar.sync), thread 0 adds its arrival to its
+// group's counter with release semantics.  Work that the
 // next op does not read (the next GEMV's weight copies, K/V prefetch) runs
 // between the phases.  grid_wait: lanes 0..7 of warp 0 poll one counter each
 // until every group is complete, the abort flag is set, or the wait limit
 // passes (then they set the flag); meanwhile the other warps copy the next op
 // into `next_op` (the op list is constant).  Returns false when the CTA must
 // leave.
+// The arrival is one release add: the CTA barrier before it orders every
+// thread's writes before thread 0's release, and release is cumulative, so no
+// separate fence (a second round trip to L2) is needed.  Likewise the
+// pollers' acquire loads plus the CTA barrier after them order every thread's
+// later reads.
 __device__ __forceinline__ void grid_arrive(StepCtl *ctl) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(&ctl->cnt[blockIdx.x % BAR_GROUPS].v, 1u);
-    }
+    if (threadIdx.x == 0)
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&ctl->cnt[blockIdx.x % BAR_GROUPS].v)
+                     : "memory");
 }
 __device__ __forceinline__ bool grid_wait(StepCtl *ctl, const unsigned *base, unsigned passed, int where, int *sh_ok,
                                           const DOp *next_src, DOp *next_op) {
@@ -171,7 +184,6 @@ __device__ __forceinline__ bool grid_wait(StepCtl *ctl, const unsigned *base, un
                 }
             }
         }
-        __threadfence();
         if (lane == 0) *sh_ok = ok;
     } else if (next_src) {
         const int4 *src = reinterpret_cast<const int4 *>(next_src);
@@ -235,9 +247,10 @@ __device__ __forceinline__ void ring_prefill(Ring &r, const TArgs &a, int qt, in
 
 // Ask L2 for the K/V rows the coming attention op reads (positions 0..pos-1
 // of each sequence and kv head; the rows were written by earlier steps), in
-// 16 KB pieces, one (sequence, kv head, K or V) range per CTA.
+// 16 KB pieces, one (sequence, kv head, K or V) range per CTA.  Issued by
+// warp 1, so that warp 0 (the barrier's poller) is not held up.
 __device__ __forceinline__ void kv_prefetch(const KvPf &k) {
-    if (threadIdx.x != 0) return;
+    if (threadIdx.x != 32) return;
     const int items = k.nb * k.Hkv * 2;
     for (int it = blockIdx.x; it < items; it += gridDim.x) {
         const int half = it & 1, bh = it >> 1, b = bh / k.Hkv, kh = bh % k.Hkv;
@@ -249,33 +262,26 @@ __device__ __forceinline__ void kv_prefetch(const KvPf &k) {
     }
 }
 
-// The outputs e = lane + 32 j (e < 16 nb: batch row e / 16, tile row e % 16)
-// of one row tile: bias (preloaded in pbias when given), GELU, residual add
-// (the old values preloaded in `pre` when given), the greedy-pick key, and
-// the sums of the final values for the norm that reads them next.
+// The output of this lane in one row tile (batch <= 2, so a tile has at most
+// 32 outputs: lane = 16 * batch row + tile row): bias (preloaded in pbias when
+// given), GELU, residual add (the old value preloaded in `pre` when given),
+// the greedy-pick key, and the sums of the final values for the norm that
+// reads them next.
 __device__ __forceinline__ void step_epilogue_tile(const TArgs &a, int row0, const float *ar, int lane,
-                                                   unsigned long long (&best)[4], const float *pre,
-                                                   const float *pbias, double (&st)[2][2]) {
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int e = lane + 32 * j, b = e >> 4, row = row0 + (e & 15);
-        if (e >= 16 * a.nb || row >= a.M) continue;
-        float v = ar[e];
-        if (a.bias) v += pbias ? pbias[j] : __ldg(a.bias + row);
-        if (a.epi & LMC_EPI_GELU) v = lmc_gelu_f(v);
-        float *o = a.y + (size_t)b * a.ldy + row;
-        const float out = (a.epi & LMC_EPI_ACCUM) ? (pre ? pre[j] : __ldcg(o)) + v : v;
-        *o = out;
-        const unsigned long long k = lmc_argmax_key(v, row + a.key_base);
-        best[j] = k > best[j] ? k : best[j];
-        if (b == 0) {
-            st[0][0] += (double)out;
-            st[0][1] += (double)out * (double)out;
-        } else {
-            st[1][0] += (double)out;
-            st[1][1] += (double)out * (double)out;
-        }
-    }
+                                                   unsigned long long &best, const float *pre, const float *pbias,
+                                                   double (&st)[2]) {
+    const int b = lane >> 4, row = row0 + (lane & 15);
+    if (b >= a.nb || row >= a.M) return;
+    float v = ar[lane];
+    if (a.bias) v += pbias ? *pbias : __ldg(a.bias + row);
+    if (a.epi & LMC_EPI_GELU) v = lmc_gelu_f(v);
+    float *o = a.y + (size_t)b * a.ldy + row;
+    const float out = (a.epi & LMC_EPI_ACCUM) ? (pre ? *pre : __ldcg(o)) + v : v;
+    *o = out;
+    const unsigned long long k = lmc_argmax_key(v, row + a.key_base);
+    best = k > best ? k : best;
+    st[0] += (double)out;
+    st[1] += (double)out * (double)out;
 }
 
 // ---------------------------------------------------------------------------
@@ -512,17 +518,14 @@ __device__ __forceinline__ int gemv_op_impl(uint8_t *smem, const DOp &op, Ring &
     const bool mine = warp_units(a, blockIdx.x, wid, w0, w1, t0, t1);
     // the residual this warp's first tile adds to, loaded now (it is only
     // needed in the epilogue) so its latency hides behind the work below
-    float pre[4] = {0.0f, 0.0f, 0.0f, 0.0f}, pbias[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float pre = 0.0f, pbias = 0.0f;
     const bool has_pre = mine && (a.epi & LMC_EPI_ACCUM) && wid < t1 - t0;
     const bool has_pb = mine && a.bias && wid < t1 - t0;
     if (has_pre || has_pb) {
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int e = lane + 32 * j, row = (t0 + wid) * 16 + (e & 15);
-            if (e < 16 * a.nb && row < a.M) {
-                if (has_pre) pre[j] = __ldcg(a.y + (size_t)(e >> 4) * a.ldy + row);
-                if (has_pb) pbias[j] = __ldg(a.bias + row);
-            }
+        const int row = (t0 + wid) * 16 + (lane & 15);
+        if ((lane >> 4) < a.nb && row < a.M) {
+            if (has_pre) pre = __ldcg(a.y + (size_t)(lane >> 4) * a.ldy + row);
+            if (has_pb) pbias = __ldg(a.bias + row);
         }
     }
     const Smem<1, QT> L{a.KB, a.XL, a.maxrt, 0};
@@ -612,35 +615,30 @@ __device__ __forceinline__ int gemv_op_impl(uint8_t *smem, const DOp &op, Ring &
     }
     if (!mine) return ok ? GEMV_OK : 0;
     __syncthreads();
-    unsigned long long best[4] = {0ull, 0ull, 0ull, 0ull};
-    double st[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
+    unsigned long long best = 0ull;
+    double st[2] = {0.0, 0.0};
     for (int T = wid; T < t1 - t0; T += WARPS)
-        step_epilogue_tile(a, (t0 + T) * 16, acc + T * NB * 16, lane, best, T == wid && has_pre ? pre : nullptr,
-                           T == wid && has_pb ? pbias : nullptr, st);
-    if (a.stats_out) {  // sums of this CTA's outputs for the next norm: fp32 in the warp, fp64 across
+        step_epilogue_tile(a, (t0 + T) * 16, acc + T * NB * 16, lane, best, T == wid && has_pre ? &pre : nullptr,
+                           T == wid && has_pb ? &pbias : nullptr, st);
+    if (a.stats_out) {  // sums of this CTA's outputs for the next norm: fp32 in the half-warp of a batch row, fp64 across
 #pragma unroll
-        for (int b = 0; b < 2; b++)
+        for (int q = 0; q < 2; q++) {
+            float v = (float)st[q];
 #pragma unroll
-            for (int q = 0; q < 2; q++) {
-                float v = (float)st[b][q];
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-                if (lane == 0 && b < a.nb && v != 0.0f) atomicAdd(a.stats_out + 2 * b + q, (double)v);
-            }
+            for (int off = 8; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if ((lane & 15) == 0 && (lane >> 4) < a.nb && v != 0.0f) atomicAdd(a.stats_out + 2 * (lane >> 4) + q, (double)v);
+        }
     }
     if (a.keys) {  // greedy keys: half-warp maxima, then one atomic per CTA and batch row
-        auto kbest = reinterpret_cast<unsigned long long(*)[8]>(smem);
+        auto kbest = reinterpret_cast<unsigned long long(*)[2]>(smem);
         __syncthreads();  // the x fragments at offset 0 are dead
+        unsigned long long k = best;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            unsigned long long k = best[j];
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) {
-                const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, off);
-                k = o > k ? o : k;
-            }
-            if ((lane & 15) == 0) kbest[wid][2 * j + (lane >> 4)] = k;
+        for (int off = 8; off > 0; off >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, off);
+            k = o > k ? o : k;
         }
+        if ((lane & 15) == 0) kbest[wid][lane >> 4] = k;
         __syncthreads();
         if ((int)threadIdx.x < a.nb) {
             unsigned long long k = 0ull;
@@ -653,19 +651,29 @@ __device__ __forceinline__ int gemv_op_impl(uint8_t *smem, const DOp &op, Ring &
 
 // Attention work items (split, kv head, sequence), dealt round-robin to the
 // CTAs; the last split of each (sequence, kv head) to finish merges them.
+// The plan's splits are sized for the longest context; at the current
+// position they are coarsened (doubled) up to ATT_ONE_SPLIT positions, so a
+// context that short is one split per head (no merge, which costs a
+// fence, an arrival atomic and a read-back of the partials), and a longer
+// one is split into pieces of at least that many positions.
+constexpr int ATT_ONE_SPLIT = 256;  // one scores pass of 8 warps x 32 lanes
 template <typename KV, int DH>
 __device__ __forceinline__ void attn_op(uint8_t *smem, const AttnArgs &a, int items, int *sh_last) {
-    const int G = a.H / a.Hkv, Dh = a.Dh, CH = a.CH;
+    const int G = a.H / a.Hkv, Dh = a.Dh;
     for (int it = blockIdx.x; it < items; it += gridDim.x) {
         const int sp = it % a.nsplit, r2 = it / a.nsplit, kh = r2 % a.Hkv, b = r2 / a.Hkv;
         const int pos = __ldcg(a.pos + b);
         if (pos < 0 || pos >= a.S) continue;  // the host validates positions
+        int CH = a.CH;
+        while (CH < ATT_ONE_SPLIT && CH <= pos) CH *= 2;
         const int t0 = sp * CH, t1 = min(t0 + CH, pos + 1);
         if (t0 > pos) continue;
+        const bool single = pos < CH;
         float *wsb = a.ws + (((size_t)b * a.H + (size_t)kh * G) * a.nsplit + sp) * (Dh + 2);
         const size_t hstride = (size_t)a.nsplit * (Dh + 2);
-        split_body<KV, DH, NTHR, 128>(a, reinterpret_cast<float *>(smem), sp, kh, b, pos, t0, t1, wsb, hstride);
-        if (a.nsplit > 1) attn_merge_last<NTHR>(a, wsb, hstride, kh, b, pos, sh_last);
+        split_body<KV, DH, NTHR, 128>(a, reinterpret_cast<float *>(smem), sp, kh, b, pos, t0, t1, wsb, hstride, CH,
+                                      single);
+        if (!single) attn_merge_last<NTHR>(a, wsb, hstride, kh, b, pos, sh_last, CH);
         __syncthreads();  // shared memory is reused by the next item
     }
 }
@@ -786,6 +794,8 @@ __global__ void __launch_bounds__(NTHR, 2) k_step(StepParams P) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncwarp();
+    if (threadIdx.x == 64)
+        for (int k = blockIdx.x; k < P.pf_n; k += gridDim.x) prefetch_l2(P.pf[k].p, P.pf[k].bytes);
     if (P.first_gemv >= 0) ring_prefill(r, P.ops[P.first_gemv].g, P.ops[P.first_gemv].qt, lane, wid);
     unsigned passed = 0;
     bool alive = true;
@@ -883,6 +893,8 @@ struct lmc_step_prog {
     StepCtl *ctl;
     double *stats;
     int stats_n;
+    PfRange *pf;
+    int pf_n;
 };
 constexpr int STATS_STRIDE = 4;  // doubles per slot: {sum, sum of squares} x 2 batch rows
 
@@ -941,7 +953,9 @@ static size_t plan_gemv(const lmc_step_op *o, int grid, int stages, DOp *d) {
     const char *env = getenv("LMC_STEP_FF");
     const long long per_warp = ((long long)(a.maxrt - 1) * a.KB + WARPS - 1) / WARPS;
     const bool norm = a.pro == LMC_PRO_LAYERNORM || a.pro == LMC_PRO_RMSNORM;
-    d->ff = !(env && env[0] == '0') && per_warp <= 8 && (size_t)o->batch * a.KB * 1024 <= 64 * 1024 &&
+    const char *fenv = getenv("LMC_STEP_FFMAX");
+    const long long ffmax = fenv ? atoll(fenv) : 8;
+    d->ff = !(env && env[0] == '0') && per_warp <= ffmax && (size_t)o->batch * a.KB * 1024 <= 64 * 1024 &&
             (!norm || o->stats_in);
     return d->ff ? fgemv_smem(a.KB, o->batch, a.maxrt) : gemv_smem(qt, a.KB, a.XL, a.maxrt);
 }
@@ -980,7 +994,8 @@ static size_t plan_attn(const lmc_step_op *o, DOp *d) {
     d->dh = o->Dh;
     d->items = a.nsplit * o->Hkv * o->batch;
     const int G = o->H / o->Hkv;
-    return (size_t)(G * o->Dh + G * a.CH + 2 * G + WARPS * ATT_GROUP * o->Dh) * sizeof(float);
+    // scores of up to max(CH, ATT_ONE_SPLIT) positions per split (attn_op coarsens the plan)
+    return (size_t)(G * o->Dh + G * std::max(a.CH, ATT_ONE_SPLIT) + 2 * G + WARPS * ATT_GROUP * o->Dh) * sizeof(float);
 }
 
 extern "C" int lmc_step_prog_build(const lmc_step_op *ops, int n, lmc_step_prog **out) {
@@ -1118,6 +1133,27 @@ extern "C" int lmc_step_prog_build(const lmc_step_op *ops, int n, lmc_step_prog 
         if (d[i].next_gemv >= 0) d[i].ng = d[d[i].next_gemv].g;
     if (e == cudaSuccess) e = cudaMemcpy(p->d_ops, d.data(), sizeof(DOp) * n, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(p->ctl, 0, sizeof(StepCtl));
+    // the small vectors of every GEMV (norm weights and biases), asked of L2
+    // when the step starts
+    std::vector<PfRange> pf;
+    auto add_pf = [&pf](const void *v, size_t bytes) {
+        if (!v || !bytes) return;
+        const uintptr_t a0 = (uintptr_t)v & ~(uintptr_t)15, a1 = ((uintptr_t)v + bytes + 15) & ~(uintptr_t)15;
+        pf.push_back(PfRange{(const void *)a0, (unsigned)(a1 - a0)});
+    };
+    for (int i = 0; i < n; i++)
+        if (d[i].kind == LMC_OP_GEMV) {
+            const TArgs &g = d[i].g;
+            const size_t K = (size_t)g.KB * 256;
+            add_pf(g.bias, (size_t)g.M * sizeof(float));
+            if (g.pro == LMC_PRO_LAYERNORM || g.pro == LMC_PRO_RMSNORM) add_pf(g.pw, K * sizeof(float));
+            if (g.pro == LMC_PRO_LAYERNORM) add_pf(g.pb, K * sizeof(float));
+        }
+    if (e == cudaSuccess && !pf.empty()) {
+        e = cudaMalloc((void **)&p->pf, sizeof(PfRange) * pf.size());
+        if (e == cudaSuccess) e = cudaMemcpy(p->pf, pf.data(), sizeof(PfRange) * pf.size(), cudaMemcpyHostToDevice);
+        p->pf_n = (int)pf.size();
+    }
     if (e != cudaSuccess) {
         lmc_step_prog_free(p);
         return lmc_set_error(LMC_ERR_CUDA, "step_prog: %s", cudaGetErrorString(e));
@@ -1141,6 +1177,8 @@ extern "C" int lmc_step_prog_launch(const lmc_step_prog *p, cudaStream_t s) {
     P.ctl = p->ctl;
     P.stats = p->stats;
     P.stats_n = p->stats_n;
+    P.pf = p->pf;
+    P.pf_n = p->pf_n;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p->grid);
     cfg.blockDim = dim3(NTHR);
@@ -1168,6 +1206,7 @@ extern "C" void lmc_step_prog_free(lmc_step_prog *p) {
     if (p->d_ops) cudaFree(p->d_ops);
     if (p->ctl) cudaFree(p->ctl);
     if (p->stats) cudaFree(p->stats);
+    if (p->pf) cudaFree(p->pf);
     free(p);
 }
 
