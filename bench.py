@@ -411,7 +411,7 @@ def run_model(args, rank, world, local_rank, dist):
         obj = [path]
         dist.broadcast_object_list(obj, src=0)
         path = obj[0]
-    kvd = rt.KV_F16 if args.kv == "f16" else rt.KV_F32
+    kvd = {"f16": rt.KV_F16, "f32": rt.KV_F32, "q8": rt.KV_Q8}[args.kv]
     B = args.batch
     rows = args.prefill_rows or None
     if dist and world > 1:
@@ -485,7 +485,7 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--gen", type=int, default=64)
-    ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
+    ap.add_argument("--kv", choices=["f16", "f32", "q8"], default="f16")
     ap.add_argument("--prefill-rows", type=int, default=0)
     ap.add_argument("--tp", action="store_true", help="tensor parallel over the torchrun ranks (llama8b)")
     args = ap.parse_args()

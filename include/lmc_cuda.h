@@ -179,8 +179,13 @@ unsigned long long lmc_rng_seed(unsigned long long seed);
 /* ---- K4: attention over the head-major KV cache -------------------------------
  * Replaces the cache write and per-head read of attention_forward
  * (src/ops.c:122-178) and llama_attention_forward (src/ops_llama.c:80-134).
- * Cache layout per layer: [Hkv][S][Dh] (src/models.h:149-162), fp32
- * (LMC_KV_F32, LMc's layout) or fp16 (LMC_KV_F16).  For `batch` sequences
+ * Cache layout per layer: [Hkv][S][row] (src/models.h:149-162), a row being
+ * Dh fp32 values (LMC_KV_F32, LMc's layout), Dh fp16 values (LMC_KV_F16), or
+ * Dh int8 codes followed by a 16-byte tail whose first 4 bytes hold the
+ * row's fp32 scale (LMC_KV_Q8: value = code * scale; a new row is quantized
+ * with m = max|x|, code = clamp(rint(x * (127 / m)), +-127), scale = m / 127;
+ * Dh + 16 bytes per row, head sizes that are multiples of 16 up to 512;
+ * LMC_KV_ROW_BYTES gives the row size).  For `batch` sequences
  * the caches are batch consecutive [Hkv][S][Dh] slabs and q/k_new/v_new/out
  * are batch rows of H*Dh (q, out) and Hkv*Dh (k_new, v_new) floats.
  * d_pos[b] is the position written this step; positions 0..d_pos[b] are
@@ -190,6 +195,9 @@ unsigned long long lmc_rng_seed(unsigned long long seed);
  * lmc_attention_workspace_bytes(batch, H, Dh, S) bytes (0 = none needed). */
 #define LMC_KV_F32 0
 #define LMC_KV_F16 1
+#define LMC_KV_Q8 2
+#define LMC_KV_ROW_BYTES(kv_dtype, Dh) \
+    ((kv_dtype) == LMC_KV_F32 ? 4 * (size_t)(Dh) : (kv_dtype) == LMC_KV_F16 ? 2 * (size_t)(Dh) : (size_t)(Dh) + 16)
 size_t lmc_attention_workspace_bytes(int batch, int H, int Dh, int S);
 int lmc_attention_decode(float *d_out, const float *d_q, const float *d_k_new,
                          const float *d_v_new, void *d_k_cache, void *d_v_cache,

@@ -261,12 +261,20 @@ __global__ void k_kv_append(AttnArgs a) {
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.S) return;
     const size_t cs = (size_t)a.seq[b];
-    KV *kc = reinterpret_cast<KV *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * Dh + (size_t)pos * Dh;
-    KV *vc = reinterpret_cast<KV *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * Dh + (size_t)pos * Dh;
+    const int RS = kv_rs<KV>(Dh);
+    KV *kc = reinterpret_cast<KV *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * RS + (size_t)pos * RS;
+    KV *vc = reinterpret_cast<KV *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * RS + (size_t)pos * RS;
     const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
     const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
     const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (Dh / 2) : nullptr;
     const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (Dh / 2) : nullptr;
+    if constexpr (KvT<KV>::Q8) {  // two warps: K, V
+        const int w = threadIdx.x >> 5;
+        if (w < 2)
+            kv_q8_store_row(reinterpret_cast<KvQ8 *>(w ? vc : kc), w ? vn : kn, w ? nullptr : rc, rs, Dh,
+                            threadIdx.x & 31);
+        return;
+    }
     for (int d = threadIdx.x; d < Dh / 2; d += blockDim.x) {
         float k0 = kn[2 * d], k1 = kn[2 * d + 1];
         if (rc) {
@@ -275,10 +283,12 @@ __global__ void k_kv_append(AttnArgs a) {
             k0 = r0;
             k1 = r1;
         }
-        kc[2 * d] = kv_cvt<KV>(k0);
-        kc[2 * d + 1] = kv_cvt<KV>(k1);
-        vc[2 * d] = kv_cvt<KV>(vn[2 * d]);
-        vc[2 * d + 1] = kv_cvt<KV>(vn[2 * d + 1]);
+        if constexpr (!KvT<KV>::Q8) {
+            kc[2 * d] = kv_cvt<KV>(k0);
+            kc[2 * d + 1] = kv_cvt<KV>(k1);
+            vc[2 * d] = kv_cvt<KV>(vn[2 * d]);
+            vc[2 * d + 1] = kv_cvt<KV>(vn[2 * d + 1]);
+        }
     }
 }
 
@@ -356,8 +366,10 @@ extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, in
     if (batch <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh % 32 || Dh > 256 || S <= 0)
         return lmc_set_error(LMC_ERR_INVALID, "attention: H=%d Hkv=%d Dh=%d S=%d (need H%%Hkv==0, Dh%%32==0, Dh<=256)",
                              H, Hkv, Dh, S);
-    if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16)
+    if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16 && kv_dtype != LMC_KV_Q8)
         return lmc_set_error(LMC_ERR_UNSUPPORTED, "attention: kv dtype %d", kv_dtype);
+    if (kv_dtype == LMC_KV_Q8 && (Dh % 16 || Dh > 512))
+        return lmc_set_error(LMC_ERR_UNSUPPORTED, "attention: int8 rows need a head size that is a multiple of 16, <= 512");
     AttnArgs a;
     a.out = out; a.q = q; a.k_new = k_new; a.v_new = v_new; a.k_cache = k_cache; a.v_cache = v_cache;
     a.pos = d_pos; a.H = H; a.Hkv = Hkv; a.Dh = Dh; a.S = S;
@@ -383,11 +395,17 @@ extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, in
     dim3 grid(a.nsplit, Hkv, batch);
     if (d_seq) {  // rows share cache sequences: append every row's K/V first
         if (kv_dtype == LMC_KV_F32) LMC_LAUNCH("kv append", k_kv_append<float>, dim3(Hkv, batch), 64, 0, s, a);
+        else if (kv_dtype == LMC_KV_Q8) LMC_LAUNCH("kv append", k_kv_append<KvQ8>, dim3(Hkv, batch), 64, 0, s, a);
         else LMC_LAUNCH("kv append", k_kv_append<__half>, dim3(Hkv, batch), 64, 0, s, a);
     }
     if (kv_dtype == LMC_KV_F32) {
         void (*fn)(AttnArgs) = Dh == 64 ? k_attn_split<float, 64, false> : Dh == 128 ? k_attn_split<float, 128, false>
                                                                       : k_attn_split<float, 0, false>;
+        if (smem > 48 * 1024) LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        LMC_LAUNCH("attention", fn, grid, ATT_THREADS, smem, s, a);
+    } else if (kv_dtype == LMC_KV_Q8) {
+        void (*fn)(AttnArgs) = Dh == 64 ? k_attn_split<KvQ8, 64, false> : Dh == 128 ? k_attn_split<KvQ8, 128, false>
+                                                                     : k_attn_split<KvQ8, 0, false>;
         if (smem > 48 * 1024) LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         LMC_LAUNCH("attention", fn, grid, ATT_THREADS, smem, s, a);
     } else {
@@ -446,7 +464,7 @@ extern "C" int lmc_attention_decode_noalloc(float *out, const float *q, const fl
     if (batch <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh <= 0 || Dh % 32 || Dh > 256 || S <= 0)
         return lmc_set_error(LMC_ERR_INVALID, "attention_noalloc: batch=%d H=%d Hkv=%d Dh=%d S=%d", batch, H, Hkv,
                              Dh, S);
-    if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16)
+    if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16 && kv_dtype != LMC_KV_Q8)
         return lmc_set_error(LMC_ERR_UNSUPPORTED, "attention_noalloc: kv dtype %d", kv_dtype);
     const size_t need = lmc_attention_workspace_bytes(batch, H, Dh, S);
     if (need > LMC_ATTN_STATIC_SCRATCH_BYTES)

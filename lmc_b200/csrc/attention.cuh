@@ -20,6 +20,65 @@ template <typename KV> __device__ __forceinline__ KV kv_cvt(float v);
 template <> __device__ __forceinline__ float kv_cvt<float>(float v) { return v; }
 template <> __device__ __forceinline__ __half kv_cvt<__half>(float v) { return __float2half_rn(v); }
 
+// int8 K/V rows (LMC_KV_Q8): a row is Dh int8 codes followed by a 16-byte
+// tail whose first 4 bytes are the row's fp32 scale; value = code * scale.
+// KvQ8 is the element type of such a cache (one byte); its row stride in
+// elements is Dh + 16.
+struct KvQ8 {
+    int8_t v;
+};
+template <typename KV> struct KvT {
+    static constexpr bool Q8 = false;
+};
+template <> struct KvT<KvQ8> {
+    static constexpr bool Q8 = true;
+};
+template <typename KV> __host__ __device__ constexpr int kv_rs(int Dh) { return KvT<KV>::Q8 ? Dh + 16 : Dh; }
+template <> __device__ __forceinline__ float kv_ld<KvQ8>(const KvQ8 *p) { return (float)p->v; }
+__device__ __forceinline__ float kv_q8_scale(const KvQ8 *row, int Dh) {
+    return *reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(row) + Dh);
+}
+// One warp quantizes one new row (K rotated first when rc is given): m =
+// max|x|, code = clamp(rint(x * (127 / m)), +-127), scale = m / 127 (all zero
+// when m is 0).  Lane takes element pairs d = lane + 32 i (Dh <= 512).
+__device__ __forceinline__ void kv_q8_store_row(KvQ8 *row, const float *src, const float *rc, const float *rs, int Dh,
+                                                int lane) {
+    float v[16];
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int d = lane + 32 * i;
+        v[2 * i] = v[2 * i + 1] = 0.0f;
+        if (2 * d < Dh) {
+            float x0 = src[2 * d], x1 = src[2 * d + 1];
+            if (rc) {
+                const float c = rc[d], sn = rs[d];
+                const float r0 = x0 * c - x1 * sn, r1 = x0 * sn + x1 * c;
+                x0 = r0;
+                x1 = r1;
+            }
+            v[2 * i] = x0;
+            v[2 * i + 1] = x1;
+            m = fmaxf(m, fmaxf(fabsf(x0), fabsf(x1)));
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const float inv = m > 0.0f ? 127.0f / m : 0.0f;
+    int8_t *q = reinterpret_cast<int8_t *>(row);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int d = lane + 32 * i;
+        if (2 * d < Dh) {
+            const int q0 = max(-127, min(127, __float2int_rn(__fmul_rn(v[2 * i], inv))));
+            const int q1 = max(-127, min(127, __float2int_rn(__fmul_rn(v[2 * i + 1], inv))));
+            q[2 * d] = (int8_t)q0;
+            q[2 * d + 1] = (int8_t)q1;
+        }
+    }
+    if (lane == 0) *reinterpret_cast<float *>(q + Dh) = m / 127.0f;
+}
+
 struct AttnArgs {
     float *out;
     const float *q, *k_new, *v_new;
@@ -62,6 +121,15 @@ template <int NV> __device__ __forceinline__ void kv_chunk_f32(const uint4 (&raw
     v[0] = __uint_as_float(x.x); v[1] = __uint_as_float(x.y); v[2] = __uint_as_float(x.z); v[3] = __uint_as_float(x.w);
     v[4] = __uint_as_float(y.x); v[5] = __uint_as_float(y.y); v[6] = __uint_as_float(y.z); v[7] = __uint_as_float(y.w);
 }
+template <int NV> __device__ __forceinline__ void kv_chunk_q8(const uint4 (&raw)[NV], int c, float (&v)[8]) {
+    const uint4 u = raw[c >> 1];
+    const uint32_t w0 = (c & 1) ? u.z : u.x, w1 = (c & 1) ? u.w : u.y;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        v[i] = (float)(int)(int8_t)(w0 >> (8 * i));
+        v[4 + i] = (float)(int)(int8_t)(w1 >> (8 * i));
+    }
+}
 template <int NV> __device__ __forceinline__ void kv_chunk_f16(const uint4 (&raw)[NV], int c, float (&v)[8]) {
     const uint4 u = raw[c];
     const __half2 *h = reinterpret_cast<const __half2 *>(&u);
@@ -80,7 +148,8 @@ constexpr int ATT_GROUP = 8;  // query heads per pass
 template <typename KV, int DH, int NTH = ATT_THREADS, int RBMAX = 256>
 __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp, int kh, int b, int pos, int t0, int t1,
                                            float *wsb, size_t hstride, int ch = 0, bool single = false) {
-    const int G = a.H / a.Hkv, Dh = DH ? DH : a.Dh, CH = ch ? ch : a.CH;
+    const int G = a.H / a.Hkv, Dh = DH ? DH : a.Dh, CH = ch ? ch : a.CH, RS = kv_rs<KV>(Dh);
+    constexpr bool Q8 = KvT<KV>::Q8;
     constexpr int ESZ = (int)sizeof(KV);
     constexpr int RB = DH ? (DH * ESZ < RBMAX ? DH * ESZ : RBMAX) : 128;  // K bytes per load block
     constexpr int NV = RB / 16, NC = RB / (8 * ESZ);                  // 16-byte words, 8-element chunks
@@ -91,11 +160,16 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
     float *ml = sc + G * CH;        // [G][2]
     float *red = ml + 2 * G;        // [nw][ATT_GROUP][Dh]
     const size_t cs = a.seq ? (size_t)a.seq[b] : (size_t)b;  // cache sequence of this row
-    KV *kc = reinterpret_cast<KV *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * Dh;
-    KV *vc = reinterpret_cast<KV *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * Dh;
+    KV *kc = reinterpret_cast<KV *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * RS;
+    KV *vc = reinterpret_cast<KV *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * RS;
     const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (Dh / 2) : nullptr;
     const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (Dh / 2) : nullptr;
-    if (a.append && pos >= t0 && pos < t1) {  // append this step's K/V row (K rotated first when RoPE applies)
+    if (Q8 && a.append && pos >= t0 && pos < t1) {  // quantize the new rows: warp 0 K, warp 1 V
+        if (warp < 2)
+            kv_q8_store_row(reinterpret_cast<KvQ8 *>((warp ? vc : kc) + (size_t)pos * RS),
+                            (warp ? a.v_new : a.k_new) + (size_t)b * a.ldkv + (size_t)kh * Dh, warp ? nullptr : rc,
+                            rs, Dh, lane);
+    } else if (a.append && pos >= t0 && pos < t1) {  // append this step's K/V row (K rotated first when RoPE applies)
         const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
         const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
         for (int d = threadIdx.x; d < Dh / 2; d += NTH) {
@@ -106,10 +180,12 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
                 k0 = r0;
                 k1 = r1;
             }
-            kc[(size_t)pos * Dh + 2 * d] = kv_cvt<KV>(k0);
-            kc[(size_t)pos * Dh + 2 * d + 1] = kv_cvt<KV>(k1);
-            vc[(size_t)pos * Dh + 2 * d] = kv_cvt<KV>(vn[2 * d]);
-            vc[(size_t)pos * Dh + 2 * d + 1] = kv_cvt<KV>(vn[2 * d + 1]);
+            if constexpr (!Q8) {
+                kc[(size_t)pos * Dh + 2 * d] = kv_cvt<KV>(k0);
+                kc[(size_t)pos * Dh + 2 * d + 1] = kv_cvt<KV>(k1);
+                vc[(size_t)pos * Dh + 2 * d] = kv_cvt<KV>(vn[2 * d]);
+                vc[(size_t)pos * Dh + 2 * d + 1] = kv_cvt<KV>(vn[2 * d + 1]);
+            }
         }
     }
     const float *qb = a.q + (size_t)b * a.ldq + (size_t)kh * G * Dh;
@@ -133,7 +209,7 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
         for (int tb = warp * 32; tb < n; tb += nw * 32) {
             const int tl = tb + lane;
             if (tl >= n) continue;
-            const KV *kr = kc + (size_t)(t0 + tl) * Dh;
+            const KV *kr = kc + (size_t)(t0 + tl) * RS;
             float sg[ATT_GROUP];
 #pragma unroll
             for (int g = 0; g < ATT_GROUP; g++) sg[g] = 0.0f;
@@ -149,6 +225,7 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
                 if (d0 >= Dh) break;
                 float kv[8];
                 if (ESZ == 4) kv_chunk_f32<NV>(raw, c, kv);
+                else if (Q8) kv_chunk_q8<NV>(raw, c, kv);
                 else kv_chunk_f16<NV>(raw, c, kv);
 #pragma unroll
                 for (int g = 0; g < ATT_GROUP; g++) {
@@ -169,9 +246,10 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
                 }
                 }
             }
+            const float rsc = Q8 ? kv_q8_scale(reinterpret_cast<const KvQ8 *>(kr), Dh) : 1.0f;
 #pragma unroll
             for (int g = 0; g < ATT_GROUP; g++)
-                if (g < gn) sc[(g0 + g) * CH + tl] = sg[g] * scale;
+                if (g < gn) sc[(g0 + g) * CH + tl] = (Q8 ? sg[g] * rsc : sg[g]) * scale;
         }
     }
     __syncthreads();
@@ -203,9 +281,14 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
 #pragma unroll
             for (int uu = 0; uu < U; uu++) {
                 const int tt = t + uu * nw;
-                const KV *vr = vc + (size_t)(t0 + tt) * Dh + lane;
+                const KV *vr = vc + (size_t)(t0 + tt) * RS + lane;
 #pragma unroll
                 for (int i = 0; i < DPLC; i++) v[uu][i] = (tt < n && i < dpl) ? kv_ld<KV>(vr + 32 * i) : 0.0f;
+                if (Q8 && tt < n) {
+                    const float vs = kv_q8_scale(reinterpret_cast<const KvQ8 *>(vc + (size_t)(t0 + tt) * RS), Dh);
+#pragma unroll
+                    for (int i = 0; i < DPLC; i++) v[uu][i] *= vs;
+                }
             }
 #pragma unroll
             for (int uu = 0; uu < U; uu++) {

@@ -77,7 +77,7 @@ struct alignas(16) DOp {
     int qt;           // GEMV: 4 / 6 / 8
     int next_gemv;    // index of the next GEMV op (its ring is filled at the end of this one), -1 none
     int nqt;          // its format
-    int kv, dh;       // ATTN: 0 fp32 / 1 fp16 cache; head size 64 / 128
+    int kv, dh;       // ATTN: cache rows LMC_KV_F32 / F16 / Q8; head size 64 / 128
     int items;        // ATTN: splits x kv heads x batch
     int kpf;          // GEMV: 1 = prefetch kp into L2 first
     int ff;           // GEMV: 1 = the latency (fp32) form, 0 = the tensor-core form
@@ -817,9 +817,12 @@ __global__ void __launch_bounds__(NTHR, 2) k_step(StepParams P) {
             alive = (gres & GEMV_OK) != 0;
             break;
         case LMC_OP_ATTN:
-            if (op.kv == 0) {
+            if (op.kv == LMC_KV_F32) {
                 if (op.dh == 64) attn_op<float, 64>(smem, op.at, op.items, &sh_last);
                 else attn_op<float, 128>(smem, op.at, op.items, &sh_last);
+            } else if (op.kv == LMC_KV_Q8) {
+                if (op.dh == 64) attn_op<KvQ8, 64>(smem, op.at, op.items, &sh_last);
+                else attn_op<KvQ8, 128>(smem, op.at, op.items, &sh_last);
             } else {
                 if (op.dh == 64) attn_op<__half, 64>(smem, op.at, op.items, &sh_last);
                 else attn_op<__half, 128>(smem, op.at, op.items, &sh_last);
@@ -964,7 +967,7 @@ static size_t plan_attn(const lmc_step_op *o, DOp *d) {
     if (!o->out || !o->q || !o->k_new || !o->v_new || !o->k_cache || !o->v_cache || !o->pos || !o->cnt) return 0;
     if (o->batch <= 0 || o->H <= 0 || o->Hkv <= 0 || o->H % o->Hkv || (o->Dh != 64 && o->Dh != 128) || o->S <= 0)
         return 0;
-    if (o->kv_dtype != LMC_KV_F32 && o->kv_dtype != LMC_KV_F16) return 0;
+    if (o->kv_dtype != LMC_KV_F32 && o->kv_dtype != LMC_KV_F16 && o->kv_dtype != LMC_KV_Q8) return 0;
     AttnArgs a = {};
     a.out = o->out;
     a.q = o->q;
@@ -990,7 +993,7 @@ static size_t plan_attn(const lmc_step_op *o, DOp *d) {
     if (need > o->ws_bytes || (need && !o->ws)) return 0;
     a.ws = (float *)o->ws;
     d->at = a;
-    d->kv = o->kv_dtype == LMC_KV_F16;
+    d->kv = o->kv_dtype;
     d->dh = o->Dh;
     d->items = a.nsplit * o->Hkv * o->batch;
     const int G = o->H / o->Hkv;
@@ -1100,7 +1103,7 @@ extern "C" int lmc_step_prog_build(const lmc_step_op *ops, int n, lmc_step_prog 
             const AttnArgs &at = d[i].at;
             d[j].kpf = 1;
             d[j].kp = KvPf{(const uint8_t *)at.k_cache, (const uint8_t *)at.v_cache, at.pos, at.Hkv, at.S,
-                           at.Dh * (d[i].kv ? 2 : 4), d[i].nb};
+                           (int)LMC_KV_ROW_BYTES(d[i].kv, at.Dh), d[i].nb};
         }
     int slots = 0;
     for (int i = 0; i < n; i++) slots = std::max(slots, std::max(ops[i].stats_in, ops[i].stats_out));

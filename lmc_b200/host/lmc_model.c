@@ -44,7 +44,7 @@ struct lmc_model {
     float *wpe, *lnf_w, *lnf_b, *rmsf, *rope_cos, *rope_sin;
     Layer *layers;
     void *kc, *vc;
-    size_t kv_layer_elems;
+    size_t kv_layer_bytes;
     float *x, *xn, *qkv, *att, *h, *h2, *logits;
     void *ws;
     size_t ws_bytes;
@@ -423,10 +423,12 @@ static int alloc_state(lmc_model *m) {
     const size_t NS = (size_t)m->max_batch, B = (size_t)m->max_rows, D = c->embed_dim, F = c->ffn_dim,
                  V = c->vocab_size;
     const size_t QD = (size_t)c->n_heads * c->head_dim, KV = (size_t)c->n_kv_heads * c->head_dim;
-    const size_t esz = m->kv_dtype == LMC_KV_F16 ? 2 : 4;
-    m->kv_layer_elems = NS * (size_t)m->hkvl * c->head_dim * (size_t)c->seq_len;  /* this rank's kv heads */
-    TRY(dev_alloc(&m->kc, esz * m->kv_layer_elems * c->n_layers));
-    TRY(dev_alloc(&m->vc, esz * m->kv_layer_elems * c->n_layers));
+    if (m->kv_dtype == LMC_KV_Q8 && (c->head_dim % 16 || c->head_dim > 512))
+        return lmc_set_error(LMC_ERR_UNSUPPORTED, "int8 KV rows need a head size that is a multiple of 16, <= 512");
+    /* this rank's kv heads, rows of LMC_KV_ROW_BYTES */
+    m->kv_layer_bytes = NS * (size_t)m->hkvl * (size_t)c->seq_len * LMC_KV_ROW_BYTES(m->kv_dtype, c->head_dim);
+    TRY(dev_alloc(&m->kc, m->kv_layer_bytes * c->n_layers));
+    TRY(dev_alloc(&m->vc, m->kv_layer_bytes * c->n_layers));
     TRY(dev_alloc((void **)&m->x, 4 * B * D));
     TRY(dev_alloc((void **)&m->xn, 4 * B * D));
     TRY(dev_alloc((void **)&m->qkv, 4 * B * (QD + 2 * KV + 3 * D)));
@@ -476,7 +478,8 @@ int lmc_nccl_unique_id(void *id) {
 static int model_load(const char *path, int max_batch, int max_rows, int kv_dtype, int tp_rank, int tp_size,
                       const void *nccl_id, lmc_model **out) {
     if (!path || !out || max_batch <= 0) return lmc_set_error(LMC_ERR_INVALID, "model_load: args");
-    if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16) return lmc_set_error(LMC_ERR_INVALID, "model_load: kv dtype");
+    if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16 && kv_dtype != LMC_KV_Q8)
+        return lmc_set_error(LMC_ERR_INVALID, "model_load: kv dtype");
     if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size || (tp_size > 1 && !nccl_id))
         return lmc_set_error(LMC_ERR_INVALID, "model_load: shard %d of %d", tp_rank, tp_size);
     *out = NULL;
@@ -653,12 +656,11 @@ static int step(lmc_model *m, int B) {
     const int D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size, H = c->n_heads;
     const int Dh = c->head_dim, S = c->seq_len;
     cudaStream_t s = m->stream;
-    const size_t esz = m->kv_dtype == LMC_KV_F16 ? 2 : 4;
     TRY(lmc_embed_launch(m->wte->type, m->wte->blocks, c->arch == 1 ? m->wpe : NULL, m->d_tok, m->d_pos, D, V, S, B,
                          m->x, s));
     for (int l = 0; l < c->n_layers; l++) {
         const Layer *w = &m->layers[l];
-        char *kc = (char *)m->kc + esz * m->kv_layer_elems * l, *vc = (char *)m->vc + esz * m->kv_layer_elems * l;
+        char *kc = (char *)m->kc + m->kv_layer_bytes * l, *vc = (char *)m->vc + m->kv_layer_bytes * l;
         if (c->arch == 1) { /* src/ops.c:182-206 */
             TRY(norm_matmul(m, w->qkv, LMC_PRO_LAYERNORM, w->ln1_w, w->ln1_b, 1e-5f, w->qkv_b, m->qkv, 3 * D, B,
                             LMC_EPI_NONE, NULL));
@@ -816,7 +818,6 @@ static int build_prog(lmc_model *m, int B, int gen, int n_prompt, int n_new, lmc
     if (!persist_enabled(m) || m->tp_size > 1 || B > 2 || !m->d_attn_cnt)
         return lmc_set_error(LMC_ERR_UNSUPPORTED, "persistent step: not for this model or batch");
     const int D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size, H = c->n_heads, Dh = c->head_dim;
-    const size_t esz = m->kv_dtype == LMC_KV_F16 ? 2 : 4;
     lmc_step_op *ops = (lmc_step_op *)calloc((size_t)(5 * c->n_layers + 5), sizeof(lmc_step_op));
     if (!ops) return lmc_set_error(LMC_ERR_OOM, "persistent step: host");
     int n = 0, rc = LMC_OK;
@@ -837,7 +838,7 @@ static int build_prog(lmc_model *m, int B, int gen, int n_prompt, int n_new, lmc
         const int s_in = l == 0 ? 1 : 3 + 2 * (l - 1), s_mid = 2 + 2 * l, s_out = 3 + 2 * l;
         const int n0 = n;
         const Layer *w = &m->layers[l];
-        char *kc = (char *)m->kc + esz * m->kv_layer_elems * l, *vc = (char *)m->vc + esz * m->kv_layer_elems * l;
+        char *kc = (char *)m->kc + m->kv_layer_bytes * l, *vc = (char *)m->vc + m->kv_layer_bytes * l;
         if (c->arch == 1) { /* src/ops.c:182-206 */
             add_gemv(ops, &n, B, w->qkv, m->x, D, w->qkv_b, m->qkv, 3 * D, LMC_EPI_NONE, LMC_PRO_LAYERNORM, w->ln1_w,
                      w->ln1_b, 1e-5f, NULL);

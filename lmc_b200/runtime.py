@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(HERE, "liblmc_b200.so")
 
 LMC_OK = 0
 EPI_NONE, EPI_GELU, EPI_ACCUM = 0, 1, 2
-KV_F32, KV_F16 = 0, 1
+KV_F32, KV_F16, KV_Q8 = 0, 1, 2
 
 _c = ctypes
 _vp, _i, _u32, _sz, _f = _c.c_void_p, _c.c_int, _c.c_uint32, _c.c_size_t, _c.c_float

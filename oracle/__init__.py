@@ -50,6 +50,11 @@ class Oracle:
         L.orc_model_free.argtypes = [ctypes.c_void_p]
         L.orc_model_config.argtypes = [ctypes.c_void_p, _i32p]
         L.orc_model_forward.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _f32p]
+        L.orc_model_set_kv.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.orc_kv_q8_row.argtypes = [_f32p, ctypes.c_int, ctypes.POINTER(ctypes.c_int8), ctypes.POINTER(ctypes.c_float)]
+        L.orc_kv_round_row.argtypes = [_f32p, ctypes.c_int, ctypes.c_int]
+        L.orc_f32_to_f16_to_f32.argtypes = [ctypes.c_float]
+        L.orc_f32_to_f16_to_f32.restype = ctypes.c_float
 
     def geometry(self, t):
         be, bb = ctypes.c_int(), ctypes.c_int()
@@ -115,6 +120,23 @@ class Oracle:
                                H, Hkv, Dh, S, pos)
         return out
 
+    def kv_q8_row(self, x):
+        """(int8 codes, scale) of one KV row as the int8 cache stores it."""
+        x = np.ascontiguousarray(x, np.float32)
+        q = np.empty(x.size, np.int8)
+        sc = ctypes.c_float()
+        self.lib.orc_kv_q8_row(_ptr(x, _f32p), x.size, q.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)), ctypes.byref(sc))
+        return q, sc.value
+
+    def kv_round_rows(self, rows, mode):
+        """rows [n][Dh] replaced by what a cache of the given mode returns."""
+        r = np.array(rows, np.float32, copy=True).reshape(-1, np.shape(rows)[-1])
+        for i in range(r.shape[0]):
+            row = np.ascontiguousarray(r[i])
+            self.lib.orc_kv_round_row(_ptr(row, _f32p), row.size, mode)
+            r[i] = row
+        return r.reshape(np.shape(rows))
+
     def argmax(self, x):
         x = np.ascontiguousarray(x, np.float32)
         return self.lib.orc_argmax(_ptr(x, _f32p), x.size)
@@ -141,6 +163,11 @@ class OracleModel:
         c = np.zeros(11, np.int32)
         self.lib.orc_model_config(self.h, _ptr(c, _i32p))
         self.arch, self.V, self.S, self.L, self.H, self.Hkv, self.D, self.F, self.Dh = (int(v) for v in c[:9])
+
+    def set_kv(self, mode):
+        """Store K/V rows as a cache of mode 0 (fp32), 1 (fp16) or 2 (int8 rows)."""
+        self.lib.orc_model_set_kv(self.h, mode)
+        return self
 
     def forward(self, tok, pos):
         out = np.empty(self.V, np.float32)

@@ -69,6 +69,50 @@ float orc_f16_to_f32(uint16_t h) {
     return f;
 }
 
+/* IEEE binary16 rounding of a float (nearest, ties to even), back in fp32:
+ * keep 11 significant bits at the half's precision (subnormal halves have a
+ * fixed 2^-24 step), overflow to infinity. */
+float orc_f32_to_f16_to_f32(float x) {
+    if (x != x) return x;
+    const float ax = fabsf(x);
+    if (ax >= 65520.0f) return x < 0 ? -INFINITY : INFINITY; /* rounds past the largest half, 65504 */
+    int e;
+    frexpf(ax, &e);                              /* ax = f * 2^e, f in [0.5, 1) */
+    const int step_e = e - 11 < -24 ? -24 : e - 11; /* ulp of the half holding ax */
+    const float step = ldexpf(1.0f, step_e);
+    const float r = rintf(ax / step) * step;     /* exact: division and product by a power of two */
+    return x < 0 ? -r : r;
+}
+
+void orc_kv_q8_row(const float *x, int n, int8_t *q, float *scale) {
+    float m = 0.0f;
+    for (int i = 0; i < n; i++) m = fmaxf(m, fabsf(x[i]));
+    if (m == 0.0f) {
+        for (int i = 0; i < n; i++) q[i] = 0;
+        *scale = 0.0f;
+        return;
+    }
+    const float inv = 127.0f / m;
+    for (int i = 0; i < n; i++) {
+        float r = rintf(x[i] * inv);
+        r = r > 127.0f ? 127.0f : r < -127.0f ? -127.0f : r;
+        q[i] = (int8_t)r;
+    }
+    *scale = m / 127.0f;
+}
+
+void orc_kv_round_row(float *row, int n, int mode) {
+    if (mode == 1) {
+        for (int i = 0; i < n; i++) row[i] = orc_f32_to_f16_to_f32(row[i]);
+    } else if (mode == 2) {
+        int8_t q[1024];
+        float sc;
+        if (n > 1024) return;
+        orc_kv_q8_row(row, n, q, &sc);
+        for (int i = 0; i < n; i++) row[i] = (float)q[i] * sc;
+    }
+}
+
 static float rd_f16(const uint8_t *p) { uint16_t h; memcpy(&h, p, 2); return orc_f16_to_f32(h); }
 static uint32_t rd_u32(const uint8_t *p) { uint32_t v; memcpy(&v, p, 4); return v; }
 
@@ -456,7 +500,7 @@ typedef struct {
 } OrcLayer;
 
 struct OrcModel {
-    int arch, V, S, L, H, Hkv, D, F, Dh;
+    int arch, V, S, L, H, Hkv, D, F, Dh, kv_mode;
     float theta, eps;
     float *wte, *wpe, *lnf_w, *lnf_b, *rmsf, *lm_head;
     float *rope_cos, *rope_sin;
@@ -647,6 +691,8 @@ void orc_model_free(OrcModel *m) {
     free(m);
 }
 
+void orc_model_set_kv(OrcModel *m, int mode) { m->kv_mode = mode; }
+
 void orc_model_config(const OrcModel *m, int *c) {
     c[0] = m->arch; c[1] = m->V; c[2] = m->S; c[3] = m->L; c[4] = m->H; c[5] = m->Hkv;
     c[6] = m->D; c[7] = m->F; c[8] = m->Dh; c[9] = (int)(m->theta * 1000.0f); c[10] = (int)(m->eps * 1e9f);
@@ -665,6 +711,8 @@ int orc_model_forward(OrcModel *m, int tok, int pos, float *logits) {
             for (int h = 0; h < H; h++) {
                 memcpy(kc + ((size_t)h * S + pos) * Dh, m->qkv + D + h * Dh, (size_t)Dh * 4);
                 memcpy(vc + ((size_t)h * S + pos) * Dh, m->qkv + 2 * D + h * Dh, (size_t)Dh * 4);
+                orc_kv_round_row(kc + ((size_t)h * S + pos) * Dh, Dh, m->kv_mode);
+                orc_kv_round_row(vc + ((size_t)h * S + pos) * Dh, Dh, m->kv_mode);
             }
             orc_attention(m->att, m->qkv, kc, vc, H, H, Dh, S, pos);
             orc_matmul_vec(m->proj, w->proj_w, w->proj_b, m->att, D, D);
@@ -691,6 +739,8 @@ int orc_model_forward(OrcModel *m, int tok, int pos, float *logits) {
             for (int h = 0; h < Hkv; h++) {
                 memcpy(kc + ((size_t)h * S + pos) * Dh, m->k + h * Dh, (size_t)Dh * 4);
                 memcpy(vc + ((size_t)h * S + pos) * Dh, m->v + h * Dh, (size_t)Dh * 4);
+                orc_kv_round_row(kc + ((size_t)h * S + pos) * Dh, Dh, m->kv_mode);
+                orc_kv_round_row(vc + ((size_t)h * S + pos) * Dh, Dh, m->kv_mode);
             }
             orc_attention(m->att, m->q, kc, vc, H, Hkv, Dh, S, pos);
             orc_matmul_vec(m->proj, w->o_w, NULL, m->att, D, D);

@@ -69,6 +69,18 @@ void  orc_attention(float *out, const float *q, const float *k_cache,
                     const float *v_cache, int H, int Hkv, int Dh, int S,
                     int pos);
 
+/* KV rows as the device cache may store them instead of LMc's fp32 rows
+ * (models.h:149-162 keeps fp32; the compact forms are this project's
+ * extension, restated here so the device path can be checked exactly):
+ *   mode 0 fp32 (LMc), 1 fp16 (round to nearest even), 2 int8 codes with one
+ *   fp32 scale per row: m = max|x|, q = clamp(rint(x * (127 / m)), +-127),
+ *   scale = m / 127, value = q * scale (m = 0: all zero).
+ * orc_kv_q8_row quantizes one row; orc_kv_round_row replaces a row by the
+ * values the cache returns for it. */
+void  orc_kv_q8_row(const float *x, int n, int8_t *q, float *scale);
+void  orc_kv_round_row(float *row, int n, int mode);
+float orc_f32_to_f16_to_f32(float x);
+
 /* First index of the maximum (strict '>' scan), lmc.c:45-47. */
 int   orc_argmax(const float *x, int n);
 
@@ -91,6 +103,8 @@ void      orc_model_config(const OrcModel *m, int *cfg);
 /* model_forward(token, pos) (ops.c:212-237 / ops_llama.c:157-192): writes
  * V logits to `logits`.  Positions must be fed in order 0,1,2,... */
 int       orc_model_forward(OrcModel *m, int token, int pos, float *logits);
+/* Store K/V rows in the given kv mode (see orc_kv_round_row); default 0. */
+void      orc_model_set_kv(OrcModel *m, int mode);
 
 #ifdef __cplusplus
 }

@@ -281,3 +281,59 @@ def test_attention(cuda, orc, H, Hkv, Dh, S, pos, kvd):
     # the new row was appended to the cache
     assert np.allclose(dk[1, :, poss[1]].float().cpu().numpy().reshape(-1),
                        kn[1].astype(np.float16 if kvd == rt.KV_F16 else np.float32).astype(np.float32))
+
+
+def q8_cache(orc, rows):
+    """[..., Dh] fp32 rows -> (the int8-row cache bytes [..., Dh + 16], the
+    values it holds as fp32)."""
+    Dh = rows.shape[-1]
+    flat = rows.reshape(-1, Dh)
+    raw = np.zeros((flat.shape[0], Dh + 16), np.uint8)
+    vals = np.empty_like(flat)
+    for i, r in enumerate(flat):
+        q, sc = orc.kv_q8_row(r)
+        raw[i, :Dh] = q.view(np.uint8)
+        raw[i, Dh:Dh + 4] = np.frombuffer(np.float32(sc).tobytes(), np.uint8)
+        vals[i] = q.astype(np.float32) * np.float32(sc)
+    return raw.reshape(rows.shape[:-1] + (Dh + 16,)), vals.reshape(rows.shape)
+
+
+@pytest.mark.parametrize("H,Hkv,Dh,S,pos", [
+    (12, 12, 64, 1024, 0), (12, 12, 64, 1024, 135), (32, 4, 64, 2048, 700), (32, 8, 128, 4096, 1500),
+    (6, 2, 96, 256, 200)])
+def test_attention_int8_rows(cuda, orc, H, Hkv, Dh, S, pos):
+    """LMC_KV_Q8: rows of int8 codes and one fp32 scale.  The appended rows'
+    codes and scales are the oracle's quantization bit for bit; the output
+    is attention over the values the cache holds (rel-err 1e-5)."""
+    rng = np.random.default_rng(pos + 7 * H)
+    B = 2
+    base = rng.normal(0, 1, (B, Hkv, S, Dh)).astype(np.float32)
+    kraw, kvals = q8_cache(orc, base)
+    vraw, vvals = q8_cache(orc, rng.normal(0, 1, (B, Hkv, S, Dh)).astype(np.float32))
+    q = rng.normal(0, 1, (B, H * Dh)).astype(np.float32)
+    kn = rng.normal(0, 1, (B, Hkv * Dh)).astype(np.float32)
+    vn = rng.normal(0, 1, (B, Hkv * Dh)).astype(np.float32)
+    kn[0, :Dh] = 0.0  # an all-zero row: scale 0, codes 0
+    poss = np.array([pos, max(pos // 2, 0)], np.int32)
+    want, knew = [], []
+    for b in range(B):
+        k2, v2 = kvals[b].copy(), vvals[b].copy()
+        kq, kv_ = q8_cache(orc, kn[b].reshape(Hkv, Dh))
+        vq, vv_ = q8_cache(orc, vn[b].reshape(Hkv, Dh))
+        k2[:, poss[b]], v2[:, poss[b]] = kv_, vv_
+        knew.append((kq, vq))
+        want.append(orc.attention(q[b], k2, v2, H, Hkv, Dh, S, int(poss[b])))
+    want = np.stack(want)
+    dk, dv = dev(cuda, kraw), dev(cuda, vraw)
+    out = cuda.empty((B, H * Dh), dtype=cuda.float32, device="cuda")
+    wsb = rt.lib().lmc_attention_workspace_bytes(B, H, Dh, S)
+    ws = cuda.empty(max(wsb, 4), dtype=cuda.uint8, device="cuda")
+    dq, dkn, dvn, dpos = dev(cuda, q), dev(cuda, kn), dev(cuda, vn), dev(cuda, poss)
+    rt.call("lmc_attention_decode", out.data_ptr(), dq.data_ptr(), dkn.data_ptr(), dvn.data_ptr(), dk.data_ptr(),
+            dv.data_ptr(), rt.KV_Q8, dpos.data_ptr(), B, H, Hkv, Dh, S, ws.data_ptr(), wsb, None)
+    assert rel_err(out.cpu().numpy(), want) < 1e-5
+    kc, vc = dk.cpu().numpy(), dv.cpu().numpy()
+    for b in range(B):
+        assert (kc[b, :, poss[b], :Dh + 4] == knew[b][0][:, :Dh + 4]).all()
+        assert (vc[b, :, poss[b], :Dh + 4] == knew[b][1][:, :Dh + 4]).all()
+    assert rt.lib().lmc_device_status() == 0

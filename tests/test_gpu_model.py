@@ -129,19 +129,20 @@ def test_batched_gemm_path_matches_oracle(cuda, orc, model_dir, kind, kw):
     ("gpt2", dict(L=2, D=256, H=4, S=128, V=1000, seed=5)),
     ("llama", dict(L=2, D=256, H=8, Hkv=2, F=512, S=128, V=1000, seed=5)),
 ])
-@pytest.mark.parametrize("kvd", [rt.KV_F32, rt.KV_F16])
+@pytest.mark.parametrize("kvd", [rt.KV_F32, rt.KV_F16, rt.KV_Q8])
 def test_prefill_matches_oracle(cuda, orc, model_dir, kind, kw, kvd):
     """Batched prefill (lmc_model_prefill): a 21-token prompt of sequence 1 in
     chunks of 16 and 5 rows (the first through the tensor-core GEMM) gives
     the oracle's last-position logits and next id, and greedy decoding then
-    continues with the oracle's ids from the cache the prefill wrote."""
+    continues with the oracle's ids from the cache the prefill wrote.  The
+    oracle stores its K/V rows as the cache does (fp32, fp16, int8 rows)."""
     path = tiny(kind, model_dir, **kw)
     prompt = np.random.default_rng(3).integers(0, kw["V"], 21).astype(np.int32)
-    om = orc.model(path)
+    om = orc.model(path).set_kv(kvd)
     lg = None
     for pos, t in enumerate(prompt):
         lg = om.forward(int(t), pos)
-    tol = 1e-3 if kvd == rt.KV_F32 else 5e-3
+    tol = 1e-3
     m = rt.Model(path, max_batch=2, kv_dtype=kvd, max_rows=16)
     got, nxt = m.prefill(1, prompt)
     assert rel_err(got, lg) < tol
@@ -185,3 +186,37 @@ def test_generate_with_prefill_matches_oracle(cuda, orc, model_dir, kind, kw):
     assert got.tolist() == want
     got2 = m.generate(prompts, 16, use_graph=False)
     assert got2.tolist() == want
+
+
+@pytest.mark.parametrize("kind,kw", [
+    ("gpt2", dict(L=2, D=256, H=4, S=128, V=1000, seed=9)),
+    ("llama", dict(L=2, D=512, H=8, Hkv=2, F=768, S=128, V=1000, seed=9)),
+])
+@pytest.mark.parametrize("persistent", ["1", "0"])
+def test_int8_kv_generate_matches_oracle(cuda, orc, model_dir, monkeypatch, kind, kw, persistent):
+    """int8 K/V rows (LMC_KV_Q8) through the whole model, in the persistent
+    step and kernel by kernel: teacher-forced logits within 1e-3 of the
+    oracle storing its rows the same way, its greedy ids for 24 tokens, and
+    within the int8 rounding (3e-2) of LMc's fp32 cache."""
+    monkeypatch.setenv("LMC_PERSISTENT", persistent)
+    path = tiny(kind, model_dir, **kw)
+    prompt = np.random.default_rng(4).integers(0, kw["V"], 6).astype(np.int32)
+    om, of = orc.model(path).set_kv(rt.KV_Q8), orc.model(path)
+    m = rt.Model(path, max_batch=1, kv_dtype=rt.KV_Q8)
+    for pos, t in enumerate(prompt):
+        got, _ = m.forward([int(t)], [pos])
+        want = om.forward(int(t), pos)
+        assert rel_err(got[0], want) < 1e-3
+        assert rel_err(got[0], of.forward(int(t), pos)) < 3e-2
+    om2 = orc.model(path).set_kv(rt.KV_Q8)
+    lg = None
+    for pos, t in enumerate(prompt):
+        lg = om2.forward(int(t), pos)
+    ids, pos = [], len(prompt)
+    for _ in range(24):
+        ids.append(orc.argmax(lg))
+        lg = om2.forward(ids[-1], pos)
+        pos += 1
+    m2 = rt.Model(path, max_batch=1, kv_dtype=rt.KV_Q8)
+    assert m2.generate(prompt[None], 24, use_graph=True)[0].tolist() == ids
+    assert rt.lib().lmc_device_status() == 0

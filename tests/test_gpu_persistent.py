@@ -35,14 +35,14 @@ def oracle_ids(orc, path, prompt, n):
 
 
 @pytest.mark.parametrize("kind,kw", MODELS)
-@pytest.mark.parametrize("kvd", [rt.KV_F32, rt.KV_F16])
+@pytest.mark.parametrize("kvd", [rt.KV_F32, rt.KV_F16, rt.KV_Q8])
 @pytest.mark.parametrize("B", [1, 2])
 def test_persistent_forward_logits(cuda, orc, model_dir, kind, kw, kvd, B):
     path = synth.cached_model(kind, model_dir, **kw)
-    om = [orc.model(path) for _ in range(B)]
+    om = [orc.model(path).set_kv(kvd) for _ in range(B)]  # the oracle stores K/V rows as the cache does
     m = rt.Model(path, max_batch=B, kv_dtype=kvd)
     toks = np.random.default_rng(5).integers(0, kw["V"], (B, 9))
-    tol = 1e-3 if kvd == rt.KV_F32 else 5e-3
+    tol = 1e-3
     for pos in range(toks.shape[1]):
         got, nxt = m.forward(toks[:, pos], [pos] * B)
         for b in range(B):

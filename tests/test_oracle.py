@@ -194,3 +194,24 @@ def test_rope_and_activations_vs_float64(orc):
     xd = x.astype(np.float64)
     assert np.allclose(orc.gelu(x), xd / (1 + np.exp(-1.702 * xd)), rtol=1e-5, atol=1e-6)
     assert np.allclose(orc.silu(x), xd / (1 + np.exp(-xd)), rtol=1e-5, atol=1e-6)
+
+
+def test_kv_row_forms(orc):
+    """The compact KV row forms the device cache offers: fp16 rounding equals
+    IEEE half rounding (numpy), and the int8 row quantization keeps every
+    value within half a step (scale / 2) with the maximum at +-127."""
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.normal(0, 1, 4000), rng.normal(0, 1e-5, 1000), rng.normal(0, 3e4, 1000),
+                        [65504.0, 65519.0, 65520.0, -65520.0, 6e-8, 3e-8, 0.0]]).astype(np.float32)
+    with np.errstate(over="ignore"):
+        want = x.astype(np.float16).astype(np.float32)
+    got = orc.kv_round_rows(x[None], 1)[0]
+    assert np.array_equal(got, want)
+    for scale in (1.0, 1e-3, 50.0):
+        r = rng.normal(0, scale, 128).astype(np.float32)
+        q, sc = orc.kv_q8_row(r)
+        assert np.abs(q).max() == 127 and np.abs(q.astype(np.int32)).max() <= 127
+        assert np.float32(sc) == np.float32(np.abs(r).max() / np.float32(127.0))
+        assert np.abs(q * np.float32(sc) - r).max() <= sc / 2 * (1 + 1e-6)
+    q, sc = orc.kv_q8_row(np.zeros(64, np.float32))
+    assert sc == 0.0 and not q.any()
