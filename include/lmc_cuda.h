@@ -222,6 +222,26 @@ int lmc_attention_decode_noalloc(float *d_out, const float *d_q, const float *d_
                                  const float *d_v_new, void *d_k_cache, void *d_v_cache,
                                  int kv_dtype, const int *d_pos, int batch, int H, int Hkv,
                                  int Dh, int S, void *stream);
+/* lmc_attention_decode over a paged cache, for servers that keep many
+ * sequences of different lengths in one pool (LMc's cache is one contiguous
+ * [Hkv][S][Dh] slab per layer, src/models.h:149-162; paging is an addition
+ * of this library).  d_k_pool / d_v_pool hold n_pages pages; page p is
+ * [Hkv][page_size][row] (rows as in lmc_attention_decode, kv_dtype any of
+ * LMC_KV_*) and holds page_size consecutive positions of one sequence.
+ * d_pages[b * max_pages + j] is the page of positions
+ * [j * page_size, (j + 1) * page_size) of sequence b; page_size is a power of
+ * two >= 16 and the context limit is max_pages * page_size.  The new K/V row
+ * is written at d_pos[b] through the table, so the page of that position
+ * must be assigned before the call.  A page id outside [0, n_pages) is not
+ * read (page 0 is) and lmc_device_status() then reports LMC_ERR_INVALID.
+ * d_workspace: lmc_attention_workspace_bytes(batch, H, Dh, max_pages *
+ * page_size) bytes. */
+int lmc_attention_decode_paged(float *d_out, const float *d_q, const float *d_k_new,
+                               const float *d_v_new, void *d_k_pool, void *d_v_pool,
+                               int kv_dtype, int n_pages, const int *d_pages, int max_pages,
+                               int page_size, const int *d_pos, int batch, int H, int Hkv,
+                               int Dh, void *d_workspace, size_t workspace_bytes,
+                               void *stream);
 
 /* ---- whole model: load_model + model_forward on the device -------------------
  * lmc_model_load parses a GGUF v1-3 file the way load_model does

@@ -356,11 +356,12 @@ extern "C" int lmc_attention_rope_launch(float *out, int ldo, const float *q, in
                                      batch, H, Hkv, Dh, S, d_ws, ws_bytes, rope_cos, rope_sin, d_cnt, s);
 }
 
-extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, int ldq, const float *k_new,
-                                         const float *v_new, int ldkv, void *k_cache, void *v_cache, int kv_dtype,
-                                         const int *d_pos, const int *d_seq, int batch, int H, int Hkv, int Dh, int S,
-                                         void *d_ws, size_t ws_bytes, const float *rope_cos, const float *rope_sin,
-                                         int *d_cnt, cudaStream_t s) {
+// pages: NULL, or the page table of a paged cache (attention.cuh AttnArgs)
+static int attention_impl(float *out, int ldo, const float *q, int ldq, const float *k_new, const float *v_new,
+                          int ldkv, void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, const int *d_seq,
+                          int batch, int H, int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes,
+                          const float *rope_cos, const float *rope_sin, int *d_cnt, const int *pages, int page_shift,
+                          int max_pages, int n_pages, cudaStream_t s) {
     if (!out || !q || !k_new || !v_new || !k_cache || !v_cache || !d_pos)
         return lmc_set_error(LMC_ERR_INVALID, "attention: null pointer");
     if (batch <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || Dh % 32 || Dh > 256 || S <= 0)
@@ -378,6 +379,10 @@ extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, in
     a.cnt = d_cnt;
     a.seq = d_seq;
     a.append = d_seq ? 0 : 1;
+    a.pages = pages;
+    a.page_shift = page_shift;
+    a.max_pages = max_pages;
+    a.n_pages = n_pages;
     attn_plan(S, batch * H, d_cnt != NULL, &a.CH, &a.nsplit);
     const size_t need = a.nsplit > 1 ? (size_t)batch * H * a.nsplit * (Dh + 2) * sizeof(float) : 0;  // this launch's plan
     if (need > ws_bytes || (need && !d_ws))
@@ -387,7 +392,7 @@ extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, in
     // tensor-core body: fp16 cache, head 64 / 128, 1-8 query heads per kv head
     // (LMC_ATTN_TC=0 selects the CUDA-core body; both give the same result)
     const char *tce = getenv("LMC_ATTN_TC");
-    const bool tc = kv_dtype == LMC_KV_F16 && (Dh == 64 || Dh == 128) && G <= 8 && !(tce && tce[0] == '0');
+    const bool tc = kv_dtype == LMC_KV_F16 && (Dh == 64 || Dh == 128) && G <= 8 && !(tce && tce[0] == '0') && !pages;
     const int CH16 = (a.CH + 15) & ~15;
     const size_t smem = tc ? (size_t)(G * Dh + G * CH16 + 2 * G + 2) * sizeof(float) + 16 + (size_t)CH16 * (Dh + 8) * 2
                            : (size_t)(G * Dh + G * a.CH + 2 * G + (ATT_THREADS / 32) * ATT_GROUP * Dh) * sizeof(float);
@@ -419,6 +424,41 @@ extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, in
         LMC_LAUNCH("attention combine", k_attn_combine, dim3(H, batch), Dh, 0, s, a);
     }
     return LMC_OK;
+}
+
+extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, int ldq, const float *k_new,
+                                         const float *v_new, int ldkv, void *k_cache, void *v_cache, int kv_dtype,
+                                         const int *d_pos, const int *d_seq, int batch, int H, int Hkv, int Dh, int S,
+                                         void *d_ws, size_t ws_bytes, const float *rope_cos, const float *rope_sin,
+                                         int *d_cnt, cudaStream_t s) {
+    return attention_impl(out, ldo, q, ldq, k_new, v_new, ldkv, k_cache, v_cache, kv_dtype, d_pos, d_seq, batch, H,
+                          Hkv, Dh, S, d_ws, ws_bytes, rope_cos, rope_sin, d_cnt, NULL, 0, 0, 0, s);
+}
+
+extern "C" int lmc_attention_decode_paged(float *out, const float *q, const float *k_new, const float *v_new,
+                                          void *k_pool, void *v_pool, int kv_dtype, int n_pages, const int *d_pages,
+                                          int max_pages, int page_size, const int *d_pos, int batch, int H, int Hkv,
+                                          int Dh, void *d_ws, size_t ws_bytes, void *stream) {
+    if (!d_pages || n_pages <= 0 || max_pages <= 0 || page_size < 16 || (page_size & (page_size - 1)) ||
+        (long long)max_pages * page_size > (1 << 24))
+        return lmc_set_error(LMC_ERR_INVALID, "attention_paged: pages %d, table %d x page %d", n_pages, max_pages,
+                             page_size);
+    int shift = 0;
+    while ((1 << shift) < page_size) shift++;
+    return attention_impl(out, H * Dh, q, H * Dh, k_new, v_new, Hkv * Dh, k_pool, v_pool, kv_dtype, d_pos, NULL,
+                          batch, H, Hkv, Dh, max_pages * page_size, d_ws, ws_bytes, NULL, NULL, NULL, d_pages, shift,
+                          max_pages, n_pages, lmc_stream(stream));
+}
+
+// LMC_OK, or LMC_ERR_INVALID once after a paged attention met a page id
+// outside its pool (the flag is cleared).
+extern "C" int lmc_attn_status(void) {
+    int v = 0;
+    LMC_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_attn_page_err, sizeof(int)));
+    if (!v) return LMC_OK;
+    const int zero = 0;
+    LMC_CUDA_TRY(cudaMemcpyToSymbol(g_attn_page_err, &zero, sizeof(int)));
+    return lmc_set_error(LMC_ERR_INVALID, "paged attention: a page id outside the pool (page 0 read instead)");
 }
 
 extern "C" int lmc_attention_decode(float *out, const float *q, const float *k_new, const float *v_new,

@@ -97,7 +97,14 @@ struct AttnArgs {
     // `append` is 0, so every row sees the rows of earlier positions.
     const int *seq;
     int append;
+    // Paged cache (NULL: contiguous [batch][Hkv][S][row]): k_cache / v_cache
+    // are pools of pages [page][Hkv][P][row], P = 1 << page_shift positions;
+    // pages[seq * max_pages + t / P] is the page of position t.  A page id
+    // outside [0, n_pages) is not read (page 0 is, and g_attn_page_err is set).
+    const int *pages;
+    int page_shift, max_pages, n_pages;
 };
+__device__ int g_attn_page_err;  // an out-of-range page id was met (lmc_device_status)
 
 
 // One non-empty split: append the new K/V row when it falls here, scores,
@@ -160,18 +167,30 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
     float *ml = sc + G * CH;        // [G][2]
     float *red = ml + 2 * G;        // [nw][ATT_GROUP][Dh]
     const size_t cs = a.seq ? (size_t)a.seq[b] : (size_t)b;  // cache sequence of this row
-    KV *kc = reinterpret_cast<KV *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * RS;
-    KV *vc = reinterpret_cast<KV *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * RS;
+    KV *const kpool = reinterpret_cast<KV *>(a.k_cache), *const vpool = reinterpret_cast<KV *>(a.v_cache);
+    KV *kc = kpool + (cs * a.Hkv + kh) * a.S * RS;
+    KV *vc = vpool + (cs * a.Hkv + kh) * a.S * RS;
+    // row t of this (sequence, kv head): contiguous, or through the page table
+    auto row = [&](KV *seqbase, KV *pool, int t) -> KV * {
+        if (!a.pages) return seqbase + (size_t)t * RS;
+        int pg = __ldg(a.pages + cs * a.max_pages + (t >> a.page_shift));
+        if (pg < 0 || pg >= a.n_pages) {
+            atomicExch(&g_attn_page_err, 1);
+            pg = 0;
+        }
+        return pool + ((((size_t)pg * a.Hkv + kh) << a.page_shift) + (t & ((1 << a.page_shift) - 1))) * RS;
+    };
     const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (Dh / 2) : nullptr;
     const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (Dh / 2) : nullptr;
     if (Q8 && a.append && pos >= t0 && pos < t1) {  // quantize the new rows: warp 0 K, warp 1 V
         if (warp < 2)
-            kv_q8_store_row(reinterpret_cast<KvQ8 *>((warp ? vc : kc) + (size_t)pos * RS),
+            kv_q8_store_row(reinterpret_cast<KvQ8 *>(warp ? row(vc, vpool, pos) : row(kc, kpool, pos)),
                             (warp ? a.v_new : a.k_new) + (size_t)b * a.ldkv + (size_t)kh * Dh, warp ? nullptr : rc,
                             rs, Dh, lane);
     } else if (a.append && pos >= t0 && pos < t1) {  // append this step's K/V row (K rotated first when RoPE applies)
         const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
         const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
+        KV *kp = row(kc, kpool, pos), *vp = row(vc, vpool, pos);
         for (int d = threadIdx.x; d < Dh / 2; d += NTH) {
             float k0 = kn[2 * d], k1 = kn[2 * d + 1];
             if (rc) {
@@ -181,10 +200,10 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
                 k1 = r1;
             }
             if constexpr (!Q8) {
-                kc[(size_t)pos * Dh + 2 * d] = kv_cvt<KV>(k0);
-                kc[(size_t)pos * Dh + 2 * d + 1] = kv_cvt<KV>(k1);
-                vc[(size_t)pos * Dh + 2 * d] = kv_cvt<KV>(vn[2 * d]);
-                vc[(size_t)pos * Dh + 2 * d + 1] = kv_cvt<KV>(vn[2 * d + 1]);
+                kp[2 * d] = kv_cvt<KV>(k0);
+                kp[2 * d + 1] = kv_cvt<KV>(k1);
+                vp[2 * d] = kv_cvt<KV>(vn[2 * d]);
+                vp[2 * d + 1] = kv_cvt<KV>(vn[2 * d + 1]);
             }
         }
     }
@@ -209,7 +228,7 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
         for (int tb = warp * 32; tb < n; tb += nw * 32) {
             const int tl = tb + lane;
             if (tl >= n) continue;
-            const KV *kr = kc + (size_t)(t0 + tl) * RS;
+            const KV *kr = row(kc, kpool, t0 + tl);
             float sg[ATT_GROUP];
 #pragma unroll
             for (int g = 0; g < ATT_GROUP; g++) sg[g] = 0.0f;
@@ -281,11 +300,11 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
 #pragma unroll
             for (int uu = 0; uu < U; uu++) {
                 const int tt = t + uu * nw;
-                const KV *vr = vc + (size_t)(t0 + tt) * RS + lane;
+                const KV *vrow = row(vc, vpool, t0 + min(tt, n - 1)), *vr = vrow + lane;
 #pragma unroll
                 for (int i = 0; i < DPLC; i++) v[uu][i] = (tt < n && i < dpl) ? kv_ld<KV>(vr + 32 * i) : 0.0f;
                 if (Q8 && tt < n) {
-                    const float vs = kv_q8_scale(reinterpret_cast<const KvQ8 *>(vc + (size_t)(t0 + tt) * RS), Dh);
+                    const float vs = kv_q8_scale(reinterpret_cast<const KvQ8 *>(vrow), Dh);
 #pragma unroll
                     for (int i = 0; i < DPLC; i++) v[uu][i] *= vs;
                 }

@@ -111,6 +111,9 @@ int lmc_sample_launch(const float *d_logits, int n, int ld, int rows, float temp
  * and split count for context S and bh = batch x heads; fine = the splits
  * are merged inside the launch (arrival counters). */
 void lmc_attn_plan(int S, int bh, int fine, int *CH, int *nsplit);
+/* LMC_OK, or LMC_ERR_INVALID once after a paged attention met a page id
+ * outside its pool. */
+int lmc_attn_status(void);
 
 /* ---- persistent decode step (step_kernel.cu) -------------------------------
  * A whole decode step as ONE cooperative launch: every CTA walks the same list

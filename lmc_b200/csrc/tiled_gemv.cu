@@ -309,6 +309,8 @@ __global__ void __launch_bounds__(NTHR, 2) k_gemv_tiled(TArgs a) {
 extern "C" int lmc_device_status(void) {
     const int st = lmc_step_status();
     if (st != LMC_OK) return st;
+    const int at = lmc_attn_status();
+    if (at != LMC_OK) return at;
     int v = 0;
     LMC_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_tiled_timeout, sizeof(int)));
     const int g = lmc_gemm_status();

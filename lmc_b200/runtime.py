@@ -42,6 +42,8 @@ SIGNATURES = {
     "lmc_attention_workspace_bytes": ([_i, _i, _i, _i], _sz),
     "lmc_attention_decode": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp], _i),
     "lmc_attention_decode_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _vp], _i),
+    "lmc_attention_decode_paged": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _i, _i, _i, _vp, _sz,
+                                    _vp], _i),
     "lmc_model_load": ([_c.c_char_p, _i, _i, _c.POINTER(_vp)], _i),
     "lmc_nccl_unique_id": ([_vp], _i),
     "lmc_model_load_tp": ([_c.c_char_p, _i, _i, _i, _i, _vp, _c.POINTER(_vp)], _i),

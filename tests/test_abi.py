@@ -151,6 +151,11 @@ def test_entry_points_validate_arguments_first():
         ("lmc_attention_decode_noalloc", (None, p, p, p, p, p, 0, p, 1, 32, 8, 128, 1024, None), b"null"),
         ("lmc_attention_decode_noalloc", (p, p, p, p, p, None, 0, p, 1, 32, 8, 128, 1024, None), b"null"),
         ("lmc_attention_decode_noalloc", (p, p, p, p, p, p, 0, p, 1, 30, 8, 128, 1024, None), b"Hkv=8"),
+        # paged cache: a page size that is not a power of two, an empty pool
+        ("lmc_attention_decode_paged", (p, p, p, p, p, p, 0, 8, p, 4, 24, p, 1, 32, 8, 128, p, 0, None),
+         b"attention_paged"),
+        ("lmc_attention_decode_paged", (p, p, p, p, p, p, 0, 0, p, 4, 64, p, 1, 32, 8, 128, p, 0, None),
+         b"attention_paged"),
         ("lmc_set_wait_limit", (ctypes.c_longlong(-5),), b"set_wait_limit"),
         ("lmc_wait_selftest", (7,), b"wait_selftest"),
         ("lmc_sample_top_p", (None, 10, 1, 1.0, 0.9, None, None, None), b"sample_top_p"),

@@ -337,3 +337,64 @@ def test_attention_int8_rows(cuda, orc, H, Hkv, Dh, S, pos):
         assert (kc[b, :, poss[b], :Dh + 4] == knew[b][0][:, :Dh + 4]).all()
         assert (vc[b, :, poss[b], :Dh + 4] == knew[b][1][:, :Dh + 4]).all()
     assert rt.lib().lmc_device_status() == 0
+
+
+@pytest.mark.parametrize("kvd", [rt.KV_F32, rt.KV_F16, rt.KV_Q8])
+@pytest.mark.parametrize("H,Hkv,Dh,P,pos", [(12, 12, 64, 16, 135), (32, 4, 64, 64, 700), (32, 8, 128, 256, 1500),
+                                           (8, 8, 64, 16, 0)])
+def test_attention_paged(cuda, orc, kvd, H, Hkv, Dh, P, pos):
+    """lmc_attention_decode_paged: the pages of two sequences scattered over
+    a pool (in shuffled order) give the same output as the contiguous cache
+    (the oracle on the rows the cache holds), and the new row lands in the
+    page the table names."""
+    rng = np.random.default_rng(pos + P)
+    B, maxp = 2, (pos + P) // P + 1
+    S = maxp * P
+    npages = 2 * B * maxp + 3
+    cont = rng.normal(0, 1, (B, Hkv, S, Dh)).astype(np.float32)
+    vcont = rng.normal(0, 1, (B, Hkv, S, Dh)).astype(np.float32)
+    if kvd == rt.KV_Q8:
+        kraw, kvals = q8_cache(orc, cont)
+        vraw, vvals = q8_cache(orc, vcont)
+    else:
+        dt = np.float16 if kvd == rt.KV_F16 else np.float32
+        kraw, vraw = cont.astype(dt), vcont.astype(dt)
+        kvals, vvals = kraw.astype(np.float32), vraw.astype(np.float32)
+    RB = kraw.shape[-1]
+    table = rng.permutation(npages)[:B * maxp].astype(np.int32).reshape(B, maxp)
+    kpool = np.zeros((npages, Hkv, P, RB), kraw.dtype)
+    vpool = np.zeros((npages, Hkv, P, RB), vraw.dtype)
+    for b in range(B):
+        for j in range(maxp):
+            kpool[table[b, j]] = kraw[b, :, j * P:(j + 1) * P]
+            vpool[table[b, j]] = vraw[b, :, j * P:(j + 1) * P]
+    q = rng.normal(0, 1, (B, H * Dh)).astype(np.float32)
+    kn = rng.normal(0, 1, (B, Hkv * Dh)).astype(np.float32)
+    vn = rng.normal(0, 1, (B, Hkv * Dh)).astype(np.float32)
+    poss = np.array([pos, max(pos // 3, 0)], np.int32)
+    want = []
+    for b in range(B):
+        k2, v2 = kvals[b].copy(), vvals[b].copy()
+        k2[:, poss[b]] = orc.kv_round_rows(kn[b].reshape(Hkv, Dh), kvd)
+        v2[:, poss[b]] = orc.kv_round_rows(vn[b].reshape(Hkv, Dh), kvd)
+        want.append(orc.attention(q[b], k2, v2, H, Hkv, Dh, S, int(poss[b])))
+    want = np.stack(want)
+    dk, dv, dt_ = dev(cuda, kpool), dev(cuda, vpool), dev(cuda, table)
+    out = cuda.empty((B, H * Dh), dtype=cuda.float32, device="cuda")
+    wsb = rt.lib().lmc_attention_workspace_bytes(B, H, Dh, S)
+    ws = cuda.empty(max(wsb, 4), dtype=cuda.uint8, device="cuda")
+    dq, dkn, dvn, dpos = dev(cuda, q), dev(cuda, kn), dev(cuda, vn), dev(cuda, poss)
+    rt.call("lmc_attention_decode_paged", out.data_ptr(), dq.data_ptr(), dkn.data_ptr(), dvn.data_ptr(),
+            dk.data_ptr(), dv.data_ptr(), kvd, npages, dt_.data_ptr(), maxp, P, dpos.data_ptr(), B, H, Hkv, Dh,
+            ws.data_ptr(), wsb, None)
+    assert rel_err(out.cpu().numpy(), want) < 1e-5
+    kp = dk.cpu().numpy()
+    for b in range(B):
+        page, off = table[b, poss[b] // P], poss[b] % P
+        got_row = kp[page, :, off]
+        if kvd == rt.KV_Q8:
+            got_vals = got_row[:, :Dh].view(np.int8).astype(np.float32) * got_row[:, Dh:Dh + 4].copy().view(np.float32)
+        else:
+            got_vals = got_row.astype(np.float32)
+        assert np.array_equal(got_vals, orc.kv_round_rows(kn[b].reshape(Hkv, Dh), kvd))
+    assert rt.lib().lmc_device_status() == 0
