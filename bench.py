@@ -414,12 +414,15 @@ def run_model(args, rank, world, local_rank, dist):
     kvd = {"f16": rt.KV_F16, "f32": rt.KV_F32, "q8": rt.KV_Q8}[args.kv]
     B = args.batch
     rows = args.prefill_rows or None
+    t_load = time.perf_counter()  # GGUF parse + weight upload (the file is in the page cache: just written)
     if dist and world > 1:
         from lmc_b200 import tp as tpm
         nid = tpm.exchange_id(dist, rt.nccl_unique_id)
         m = rt.Model(path, max_batch=B, kv_dtype=kvd, tp=(rank, world, nid), max_rows=rows)
     else:
         m = rt.Model(path, max_batch=B, kv_dtype=kvd, max_rows=rows)
+    torch.cuda.synchronize()
+    t_load = time.perf_counter() - t_load
     prompts = np.random.default_rng(0).integers(0, m.cfg.vocab_size, (B, args.prompt)).astype(np.int32)
 
     def slowest(dt):
@@ -465,6 +468,7 @@ def run_model(args, rank, world, local_rank, dist):
                "graph_kernels_per_step": m.graph_kernels(), "weights_bytes": wbytes,
                "weights_hbm_frac_per_rank": round(wbytes / world / step_s / 1e9 / peak, 4),
                "tensor_parallel": world, "data": "synthetic (random blocks of the named formats)",
+               "load_s": round(t_load, 3), "load_gbs": round(wbytes / max(t_load, 1e-9) / 1e9, 2),
                "timing": "host clock around synchronised generate runs (second of two)", "peak_kind": kind_p}
         if t_prefill:
             res.update({"prefill_rows": rows, "prefill_tok_s": round(B * args.prompt / t_prefill, 2)})

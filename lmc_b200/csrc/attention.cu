@@ -273,8 +273,7 @@ __global__ void k_kv_append(AttnArgs a) {
         if (w < 2)
             kv_q8_store_row(reinterpret_cast<KvQ8 *>(w ? vc : kc), w ? vn : kn, w ? nullptr : rc, rs, Dh,
                             threadIdx.x & 31);
-        return;
-    }
+    } else {
     for (int d = threadIdx.x; d < Dh / 2; d += blockDim.x) {
         float k0 = kn[2 * d], k1 = kn[2 * d + 1];
         if (rc) {
@@ -283,12 +282,11 @@ __global__ void k_kv_append(AttnArgs a) {
             k0 = r0;
             k1 = r1;
         }
-        if constexpr (!KvT<KV>::Q8) {
-            kc[2 * d] = kv_cvt<KV>(k0);
-            kc[2 * d + 1] = kv_cvt<KV>(k1);
-            vc[2 * d] = kv_cvt<KV>(vn[2 * d]);
-            vc[2 * d + 1] = kv_cvt<KV>(vn[2 * d + 1]);
-        }
+        kc[2 * d] = kv_cvt<KV>(k0);
+        kc[2 * d + 1] = kv_cvt<KV>(k1);
+        vc[2 * d] = kv_cvt<KV>(vn[2 * d]);
+        vc[2 * d + 1] = kv_cvt<KV>(vn[2 * d + 1]);
+    }
     }
 }
 

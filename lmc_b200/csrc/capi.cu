@@ -7,6 +7,11 @@
 #include "lmc_common.cuh"
 #include "lmc_internal.h"
 
+#include <algorithm>
+#include <mutex>
+#include <thread>
+#include <vector>
+
 static thread_local char g_err[1024];
 
 extern "C" int lmc_set_error(int code, const char *fmt, ...) {
@@ -114,6 +119,80 @@ extern "C" int lmc_tensor_bytes(uint32_t type, size_t n_elements, size_t *bytes)
 // ---------------------------------------------------------------------------
 // qtensor: raw GGUF blocks on the device (+ a tiled copy for tensor-core GEMV)
 // ---------------------------------------------------------------------------
+// ---------------------------------------------------------------------------
+// Host -> device copies of model weights through pinned staging buffers.
+// A copy from pageable memory (or a mapped file, whose pages are read on
+// first touch) is split into chunks: host threads copy chunk i into one of
+// two pinned buffers while the DMA engine moves chunk i - 1 to the device,
+// so reading the file and the PCIe transfer overlap.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t STAGE_BYTES = 32u << 20;  // per buffer
+constexpr int STAGE_THREADS = 8;           // host threads filling a buffer
+struct Stage {
+    std::mutex mu;
+    void *buf[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    cudaStream_t st = nullptr;
+    int dev = -1;
+};
+Stage g_stage;
+
+void par_copy(void *dst, const void *src, size_t n) {
+    const size_t piece = (n + STAGE_THREADS - 1) / STAGE_THREADS;
+    if (n < (4u << 20)) {
+        memcpy(dst, src, n);
+        return;
+    }
+    std::vector<std::thread> th;
+    for (int i = 1; i < STAGE_THREADS; i++) {
+        const size_t o = piece * i;
+        if (o >= n) break;
+        th.emplace_back([=] { memcpy((char *)dst + o, (const char *)src + o, std::min(piece, n - o)); });
+    }
+    memcpy(dst, src, std::min(piece, n));
+    for (auto &t : th) t.join();
+}
+}  // namespace
+
+extern "C" int lmc_h2d_staged(void *d_dst, const void *h_src, size_t bytes) {
+    if (!bytes) return LMC_OK;
+    if (bytes < (1u << 20)) {  // small: one plain copy
+        const cudaError_t e = cudaMemcpy(d_dst, h_src, bytes, cudaMemcpyHostToDevice);
+        return e == cudaSuccess ? LMC_OK : lmc_set_error(LMC_ERR_CUDA, "h2d: %s", cudaGetErrorString(e));
+    }
+    std::lock_guard<std::mutex> lock(g_stage.mu);
+    int dev = 0;
+    LMC_CUDA_TRY(cudaGetDevice(&dev));
+    if (g_stage.dev != dev) {  // (re)create the staging set on this device
+        for (int i = 0; i < 2; i++) {
+            if (g_stage.buf[i]) cudaFreeHost(g_stage.buf[i]);
+            if (g_stage.done[i]) cudaEventDestroy(g_stage.done[i]);
+            g_stage.buf[i] = nullptr;
+            g_stage.done[i] = nullptr;
+        }
+        if (g_stage.st) cudaStreamDestroy(g_stage.st);
+        g_stage.st = nullptr;
+        g_stage.dev = -1;
+        for (int i = 0; i < 2; i++) {
+            LMC_CUDA_TRY(cudaHostAlloc(&g_stage.buf[i], STAGE_BYTES, cudaHostAllocDefault));
+            LMC_CUDA_TRY(cudaEventCreateWithFlags(&g_stage.done[i], cudaEventDisableTiming));
+        }
+        LMC_CUDA_TRY(cudaStreamCreateWithFlags(&g_stage.st, cudaStreamNonBlocking));
+        g_stage.dev = dev;
+    }
+    int k = 0;
+    for (size_t o = 0; o < bytes; o += STAGE_BYTES, k ^= 1) {
+        const size_t n = std::min(STAGE_BYTES, bytes - o);
+        LMC_CUDA_TRY(cudaEventSynchronize(g_stage.done[k]));  // the DMA that last read buffer k is over
+        par_copy(g_stage.buf[k], (const char *)h_src + o, n);
+        LMC_CUDA_TRY(cudaMemcpyAsync((char *)d_dst + o, g_stage.buf[k], n, cudaMemcpyHostToDevice, g_stage.st));
+        LMC_CUDA_TRY(cudaEventRecord(g_stage.done[k], g_stage.st));
+    }
+    LMC_CUDA_TRY(cudaStreamSynchronize(g_stage.st));
+    return LMC_OK;
+}
+
 extern "C" int lmc_qtensor_upload(uint32_t type, int rows, int cols, const void *h_blocks, size_t bytes,
                                   lmc_qtensor **out) {
     if (!out || !h_blocks || rows <= 0 || cols <= 0) return lmc_set_error(LMC_ERR_INVALID, "qtensor_upload: args");
@@ -132,8 +211,13 @@ extern "C" int lmc_qtensor_upload(uint32_t type, int rows, int cols, const void 
     // bytes past the last block (src/quant.c:506,515).
     cudaError_t e = cudaMalloc(&t->blocks, need + LMC_BLOCK_PAD);
     if (e != cudaSuccess) { free(t); return lmc_set_error(LMC_ERR_OOM, "qtensor_upload: %s", cudaGetErrorString(e)); }
-    e = cudaMemcpy(t->blocks, h_blocks, need, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemset((char *)t->blocks + need, 0, LMC_BLOCK_PAD);
+    rc = lmc_h2d_staged(t->blocks, h_blocks, need);
+    if (rc) {
+        cudaFree(t->blocks);
+        free(t);
+        return rc;
+    }
+    e = cudaMemset((char *)t->blocks + need, 0, LMC_BLOCK_PAD);
     if (e != cudaSuccess) {
         cudaFree(t->blocks);
         free(t);

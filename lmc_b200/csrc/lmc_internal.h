@@ -30,6 +30,9 @@ struct lmc_qtensor {
 };
 
 int lmc_set_error(int code, const char *fmt, ...);
+/* Host -> device copy through pinned staging buffers (chunks filled by
+ * host threads while the previous chunk's DMA runs); synchronous. */
+int lmc_h2d_staged(void *d_dst, const void *h_src, size_t bytes);
 int lmc_qtensor_concat(const struct lmc_qtensor *const *parts, int n, struct lmc_qtensor **out);
 int lmc_tensor_bytes(uint32_t type, size_t n_elements, size_t *bytes);
 int lmc_sm_count(void);

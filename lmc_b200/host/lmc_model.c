@@ -10,12 +10,16 @@
  * captured once as a CUDA graph and replayed for every position, and greedy
  * generation runs without the host waiting between tokens.
  */
-#define _POSIX_C_SOURCE 200809L
+#define _DEFAULT_SOURCE
+#include <fcntl.h>
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
 #include <time.h>
+#include <unistd.h>
 
 #include <nccl.h>
 
@@ -272,18 +276,65 @@ static int check_complete(const lmc_model *m) {
     return LMC_OK;
 }
 
+/* The GGUF file mapped read-only (pages are read from the file as the
+ * parser and the staged uploads touch them: no whole-file copy in host
+ * memory); a plain read into a heap buffer when mapping fails. */
+typedef struct {
+    unsigned char *p;
+    size_t n;
+    int mapped;
+} FileView;
+static int file_open(const char *path, FileView *v) {
+    v->p = NULL;
+    v->n = 0;
+    v->mapped = 0;
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return lmc_set_error(LMC_ERR_IO, "cannot open %s", path);
+    struct stat st;
+    if (fstat(fd, &st) || st.st_size <= 0) {
+        close(fd);
+        return lmc_set_error(LMC_ERR_IO, "cannot stat %s", path);
+    }
+    v->n = (size_t)st.st_size;
+    void *p = mmap(NULL, v->n, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (p != MAP_FAILED) {
+        madvise(p, v->n, MADV_SEQUENTIAL);
+        close(fd);
+        v->p = (unsigned char *)p;
+        v->mapped = 1;
+        return LMC_OK;
+    }
+    v->p = (unsigned char *)malloc(v->n);
+    if (!v->p) {
+        close(fd);
+        return lmc_set_error(LMC_ERR_OOM, "host buffer for %s", path);
+    }
+    size_t got = 0;
+    while (got < v->n) {
+        const ssize_t k = read(fd, v->p + got, v->n - got);
+        if (k <= 0) break;
+        got += (size_t)k;
+    }
+    close(fd);
+    if (got != v->n) {
+        free(v->p);
+        v->p = NULL;
+        return lmc_set_error(LMC_ERR_IO, "short read of %s", path);
+    }
+    return LMC_OK;
+}
+static void file_close(FileView *v) {
+    if (!v->p) return;
+    if (v->mapped) munmap(v->p, v->n);
+    else free(v->p);
+    v->p = NULL;
+}
+
 static int load(lmc_model *m, const char *path) {
-    FILE *f = fopen(path, "rb");
-    if (!f) return lmc_set_error(LMC_ERR_IO, "cannot open %s", path);
-    fseek(f, 0, SEEK_END);
-    long fsz = ftell(f);
-    fseek(f, 0, SEEK_SET);
-    unsigned char *buf = (unsigned char *)malloc((size_t)fsz + 64);
-    if (!buf) { fclose(f); return lmc_set_error(LMC_ERR_OOM, "host buffer for %s", path); }
-    size_t got = fread(buf, 1, (size_t)fsz, f);
-    fclose(f);
-    if (got != (size_t)fsz) { free(buf); return lmc_set_error(LMC_ERR_IO, "short read of %s", path); }
-    memset(buf + fsz, 0, 64);
+    FileView fv;
+    TRY(file_open(path, &fv));
+    unsigned char *buf = fv.p;
+    const size_t fsz = fv.n;
     Rd r = {buf, buf + fsz, 0};
     lmc_model_config *c = &m->cfg;
     int rc = LMC_OK;
@@ -391,7 +442,7 @@ static int load(lmc_model *m, const char *path) {
     }
 done:
     free(ti);
-    free(buf);
+    file_close(&fv);
     return rc;
 }
 
