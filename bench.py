@@ -15,7 +15,10 @@ half of the metric) with LMc's matmul_vec time on the same weights beside it.
 
 GPT-2 Small does not shard: with --gpus N each rank decodes its own replica
 (weak scaling, no collective on the data path); value = all ranks' tokens /
-the slowest rank's time.
+the slowest rank's time.  With N > 1 the line also carries "tp": the 8B
+shape decoded tensor parallel over the same N ranks (batch 1 and 32; heads,
+FFN rows and vocabulary sharded, two NCCL all-reduces per layer); --no-tp
+skips it.
 
 Other workloads (--workload), one JSON line each (sweep: one per case):
   gemv       one GEMV (--type/--rows/--cols/--batch; default Q4_K 3072x768 B=1)
@@ -337,8 +340,22 @@ def run_gpt2(args, rank, world, local_rank, dist):
                             "reference_matmul_vec_us": round(ref_c1 * 1e6, 2) if ref_c1 else None},
                 "cpu_baseline": cpu,
                 "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
     m.close()
+    if world > 1 and dist and not args.no_tp:
+        # GPT-2 Small does not shard (replicas above); the 8B shape decodes
+        # tensor parallel over the same ranks: batch 1 and batch 32
+        tp = {"model": "llama-8b shape (32 x 4096, FFN 14336, 32/8 heads, vocab 128256), random Q4_K/Q6_K blocks",
+              "tensor_parallel": world, "kv": "f16", "prompt": 16, "gen": 16}
+        for B in (1, 32):
+            a = argparse.Namespace(workload="llama8b", kv="f16", batch=B, prompt=16, gen=16, prefill_rows=0)
+            r = model_decode(a, rank, world, local_rank, dist)
+            if rank == 0:
+                tp[f"batch{B}_tok_s"] = r["value"]
+                tp[f"batch{B}_ms_per_step"] = r["ms_per_step_decode"]
+        if rank == 0:
+            line["tp"] = tp
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
@@ -394,9 +411,16 @@ def run_gemv(args):
 
 
 def run_model(args, rank, world, local_rank, dist):
+    res = model_decode(args, rank, world, local_rank, dist)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+def model_decode(args, rank, world, local_rank, dist):
     """Prompt feed + greedy decode through lmc_model_generate (one graph
-    launch per step for the whole batch); with --tp every rank holds its
-    tensor-parallel shard and the times are the maximum over the ranks."""
+    launch per step for the whole batch); with a process group every rank
+    holds its tensor-parallel shard and the times are the maximum over the
+    ranks.  Returns the result line on rank 0 (None elsewhere)."""
     import torch
     from lmc_b200 import runtime as rt
     from lmc_b200 import synth
@@ -414,6 +438,7 @@ def run_model(args, rank, world, local_rank, dist):
     kvd = {"f16": rt.KV_F16, "f32": rt.KV_F32, "q8": rt.KV_Q8}[args.kv]
     B = args.batch
     rows = args.prefill_rows or None
+    res = None
     t_load = time.perf_counter()  # GGUF parse + weight upload (the file is in the page cache: just written)
     if dist and world > 1:
         from lmc_b200 import tp as tpm
@@ -472,8 +497,8 @@ def run_model(args, rank, world, local_rank, dist):
                "timing": "host clock around synchronised generate runs (second of two)", "peak_kind": kind_p}
         if t_prefill:
             res.update({"prefill_rows": rows, "prefill_tok_s": round(B * args.prompt / t_prefill, 2)})
-        print(json.dumps(res), flush=True)
     m.close()
+    return res if rank == 0 else None
 
 
 def main():
@@ -492,6 +517,8 @@ def main():
     ap.add_argument("--kv", choices=["f16", "f32", "q8"], default="f16")
     ap.add_argument("--prefill-rows", type=int, default=0)
     ap.add_argument("--tp", action="store_true", help="tensor parallel over the torchrun ranks (llama8b)")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="gpt2 on several GPUs: skip the tensor-parallel 8B line (tp sub-object)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
