@@ -471,6 +471,42 @@ __device__ __forceinline__ void fflush(const FAcc &o, float *acc_rt, int nb, int
 __device__ __forceinline__ void load_x_f32(float *xs, float *mr, const TArgs &a) {
     const int K = a.KB * 256, tid = threadIdx.x;
     float *mean = mr, *rstd = mr + 2;
+    const bool ln = a.pro == LMC_PRO_LAYERNORM;
+    if ((ln || a.pro == LMC_PRO_RMSNORM) && K <= NTHR * 4) {
+        // rows of at most one float4 per thread: the x, weight and bias loads
+        // are issued before the statistics are waited for (one trip to L2)
+        const int k = tid * 4;
+        const bool act = k < K;
+        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0, w = v0, c = v0;
+        if (act) {
+            v0 = __ldcg(reinterpret_cast<const float4 *>(a.x + k));
+            if (a.nb > 1) v1 = __ldcg(reinterpret_cast<const float4 *>(a.x + a.ldx + k));
+            w = __ldg(reinterpret_cast<const float4 *>(a.pw + k));
+            if (ln) c = __ldg(reinterpret_cast<const float4 *>(a.pb + k));
+        }
+        if (tid < a.nb) {
+            const double sx = __ldcg(a.stats + 2 * tid), sq = __ldcg(a.stats + 2 * tid + 1);
+            const double mu = ln ? sx / (double)K : 0.0;
+            const double var = fmax(sq / (double)K - mu * mu, 0.0);
+            mean[tid] = (float)mu;
+            rstd[tid] = 1.0f / sqrtf((float)var + (ln ? 1e-5f : a.eps));
+        }
+        __syncthreads();
+        if (act) {
+#pragma unroll
+            for (int b = 0; b < 2; b++) {
+                if (b >= a.nb) break;
+                const float4 v = b ? v1 : v0;
+                const float m = mean[b], r = rstd[b];
+                const float4 o = ln ? make_float4((v.x - m) * r * w.x + c.x, (v.y - m) * r * w.y + c.y,
+                                                  (v.z - m) * r * w.z + c.z, (v.w - m) * r * w.w + c.w)
+                                    : make_float4(w.x * r * v.x, w.y * r * v.y, w.z * r * v.z, w.w * r * v.w);
+                *reinterpret_cast<float4 *>(xs + b * K + k) = o;
+            }
+        }
+        __syncthreads();
+        return;
+    }
     if (a.pro == LMC_PRO_LAYERNORM || a.pro == LMC_PRO_RMSNORM) {
         if (tid < a.nb) {
             const double sx = __ldcg(a.stats + 2 * tid), sq = __ldcg(a.stats + 2 * tid + 1);
@@ -649,6 +685,209 @@ __device__ __forceinline__ int gemv_op_impl(uint8_t *smem, const DOp &op, Ring &
     return (ok ? GEMV_OK : 0) | (late_prefill ? GEMV_LATE : 0);
 }
 
+// The attention body of the persistent step for at most two query heads per
+// kv head.  Warp w takes positions t0 + w, t0 + w + 8, ...; lane l holds dims
+// [DPL l, DPL l + DPL) of q, of the K and V rows and of the output, so a
+// score is DPL FMAs per lane and a warp reduction, and a K or V row is one
+// vector load per lane.  Each warp keeps an online softmax over its
+// positions (running max, sum and accumulator), with the loads of a pass of
+// PP positions issued before any is used; the eight warps' states are then
+// merged in shared memory.  The new row (position pos) is made in registers
+// by the warp that owns it - K rotated, rounded to the cache form - and
+// stored to the cache from there.  One L2 round trip for q and the rows
+// instead of the split body's five.  Same statistics and output format as
+// split_body (so attn_merge_last merges either).
+template <typename KV, int DH>
+__device__ __forceinline__ void attn_short(const AttnArgs &a, float *sm, int kh, int b, int pos, int t0, int t1,
+                                           float *wsb, size_t hstride, bool single) {
+    constexpr int DPL = DH / 32, PP = DH == 64 ? 8 : 4;
+    constexpr bool Q8 = KvT<KV>::Q8, F16 = sizeof(KV) == 2;
+    const int G = a.H / a.Hkv, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, d0 = DPL * lane;
+    const int RS = kv_rs<KV>(DH), n = t1 - t0;
+    KV *kc = reinterpret_cast<KV *>(a.k_cache) + ((size_t)b * a.Hkv + kh) * a.S * RS;
+    KV *vc = reinterpret_cast<KV *>(a.v_cache) + ((size_t)b * a.Hkv + kh) * a.S * RS;
+    const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (DH / 2) : nullptr;
+    const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (DH / 2) : nullptr;
+    const float scale = 1.0f / sqrtf((float)DH);
+    // q of the group's heads (rotated when RoPE applies)
+    float q[2][DPL];
+#pragma unroll
+    for (int g = 0; g < 2; g++) {
+        const float *qb = a.q + (size_t)b * a.ldq + ((size_t)kh * G + (g < G ? g : 0)) * DH + d0;
+#pragma unroll
+        for (int i = 0; i < DPL; i += 2) {
+            float x0 = __ldcg(qb + i), x1 = __ldcg(qb + i + 1);
+            if (rc) {
+                const float c = rc[d0 / 2 + i / 2], sn = rs[d0 / 2 + i / 2];
+                const float r0 = x0 * c - x1 * sn, r1 = x0 * sn + x1 * c;
+                x0 = r0;
+                x1 = r1;
+            }
+            q[g][i] = x0;
+            q[g][i + 1] = x1;
+        }
+    }
+    // the new row, made by the warp whose positions include it
+    const int tp = pos - t0;
+    const bool mine_new = tp >= 0 && tp < n && (tp & 7) == warp;
+    float kn[DPL], vn[DPL], kns = 1.0f, vns = 1.0f;
+    if (mine_new) {
+        const float *kp = a.k_new + (size_t)b * a.ldkv + (size_t)kh * DH + d0;
+        const float *vp = a.v_new + (size_t)b * a.ldkv + (size_t)kh * DH + d0;
+#pragma unroll
+        for (int i = 0; i < DPL; i += 2) {
+            float x0 = __ldcg(kp + i), x1 = __ldcg(kp + i + 1);
+            if (rc) {
+                const float c = rc[d0 / 2 + i / 2], sn = rs[d0 / 2 + i / 2];
+                const float r0 = x0 * c - x1 * sn, r1 = x0 * sn + x1 * c;
+                x0 = r0;
+                x1 = r1;
+            }
+            kn[i] = x0;
+            kn[i + 1] = x1;
+            vn[i] = __ldcg(vp + i);
+            vn[i + 1] = __ldcg(vp + i + 1);
+        }
+        KV *kr = kc + (size_t)pos * RS, *vr = vc + (size_t)pos * RS;
+        if constexpr (Q8) {  // as kv_q8_store_row: m = max|x| over the row, codes, scale
+            float mk = 0.0f, mv = 0.0f;
+#pragma unroll
+            for (int i = 0; i < DPL; i++) {
+                mk = fmaxf(mk, fabsf(kn[i]));
+                mv = fmaxf(mv, fabsf(vn[i]));
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                mk = fmaxf(mk, __shfl_xor_sync(0xffffffffu, mk, off));
+                mv = fmaxf(mv, __shfl_xor_sync(0xffffffffu, mv, off));
+            }
+            const float ik = mk > 0.0f ? 127.0f / mk : 0.0f, iv = mv > 0.0f ? 127.0f / mv : 0.0f;
+            int8_t *kq = reinterpret_cast<int8_t *>(kr), *vq = reinterpret_cast<int8_t *>(vr);
+#pragma unroll
+            for (int i = 0; i < DPL; i++) {
+                const int ck = max(-127, min(127, __float2int_rn(__fmul_rn(kn[i], ik))));
+                const int cv = max(-127, min(127, __float2int_rn(__fmul_rn(vn[i], iv))));
+                kq[d0 + i] = (int8_t)ck;
+                vq[d0 + i] = (int8_t)cv;
+                kn[i] = (float)ck;  // K: codes (the score takes the row scale after the dot)
+                vn[i] = (float)cv;
+            }
+            kns = mk / 127.0f;
+            vns = mv / 127.0f;
+            if (lane == 0) {
+                *reinterpret_cast<float *>(kq + DH) = kns;
+                *reinterpret_cast<float *>(vq + DH) = vns;
+            }
+#pragma unroll
+            for (int i = 0; i < DPL; i++) vn[i] *= vns;
+        } else {
+#pragma unroll
+            for (int i = 0; i < DPL; i++) {
+                kr[d0 + i] = kv_cvt<KV>(kn[i]);
+                vr[d0 + i] = kv_cvt<KV>(vn[i]);
+                if (F16) {
+                    kn[i] = __half2float(__float2half_rn(kn[i]));
+                    vn[i] = __half2float(__float2half_rn(vn[i]));
+                }
+            }
+        }
+    }
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}, acc[2][DPL];
+#pragma unroll
+    for (int g = 0; g < 2; g++)
+#pragma unroll
+        for (int i = 0; i < DPL; i++) acc[g][i] = 0.0f;
+    for (int p0 = warp; p0 < n; p0 += 8 * PP) {
+        float kr[PP][DPL], vr[PP][DPL], ks[PP], vs[PP];
+#pragma unroll
+        for (int j = 0; j < PP; j++) {  // every load of the pass in flight
+            const int t = p0 + 8 * j;
+            ks[j] = vs[j] = 1.0f;
+#pragma unroll
+            for (int i = 0; i < DPL; i++) kr[j][i] = vr[j][i] = 0.0f;
+            if (t < n && t != tp) {
+                const KV *kp = kc + (size_t)(t0 + t) * RS + d0, *vp = vc + (size_t)(t0 + t) * RS + d0;
+#pragma unroll
+                for (int i = 0; i < DPL; i++) {
+                    kr[j][i] = kv_ld<KV>(kp + i);
+                    vr[j][i] = kv_ld<KV>(vp + i);
+                }
+                if constexpr (Q8) {
+                    ks[j] = kv_q8_scale(reinterpret_cast<const KvQ8 *>(kc + (size_t)(t0 + t) * RS), DH);
+                    vs[j] = kv_q8_scale(reinterpret_cast<const KvQ8 *>(vc + (size_t)(t0 + t) * RS), DH);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < PP; j++) {
+            const int t = p0 + 8 * j;
+            if (t >= n) break;
+            if (t == tp) {
+#pragma unroll
+                for (int i = 0; i < DPL; i++) {
+                    kr[j][i] = kn[i];
+                    vr[j][i] = vn[i];
+                }
+                ks[j] = kns;
+            } else if (Q8) {
+#pragma unroll
+                for (int i = 0; i < DPL; i++) vr[j][i] *= vs[j];
+            }
+#pragma unroll
+            for (int g = 0; g < 2; g++) {
+                if (g >= G) break;
+                float s = 0.0f;
+#pragma unroll
+                for (int i = 0; i < DPL; i++) s = fmaf(q[g][i], kr[j][i], s);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+                s = (Q8 ? s * ks[j] : s) * scale;
+                const float mn = fmaxf(m[g], s), c = expf(m[g] - mn), e = expf(s - mn);
+                l[g] = l[g] * c + e;
+#pragma unroll
+                for (int i = 0; i < DPL; i++) acc[g][i] = fmaf(e, vr[j][i], acc[g][i] * c);
+                m[g] = mn;
+            }
+        }
+    }
+    // merge the warps: [warp][g][DH + 2]
+    float *st = sm;
+#pragma unroll
+    for (int g = 0; g < 2; g++) {
+        if (g >= G) break;
+        float *w = st + (warp * 2 + g) * (DH + 2);
+#pragma unroll
+        for (int i = 0; i < DPL; i++) w[d0 + i] = acc[g][i];
+        if (lane == 0) {
+            w[DH] = m[g];
+            w[DH + 1] = l[g];
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * DH; idx += NTHR) {
+        const int g = idx / DH, d = idx % DH;
+        float M = -INFINITY;
+        for (int w = 0; w < WARPS; w++) M = fmaxf(M, st[(w * 2 + g) * (DH + 2) + DH]);
+        float L = 0.0f, o = 0.0f;
+        for (int w = 0; w < WARPS; w++) {
+            const float *x = st + (w * 2 + g) * (DH + 2);
+            if (x[DH + 1] == 0.0f) continue;  // a warp with no positions
+            const float f = expf(x[DH] - M);
+            L += x[DH + 1] * f;
+            o += x[d] * f;
+        }
+        if (single) {
+            a.out[(size_t)b * a.ldo + ((size_t)kh * G + g) * DH + d] = o / L;
+        } else {
+            wsb[g * hstride + d] = o;
+            if (d == 0) {
+                wsb[g * hstride + DH] = M;
+                wsb[g * hstride + DH + 1] = L;
+            }
+        }
+    }
+}
+
 // Attention work items (split, kv head, sequence), dealt round-robin to the
 // CTAs; the last split of each (sequence, kv head) to finish merges them.
 // The plan's splits are sized for the longest context; at the current
@@ -671,8 +910,13 @@ __device__ __forceinline__ void attn_op(uint8_t *smem, const AttnArgs &a, int it
         const bool single = pos < CH;
         float *wsb = a.ws + (((size_t)b * a.H + (size_t)kh * G) * a.nsplit + sp) * (Dh + 2);
         const size_t hstride = (size_t)a.nsplit * (Dh + 2);
-        split_body<KV, DH, NTHR, 128>(a, reinterpret_cast<float *>(smem), sp, kh, b, pos, t0, t1, wsb, hstride, CH,
-                                      single);
+        // the short body for head size 64 with fp32 rows (LMc's cache); with
+        // the other forms as well the kernel would exceed its 128 registers
+        if (DH == 64 && sizeof(KV) == 4 && G <= 2 && t1 - t0 <= ATT_ONE_SPLIT)
+            attn_short<KV, DH>(a, reinterpret_cast<float *>(smem), kh, b, pos, t0, t1, wsb, hstride, single);
+        else
+            split_body<KV, DH, NTHR, 128>(a, reinterpret_cast<float *>(smem), sp, kh, b, pos, t0, t1, wsb, hstride,
+                                          CH, single);
         if (!single) attn_merge_last<NTHR>(a, wsb, hstride, kh, b, pos, sh_last, CH);
         __syncthreads();  // shared memory is reused by the next item
     }
