@@ -301,6 +301,18 @@ __device__ __forceinline__ void step_epilogue_tile(const TArgs &a, int row0, con
 template <int I> __device__ __forceinline__ float byte_2p23(uint32_t w) {
     return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u + I));
 }
+// Byte i of w (which has its top bit set) as the float 0x3F 0x(80|v) 0 0 =
+// 1 + v * 2^-7: one PRMT, no subtraction.  The Q4_K / Q6_K bodies place a
+// 4-bit code at bits 3..6 (1 + q / 16) or a 6-bit code at bits 1..6
+// (1 + q / 64) of each byte, so a dot product of n such weights with x is
+// sum x + sum q x / 2^k: the sum of x (needed anyway for the mins and the
+// offset) is subtracted once per 32 (16) columns, and 2^k goes into the
+// block scale.  The subtraction cancels at most the 1 + ... part, so the
+// relative rounding of the result stays near 2^-24 times the number of
+// terms of the chunk, far inside the 1e-3 bound.
+template <int I> __device__ __forceinline__ float byte_1p(uint32_t w) {
+    return __uint_as_float(__byte_perm(w, 0x3F000000u, 0x7044u + (I << 8)));
+}
 
 struct FAcc {
     float v[2][2];  // [batch row][row half: g, g + 8]
@@ -329,11 +341,13 @@ __device__ __forceinline__ void funit_q4k(FAcc &o, const uint8_t *u, const float
     for (int j = 0; j < 8; j++) {
         // byte i of P: code(32j + 4c + i) | code(32j + 16 + 4c + i) << 4 (row g); Q: row g + 8
         const uint32_t P = qs[2 * j], Q = qs[2 * j + 1];
-        const uint32_t Pl = P & LO4, Ph = (P >> 4) & LO4, Ql = Q & LO4, Qh = (Q >> 4) & LO4;
-        const float ag[8] = {byte_2p23<0>(Pl), byte_2p23<1>(Pl), byte_2p23<2>(Pl), byte_2p23<3>(Pl),
-                             byte_2p23<0>(Ph), byte_2p23<1>(Ph), byte_2p23<2>(Ph), byte_2p23<3>(Ph)};
-        const float a8[8] = {byte_2p23<0>(Ql), byte_2p23<1>(Ql), byte_2p23<2>(Ql), byte_2p23<3>(Ql),
-                             byte_2p23<0>(Qh), byte_2p23<1>(Qh), byte_2p23<2>(Qh), byte_2p23<3>(Qh)};
+        // codes at bits 3..6 under the top bit: 1 + q / 16
+        const uint32_t Pl = ((P << 3) & 0x78787878u) | 0x80808080u, Ph = ((P >> 1) & 0x78787878u) | 0x80808080u;
+        const uint32_t Ql = ((Q << 3) & 0x78787878u) | 0x80808080u, Qh = ((Q >> 1) & 0x78787878u) | 0x80808080u;
+        const float ag[8] = {byte_1p<0>(Pl), byte_1p<1>(Pl), byte_1p<2>(Pl), byte_1p<3>(Pl),
+                             byte_1p<0>(Ph), byte_1p<1>(Ph), byte_1p<2>(Ph), byte_1p<3>(Ph)};
+        const float a8[8] = {byte_1p<0>(Ql), byte_1p<1>(Ql), byte_1p<2>(Ql), byte_1p<3>(Ql),
+                             byte_1p<0>(Qh), byte_1p<1>(Qh), byte_1p<2>(Qh), byte_1p<3>(Qh)};
         const int sh = 8 * (j & 3);
         const float scg = (float)((sc0[j >> 2] >> sh) & 63u), sc8 = (float)((sc1[j >> 2] >> sh) & 63u);
         const float mng = (float)((mn0[j >> 2] >> sh) & 63u), mn8 = (float)((mn1[j >> 2] >> sh) & 63u);
@@ -342,13 +356,13 @@ __device__ __forceinline__ void funit_q4k(FAcc &o, const uint8_t *u, const float
             const float4 xa = *reinterpret_cast<const float4 *>(xs + b * K + k0 + 32 * j + 4 * c);
             const float4 xb = *reinterpret_cast<const float4 *>(xs + b * K + k0 + 32 * j + 16 + 4 * c);
             const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-            // ag[i] - 2^23 is the code q exactly
-            float pg = 0.0f, p8 = 0.0f, X = 0.0f;
+            // ag[i] = 1 + q / 16: sum ag x - sum x = sum q x / 16 (the chain starts at -sum x)
+            const float X = ((xv[0] + xv[1]) + (xv[2] + xv[3])) + ((xv[4] + xv[5]) + (xv[6] + xv[7]));
+            float pg = -X, p8 = -X;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-                pg = fmaf(ag[i] - 8388608.0f, xv[i], pg);
-                p8 = fmaf(a8[i] - 8388608.0f, xv[i], p8);
-                X += xv[i];
+                pg = fmaf(ag[i], xv[i], pg);
+                p8 = fmaf(a8[i], xv[i], p8);
             }
             sg[b] = fmaf(scg, pg, sg[b]);
             s8[b] = fmaf(sc8, p8, s8[b]);
@@ -360,8 +374,8 @@ __device__ __forceinline__ void funit_q4k(FAcc &o, const uint8_t *u, const float
     const float2 dd1 = __half22float2(*reinterpret_cast<const __half2 *>(&H1.x));
 #pragma unroll
     for (int b = 0; b < NBR; b++) {
-        o.v[b][0] += dd0.x * sg[b] - dd0.y * mg[b];
-        o.v[b][1] += dd1.x * s8[b] - dd1.y * m8[b];
+        o.v[b][0] += (16.0f * dd0.x) * sg[b] - dd0.y * mg[b];
+        o.v[b][1] += (16.0f * dd1.x) * s8[b] - dd1.y * m8[b];
     }
 }
 
@@ -388,27 +402,28 @@ __device__ __forceinline__ void funit_q6k(FAcc &o, const uint8_t *u, const float
         // byte i of P: lo(g, k) | lo(g + 8, k) << 4, k = 16 j + 4 c + i; H (chunk
         // pair j / 2): hi(g, k) | hi(g+8, k) << 2 | hi(g, k+16) << 4 | hi(g+8, k+16) << 6
         const uint32_t P = lo[j], H = (j & 1) ? hs[j >> 1] >> 4 : hs[j >> 1];
-        const uint32_t wg = (P & LO4) | ((H << 4) & 0x30303030u);         // q, row g
-        const uint32_t w8 = ((P >> 4) & LO4) | ((H << 2) & 0x30303030u);  // q, row g + 8
-        const float vg[4] = {byte_2p23<0>(wg) - 8388640.0f, byte_2p23<1>(wg) - 8388640.0f,
-                             byte_2p23<2>(wg) - 8388640.0f, byte_2p23<3>(wg) - 8388640.0f};  // q - 32
-        const float v8[4] = {byte_2p23<0>(w8) - 8388640.0f, byte_2p23<1>(w8) - 8388640.0f,
-                             byte_2p23<2>(w8) - 8388640.0f, byte_2p23<3>(w8) - 8388640.0f};
+        // the 6-bit code at bits 1..6 under the top bit: 1 + q / 64
+        const uint32_t wg = ((P << 1) & 0x1E1E1E1Eu) | ((H << 5) & 0x60606060u) | 0x80808080u;  // row g
+        const uint32_t w8 = ((P >> 3) & 0x1E1E1E1Eu) | ((H << 3) & 0x60606060u) | 0x80808080u;  // row g + 8
+        const float vg[4] = {byte_1p<0>(wg), byte_1p<1>(wg), byte_1p<2>(wg), byte_1p<3>(wg)};
+        const float v8[4] = {byte_1p<0>(w8), byte_1p<1>(w8), byte_1p<2>(w8), byte_1p<3>(w8)};
         const float scg = (float)(int)(int8_t)(sw0[j >> 2] >> (8 * (j & 3)));
         const float sc8 = (float)(int)(int8_t)(sw1[j >> 2] >> (8 * (j & 3)));
 #pragma unroll
         for (int b = 0; b < NBR; b++) {
             const float4 x = *reinterpret_cast<const float4 *>(xs + b * K + k0 + 16 * j + 4 * c);
-            const float pg = fmaf(vg[3], x.w, fmaf(vg[2], x.z, fmaf(vg[1], x.y, vg[0] * x.x)));
-            const float p8 = fmaf(v8[3], x.w, fmaf(v8[2], x.z, fmaf(v8[1], x.y, v8[0] * x.x)));
+            // v = 1 + q / 64: sum v x - 1.5 sum x = sum (q - 32) x / 64 (the chain starts at -1.5 sum x)
+            const float X15 = -1.5f * ((x.x + x.y) + (x.z + x.w));
+            const float pg = fmaf(vg[3], x.w, fmaf(vg[2], x.z, fmaf(vg[1], x.y, fmaf(vg[0], x.x, X15))));
+            const float p8 = fmaf(v8[3], x.w, fmaf(v8[2], x.z, fmaf(v8[1], x.y, fmaf(v8[0], x.x, X15))));
             sg[b] = fmaf(scg, pg, sg[b]);
             s8[b] = fmaf(sc8, p8, s8[b]);
         }
     }
 #pragma unroll
     for (int b = 0; b < NBR; b++) {
-        o.v[b][0] += d0 * sg[b];
-        o.v[b][1] += d1 * s8[b];
+        o.v[b][0] += (64.0f * d0) * sg[b];
+        o.v[b][1] += (64.0f * d1) * s8[b];
     }
 }
 
