@@ -272,6 +272,39 @@ extern "C" int lmc_qtensor_concat(const lmc_qtensor *const *parts, int n, lmc_qt
     return LMC_OK;
 }
 
+// Two tensors of the same shape with their row tiles interleaved:
+// [a rows 0..T-1][b rows 0..T-1][a rows T..2T-1][b rows T..2T-1]... (T =
+// tile_rows; each row a whole block stream).  Used for the gate and up
+// projections of a SwiGLU FFN, so that one CTA owns both halves of the rows
+// it finishes.
+extern "C" int lmc_qtensor_interleave(const lmc_qtensor *a, const lmc_qtensor *b, int tile_rows, lmc_qtensor **out) {
+    *out = NULL;
+    size_t rb;
+    if (!a || !b || a->type != b->type || a->rows != b->rows || a->cols != b->cols || tile_rows <= 0 ||
+        a->rows % tile_rows || lmc_tensor_bytes(a->type, (size_t)a->cols, &rb))
+        return lmc_set_error(LMC_ERR_INVALID, "qtensor_interleave: shapes");
+    lmc_qtensor *t = (lmc_qtensor *)calloc(1, sizeof(lmc_qtensor));
+    if (!t) return lmc_set_error(LMC_ERR_OOM, "qtensor_interleave: host alloc");
+    t->type = a->type;
+    t->rows = 2 * a->rows;
+    t->cols = a->cols;
+    t->bytes = a->bytes + b->bytes;
+    cudaError_t e = cudaMalloc(&t->blocks, t->bytes + LMC_BLOCK_PAD);
+    if (e != cudaSuccess) { free(t); return lmc_set_error(LMC_ERR_OOM, "qtensor_interleave: %s", cudaGetErrorString(e)); }
+    const size_t tb = rb * tile_rows, nt = (size_t)a->rows / tile_rows;
+    e = cudaMemcpy2D(t->blocks, 2 * tb, a->blocks, tb, tb, nt, cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy2D((char *)t->blocks + tb, 2 * tb, b->blocks, tb, tb, nt, cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess) e = cudaMemset((char *)t->blocks + t->bytes, 0, LMC_BLOCK_PAD);
+    if (e != cudaSuccess) {
+        lmc_qtensor_free(t);
+        return lmc_set_error(LMC_ERR_CUDA, "qtensor_interleave: %s", cudaGetErrorString(e));
+    }
+    const int rc = lmc_tiled_build(t);
+    if (rc) { lmc_qtensor_free(t); return rc; }
+    *out = t;
+    return LMC_OK;
+}
+
 extern "C" int lmc_qtensor_free(lmc_qtensor *t) {
     if (!t) return LMC_OK;
     if (t->blocks) cudaFree(t->blocks);

@@ -34,6 +34,13 @@ int lmc_set_error(int code, const char *fmt, ...);
  * host threads while the previous chunk's DMA runs); synchronous. */
 int lmc_h2d_staged(void *d_dst, const void *h_src, size_t bytes);
 int lmc_qtensor_concat(const struct lmc_qtensor *const *parts, int n, struct lmc_qtensor **out);
+/* Row tiles of a and b interleaved (a tile, b tile, a tile, ...); tiled copy built. */
+int lmc_qtensor_interleave(const struct lmc_qtensor *a, const struct lmc_qtensor *b, int tile_rows,
+                           struct lmc_qtensor **out);
+/* Persistent step GEMV epilogue: the row tiles come in (gate, up) pairs
+ * (lmc_qtensor_interleave with 16-row tiles) and y = silu(gate) * up, one
+ * output row per row of a pair (src/ops_llama.c:150-151). */
+#define LMC_EPI_GLU_PAIRS 16
 int lmc_tensor_bytes(uint32_t type, size_t n_elements, size_t *bytes);
 int lmc_sm_count(void);
 

@@ -215,9 +215,15 @@ __device__ __forceinline__ bool warp_units(const TArgs &a, int cid, int wid, int
         w0 = w1 = t0 = t1 = 0;
         return false;
     }
-    // 32-bit products: cid * RT < 2^31 for every shape the host plans here
-    t0 = cid * a.RT / a.NC;
-    t1 = (cid + 1) * a.RT / a.NC;
+    // 32-bit products: cid * RT < 2^31 for every shape the host plans here;
+    // (gate, up) tile pairs stay in one CTA
+    if (a.epi & LMC_EPI_GLU_PAIRS) {
+        t0 = 2 * (cid * (a.RT >> 1) / a.NC);
+        t1 = 2 * ((cid + 1) * (a.RT >> 1) / a.NC);
+    } else {
+        t0 = cid * a.RT / a.NC;
+        t1 = (cid + 1) * a.RT / a.NC;
+    }
     const int Uc = (t1 - t0) * a.KB;
     w0 = Uc * wid / WARPS;
     w1 = Uc * (wid + 1) / WARPS;
@@ -668,6 +674,16 @@ __device__ __forceinline__ int gemv_op_impl(uint8_t *smem, const DOp &op, Ring &
     __syncthreads();
     unsigned long long best = 0ull;
     double st[2] = {0.0, 0.0};
+    if (a.epi & LMC_EPI_GLU_PAIRS) {  // y = silu(gate) * up per row of each (gate, up) tile pair
+        for (int T = wid; T < (t1 - t0) >> 1; T += WARPS) {
+            const int bb = lane >> 4, row = ((t0 >> 1) + T) * 16 + (lane & 15);
+            if (bb < a.nb && 2 * row < a.M) {
+                const float gv = acc[2 * T * NB * 16 + lane], uv = acc[(2 * T + 1) * NB * 16 + lane];
+                a.y[(size_t)bb * a.ldy + row] = silu_short(gv) * uv;
+            }
+        }
+        return (ok ? GEMV_OK : 0) | (late_prefill ? GEMV_LATE : 0);
+    }
     for (int T = wid; T < t1 - t0; T += WARPS)
         step_epilogue_tile(a, (t0 + T) * 16, acc + T * NB * 16, lane, best, T == wid && has_pre ? &pre : nullptr,
                            T == wid && has_pb ? &pbias : nullptr, st);
@@ -1201,11 +1217,23 @@ static size_t plan_gemv(const lmc_step_op *o, int grid, int stages, DOp *d) {
     a.key_base = ex->key_base;
     a.XL = 12 * o->batch;
     a.CL = 1;
-    a.NC = std::min(grid, a.RT);
-    a.maxrt = (a.RT + a.NC - 1) / a.NC + 1;
+    if (a.epi & LMC_EPI_GLU_PAIRS) {
+        if ((a.RT & 1) || t->rows != t->tiled_rows || ex->keys || o->bias) return 0;
+        a.NC = std::min(grid, a.RT / 2);
+        a.maxrt = 2 * ((a.RT / 2 + a.NC - 1) / a.NC) + 1;
+    } else {
+        a.NC = std::min(grid, a.RT);
+        a.maxrt = (a.RT + a.NC - 1) / a.NC + 1;
+    }
     a.stages = stages;
     const int qt = qt_of_type(t->type), unit = unit_bytes(qt);
-    a.pf = (int)std::min<long long>(64, PF_BYTES / ((long long)a.NC * WARPS * unit));
+    const char *pfe = getenv("LMC_STEP_PF_MB");
+    // no L2 prefetch of the units beyond the ring by default: with the ring
+    // prefill in the barrier's shadow it only queued HBM traffic ahead of
+    // the ops' demand loads (GPT-2 Small 0.396 -> 0.393 ms, 8B shape
+    // 3.33 -> 3.24 ms per step without it)
+    const long long pfb = pfe ? atoll(pfe) << 20 : 0;
+    a.pf = (int)std::min<long long>(64, pfb / ((long long)a.NC * WARPS * unit));
     d->g = a;
     d->qt = qt;
     // the latency form when a warp gets few units, x fits in shared memory as

@@ -35,6 +35,9 @@ typedef struct {
     /* q|k|v and gate|up concatenated by rows (same type and width), so each
      * pair of projections is one launch; NULL when they cannot be fused */
     lmc_qtensor *qkv_cat, *gateup_cat;
+    /* gate and up with their 16-row tiles interleaved, built for the
+     * persistent step (whose gate|up GEMV then finishes silu(gate) * up) */
+    lmc_qtensor *gateup_il;
 } Layer;
 
 struct lmc_model {
@@ -601,7 +604,7 @@ int lmc_model_free(lmc_model *m) {
         for (int l = 0; l < m->cfg.n_layers; l++) {
             Layer *w = &m->layers[l];
             lmc_qtensor *qs[] = {w->qkv, w->proj, w->fc, w->fc2, w->q, w->k, w->v, w->o, w->gate, w->up, w->down,
-                                 w->qkv_cat, w->gateup_cat};
+                                 w->qkv_cat, w->gateup_cat, w->gateup_il};
             for (size_t i = 0; i < sizeof qs / sizeof qs[0]; i++) lmc_qtensor_free(qs[i]);
             float *vs[] = {w->ln1_w, w->ln1_b, w->ln2_w, w->ln2_b, w->qkv_b, w->proj_b, w->fc_b, w->fc2_b, w->rms_attn, w->rms_ffn};
             for (size_t i = 0; i < sizeof vs / sizeof vs[0]; i++) if (vs[i]) cudaFree(vs[i]);
@@ -888,7 +891,7 @@ static int build_prog(lmc_model *m, int B, int gen, int n_prompt, int n_new, lmc
     for (int l = 0; l < c->n_layers && !rc; l++) {
         const int s_in = l == 0 ? 1 : 3 + 2 * (l - 1), s_mid = 2 + 2 * l, s_out = 3 + 2 * l;
         const int n0 = n;
-        const Layer *w = &m->layers[l];
+        Layer *w = &m->layers[l];
         char *kc = (char *)m->kc + m->kv_layer_bytes * l, *vc = (char *)m->vc + m->kv_layer_bytes * l;
         if (c->arch == 1) { /* src/ops.c:182-206 */
             add_gemv(ops, &n, B, w->qkv, m->x, D, w->qkv_b, m->qkv, 3 * D, LMC_EPI_NONE, LMC_PRO_LAYERNORM, w->ln1_w,
@@ -912,10 +915,24 @@ static int build_prog(lmc_model *m, int B, int gen, int n_prompt, int n_new, lmc
             add_attn(ops, &n, m, B, m->att, QD, m->qkv, LQ, m->qkv + QD, m->qkv + QD + KVD, LQ, kc, vc, H,
                      c->n_kv_heads, m->rope_cos, m->rope_sin);
             add_gemv(ops, &n, B, w->o, m->att, QD, NULL, m->x, D, LMC_EPI_ACCUM, LMC_PRO_NONE, NULL, NULL, 0.0f, NULL);
-            add_gemv(ops, &n, B, w->gateup_cat, m->x, D, NULL, m->h, 2 * F, LMC_EPI_NONE, LMC_PRO_RMSNORM, w->rms_ffn,
-                     NULL, c->norm_eps, NULL);
-            add_gemv(ops, &n, B, w->down, m->h, 2 * F, NULL, m->x, D, LMC_EPI_ACCUM, LMC_PRO_SWIGLU, NULL, NULL, 0.0f,
-                     m->h + F);
+            /* gate and up interleaved by row tile: the gate|up GEMV finishes
+             * h = silu(gate) * up itself, so the down projection reads h as
+             * it is instead of every CTA redoing the SwiGLU on its input */
+            if (!w->gateup_il && F % 16 == 0 && lmc_qtensor_has_tiled(w->gate) && lmc_qtensor_has_tiled(w->up)) {
+                rc = lmc_qtensor_interleave(w->gate, w->up, 16, &w->gateup_il);
+                if (rc) break;
+            }
+            if (w->gateup_il && w->gateup_il->tiled) {
+                add_gemv(ops, &n, B, w->gateup_il, m->x, D, NULL, m->h, 2 * F, LMC_EPI_GLU_PAIRS, LMC_PRO_RMSNORM,
+                         w->rms_ffn, NULL, c->norm_eps, NULL);
+                add_gemv(ops, &n, B, w->down, m->h, 2 * F, NULL, m->x, D, LMC_EPI_ACCUM, LMC_PRO_NONE, NULL, NULL, 0.0f,
+                         NULL);
+            } else {
+                add_gemv(ops, &n, B, w->gateup_cat, m->x, D, NULL, m->h, 2 * F, LMC_EPI_NONE, LMC_PRO_RMSNORM,
+                         w->rms_ffn, NULL, c->norm_eps, NULL);
+                add_gemv(ops, &n, B, w->down, m->h, 2 * F, NULL, m->x, D, LMC_EPI_ACCUM, LMC_PRO_SWIGLU, NULL, NULL,
+                         0.0f, m->h + F);
+            }
         }
         /* this layer's five ops: norm-in, attention, residual, norm-in, residual */
         ops[n0].stats_in = s_in;

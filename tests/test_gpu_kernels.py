@@ -398,3 +398,26 @@ def test_attention_paged(cuda, orc, kvd, H, Hkv, Dh, P, pos):
             got_vals = got_row.astype(np.float32)
         assert np.array_equal(got_vals, orc.kv_round_rows(kn[b].reshape(Hkv, Dh), kvd))
     assert rt.lib().lmc_device_status() == 0
+
+
+def test_softmax_edge_rows(cuda, orc):
+    """Softmax rows as LMc's softmax (src/ops.c:31-43) treats them: masked
+    entries (-inf) give 0, one element gives 1, a constant row is uniform,
+    values near the float range do not overflow (the max is subtracted
+    first).  LMc's sum < 1e-30 branch cannot be taken by finite rows (the
+    maximum contributes e^0 = 1); the oracle restates it as written."""
+    rows = [
+        np.array([0.5, -np.inf, 2.0, -np.inf, -1.0], np.float32),
+        np.array([7.0], np.float32),
+        np.full(33, 3.25, np.float32),
+        np.array([3e38, -3e38, 1e38, 0.0], np.float32),
+        np.array([-1e30, -1e30 + 1e23, -1e30], np.float32),
+    ]
+    for r in rows:
+        d = dev(cuda, r[None])
+        rt.call("lmc_softmax", d.data_ptr(), r.size, 1, None)
+        got = d.cpu().numpy()[0]
+        want = orc.softmax(r)
+        assert np.all(np.isfinite(got))
+        assert np.allclose(got, want, rtol=1e-6, atol=1e-7), (r, got, want)
+        assert abs(float(got.sum()) - 1.0) < 1e-5
