@@ -164,6 +164,7 @@ typedef struct {
     int *tok, *pos;
     unsigned long long *keys;
     int *next, *step, *ids;
+    int *next_host; /* KEYS: picks also written to this mapped host memory (NULL: none) */
     const int *prompt;
     int n_prompt, n_new;
     /* SAMPLE (logits in y, V, rng, next, step, n_prompt); ADVANCE: from_next */
@@ -181,6 +182,10 @@ typedef struct lmc_step_prog lmc_step_prog;
  * (the caller then launches the step kernel by kernel). */
 int lmc_step_prog_build(const lmc_step_op *ops, int n, lmc_step_prog **out);
 int lmc_step_prog_launch(const lmc_step_prog *p, cudaStream_t s);
+/* The same, with this step's tokens and positions passed in the launch
+ * (no host -> device copies): the kernel stores them to d_tok / d_pos. */
+int lmc_step_prog_launch_imm(const lmc_step_prog *p, cudaStream_t s, const int *h_tok, const int *h_pos, int nb,
+                             int *d_tok, int *d_pos);
 void lmc_step_prog_free(lmc_step_prog *p);
 /* LMC_OK, or LMC_ERR_TIMEOUT once after a persistent step gave up a bounded
  * wait (its barrier state is then reset for the next launch). */

@@ -60,6 +60,7 @@ struct KvPf {
 struct AdvArgs {
     unsigned long long *keys;
     int *next, *tok, *pos, *step, *ids;
+    int *next_host;  // KEYS: the picks also written here (mapped host memory), or NULL
     const int *prompt;
     int n_prompt, n_new, generate, from_next;
 };
@@ -116,6 +117,11 @@ struct StepParams {
     int stats_n;    // doubles in the slots
     const PfRange *pf;
     int pf_n;
+    // Tokens and positions passed with the launch (lmc_step_prog_launch_imm):
+    // CTA b stores row b's into tok_dst / pos_dst before its first op (the
+    // embedding, which CTA b runs); every other reader comes after a barrier.
+    int imm_n, imm_tok[2], imm_pos[2];
+    int *tok_dst, *pos_dst;
 };
 
 __device__ long long g_step_wait_ns = 1000000000ll;
@@ -1017,6 +1023,7 @@ __device__ __forceinline__ void advance_op(const AdvArgs &v, int nb) {
         const int nx = v.from_next ? __ldcg(v.next + b) : lmc_key_index(__ldcg(v.keys + b));
         v.keys[b] = 0ull;
         v.next[b] = nx;
+        if (v.next_host) v.next_host[b] = nx;
         if (!v.generate) continue;
         if (step + 1 < v.n_prompt) {
             v.tok[b] = v.prompt[(size_t)b * v.n_prompt + step + 1];
@@ -1054,6 +1061,10 @@ __global__ void __launch_bounds__(NTHR, 2) k_step(StepParams P) {
         const int4 *src = reinterpret_cast<const int4 *>(P.ops);
         int4 *dst = reinterpret_cast<int4 *>(&ops[0]);
         for (int w = threadIdx.x; w < (int)(sizeof(DOp) / 16); w += NTHR) dst[w] = __ldg(src + w);
+    }
+    if (threadIdx.x == 0 && (int)blockIdx.x < P.imm_n) {
+        P.tok_dst[blockIdx.x] = P.imm_tok[blockIdx.x];
+        P.pos_dst[blockIdx.x] = P.imm_pos[blockIdx.x];
     }
     __syncthreads();
     if (!sh_ok) return;
@@ -1333,8 +1344,8 @@ extern "C" int lmc_step_prog_build(const lmc_step_op *ops, int n, lmc_step_prog 
             case LMC_OP_KEYS:
             case LMC_OP_ADVANCE:
                 d[i].v = AdvArgs{ops[i].keys, ops[i].next, ops[i].tok, ops[i].pos, ops[i].step, ops[i].ids,
-                                 ops[i].prompt, ops[i].n_prompt, ops[i].n_new, ops[i].kind == LMC_OP_ADVANCE,
-                                 ops[i].from_next};
+                                 ops[i].next_host, ops[i].prompt, ops[i].n_prompt, ops[i].n_new,
+                                 ops[i].kind == LMC_OP_ADVANCE, ops[i].from_next};
                 if (!ops[i].keys || !ops[i].next ||
                     (ops[i].kind == LMC_OP_ADVANCE && (!ops[i].tok || !ops[i].pos || !ops[i].step || !ops[i].prompt ||
                                                        !ops[i].ids)))
@@ -1456,9 +1467,28 @@ extern "C" int lmc_step_prog_build(const lmc_step_op *ops, int n, lmc_step_prog 
     return LMC_OK;
 }
 
+static int step_launch(const lmc_step_prog *p, cudaStream_t s, const int *h_tok, const int *h_pos, int nb,
+                       int *d_tok, int *d_pos);
 extern "C" int lmc_step_prog_launch(const lmc_step_prog *p, cudaStream_t s) {
+    return step_launch(p, s, NULL, NULL, 0, NULL, NULL);
+}
+extern "C" int lmc_step_prog_launch_imm(const lmc_step_prog *p, cudaStream_t s, const int *h_tok, const int *h_pos,
+                                        int nb, int *d_tok, int *d_pos) {
+    if (!h_tok || !h_pos || !d_tok || !d_pos || nb < 1 || nb > 2)
+        return lmc_set_error(LMC_ERR_INVALID, "step_prog_launch_imm: args");
+    return step_launch(p, s, h_tok, h_pos, nb, d_tok, d_pos);
+}
+static int step_launch(const lmc_step_prog *p, cudaStream_t s, const int *h_tok, const int *h_pos, int nb,
+                       int *d_tok, int *d_pos) {
     if (!p) return lmc_set_error(LMC_ERR_INVALID, "step_prog_launch: null");
     StepParams P;
+    P.imm_n = nb;
+    for (int b = 0; b < 2; b++) {
+        P.imm_tok[b] = b < nb ? h_tok[b] : 0;
+        P.imm_pos[b] = b < nb ? h_pos[b] : 0;
+    }
+    P.tok_dst = d_tok;
+    P.pos_dst = d_pos;
     P.ops = p->d_ops;
     P.nops = p->nops;
     P.first_gemv = p->first_gemv;

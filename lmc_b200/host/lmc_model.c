@@ -59,6 +59,7 @@ struct lmc_model {
     unsigned long long *d_keys; /* per sequence greedy-pick key of the step */
     int *d_attn_cnt;            /* attention split arrival counters [batch][kv heads] */
     int *h_stage; /* pinned: tokens, positions, next ids */
+    int *h_next_map; /* mapped pinned: the persistent forward step writes its picks here */
     int prompt_cap, ids_cap;
     cudaStream_t stream;
     cudaGraphExec_t gexec;
@@ -511,6 +512,7 @@ static int alloc_state(lmc_model *m) {
     TRY(dev_alloc((void **)&m->d_step, 16));
     TRY(dev_alloc((void **)&m->d_rng, 8 * B));
     CUTRY(cudaMallocHost((void **)&m->h_stage, 3 * sizeof(int) * B));
+    CUTRY(cudaHostAlloc((void **)&m->h_next_map, sizeof(int) * B, cudaHostAllocMapped));
     CUTRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     if (B > 8) { /* the batched GEMM's activation workspace, sized before any graph capture */
         const size_t kmax = D > F ? (D > QD ? D : QD) : (F > QD ? F : QD);
@@ -618,6 +620,7 @@ int lmc_model_free(lmc_model *m) {
                   m->d_keys, m->d_attn_cnt, m->d_seq, m->d_rng};
     for (size_t i = 0; i < sizeof ps / sizeof ps[0]; i++) if (ps[i]) cudaFree(ps[i]);
     if (m->h_stage) cudaFreeHost(m->h_stage);
+    if (m->h_next_map) cudaFreeHost(m->h_next_map);
     if (m->stream) cudaStreamDestroy(m->stream);
     free(m);
     return LMC_OK;
@@ -963,6 +966,11 @@ static int build_prog(lmc_model *m, int B, int gen, int n_prompt, int n_new, lmc
         }
         lmc_step_op *k = add_op(ops, &n, gen ? LMC_OP_ADVANCE : LMC_OP_KEYS, B);
         k->from_next = gen && m->smp;
+        if (!gen && cudaHostGetDevicePointer((void **)&k->next_host, m->h_next_map, 0) != cudaSuccess) {
+            (void)cudaGetLastError(); /* lmc_model_forward reads the picks there: no persistent step without it */
+            free(ops);
+            return lmc_set_error(LMC_ERR_CUDA, "persistent step: no device address for the mapped picks");
+        }
         k->keys = m->d_keys;
         k->next = m->d_next;
         k->tok = m->d_tok;
@@ -994,23 +1002,25 @@ int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B
         if (h_pos[b] < 0 || h_pos[b] >= m->cfg.seq_len)
             return lmc_set_error(LMC_ERR_INVALID, "model_forward: position %d outside [0, %d)", h_pos[b], m->cfg.seq_len);
     }
-    memcpy(m->h_stage, h_tokens, sizeof(int) * B);
-    memcpy(m->h_stage + B, h_pos, sizeof(int) * B);
-    CUTRY(cudaMemcpyAsync(m->d_tok, m->h_stage, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
-    CUTRY(cudaMemcpyAsync(m->d_pos, m->h_stage + B, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
     lmc_step_prog *p = fwd_prog(m, B);
     if (p) {
-        TRY(lmc_step_prog_launch(p, m->stream));
+        /* the persistent step takes the tokens and positions in its launch
+         * and writes its picks into mapped host memory: no copies */
+        TRY(lmc_step_prog_launch_imm(p, m->stream, h_tokens, h_pos, B, m->d_tok, m->d_pos));
     } else {
+        memcpy(m->h_stage, h_tokens, sizeof(int) * B);
+        memcpy(m->h_stage + B, h_pos, sizeof(int) * B);
+        CUTRY(cudaMemcpyAsync(m->d_tok, m->h_stage, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
+        CUTRY(cudaMemcpyAsync(m->d_pos, m->h_stage + B, sizeof(int) * B, cudaMemcpyHostToDevice, m->stream));
         TRY(step(m, B));
         TRY(lmc_keys_to_ids_launch(m->d_keys, m->d_next, B, m->stream));
     }
     if (h_logits) /* [B][vocab rows of this rank] (the whole vocabulary without sharding) */
         CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * (size_t)B * m->vl, cudaMemcpyDeviceToHost,
                               m->stream));
-    CUTRY(cudaMemcpyAsync(m->h_stage + 2 * B, m->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, m->stream));
+    if (!p) CUTRY(cudaMemcpyAsync(m->h_stage + 2 * B, m->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, m->stream));
     TRY(model_sync(m));
-    if (h_next) memcpy(h_next, m->h_stage + 2 * B, sizeof(int) * B);
+    if (h_next) memcpy(h_next, p ? m->h_next_map : m->h_stage + 2 * B, sizeof(int) * B);
     return LMC_OK;
 }
 
