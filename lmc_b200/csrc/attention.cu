@@ -23,7 +23,7 @@
 
 #include "attention.cuh"
 
-template <int DH>
+template <typename KV, int DH>
 __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int kh, int b, int pos, int t0, int t1,
                                               float *wsb, size_t hstride);
 
@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_split(AttnArgs a) {
             }
         return;
     }
-    if constexpr (TC) split_body_tc<DH>(a, sm, kh, b, pos, t0, t1, wsb, hstride);
+    if constexpr (TC) split_body_tc<KV, DH>(a, sm, kh, b, pos, t0, t1, wsb, hstride);
     else split_body<KV, DH>(a, sm, sp, kh, b, pos, t0, t1, wsb, hstride);
     if (!a.cnt || a.nsplit == 1) return;
     __shared__ int last;
@@ -86,10 +86,33 @@ __device__ __forceinline__ int qk_dim(int ks, int tig, int e, bool second) {
     return 32 * (ks >> 1) + 8 * tig + 4 * (ks & 1) + (second ? 2 : 0) + e;
 }
 
-template <int DH>
+// 8 int8 codes (one 8-byte word) -> 8 exact halves: (code ^ 0x80) under the
+// fp16 1024 (0x64xx = 1024 + byte), minus 1152.
+__device__ __forceinline__ uint4 q8x8_to_h8(uint2 w) {
+    const uint32_t a = w.x ^ 0x80808080u, c = w.y ^ 0x80808080u;
+    const __half2 off = __floats2half2_rn(1152.0f, 1152.0f);
+    uint4 r;
+    __half2 h;
+    h = __hsub2(*reinterpret_cast<const __half2 *>(&(const uint32_t &)__byte_perm(a, 0x64646464u, 0x4140u)), off);
+    r.x = *reinterpret_cast<uint32_t *>(&h);
+    h = __hsub2(*reinterpret_cast<const __half2 *>(&(const uint32_t &)__byte_perm(a, 0x64646464u, 0x4342u)), off);
+    r.y = *reinterpret_cast<uint32_t *>(&h);
+    h = __hsub2(*reinterpret_cast<const __half2 *>(&(const uint32_t &)__byte_perm(c, 0x64646464u, 0x4140u)), off);
+    r.z = *reinterpret_cast<uint32_t *>(&h);
+    h = __hsub2(*reinterpret_cast<const __half2 *>(&(const uint32_t &)__byte_perm(c, 0x64646464u, 0x4342u)), off);
+    r.w = *reinterpret_cast<uint32_t *>(&h);
+    return r;
+}
+
+// KV: __half (fp16 rows) or KvQ8 (int8 rows: the codes go into the MMAs as
+// exact halves; the K row scale multiplies the score, the V row scale is
+// folded into the probability after the softmax sum).
+template <typename KV, int DH>
 __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int kh, int b, int pos, int t0, int t1,
                                               float *wsb, size_t hstride) {
     constexpr int KS = DH / 16, VSTR = DH + 8;  // k slices; V staging row stride (halves, conflict-free ldmatrix)
+    constexpr bool Q8 = KvT<KV>::Q8;
+    constexpr int RS = kv_rs<KV>(DH);  // row stride in elements of KV
     const int G = a.H / a.Hkv, CH = a.CH;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = ATT_THREADS / 32;
     const int g = lane >> 2, tig = lane & 3;
@@ -97,13 +120,19 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
     float *sc = sm + G * DH;   // [G][CH16]
     const int CH16 = (CH + 15) & ~15;
     float *ml = sc + G * CH16;  // [G][2]
-    __half *vt = reinterpret_cast<__half *>(sm + ((G * DH + G * CH16 + 2 * G + 3) & ~3));  // [CH16][VSTR], 16-byte aligned
+    float *vsc = ml + 2 * G;    // [CH16] V row scales (int8 rows)
+    __half *vt = reinterpret_cast<__half *>(sm + ((G * DH + G * CH16 + 2 * G + (Q8 ? CH16 : 0) + 3) & ~3));  // [CH16][VSTR], 16-byte aligned
     const size_t cs = a.seq ? (size_t)a.seq[b] : (size_t)b;
-    __half *kc = reinterpret_cast<__half *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * DH;
-    __half *vc = reinterpret_cast<__half *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * DH;
+    KV *kc = reinterpret_cast<KV *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * RS;
+    KV *vc = reinterpret_cast<KV *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * RS;
     const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (DH / 2) : nullptr;
     const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (DH / 2) : nullptr;
-    if (a.append && pos >= t0 && pos < t1) {  // append this step's K/V row (K rotated first when RoPE applies)
+    if (Q8 && a.append && pos >= t0 && pos < t1) {  // quantize the new rows: warp 0 K, warp 1 V
+        if (warp < 2)
+            kv_q8_store_row(reinterpret_cast<KvQ8 *>((warp ? vc : kc) + (size_t)pos * RS),
+                            (warp ? a.v_new : a.k_new) + (size_t)b * a.ldkv + (size_t)kh * DH, warp ? nullptr : rc,
+                            rs, DH, lane);
+    } else if (a.append && pos >= t0 && pos < t1) {  // append this step's K/V row (K rotated first when RoPE applies)
         const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * DH;
         const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * DH;
         for (int d = threadIdx.x; d < DH / 2; d += ATT_THREADS) {
@@ -114,10 +143,12 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
                 k0 = r0;
                 k1 = r1;
             }
-            kc[(size_t)pos * DH + 2 * d] = __float2half_rn(k0);
-            kc[(size_t)pos * DH + 2 * d + 1] = __float2half_rn(k1);
-            vc[(size_t)pos * DH + 2 * d] = __float2half_rn(vn[2 * d]);
-            vc[(size_t)pos * DH + 2 * d + 1] = __float2half_rn(vn[2 * d + 1]);
+            if constexpr (!Q8) {
+                kc[(size_t)pos * DH + 2 * d] = __float2half_rn(k0);
+                kc[(size_t)pos * DH + 2 * d + 1] = __float2half_rn(k1);
+                vc[(size_t)pos * DH + 2 * d] = __float2half_rn(vn[2 * d]);
+                vc[(size_t)pos * DH + 2 * d + 1] = __float2half_rn(vn[2 * d + 1]);
+            }
         }
     }
     const float *qb = a.q + (size_t)b * a.ldq + (size_t)kh * G * DH;
@@ -135,16 +166,29 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
     }
     __syncthreads();  // the new row (read back below) and q are in place
     const int n = t1 - t0, n16 = (n + 15) & ~15;
-    // stage V rows [t0, t0 + n) (zero rows up to n16) by asynchronous 16-byte
-    // copies: they land while the scores are computed (waited before the output)
-    for (int i = threadIdx.x; i < n16 * (DH / 8); i += ATT_THREADS) {
-        const int r = i / (DH / 8), c8 = i % (DH / 8);
-        const __half *src = vc + (size_t)(t0 + (r < n ? r : 0)) * DH + 8 * c8;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(vt + r * VSTR + 8 * c8)),
-                     "l"(src), "r"(r < n ? 16 : 0)
-                     : "memory");
+    // stage V rows [t0, t0 + n) (zero rows up to n16): fp16 rows by
+    // asynchronous 16-byte copies that land while the scores are computed
+    // (waited before the output); int8 rows converted to halves here, their
+    // scales kept in vsc
+    if constexpr (Q8) {
+        for (int i = threadIdx.x; i < n16 * (DH / 8); i += ATT_THREADS) {
+            const int r = i / (DH / 8), c8 = i % (DH / 8);
+            const KV *row = vc + (size_t)(t0 + (r < n ? r : 0)) * RS;
+            const uint2 w = r < n ? *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint8_t *>(row) + 8 * c8)
+                                  : make_uint2(0x80808080u ^ 0x80808080u, 0u);
+            *reinterpret_cast<uint4 *>(vt + r * VSTR + 8 * c8) = r < n ? q8x8_to_h8(w) : make_uint4(0u, 0u, 0u, 0u);
+            if (c8 == 0) vsc[r] = r < n ? kv_q8_scale(reinterpret_cast<const KvQ8 *>(row), DH) : 0.0f;
+        }
+    } else {
+        for (int i = threadIdx.x; i < n16 * (DH / 8); i += ATT_THREADS) {
+            const int r = i / (DH / 8), c8 = i % (DH / 8);
+            const KV *src = vc + (size_t)(t0 + (r < n ? r : 0)) * DH + 8 * c8;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(vt + r * VSTR + 8 * c8)),
+                         "l"(src), "r"(r < n ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
     // q fragments: row g (query head g of the group), hi and lo
     uint32_t qa0h[KS], qa0l[KS], qa2h[KS], qa2l[KS];
 #pragma unroll
@@ -162,13 +206,25 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
     constexpr int TB = DH == 128 ? 2 : 4;  // tiles per warp whose K loads are issued together
     for (int j0 = warp; 8 * j0 < n; j0 += TB * nw) {  // 8-position tiles j0, j0 + nw, ...
         uint4 kv[TB][KS / 2];
+        float ksc[TB];  // int8 rows: the scale of this lane's K row
 #pragma unroll
         for (int u = 0; u < TB; u++) {
             const int p = 8 * (j0 + u * nw) + g;  // this lane's B column (position within the split)
-            const __half *kr = kc + (size_t)(t0 + (p < n ? p : 0)) * DH + 8 * tig;
+            if constexpr (Q8) {
+                const KV *row = kc + (size_t)(t0 + (p < n ? p : 0)) * RS;
+                const uint8_t *kr = reinterpret_cast<const uint8_t *>(row) + 8 * tig;
 #pragma unroll
-            for (int kp = 0; kp < KS / 2; kp++)
-                kv[u][kp] = p < n ? *reinterpret_cast<const uint4 *>(kr + 32 * kp) : make_uint4(0u, 0u, 0u, 0u);
+                for (int kp = 0; kp < KS / 2; kp++)
+                    kv[u][kp] = p < n ? q8x8_to_h8(*reinterpret_cast<const uint2 *>(kr + 32 * kp))
+                                      : make_uint4(0u, 0u, 0u, 0u);
+                ksc[u] = p < n ? kv_q8_scale(reinterpret_cast<const KvQ8 *>(row), DH) : 0.0f;
+            } else {
+                const KV *kr = kc + (size_t)(t0 + (p < n ? p : 0)) * DH + 8 * tig;
+#pragma unroll
+                for (int kp = 0; kp < KS / 2; kp++)
+                    kv[u][kp] = p < n ? *reinterpret_cast<const uint4 *>(kr + 32 * kp) : make_uint4(0u, 0u, 0u, 0u);
+                ksc[u] = 1.0f;
+            }
         }
 #pragma unroll
         for (int u = 0; u < TB; u++) {
@@ -184,6 +240,10 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
             }
             // d[0], d[1]: head g at positions 8 j + 2 tig, + 1 (rows 8-15 are padding)
             const int c0 = 8 * j + 2 * tig;
+            if (Q8) {  // K row scales of positions 2 tig, 2 tig + 1: held by lanes with g = 2 tig, 2 tig + 1
+                d[0] *= __shfl_sync(0xffffffffu, ksc[u], 8 * tig);
+                d[1] *= __shfl_sync(0xffffffffu, ksc[u], 8 * tig + 4);
+            }
             if (g < G) {
                 if (c0 < n) sc[g * CH16 + c0] = d[0] * scale;
                 if (c0 + 1 < n) sc[g * CH16 + c0 + 1] = d[1] * scale;
@@ -203,6 +263,10 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
         }
         l = warp_sum(l);
         if (lane == 0) { ml[2 * gg] = m; ml[2 * gg + 1] = l; }
+    }
+    if (Q8) {  // the V row scales into the probabilities (the sum above is of the unscaled ones)
+        __syncthreads();  // vsc is written by the staging loop
+        for (int i = threadIdx.x; i < G * n16; i += ATT_THREADS) sc[(i / n16) * CH16 + i % n16] *= vsc[i % n16];
     }
     asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's V copies landed
     __syncthreads();                                   // and every thread's
@@ -390,9 +454,10 @@ static int attention_impl(float *out, int ldo, const float *q, int ldq, const fl
     // tensor-core body: fp16 cache, head 64 / 128, 1-8 query heads per kv head
     // (LMC_ATTN_TC=0 selects the CUDA-core body; both give the same result)
     const char *tce = getenv("LMC_ATTN_TC");
-    const bool tc = kv_dtype == LMC_KV_F16 && (Dh == 64 || Dh == 128) && G <= 8 && !(tce && tce[0] == '0') && !pages;
+    const bool tc = (kv_dtype == LMC_KV_F16 || kv_dtype == LMC_KV_Q8) && (Dh == 64 || Dh == 128) && G <= 8 &&
+                    !(tce && tce[0] == '0') && !pages;
     const int CH16 = (a.CH + 15) & ~15;
-    const size_t smem = tc ? (size_t)(G * Dh + G * CH16 + 2 * G + 2) * sizeof(float) + 16 + (size_t)CH16 * (Dh + 8) * 2
+    const size_t smem = tc ? (size_t)(G * Dh + G * CH16 + 2 * G + CH16 + 2) * sizeof(float) + 16 + (size_t)CH16 * (Dh + 8) * 2
                            : (size_t)(G * Dh + G * a.CH + 2 * G + (ATT_THREADS / 32) * ATT_GROUP * Dh) * sizeof(float);
     if (smem > 200 * 1024) return lmc_set_error(LMC_ERR_UNSUPPORTED, "attention: group too large");
     dim3 grid(a.nsplit, Hkv, batch);
@@ -407,8 +472,9 @@ static int attention_impl(float *out, int ldo, const float *q, int ldq, const fl
         if (smem > 48 * 1024) LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         LMC_LAUNCH("attention", fn, grid, ATT_THREADS, smem, s, a);
     } else if (kv_dtype == LMC_KV_Q8) {
-        void (*fn)(AttnArgs) = Dh == 64 ? k_attn_split<KvQ8, 64, false> : Dh == 128 ? k_attn_split<KvQ8, 128, false>
-                                                                     : k_attn_split<KvQ8, 0, false>;
+        void (*fn)(AttnArgs) = tc ? (Dh == 64 ? k_attn_split<KvQ8, 64, true> : k_attn_split<KvQ8, 128, true>)
+                                  : Dh == 64 ? k_attn_split<KvQ8, 64, false> : Dh == 128 ? k_attn_split<KvQ8, 128, false>
+                                                                                : k_attn_split<KvQ8, 0, false>;
         if (smem > 48 * 1024) LMC_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         LMC_LAUNCH("attention", fn, grid, ATT_THREADS, smem, s, a);
     } else {
