@@ -334,7 +334,7 @@ def run_gpt2(args, rank, world, local_rank, dist):
                              "traffic": tr["bytes"] if tr else None,
                              "traffic_source": tr["source"] if tr else None,
                              "algorithmic_bytes": int(alg), "avg_launch_ms": round(step_ms_avg, 5)},
-                "gemv_c1": {"kernel": "tiled tensor-core GEMV Q4_K 3072x768, batch 1, rotated copies > 2x L2",
+                "gemv_c1": {"kernel": f"{c1['kernel']}: Q4_K 3072x768, batch 1, rotated copies > 2x L2",
                             "us": round(c1["ms"] * 1e3, 3), "gbs": round(c1["gbs"], 1),
                             "frac": round(c1["gbs"] / peak, 4), "algorithmic_bytes": c1["bytes"],
                             "reference_matmul_vec_us": round(ref_c1 * 1e6, 2) if ref_c1 else None},
@@ -372,14 +372,6 @@ MODELS = {
 }
 
 
-def kernel_family(qtype, cols, batch):
-    from lmc_b200 import synth
-    tiled = qtype in (synth.Q4_K, synth.Q6_K, synth.Q8_0) and cols % 256 == 0
-    if batch > 8:
-        return "tcgen05 gemm (tiled fast path)" if tiled else "tcgen05 gemm (generic decoders)"
-    return "tensor-core gemv (tiled)" if tiled else "generic gemv"
-
-
 def run_gemv(args):
     import torch
     from lmc_b200 import microbench as mb
@@ -403,7 +395,7 @@ def run_gemv(args):
         r = mb.run(torch, t, rows, cols, b, iters=max(args.steps, 20), seed=0)
         fl = 2.0 * rows * cols * b / (r["ms"] * 1e-3) / 1e12
         print(json.dumps({"metric": "GEMV/GEMM throughput", "workload": "gemv", "type": tn, "rows": rows,
-                          "cols": cols, "batch": b, "kernel": kernel_family(t, cols, b),
+                          "cols": cols, "batch": b, "kernel": r["kernel"],
                           "us": round(r["ms"] * 1e3, 3), "gbs": round(r["gbs"], 1),
                           "hbm_frac": round(r["gbs"] / peak, 4), "tflops": round(fl, 2),
                           "algorithmic_bytes": r["bytes"], "peak_kind": kind,

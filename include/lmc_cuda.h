@@ -123,6 +123,11 @@ int lmc_qtensor_has_tiled(const lmc_qtensor *t);
 #define LMC_EPI_ACCUM 2
 int lmc_matmul(const lmc_qtensor *w, const float *d_x, int ldx, const float *d_bias,
                float *d_y, int ldy, int batch, int epilogue, void *stream);
+/* Which kernel lmc_matmul runs for this tensor, batch width and epilogue
+ * (a static string, for reports): the latency GEMV (short matrices, batch
+ * <= 2), the tensor-core GEMV (tiled Q4_K / Q6_K / Q8_0), the tcgen05 GEMM
+ * (batch > 8) or the generic GEMV. */
+const char *lmc_matmul_kernel(const lmc_qtensor *w, int batch, int epilogue);
 int lmc_matmul_blocks(uint32_t type, const void *d_blocks, int rows, int cols,
                       const float *d_x, int ldx, const float *d_bias, float *d_y,
                       int ldy, int batch, int epilogue, void *stream);

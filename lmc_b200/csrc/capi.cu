@@ -378,6 +378,16 @@ extern "C" int lmc_matmul_blocks(uint32_t type, const void *d_blocks, int rows, 
                                    lmc_stream(stream));
 }
 
+extern "C" const char *lmc_matmul_kernel(const lmc_qtensor *w, int batch, int epi) {
+    if (!w || batch <= 0) return "none";
+    if (batch > 8 && w->gemm_wscale > 0.0f)
+        return w->tiled ? "tcgen05 GEMM (tiled units)" : "tcgen05 GEMM (generic decoders)";
+    if (w->tiled)
+        return lmc_ff_gemv_suits(w, batch, epi) ? "latency GEMV (tiled units, fp32 FMA)"
+                                                : "tensor-core GEMV (tiled units, int8 mma.sync)";
+    return "generic GEMV (bit-exact decoders, CUDA cores)";
+}
+
 extern "C" int lmc_matmul(const lmc_qtensor *w, const float *d_x, int ldx, const float *d_bias, float *d_y, int ldy,
                           int batch, int epi, void *stream) {
     if (!w) return lmc_set_error(LMC_ERR_INVALID, "matmul: null qtensor");

@@ -65,6 +65,11 @@ typedef struct {
 } lmc_gemv_extra;
 int lmc_tiled_gemv_ex(const struct lmc_qtensor *t, const float *d_x, int ldx, const float *d_bias, float *d_y, int ldy,
                       int batch, int epi, const lmc_gemv_extra *ex, cudaStream_t s);
+/* The latency (fp32) GEMV for short matrices at batch <= 2 (ff_gemv.cu);
+ * LMC_ERR_UNSUPPORTED when the shape does not suit it. */
+int lmc_ff_gemv_launch(const struct lmc_qtensor *t, const float *d_x, int ldx, const float *d_bias, float *d_y,
+                       int ldy, int batch, int epi, const lmc_gemv_extra *ex, cudaStream_t s);
+int lmc_ff_gemv_suits(const struct lmc_qtensor *t, int batch, int epi);
 /* Batched GEMM on the tcgen05 tensor cores (batch widths > 8; gemm_tc.cu).
  * lmc_gemm_prepare sets t->gemm_wscale (needs cols % 64 == 0);
  * lmc_gemm_reserve sizes the activation workspace (call before any capture);

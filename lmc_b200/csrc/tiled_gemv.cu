@@ -579,6 +579,10 @@ extern "C" int lmc_tiled_gemv_ex(const lmc_qtensor *t, const float *d_x, int ldx
     if (((uintptr_t)d_x & 15) || (ldx & 3) || (ex->x2 && ((uintptr_t)ex->x2 & 15)) ||
         (ex->w && ((uintptr_t)ex->w & 15)) || (ex->b && ((uintptr_t)ex->b & 15)))
         return lmc_set_error(LMC_ERR_INVALID, "gemv_ex: activations and prologue vectors must be 16-byte aligned");
+    {   // short matrices at batch <= 2: the latency GEMV (no per-CTA quantization of x)
+        const int rc = lmc_ff_gemv_launch(t, d_x, ldx, d_bias, d_y, ldy, batch, epi, ex, s);
+        if (rc != LMC_ERR_UNSUPPORTED) return rc;
+    }
     TArgs a = {};
     a.w = (const uint8_t *)t->tiled;
     a.bias = d_bias;

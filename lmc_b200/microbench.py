@@ -86,10 +86,12 @@ def run(torch, qtype, rows, cols, batch=1, iters=50, stream=None, generic=False,
     ms = e0.elapsed_time(e1) / (reps * iters)
     alg = algorithmic_bytes(qtype, rows, cols, batch)
     tiled = qs[0].tiled and not generic
+    kernel = ("generic GEMV (bit-exact decoders, CUDA cores)" if generic
+              else rt.lib().lmc_matmul_kernel(qs[0].h, batch, 0).decode())
     del g
     for q in qs:
         q.close()
-    return {"ms": ms, "gbs": alg / (ms * 1e-3) / 1e9, "bytes": alg, "tiled": tiled}
+    return {"ms": ms, "gbs": alg / (ms * 1e-3) / 1e9, "bytes": alg, "tiled": tiled, "kernel": kernel}
 
 
 def run_attention(torch, B, H, Hkv, Dh, S, pos, kv, iters=20):

@@ -30,6 +30,7 @@ SIGNATURES = {
     "lmc_qtensor_blocks": ([_vp], _vp),
     "lmc_qtensor_has_tiled": ([_vp], _i),
     "lmc_matmul": ([_vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp], _i),
+    "lmc_matmul_kernel": ([_vp, _i, _i], ctypes.c_char_p),
     "lmc_matmul_blocks": ([_u32, _vp, _i, _i, _vp, _i, _vp, _vp, _i, _i, _i, _vp], _i),
     "lmc_layer_norm": ([_vp, _vp, _vp, _vp, _i, _i, _vp], _i),
     "lmc_rms_norm": ([_vp, _vp, _vp, _i, _i, _f, _vp], _i),
