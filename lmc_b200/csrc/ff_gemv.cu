@@ -170,22 +170,27 @@ __global__ void __launch_bounds__(NTHR) k_gemv_ff(TArgs a) {
 
 }  // namespace
 
-// The latency GEMV when the shape suits it (batch <= 2; at most two units a
-// warp with two CTAs per SM; x and the CTA's accumulators within 100 KB of
-// shared memory); LMC_ERR_UNSUPPORTED otherwise (the caller launches the
-// tensor-core GEMV).  LMC_GEMV_FF=0 disables it.
+// The latency GEMV when the shape suits it (batch <= 2; at most three units a
+// warp at batch 1, two at batch 2, with two CTAs per SM; x and the CTA's
+// accumulators within 100 KB of shared memory); LMC_ERR_UNSUPPORTED otherwise
+// (the caller launches the tensor-core GEMV).  LMC_GEMV_FF=0 disables it.
 extern "C" int lmc_ff_gemv_suits(const lmc_qtensor *t, int batch, int epi) {
-    static int off = -1;
+    // units a warp at most: 3 at batch 1, 2 at batch 2 (TinyLlama decode: 3
+    // at batch 1 gained 3.6 %, at batch 2 it lost 7 % against 2)
+    static int off = -1, upw_env = 0;
     if (off < 0) {
         const char *e = getenv("LMC_GEMV_FF");
         off = e && e[0] == '0';
+        const char *u = getenv("LMC_GEMV_FF_UNITS");
+        if (u && atoi(u) > 0) upw_env = atoi(u);
     }
+    const int upw = upw_env ? upw_env : batch == 1 ? 3 : 2;
     if (off || !t || !t->tiled || batch < 1 || batch > 2 || (epi & ~(LMC_EPI_GELU | LMC_EPI_ACCUM))) return 0;
     if (t->type != LMC_TYPE_Q4_K && t->type != LMC_TYPE_Q6_K && t->type != LMC_TYPE_Q8_0) return 0;
     const int KB = t->cols / 256, RT = t->tiled_rows / 16;
     const int NC = std::min(RT, 2 * lmc_sm_count());
     const int maxrt = (RT + NC - 1) / NC;
-    if ((long long)maxrt * KB > 2LL * WARPS) return 0;  // more than two units a warp
+    if ((long long)maxrt * KB > (long long)upw * WARPS) return 0;  // more units a warp than that
     return ((size_t)batch * KB * 256 + 20 + (size_t)maxrt * 32) * sizeof(float) <= 100 * 1024;
 }
 
