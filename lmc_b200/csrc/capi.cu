@@ -39,6 +39,7 @@ extern "C" int lmc_set_wait_limit(long long ns) {
     int rc = lmc_tiled_set_wait_limit(ns);
     if (!rc) rc = lmc_step_set_wait_limit(ns);
     if (!rc) rc = lmc_gemm_set_wait_limit(ns);
+    if (!rc) rc = lmc_peer_set_wait_limit(ns);
     return rc;
 }
 

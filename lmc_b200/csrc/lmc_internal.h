@@ -130,6 +130,18 @@ void lmc_attn_plan(int S, int bh, int fine, int *CH, int *nsplit);
  * outside its pool. */
 int lmc_attn_status(void);
 
+/* Tensor-parallel sums over peer memory (peer_allreduce.cu): every rank
+ * allocates one region of lmc_peer_region_bytes() (zeroed) and maps every
+ * peer's (CUDA IPC); bases[p] = rank p's region as seen by this rank.  Sums
+ * of at most lmc_peer_max_floats() floats (a multiple of 4), collective:
+ * every rank calls it with the same n in the same order. */
+#define LMC_PEER_MAX 8
+size_t lmc_peer_region_bytes(void);
+int lmc_peer_max_floats(void);
+int lmc_peer_allreduce(float *d_x, int n, int rank, int size, void *const *bases, cudaStream_t s);
+int lmc_peer_status(void);
+int lmc_peer_set_wait_limit(long long ns);
+
 /* ---- persistent decode step (step_kernel.cu) -------------------------------
  * A whole decode step as ONE cooperative launch: every CTA walks the same list
  * of ops (embedding, tensor-core GEMVs with their prologue/epilogue, attention,

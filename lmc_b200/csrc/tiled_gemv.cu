@@ -311,6 +311,8 @@ extern "C" int lmc_device_status(void) {
     if (st != LMC_OK) return st;
     const int at = lmc_attn_status();
     if (at != LMC_OK) return at;
+    const int pe = lmc_peer_status();
+    if (pe != LMC_OK) return pe;
     int v = 0;
     LMC_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_tiled_timeout, sizeof(int)));
     const int g = lmc_gemm_status();

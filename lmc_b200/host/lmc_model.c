@@ -60,6 +60,10 @@ struct lmc_model {
     int *d_attn_cnt;            /* attention split arrival counters [batch][kv heads] */
     int *h_stage; /* pinned: tokens, positions, next ids */
     int *h_next_map; /* mapped pinned: the persistent forward step writes its picks here */
+    /* tensor parallel: the residual sums over peer memory (peer_allreduce.cu);
+     * peer_base[p] = rank p's region mapped here (CUDA IPC) */
+    void *peer_base[LMC_PEER_MAX];
+    int peer_on;
     int prompt_cap, ids_cap;
     cudaStream_t stream;
     cudaGraphExec_t gexec;
@@ -531,6 +535,8 @@ int lmc_nccl_unique_id(void *id) {
     return LMC_OK;
 }
 
+static int setup_peer(lmc_model *m);
+
 static int model_load(const char *path, int max_batch, int max_rows, int kv_dtype, int tp_rank, int tp_size,
                       const void *nccl_id, lmc_model **out) {
     if (!path || !out || max_batch <= 0) return lmc_set_error(LMC_ERR_INVALID, "model_load: args");
@@ -553,6 +559,8 @@ static int model_load(const char *path, int max_batch, int max_rows, int kv_dtyp
         memcpy(&u, nccl_id, sizeof u);
         ncclResult_t r = ncclCommInitRank(&m->comm, tp_size, u, tp_rank);
         if (r != ncclSuccess) { m->comm = NULL; rc = lmc_set_error(LMC_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r)); }
+        const char *pe = getenv("LMC_TP_PEER"); /* 0: the residual sums through NCCL */
+        if (!rc && !(pe && pe[0] == '0')) rc = setup_peer(m);
     }
     if (!rc && cudaDeviceSynchronize() != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "load sync");
     if (rc) {
@@ -601,6 +609,11 @@ int lmc_model_free(lmc_model *m) {
     if (m->gexec) cudaGraphExecDestroy(m->gexec); /* (it may hold the communicator's calls) */
     for (int b = 0; b < 3; b++) lmc_step_prog_free(m->pfwd[b]);
     lmc_step_prog_free(m->pgen);
+    for (int p = 0; p < LMC_PEER_MAX; p++) {
+        if (!m->peer_base[p]) continue;
+        if (p == m->tp_rank) cudaFree(m->peer_base[p]);
+        else cudaIpcCloseMemHandle(m->peer_base[p]);
+    }
     if (m->comm) ncclCommDestroy(m->comm);
     if (m->layers) {
         for (int l = 0; l < m->cfg.n_layers; l++) {
@@ -695,8 +708,57 @@ static int model_sync(lmc_model *m) {
 /* Sum of the ranks' partial x (tensor parallel): rank 0 added its partial to
  * the residual, the others wrote theirs over it, so the in-place sum is the
  * next residual on every rank. */
+/* The regions of the peer sums: allocated and zeroed here, their IPC
+ * handles exchanged over NCCL (all-gather), every peer's opened.  Collective. */
+static int setup_peer(lmc_model *m) {
+    const int R = m->tp_rank, N = m->tp_size;
+    if (N > LMC_PEER_MAX) return LMC_OK;
+    const size_t bytes = lmc_peer_region_bytes();
+    CUTRY(cudaMalloc(&m->peer_base[R], bytes));
+    CUTRY(cudaMemset(m->peer_base[R], 0, bytes));
+    CUTRY(cudaDeviceSynchronize()); /* zeroed before any peer can write into it (the all-gather below) */
+    cudaIpcMemHandle_t h;
+    CUTRY(cudaIpcGetMemHandle(&h, m->peer_base[R]));
+    char *dh = NULL, hs[LMC_PEER_MAX * sizeof(cudaIpcMemHandle_t)];
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    CUTRY(cudaMalloc((void **)&dh, hb * N));
+    int rc = LMC_OK;
+    if (cudaMemcpy(dh + hb * R, &h, hb, cudaMemcpyHostToDevice) != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "peer handles");
+    if (!rc && ncclAllGather(dh + hb * R, dh, hb, ncclChar, m->comm, m->stream) != ncclSuccess)
+        rc = lmc_set_error(LMC_ERR_NCCL, "peer handles: all-gather");
+    if (!rc) rc = model_sync(m);
+    if (!rc && cudaMemcpy(hs, dh, hb * N, cudaMemcpyDeviceToHost) != cudaSuccess) rc = lmc_set_error(LMC_ERR_CUDA, "peer handles");
+    cudaFree(dh);
+    for (int p = 0; p < N && !rc; p++) {
+        if (p == R) continue;
+        cudaIpcMemHandle_t hp;
+        memcpy(&hp, hs + hb * p, hb);
+        if (cudaIpcOpenMemHandle(&m->peer_base[p], hp, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            m->peer_base[p] = NULL;
+            rc = lmc_set_error(LMC_ERR_CUDA, "peer region of rank %d: cudaIpcOpenMemHandle", p);
+        }
+    }
+    /* every rank must take the same path: peer sums only if every rank mapped every region */
+    int *dok = NULL, ok = rc == LMC_OK;
+    if (cudaMalloc((void **)&dok, sizeof(int)) == cudaSuccess) {
+        if (cudaMemcpy(dok, &ok, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess &&
+            ncclAllReduce(dok, dok, 1, ncclInt32, ncclMin, m->comm, m->stream) == ncclSuccess && model_sync(m) == LMC_OK)
+            (void)cudaMemcpy(&ok, dok, sizeof(int), cudaMemcpyDeviceToHost);
+        else
+            ok = 0;
+        cudaFree(dok);
+    } else {
+        ok = 0;
+    }
+    m->peer_on = ok;
+    return m->comm ? LMC_OK : rc; /* without peer sums the NCCL path still works */
+}
+
 static int tp_sum_x(lmc_model *m, int B) {
     if (m->tp_size <= 1) return LMC_OK;
+    const int n = B * m->cfg.embed_dim;
+    if (m->peer_on && n <= lmc_peer_max_floats() && n % 4 == 0)
+        return lmc_peer_allreduce(m->x, n, m->tp_rank, m->tp_size, m->peer_base, m->stream);
     if (!m->comm) return lmc_set_error(LMC_ERR_NCCL, "the tensor-parallel communicator was aborted");
     ncclResult_t r = ncclAllReduce(m->x, m->x, (size_t)B * m->cfg.embed_dim, ncclFloat32, ncclSum, m->comm, m->stream);
     return r == ncclSuccess ? LMC_OK : lmc_set_error(LMC_ERR_NCCL, "ncclAllReduce: %s", ncclGetErrorString(r));

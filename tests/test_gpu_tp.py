@@ -1,4 +1,5 @@
-"""Tensor-parallel decode on two GPUs (one process each, NCCL over NVLink):
+"""Tensor-parallel decode on two GPUs (one process each; residual sums over
+peer memory or NCCL, both over NVLink):
 a LLaMA model sharded by heads / ffn rows / vocabulary must give each rank's
 vocabulary slice of the oracle's logits within 1e-3 and the oracle's greedy
 ids.  Skipped on a single-GPU machine."""
@@ -33,10 +34,13 @@ def _rank(rank, world, path, nid, prompts, n_new, q):
         q.put((rank, 0, 0, None, None, repr(e)))
 
 
-def test_tp2_matches_oracle(cuda, orc, model_dir):
+@pytest.mark.parametrize("peer", ["1", "0"], ids=["peer-sums", "nccl-sums"])
+def test_tp2_matches_oracle(cuda, orc, model_dir, monkeypatch, peer):
+    """The residual sums over peer memory (the default) and through NCCL."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
+    monkeypatch.setenv("LMC_TP_PEER", peer)  # inherited by the spawned ranks
     world, n_new = 2, 12
     path = synth.cached_model("llama", model_dir, **KW)
     rng = np.random.default_rng(11)
