@@ -1043,14 +1043,12 @@ static size_t plan_gemv(const lmc_step_op *o, int grid, int stages, DOp *d) {
         a.maxrt = (a.RT + a.NC - 1) / a.NC + 1;
     }
     a.stages = stages;
-    const int qt = qt_of_type(t->type), unit = unit_bytes(qt);
-    const char *pfe = getenv("LMC_STEP_PF_MB");
-    // no L2 prefetch of the units beyond the ring by default: with the ring
-    // prefill in the barrier's shadow it only queued HBM traffic ahead of
-    // the ops' demand loads (GPT-2 Small 0.396 -> 0.393 ms, 8B shape
-    // 3.33 -> 3.24 ms per step without it)
-    const long long pfb = pfe ? atoll(pfe) << 20 : 0;
-    a.pf = (int)std::min<long long>(64, pfb / ((long long)a.NC * WARPS * unit));
+    const int qt = qt_of_type(t->type);
+    // no L2 prefetch of the units beyond the ring: with the ring prefill in
+    // the barrier's shadow it only queued HBM traffic ahead of the ops'
+    // demand loads (GPT-2 Small 0.396 -> 0.393 ms, 8B shape 3.33 -> 3.24 ms
+    // per step without a 40 MB window)
+    a.pf = 0;
     d->g = a;
     d->qt = qt;
     // the latency form when a warp gets few units, x fits in shared memory as
@@ -1060,9 +1058,7 @@ static size_t plan_gemv(const lmc_step_op *o, int grid, int stages, DOp *d) {
     const char *env = getenv("LMC_STEP_FF");
     const long long per_warp = ((long long)(a.maxrt - 1) * a.KB + WARPS - 1) / WARPS;
     const bool norm = a.pro == LMC_PRO_LAYERNORM || a.pro == LMC_PRO_RMSNORM;
-    const char *fenv = getenv("LMC_STEP_FFMAX");
-    const long long ffmax = fenv ? atoll(fenv) : 8;
-    d->ff = !(env && env[0] == '0') && per_warp <= ffmax && (size_t)o->batch * a.KB * 1024 <= 64 * 1024 &&
+    d->ff = !(env && env[0] == '0') && per_warp <= 8 && (size_t)o->batch * a.KB * 1024 <= 64 * 1024 &&
             (!norm || o->stats_in);
     return d->ff ? fgemv_smem(a.KB, o->batch, a.maxrt) : gemv_smem(qt, a.KB, a.XL, a.maxrt);
 }
