@@ -430,14 +430,17 @@ def model_decode(args, rank, world, local_rank, dist):
     kvd = {"f16": rt.KV_F16, "f32": rt.KV_F32, "q8": rt.KV_Q8}[args.kv]
     B = args.batch
     rows = args.prefill_rows or None
+    # paged cache: just the pages prompt + gen positions of every sequence take
+    P = args.kv_page
+    paged = dict(page_size=P, n_pages=B * -(-(args.prompt + args.gen) // P)) if P else {}
     res = None
     t_load = time.perf_counter()  # GGUF parse + weight upload (the file is in the page cache: just written)
     if dist and world > 1:
         from lmc_b200 import tp as tpm
         nid = tpm.exchange_id(dist, rt.nccl_unique_id)
-        m = rt.Model(path, max_batch=B, kv_dtype=kvd, tp=(rank, world, nid), max_rows=rows)
+        m = rt.Model(path, max_batch=B, kv_dtype=kvd, tp=(rank, world, nid), max_rows=rows, **paged)
     else:
-        m = rt.Model(path, max_batch=B, kv_dtype=kvd, max_rows=rows)
+        m = rt.Model(path, max_batch=B, kv_dtype=kvd, max_rows=rows, **paged)
     torch.cuda.synchronize()
     t_load = time.perf_counter() - t_load
     prompts = np.random.default_rng(0).integers(0, m.cfg.vocab_size, (B, args.prompt)).astype(np.int32)
@@ -489,6 +492,9 @@ def model_decode(args, rank, world, local_rank, dist):
                "timing": "host clock around synchronised generate runs (second of two)", "peak_kind": kind_p}
         if t_prefill:
             res.update({"prefill_rows": rows, "prefill_tok_s": round(B * args.prompt / t_prefill, 2)})
+        if P:
+            ps, npg, _ = m.kv_pages()
+            res.update({"kv_page": ps, "kv_pages": npg})
     m.close()
     return res if rank == 0 else None
 
@@ -508,6 +514,8 @@ def main():
     ap.add_argument("--gen", type=int, default=64)
     ap.add_argument("--kv", choices=["f16", "f32", "q8"], default="f16")
     ap.add_argument("--prefill-rows", type=int, default=0)
+    ap.add_argument("--kv-page", type=int, default=0,
+                    help="paged KV cache of this many positions per page, the pool sized to prompt + gen")
     ap.add_argument("--tp", action="store_true", help="tensor parallel over the torchrun ranks (llama8b)")
     ap.add_argument("--no-tp", action="store_true",
                     help="gpt2 on several GPUs: skip the tensor-parallel 8B line (tp sub-object)")

@@ -282,6 +282,25 @@ int lmc_model_load_tp(const char *gguf_path, int max_batch, int kv_dtype, int tp
  * tp_size 1 (nccl_id NULL) loads the whole model. */
 int lmc_model_load_ex(const char *gguf_path, int max_batch, int max_rows, int kv_dtype, int tp_rank, int tp_size,
                       const void *nccl_id_128, lmc_model **out);
+/* lmc_model_load_ex with a paged KV cache, for servers whose sequences are
+ * of very different lengths.  No counterpart in LMc, whose cache is one
+ * [Hkv][S][Dh] array per layer (src/models.h:149-162).  Each layer's cache
+ * is a pool of n_pages pages of page_size positions (a power of two in
+ * [16, 65536] that divides the context; n_pages above max_batch x
+ * context / page_size is lowered to that), so max_batch sequences share
+ * n_pages x page_size positions instead of holding the whole context each.
+ * A sequence takes pages from the pool as its positions grow: forward,
+ * prefill, generate and replay take the pages their steps write before the
+ * steps run, and fail with LMC_ERR_OOM (nothing taken) when the pool has
+ * too few free.  lmc_model_release_seq gives sequence seq's pages back (its
+ * cached rows are gone: start it again at position 0).  The results are the
+ * same as with the contiguous cache (such models always run the step
+ * kernel by kernel, not as the persistent single-launch step). */
+int lmc_model_load_paged(const char *gguf_path, int max_batch, int max_rows, int kv_dtype, int page_size,
+                         int n_pages, int tp_rank, int tp_size, const void *nccl_id_128, lmc_model **out);
+int lmc_model_release_seq(lmc_model *m, int seq);
+/* Page size (0: contiguous cache), pages in the pool and pages free. */
+int lmc_model_kv_pages(const lmc_model *m, int *page_size, int *n_pages, int *n_free);
 int lmc_model_shard(const lmc_model *m, int *tp_rank, int *tp_size, int *vocab_begin, int *vocab_rows);
 int lmc_model_get_config(const lmc_model *m, lmc_model_config *cfg);
 int lmc_model_free(lmc_model *m);

@@ -123,18 +123,24 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
     float *vsc = ml + 2 * G;    // [CH16] V row scales (int8 rows)
     __half *vt = reinterpret_cast<__half *>(sm + ((G * DH + G * CH16 + 2 * G + (Q8 ? CH16 : 0) + 3) & ~3));  // [CH16][VSTR], 16-byte aligned
     const size_t cs = a.seq ? (size_t)a.seq[b] : (size_t)b;
-    KV *kc = reinterpret_cast<KV *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * RS;
-    KV *vc = reinterpret_cast<KV *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * RS;
+    KV *const kpool = reinterpret_cast<KV *>(a.k_cache), *const vpool = reinterpret_cast<KV *>(a.v_cache);
+    KV *kc = kpool + (cs * a.Hkv + kh) * a.S * RS;
+    KV *vc = vpool + (cs * a.Hkv + kh) * a.S * RS;
+    // row t of this (sequence, kv head): contiguous, or through the page table
+    auto row = [&](KV *seqbase, KV *pool, int t) -> KV * {
+        return a.pages ? kv_page_row<KV>(a, pool, cs, kh, t, RS) : seqbase + (size_t)t * RS;
+    };
     const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (DH / 2) : nullptr;
     const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (DH / 2) : nullptr;
     if (Q8 && a.append && pos >= t0 && pos < t1) {  // quantize the new rows: warp 0 K, warp 1 V
         if (warp < 2)
-            kv_q8_store_row(reinterpret_cast<KvQ8 *>((warp ? vc : kc) + (size_t)pos * RS),
+            kv_q8_store_row(reinterpret_cast<KvQ8 *>(warp ? row(vc, vpool, pos) : row(kc, kpool, pos)),
                             (warp ? a.v_new : a.k_new) + (size_t)b * a.ldkv + (size_t)kh * DH, warp ? nullptr : rc,
                             rs, DH, lane);
     } else if (a.append && pos >= t0 && pos < t1) {  // append this step's K/V row (K rotated first when RoPE applies)
         const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * DH;
         const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * DH;
+        KV *kp = row(kc, kpool, pos), *vp = row(vc, vpool, pos);
         for (int d = threadIdx.x; d < DH / 2; d += ATT_THREADS) {
             float k0 = kn[2 * d], k1 = kn[2 * d + 1];
             if (rc) {
@@ -144,10 +150,10 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
                 k1 = r1;
             }
             if constexpr (!Q8) {
-                kc[(size_t)pos * DH + 2 * d] = __float2half_rn(k0);
-                kc[(size_t)pos * DH + 2 * d + 1] = __float2half_rn(k1);
-                vc[(size_t)pos * DH + 2 * d] = __float2half_rn(vn[2 * d]);
-                vc[(size_t)pos * DH + 2 * d + 1] = __float2half_rn(vn[2 * d + 1]);
+                kp[2 * d] = __float2half_rn(k0);
+                kp[2 * d + 1] = __float2half_rn(k1);
+                vp[2 * d] = __float2half_rn(vn[2 * d]);
+                vp[2 * d + 1] = __float2half_rn(vn[2 * d + 1]);
             }
         }
     }
@@ -173,16 +179,16 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
     if constexpr (Q8) {
         for (int i = threadIdx.x; i < n16 * (DH / 8); i += ATT_THREADS) {
             const int r = i / (DH / 8), c8 = i % (DH / 8);
-            const KV *row = vc + (size_t)(t0 + (r < n ? r : 0)) * RS;
-            const uint2 w = r < n ? *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint8_t *>(row) + 8 * c8)
+            const KV *vrow = row(vc, vpool, t0 + (r < n ? r : 0));
+            const uint2 w = r < n ? *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint8_t *>(vrow) + 8 * c8)
                                   : make_uint2(0x80808080u ^ 0x80808080u, 0u);
             *reinterpret_cast<uint4 *>(vt + r * VSTR + 8 * c8) = r < n ? q8x8_to_h8(w) : make_uint4(0u, 0u, 0u, 0u);
-            if (c8 == 0) vsc[r] = r < n ? kv_q8_scale(reinterpret_cast<const KvQ8 *>(row), DH) : 0.0f;
+            if (c8 == 0) vsc[r] = r < n ? kv_q8_scale(reinterpret_cast<const KvQ8 *>(vrow), DH) : 0.0f;
         }
     } else {
         for (int i = threadIdx.x; i < n16 * (DH / 8); i += ATT_THREADS) {
             const int r = i / (DH / 8), c8 = i % (DH / 8);
-            const KV *src = vc + (size_t)(t0 + (r < n ? r : 0)) * DH + 8 * c8;
+            const KV *src = row(vc, vpool, t0 + (r < n ? r : 0)) + 8 * c8;
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(vt + r * VSTR + 8 * c8)),
                          "l"(src), "r"(r < n ? 16 : 0)
                          : "memory");
@@ -211,15 +217,15 @@ __device__ __forceinline__ void split_body_tc(const AttnArgs &a, float *sm, int 
         for (int u = 0; u < TB; u++) {
             const int p = 8 * (j0 + u * nw) + g;  // this lane's B column (position within the split)
             if constexpr (Q8) {
-                const KV *row = kc + (size_t)(t0 + (p < n ? p : 0)) * RS;
-                const uint8_t *kr = reinterpret_cast<const uint8_t *>(row) + 8 * tig;
+                const KV *krow = row(kc, kpool, t0 + (p < n ? p : 0));
+                const uint8_t *kr = reinterpret_cast<const uint8_t *>(krow) + 8 * tig;
 #pragma unroll
                 for (int kp = 0; kp < KS / 2; kp++)
                     kv[u][kp] = p < n ? q8x8_to_h8(*reinterpret_cast<const uint2 *>(kr + 32 * kp))
                                       : make_uint4(0u, 0u, 0u, 0u);
-                ksc[u] = p < n ? kv_q8_scale(reinterpret_cast<const KvQ8 *>(row), DH) : 0.0f;
+                ksc[u] = p < n ? kv_q8_scale(reinterpret_cast<const KvQ8 *>(krow), DH) : 0.0f;
             } else {
-                const KV *kr = kc + (size_t)(t0 + (p < n ? p : 0)) * DH + 8 * tig;
+                const KV *kr = row(kc, kpool, t0 + (p < n ? p : 0)) + 8 * tig;
 #pragma unroll
                 for (int kp = 0; kp < KS / 2; kp++)
                     kv[u][kp] = p < n ? *reinterpret_cast<const uint4 *>(kr + 32 * kp) : make_uint4(0u, 0u, 0u, 0u);
@@ -326,8 +332,9 @@ __global__ void k_kv_append(AttnArgs a) {
     if (pos < 0 || pos >= a.S) return;
     const size_t cs = (size_t)a.seq[b];
     const int RS = kv_rs<KV>(Dh);
-    KV *kc = reinterpret_cast<KV *>(a.k_cache) + (cs * a.Hkv + kh) * a.S * RS + (size_t)pos * RS;
-    KV *vc = reinterpret_cast<KV *>(a.v_cache) + (cs * a.Hkv + kh) * a.S * RS + (size_t)pos * RS;
+    KV *const kpool = reinterpret_cast<KV *>(a.k_cache), *const vpool = reinterpret_cast<KV *>(a.v_cache);
+    KV *kc = a.pages ? kv_page_row<KV>(a, kpool, cs, kh, pos, RS) : kpool + ((cs * a.Hkv + kh) * a.S + pos) * RS;
+    KV *vc = a.pages ? kv_page_row<KV>(a, vpool, cs, kh, pos, RS) : vpool + ((cs * a.Hkv + kh) * a.S + pos) * RS;
     const float *kn = a.k_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
     const float *vn = a.v_new + (size_t)b * a.ldkv + (size_t)kh * Dh;
     const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (Dh / 2) : nullptr;
@@ -455,7 +462,7 @@ static int attention_impl(float *out, int ldo, const float *q, int ldq, const fl
     // (LMC_ATTN_TC=0 selects the CUDA-core body; both give the same result)
     const char *tce = getenv("LMC_ATTN_TC");
     const bool tc = (kv_dtype == LMC_KV_F16 || kv_dtype == LMC_KV_Q8) && (Dh == 64 || Dh == 128) && G <= 8 &&
-                    !(tce && tce[0] == '0') && !pages;
+                    !(tce && tce[0] == '0');
     const int CH16 = (a.CH + 15) & ~15;
     const size_t smem = tc ? (size_t)(G * Dh + G * CH16 + 2 * G + CH16 + 2) * sizeof(float) + 16 + (size_t)CH16 * (Dh + 8) * 2
                            : (size_t)(G * Dh + G * a.CH + 2 * G + (ATT_THREADS / 32) * ATT_GROUP * Dh) * sizeof(float);
@@ -497,6 +504,21 @@ extern "C" int lmc_attention_rows_launch(float *out, int ldo, const float *q, in
                                          int *d_cnt, cudaStream_t s) {
     return attention_impl(out, ldo, q, ldq, k_new, v_new, ldkv, k_cache, v_cache, kv_dtype, d_pos, d_seq, batch, H,
                           Hkv, Dh, S, d_ws, ws_bytes, rope_cos, rope_sin, d_cnt, NULL, 0, 0, 0, s);
+}
+
+extern "C" int lmc_attention_rows_paged_launch(float *out, int ldo, const float *q, int ldq, const float *k_new,
+                                               const float *v_new, int ldkv, void *k_pool, void *v_pool, int kv_dtype,
+                                               const int *d_pos, const int *d_seq, int batch, int H, int Hkv, int Dh,
+                                               const int *d_pages, int max_pages, int page_shift, int n_pages,
+                                               void *d_ws, size_t ws_bytes, const float *rope_cos,
+                                               const float *rope_sin, int *d_cnt, cudaStream_t s) {
+    if (!d_pages || n_pages <= 0 || max_pages <= 0 || page_shift < 0 || page_shift > 24 ||
+        (long long)max_pages << page_shift > (1 << 24))
+        return lmc_set_error(LMC_ERR_INVALID, "attention_rows_paged: pages %d, table %d x page 2^%d", n_pages,
+                             max_pages, page_shift);
+    return attention_impl(out, ldo, q, ldq, k_new, v_new, ldkv, k_pool, v_pool, kv_dtype, d_pos, d_seq, batch, H, Hkv,
+                          Dh, max_pages << page_shift, d_ws, ws_bytes, rope_cos, rope_sin, d_cnt, d_pages, page_shift,
+                          max_pages, n_pages, s);
 }
 
 extern "C" int lmc_attention_decode_paged(float *out, const float *q, const float *k_new, const float *v_new,

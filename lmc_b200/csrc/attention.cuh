@@ -106,6 +106,20 @@ struct AttnArgs {
 };
 __device__ int g_attn_page_err;  // an out-of-range page id was met (lmc_device_status)
 
+// Row t of cache sequence cs, kv head kh in a paged pool (a.pages set):
+// page a.pages[cs * max_pages + t / P], slot t % P of that page's kv head kh.
+// A page id outside [0, n_pages) is not followed: page 0 is used instead and
+// g_attn_page_err is set.
+template <typename KV>
+__device__ __forceinline__ KV *kv_page_row(const AttnArgs &a, KV *pool, size_t cs, int kh, int t, int RS) {
+    int pg = __ldg(a.pages + cs * a.max_pages + (t >> a.page_shift));
+    if (pg < 0 || pg >= a.n_pages) {
+        atomicExch(&g_attn_page_err, 1);
+        pg = 0;
+    }
+    return pool + ((((size_t)pg * a.Hkv + kh) << a.page_shift) + (t & ((1 << a.page_shift) - 1))) * RS;
+}
+
 
 // One non-empty split: append the new K/V row when it falls here, scores,
 // softmax statistics and the unnormalised accumulator (or the final output
@@ -172,13 +186,7 @@ __device__ __forceinline__ void split_body(const AttnArgs &a, float *sm, int sp,
     KV *vc = vpool + (cs * a.Hkv + kh) * a.S * RS;
     // row t of this (sequence, kv head): contiguous, or through the page table
     auto row = [&](KV *seqbase, KV *pool, int t) -> KV * {
-        if (!a.pages) return seqbase + (size_t)t * RS;
-        int pg = __ldg(a.pages + cs * a.max_pages + (t >> a.page_shift));
-        if (pg < 0 || pg >= a.n_pages) {
-            atomicExch(&g_attn_page_err, 1);
-            pg = 0;
-        }
-        return pool + ((((size_t)pg * a.Hkv + kh) << a.page_shift) + (t & ((1 << a.page_shift) - 1))) * RS;
+        return a.pages ? kv_page_row<KV>(a, pool, cs, kh, t, RS) : seqbase + (size_t)t * RS;
     };
     const float *rc = a.rope_cos ? a.rope_cos + (size_t)pos * (Dh / 2) : nullptr;
     const float *rs = a.rope_sin ? a.rope_sin + (size_t)pos * (Dh / 2) : nullptr;

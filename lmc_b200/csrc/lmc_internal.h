@@ -111,6 +111,16 @@ int lmc_attention_rows_launch(float *out, int ldo, const float *q, int ldq, cons
                               int ldkv, void *k_cache, void *v_cache, int kv_dtype, const int *d_pos, const int *d_seq,
                               int batch, int H, int Hkv, int Dh, int S, void *d_ws, size_t ws_bytes,
                               const float *rope_cos, const float *rope_sin, int *d_cnt, cudaStream_t s);
+/* lmc_attention_rows_launch over a paged cache: k_pool / v_pool are pools of
+ * n_pages pages [page][Hkv][2^page_shift positions][row], and position t of
+ * cache sequence s lives in page d_pages[s * max_pages + (t >> page_shift)]
+ * (the context is max_pages << page_shift positions). */
+int lmc_attention_rows_paged_launch(float *out, int ldo, const float *q, int ldq, const float *k_new,
+                                    const float *v_new, int ldkv, void *k_pool, void *v_pool, int kv_dtype,
+                                    const int *d_pos, const int *d_seq, int batch, int H, int Hkv, int Dh,
+                                    const int *d_pages, int max_pages, int page_shift, int n_pages, void *d_ws,
+                                    size_t ws_bytes, const float *rope_cos, const float *rope_sin, int *d_cnt,
+                                    cudaStream_t s);
 /* Generation bookkeeping after one step (see lmc_model_generate): the greedy
  * id of each sequence is read from (and reset in) d_keys, or, with
  * from_next, the pick is the one already in d_next (a sampler wrote it; the

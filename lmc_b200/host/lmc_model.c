@@ -52,6 +52,17 @@ struct lmc_model {
     Layer *layers;
     void *kc, *vc;
     size_t kv_layer_bytes;
+    /* paged KV cache (page_size 0: contiguous [seq][kv head][seq_len][row]).
+     * Each layer's cache is a pool of n_pages pages [page][kv head][page_size]
+     * [row]; position t of sequence s lives in page
+     * d_pages[s * max_pages + t / page_size] (the same page id in every
+     * layer's pool).  The host hands pages out before the step that first
+     * writes them: h_pages mirrors the table (-1: none), seq_np[s] = pages
+     * sequence s holds (always its first seq_np[s] table entries), free_ids
+     * the n_free ids not held. */
+    int page_size, page_shift, max_pages, n_pages, n_free;
+    int *d_pages, *h_pages, *seq_np, *free_ids;
+    int g_pos; /* next position of the last generation's step loop (lmc_model_replay) */
     float *x, *xn, *qkv, *att, *h, *h2, *logits;
     void *ws;
     size_t ws_bytes;
@@ -485,7 +496,27 @@ static int alloc_state(lmc_model *m) {
     if (m->kv_dtype == LMC_KV_Q8 && (c->head_dim % 16 || c->head_dim > 512))
         return lmc_set_error(LMC_ERR_UNSUPPORTED, "int8 KV rows need a head size that is a multiple of 16, <= 512");
     /* this rank's kv heads, rows of LMC_KV_ROW_BYTES */
-    m->kv_layer_bytes = NS * (size_t)m->hkvl * (size_t)c->seq_len * LMC_KV_ROW_BYTES(m->kv_dtype, c->head_dim);
+    const size_t row_bytes = LMC_KV_ROW_BYTES(m->kv_dtype, c->head_dim);
+    if (m->page_size) {
+        if (c->seq_len % m->page_size)
+            return lmc_set_error(LMC_ERR_INVALID, "KV page size %d does not divide the context %d", m->page_size,
+                                 c->seq_len);
+        m->max_pages = c->seq_len / m->page_size;
+        const size_t table = NS * (size_t)m->max_pages;
+        if ((size_t)m->n_pages > table) m->n_pages = (int)table; /* every sequence's whole context */
+        m->kv_layer_bytes = (size_t)m->n_pages * m->hkvl * (size_t)m->page_size * row_bytes;
+        TRY(dev_alloc((void **)&m->d_pages, sizeof(int) * table));
+        CUTRY(cudaMemset(m->d_pages, 0xff, sizeof(int) * table)); /* -1: no page */
+        m->h_pages = (int *)malloc(sizeof(int) * table);
+        m->seq_np = (int *)calloc(NS, sizeof(int));
+        m->free_ids = (int *)malloc(sizeof(int) * (size_t)m->n_pages);
+        if (!m->h_pages || !m->seq_np || !m->free_ids) return lmc_set_error(LMC_ERR_OOM, "KV page table");
+        for (size_t i = 0; i < table; i++) m->h_pages[i] = -1;
+        for (int k = 0; k < m->n_pages; k++) m->free_ids[k] = m->n_pages - 1 - k; /* handed out as 0, 1, 2, ... */
+        m->n_free = m->n_pages;
+    } else {
+        m->kv_layer_bytes = NS * (size_t)m->hkvl * (size_t)c->seq_len * row_bytes;
+    }
     TRY(dev_alloc(&m->kc, m->kv_layer_bytes * c->n_layers));
     TRY(dev_alloc(&m->vc, m->kv_layer_bytes * c->n_layers));
     TRY(dev_alloc((void **)&m->x, 4 * B * D));
@@ -537,9 +568,12 @@ int lmc_nccl_unique_id(void *id) {
 
 static int setup_peer(lmc_model *m);
 
-static int model_load(const char *path, int max_batch, int max_rows, int kv_dtype, int tp_rank, int tp_size,
-                      const void *nccl_id, lmc_model **out) {
+static int model_load(const char *path, int max_batch, int max_rows, int kv_dtype, int page_size, int n_pages,
+                      int tp_rank, int tp_size, const void *nccl_id, lmc_model **out) {
     if (!path || !out || max_batch <= 0) return lmc_set_error(LMC_ERR_INVALID, "model_load: args");
+    if (page_size && (page_size < 16 || page_size > (1 << 16) || (page_size & (page_size - 1)) || n_pages <= 0))
+        return lmc_set_error(LMC_ERR_INVALID, "model_load: KV pages of %d positions, %d pages (need a power of two "
+                             "in [16, 65536] and at least one page)", page_size, n_pages);
     if (kv_dtype != LMC_KV_F32 && kv_dtype != LMC_KV_F16 && kv_dtype != LMC_KV_Q8)
         return lmc_set_error(LMC_ERR_INVALID, "model_load: kv dtype");
     if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size || (tp_size > 1 && !nccl_id))
@@ -550,6 +584,9 @@ static int model_load(const char *path, int max_batch, int max_rows, int kv_dtyp
     m->max_batch = max_batch;
     m->max_rows = max_rows > max_batch ? max_rows : max_batch;
     m->kv_dtype = kv_dtype;
+    m->page_size = page_size;
+    while (page_size && (1 << m->page_shift) < page_size) m->page_shift++;
+    m->n_pages = page_size ? n_pages : 0;
     m->tp_rank = tp_rank;
     m->tp_size = tp_size;
     int rc = load(m, path);
@@ -574,17 +611,87 @@ static int model_load(const char *path, int max_batch, int max_rows, int kv_dtyp
 }
 
 int lmc_model_load(const char *path, int max_batch, int kv_dtype, lmc_model **out) {
-    return model_load(path, max_batch, max_batch, kv_dtype, 0, 1, NULL, out);
+    return model_load(path, max_batch, max_batch, kv_dtype, 0, 0, 0, 1, NULL, out);
 }
 
 int lmc_model_load_ex(const char *path, int max_batch, int max_rows, int kv_dtype, int tp_rank, int tp_size,
                       const void *nccl_id, lmc_model **out) {
-    return model_load(path, max_batch, max_rows, kv_dtype, tp_rank, tp_size, nccl_id, out);
+    return model_load(path, max_batch, max_rows, kv_dtype, 0, 0, tp_rank, tp_size, nccl_id, out);
 }
 
 int lmc_model_load_tp(const char *path, int max_batch, int kv_dtype, int tp_rank, int tp_size, const void *nccl_id,
                       lmc_model **out) {
-    return model_load(path, max_batch, max_batch, kv_dtype, tp_rank, tp_size, nccl_id, out);
+    return model_load(path, max_batch, max_batch, kv_dtype, 0, 0, tp_rank, tp_size, nccl_id, out);
+}
+
+int lmc_model_load_paged(const char *path, int max_batch, int max_rows, int kv_dtype, int page_size, int n_pages,
+                         int tp_rank, int tp_size, const void *nccl_id, lmc_model **out) {
+    if (page_size <= 0) return lmc_set_error(LMC_ERR_INVALID, "model_load_paged: page size %d", page_size);
+    return model_load(path, max_batch, max_rows, kv_dtype, page_size, n_pages, tp_rank, tp_size, nccl_id, out);
+}
+
+/* Pages for positions [0, npos[i]) of sequence seqs[i], i < n (distinct
+ * sequences), taken from the free ids before the step that writes them; the
+ * changed table entries are copied to the device on the model's stream, so
+ * they land after every step already queued.  All or nothing: with too few
+ * free pages nothing changes and the call fails with LMC_ERR_OOM. */
+static int pages_reserve(lmc_model *m, int n, const int *seqs, const int *npos) {
+    if (!m->page_size) return LMC_OK;
+    long long want = 0;
+    for (int i = 0; i < n; i++) {
+        const int need = (npos[i] + m->page_size - 1) >> m->page_shift;
+        if (need > m->seq_np[seqs[i]]) want += need - m->seq_np[seqs[i]];
+    }
+    if (want > m->n_free)
+        return lmc_set_error(LMC_ERR_OOM, "KV pages: %lld more needed, %d of %d free", want, m->n_free, m->n_pages);
+    for (int i = 0; i < n; i++) {
+        const int sq = seqs[i], need = (npos[i] + m->page_size - 1) >> m->page_shift, first = m->seq_np[sq];
+        if (need <= first) continue;
+        int *row = m->h_pages + (size_t)sq * m->max_pages;
+        for (int k = first; k < need; k++) row[k] = m->free_ids[--m->n_free];
+        m->seq_np[sq] = need;
+        /* pageable source: the copy has taken the entries when the call returns */
+        CUTRY(cudaMemcpyAsync(m->d_pages + (size_t)sq * m->max_pages + first, row + first,
+                              sizeof(int) * (size_t)(need - first), cudaMemcpyHostToDevice, m->stream));
+    }
+    return LMC_OK;
+}
+
+/* The same pages for one position count shared by sequences 0 .. B-1. */
+static int pages_reserve_all(lmc_model *m, int B, int npos) {
+    if (!m->page_size) return LMC_OK;
+    int rc = LMC_OK;
+    int *seqs = (int *)malloc(sizeof(int) * 2 * (size_t)B);
+    if (!seqs) return lmc_set_error(LMC_ERR_OOM, "KV pages: host");
+    for (int b = 0; b < B; b++) { seqs[b] = b; seqs[B + b] = npos; }
+    rc = pages_reserve(m, B, seqs, seqs + B);
+    free(seqs);
+    return rc;
+}
+
+int lmc_model_release_seq(lmc_model *m, int seq) {
+    if (!m || seq < 0 || seq >= m->max_batch)
+        return lmc_set_error(LMC_ERR_INVALID, "model_release_seq: sequence %d (of %d)", seq, m ? m->max_batch : 0);
+    if (!m->page_size) return LMC_OK; /* the contiguous cache keeps every sequence's rows */
+    const int np = m->seq_np[seq];
+    int *row = m->h_pages + (size_t)seq * m->max_pages;
+    for (int k = np - 1; k >= 0; k--) {
+        m->free_ids[m->n_free++] = row[k];
+        row[k] = -1;
+    }
+    m->seq_np[seq] = 0;
+    if (np)
+        CUTRY(cudaMemcpyAsync(m->d_pages + (size_t)seq * m->max_pages, row, sizeof(int) * (size_t)np,
+                              cudaMemcpyHostToDevice, m->stream));
+    return LMC_OK;
+}
+
+int lmc_model_kv_pages(const lmc_model *m, int *page_size, int *n_pages, int *n_free) {
+    if (!m) return lmc_set_error(LMC_ERR_INVALID, "model_kv_pages: null");
+    if (page_size) *page_size = m->page_size;
+    if (n_pages) *n_pages = m->n_pages;
+    if (n_free) *n_free = m->n_free;
+    return LMC_OK;
 }
 
 int lmc_model_shard(const lmc_model *m, int *tp_rank, int *tp_size, int *vocab_begin, int *vocab_rows) {
@@ -632,6 +739,10 @@ int lmc_model_free(lmc_model *m) {
                   m->att, m->h, m->h2, m->logits, m->ws, m->d_tok, m->d_pos, m->d_next, m->d_step, m->d_prompt, m->d_ids,
                   m->d_keys, m->d_attn_cnt, m->d_seq, m->d_rng};
     for (size_t i = 0; i < sizeof ps / sizeof ps[0]; i++) if (ps[i]) cudaFree(ps[i]);
+    if (m->d_pages) cudaFree(m->d_pages);
+    free(m->h_pages);
+    free(m->seq_np);
+    free(m->free_ids);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_next_map) cudaFreeHost(m->h_next_map);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -764,6 +875,21 @@ static int tp_sum_x(lmc_model *m, int B) {
     return r == ncclSuccess ? LMC_OK : lmc_set_error(LMC_ERR_NCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
 }
 
+/* The attention of one layer over its cache (contiguous or paged): q of
+ * each row against the cached rows of its sequence, the new K/V rows
+ * appended, output into m->att (row stride ldo). */
+static int attn_rows(lmc_model *m, int ldo, const float *q, int ldq, const float *k, const float *v, int ldkv,
+                     void *kc, void *vc, int B, int H, int Hkv, const float *rc, const float *rs) {
+    const lmc_model_config *c = &m->cfg;
+    const int *seq = m->prefill ? m->d_seq : NULL;
+    if (m->page_size)
+        return lmc_attention_rows_paged_launch(m->att, ldo, q, ldq, k, v, ldkv, kc, vc, m->kv_dtype, m->d_pos, seq, B,
+                                               H, Hkv, c->head_dim, m->d_pages, m->max_pages, m->page_shift,
+                                               m->n_pages, m->ws, m->ws_bytes, rc, rs, m->d_attn_cnt, m->stream);
+    return lmc_attention_rows_launch(m->att, ldo, q, ldq, k, v, ldkv, kc, vc, m->kv_dtype, m->d_pos, seq, B, H, Hkv,
+                                     c->head_dim, c->seq_len, m->ws, m->ws_bytes, rc, rs, m->d_attn_cnt, m->stream);
+}
+
 /* One decode step for B sequences: tokens d_tok, positions d_pos -> logits
  * and each sequence's greedy-pick key in d_keys.  Only kernel launches on
  * m->stream, so it can be captured as a graph.  LayerNorm / RMSNorm run as
@@ -783,9 +909,7 @@ static int step(lmc_model *m, int B) {
         if (c->arch == 1) { /* src/ops.c:182-206 */
             TRY(norm_matmul(m, w->qkv, LMC_PRO_LAYERNORM, w->ln1_w, w->ln1_b, 1e-5f, w->qkv_b, m->qkv, 3 * D, B,
                             LMC_EPI_NONE, NULL));
-            TRY(lmc_attention_rows_launch(m->att, D, m->qkv, 3 * D, m->qkv + D, m->qkv + 2 * D, 3 * D, kc, vc,
-                                          m->kv_dtype, m->d_pos, m->prefill ? m->d_seq : NULL, B, H, H, Dh, S, m->ws,
-                                          m->ws_bytes, NULL, NULL, m->d_attn_cnt, s));
+            TRY(attn_rows(m, D, m->qkv, 3 * D, m->qkv + D, m->qkv + 2 * D, 3 * D, kc, vc, B, H, H, NULL, NULL));
             TRY(lmc_matmul(w->proj, m->att, D, w->proj_b, m->x, D, B, LMC_EPI_ACCUM, s));
             TRY(norm_matmul(m, w->fc, LMC_PRO_LAYERNORM, w->ln2_w, w->ln2_b, 1e-5f, w->fc_b, m->h, F, B, LMC_EPI_GELU,
                             NULL));
@@ -812,9 +936,7 @@ static int step(lmc_model *m, int B) {
                 ld = 0;
             }
             /* RoPE on q and the new K row happens inside the attention kernel */
-            TRY(lmc_attention_rows_launch(m->att, QD, q, ld ? ld : QD, k, v, ld ? ld : KVD, kc, vc, m->kv_dtype,
-                                          m->d_pos, m->prefill ? m->d_seq : NULL, B, H, Hkv, Dh, S, m->ws,
-                                          m->ws_bytes, m->rope_cos, m->rope_sin, m->d_attn_cnt, s));
+            TRY(attn_rows(m, QD, q, ld ? ld : QD, k, v, ld ? ld : KVD, kc, vc, B, H, Hkv, m->rope_cos, m->rope_sin));
             TRY(lmc_matmul(w->o, m->att, QD, NULL, m->x, D, B, rp, s));
             TRY(tp_sum_x(m, B));
             if (w->gateup_cat && (lmc_qtensor_has_tiled(w->down) || (B > 8 && w->down->gemm_wscale > 0.0f))) {
@@ -934,7 +1056,7 @@ static void add_attn(lmc_step_op *ops, int *n, lmc_model *m, int B, float *out, 
 static int build_prog(lmc_model *m, int B, int gen, int n_prompt, int n_new, lmc_step_prog **out) {
     const lmc_model_config *c = &m->cfg;
     *out = NULL;
-    if (!persist_enabled(m) || m->tp_size > 1 || B > 2 || !m->d_attn_cnt)
+    if (!persist_enabled(m) || m->tp_size > 1 || B > 2 || !m->d_attn_cnt || m->page_size)
         return lmc_set_error(LMC_ERR_UNSUPPORTED, "persistent step: not for this model or batch");
     const int D = c->embed_dim, F = c->ffn_dim, V = c->vocab_size, H = c->n_heads, Dh = c->head_dim;
     lmc_step_op *ops = (lmc_step_op *)calloc((size_t)(5 * c->n_layers + 5), sizeof(lmc_step_op));
@@ -1064,6 +1186,14 @@ int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int B
         if (h_pos[b] < 0 || h_pos[b] >= m->cfg.seq_len)
             return lmc_set_error(LMC_ERR_INVALID, "model_forward: position %d outside [0, %d)", h_pos[b], m->cfg.seq_len);
     }
+    if (m->page_size) { /* row b is sequence b: pages up to its position */
+        int *sp = (int *)malloc(sizeof(int) * 2 * (size_t)B);
+        if (!sp) return lmc_set_error(LMC_ERR_OOM, "model_forward: host");
+        for (int b = 0; b < B; b++) { sp[b] = b; sp[B + b] = h_pos[b] + 1; }
+        const int rc = pages_reserve(m, B, sp, sp + B);
+        free(sp);
+        TRY(rc);
+    }
     lmc_step_prog *p = fwd_prog(m, B);
     if (p) {
         /* the persistent step takes the tokens and positions in its launch
@@ -1122,6 +1252,8 @@ int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int sta
         if (h_tokens[i] < 0 || h_tokens[i] >= m->cfg.vocab_size)
             return lmc_set_error(LMC_ERR_INVALID, "model_prefill: token %d outside [0, %d)", h_tokens[i], m->cfg.vocab_size);
     cudaStream_t s = m->stream;
+    const int npos = start_pos + n;
+    TRY(pages_reserve(m, 1, &seq, &npos));
     TRY(prefill_chunks(m, seq, h_tokens, n, start_pos, 1));
     TRY(lmc_keys_to_ids_launch(m->d_keys, m->d_next, 1, s));
     if (h_logits) CUTRY(cudaMemcpyAsync(h_logits, m->logits, sizeof(float) * m->vl, cudaMemcpyDeviceToHost, s));
@@ -1203,6 +1335,8 @@ static int generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, int 
         if (h_prompt[i] < 0 || h_prompt[i] >= m->cfg.vocab_size)
             return lmc_set_error(LMC_ERR_INVALID, "model_generate: token %d out of range", h_prompt[i]);
     TRY(ensure_gen_buffers(m, B, n_prompt, n_new));
+    /* the loop writes positions 0 .. n_prompt + n_new - 2 of sequences 0 .. B-1 */
+    TRY(pages_reserve_all(m, B, n_prompt + n_new - 1));
     /* LMC_NO_GRAPH=1 launches the kernels directly (profilers that cannot
      * replay graph kernel nodes one by one); the kernels are the same. */
     const char *ng = getenv("LMC_NO_GRAPH");
@@ -1282,6 +1416,7 @@ static int generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, int 
      * last step's argmax (the advance kernel recorded it as well) */
     CUTRY(cudaMemcpyAsync(h_out_ids, m->d_ids, sizeof(int) * (size_t)B * n_new, cudaMemcpyDeviceToHost, s));
     TRY(model_sync(m));
+    m->g_pos = n_prompt + n_new - 1;
     return LMC_OK;
 }
 
@@ -1290,6 +1425,13 @@ static int generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, int 
  * steps continue from the current device-side position. */
 int lmc_model_replay(lmc_model *m, int n, void *stream_out) {
     if (!m || !m->g_batch) return lmc_set_error(LMC_ERR_INVALID, "model_replay: no generation to continue");
+    if (m->page_size) { /* pages for the positions these steps write */
+        if (n < 0 || m->g_pos + n > m->cfg.seq_len)
+            return lmc_set_error(LMC_ERR_INVALID, "model_replay: positions %d + %d exceed the context of %d", m->g_pos,
+                                 n, m->cfg.seq_len);
+        TRY(pages_reserve_all(m, m->g_batch, m->g_pos + n));
+    }
+    m->g_pos += n > 0 ? n : 0;
     m->smp = m->g_smp; /* the last generation's pick: greedy or its top-p draw */
     m->smp_t = m->g_t;
     m->smp_p = m->g_p;

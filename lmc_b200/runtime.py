@@ -49,6 +49,9 @@ SIGNATURES = {
     "lmc_nccl_unique_id": ([_vp], _i),
     "lmc_model_load_tp": ([_c.c_char_p, _i, _i, _i, _i, _vp, _c.POINTER(_vp)], _i),
     "lmc_model_load_ex": ([_c.c_char_p, _i, _i, _i, _i, _i, _vp, _c.POINTER(_vp)], _i),
+    "lmc_model_load_paged": ([_c.c_char_p, _i, _i, _i, _i, _i, _i, _i, _vp, _c.POINTER(_vp)], _i),
+    "lmc_model_release_seq": ([_vp, _i], _i),
+    "lmc_model_kv_pages": ([_vp, _ip, _ip, _ip], _i),
     "lmc_model_prefill": ([_vp, _i, _ip, _i, _i, _vp, _ip], _i),
     "lmc_model_shard": ([_vp, _ip, _ip, _ip, _ip], _i),
     "lmc_model_get_config": ([_vp, _vp], _i),
@@ -167,11 +170,18 @@ class Model:
     """A GGUF model loaded onto the device (lmc_model_load), or one
     tensor-parallel shard of it when tp = (rank, size, nccl_id) is given
     (lmc_model_load_tp; every rank of the group constructs its shard).
-    max_rows > max_batch: rows per step for prefill() chunks (lmc_model_load_ex)."""
+    max_rows > max_batch: rows per step for prefill() chunks (lmc_model_load_ex).
+    page_size: a paged KV cache of n_pages pages (lmc_model_load_paged)."""
 
-    def __init__(self, path, max_batch=1, kv_dtype=KV_F32, tp=None, max_rows=None):
+    def __init__(self, path, max_batch=1, kv_dtype=KV_F32, tp=None, max_rows=None, page_size=0, n_pages=0):
         h = _vp()
-        if max_rows is not None and max_rows > max_batch:
+        if page_size:
+            rank, size, nid = tp if tp is not None else (0, 1, None)
+            idbuf = ctypes.create_string_buffer(bytes(nid), 128) if nid is not None else None
+            call("lmc_model_load_paged", path.encode(), max_batch, max(max_rows or 0, max_batch), kv_dtype,
+                 page_size, n_pages, rank, size, ctypes.cast(idbuf, _vp) if idbuf is not None else None,
+                 ctypes.byref(h))
+        elif max_rows is not None and max_rows > max_batch:
             rank, size, nid = tp if tp is not None else (0, 1, None)
             idbuf = ctypes.create_string_buffer(bytes(nid), 128) if nid is not None else None
             call("lmc_model_load_ex", path.encode(), max_batch, max_rows, kv_dtype, rank, size,
@@ -222,6 +232,16 @@ class Model:
         call("lmc_model_generate", self.h, prompt.ctypes.data_as(_ip), n_prompt, B, n_new, int(use_graph),
              out.ctypes.data_as(_ip))
         return out
+
+    def release_seq(self, seq):
+        """Give sequence `seq`'s KV pages back to the pool (lmc_model_release_seq)."""
+        call("lmc_model_release_seq", self.h, seq)
+
+    def kv_pages(self):
+        """(page_size, n_pages, n_free); page_size 0 for a contiguous cache."""
+        ps, n, f = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        call("lmc_model_kv_pages", self.h, ctypes.byref(ps), ctypes.byref(n), ctypes.byref(f))
+        return ps.value, n.value, f.value
 
     def replay(self, n):
         s = _vp()

@@ -156,6 +156,18 @@ def test_entry_points_validate_arguments_first():
          b"attention_paged"),
         ("lmc_attention_decode_paged", (p, p, p, p, p, p, 0, 0, p, 4, 64, p, 1, 32, 8, 128, p, 0, None),
          b"attention_paged"),
+        # paged model cache: page size 24 (not a power of two), 8 (below
+        # 16), no pages; checked before the file is opened
+        ("lmc_model_load_paged", (b"x.gguf", 1, 1, 0, 24, 4, 0, 1, None, ctypes.byref(ctypes.c_void_p())),
+         b"KV pages"),
+        ("lmc_model_load_paged", (b"x.gguf", 1, 1, 0, 8, 4, 0, 1, None, ctypes.byref(ctypes.c_void_p())),
+         b"KV pages"),
+        ("lmc_model_load_paged", (b"x.gguf", 1, 1, 0, 16, 0, 0, 1, None, ctypes.byref(ctypes.c_void_p())),
+         b"KV pages"),
+        ("lmc_model_load_paged", (b"x.gguf", 1, 1, 0, 0, 4, 0, 1, None, ctypes.byref(ctypes.c_void_p())),
+         b"page size"),
+        ("lmc_model_release_seq", (None, 0), b"release_seq"),
+        ("lmc_model_kv_pages", (None, None, None, None), b"kv_pages"),
         ("lmc_set_wait_limit", (ctypes.c_longlong(-5),), b"set_wait_limit"),
         ("lmc_wait_selftest", (7,), b"wait_selftest"),
         ("lmc_sample_top_p", (None, 10, 1, 1.0, 0.9, None, None, None), b"sample_top_p"),
