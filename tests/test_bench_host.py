@@ -34,3 +34,25 @@ def test_clock_sampler_without_nvml(monkeypatch):
         pass
     s = c.summary()
     assert s["samples"] == 0 and s["sm_mhz"] is None and s["reasons"] == []
+
+
+def test_gpt2_step_bytes_is_the_algorithmic_count():
+    """The roofline numerator: every GPT-2 Small weight once (per layer
+    q|k|v, attention output and fc as Q4_K, fc2 as Q6_K: 4,589,568 B; the
+    Q6_K lm_head: 31,661,910 B), the fp32 norms and biases, one embedding
+    row, and 73,728 B of fp32 K/V rows per cached position."""
+    D, F, L = 768, 3072, 12
+    vectors = L * 4 * (2 * D + 3 * D + D + F + D + 2 * D) + 4 * 2 * D  # ln1/ln2, biases; ln_f
+    embed_row = 3 * 210 + 4 * D  # three Q6_K blocks of wte, one fp32 row of wpe
+    assert bench.gpt2_step_bytes(0) == L * 4_589_568 + 31_661_910 + vectors + embed_row
+    assert bench.gpt2_step_bytes(101) - bench.gpt2_step_bytes(100) == 2 * L * D * 4 == 73_728
+
+
+def test_committed_step_traffic_is_one_read_of_the_algorithmic_bytes():
+    """The ncu DRAM bytes of the step kernel in profiles/ over the
+    algorithmic bytes at the capture's context: every byte read about once
+    (no re-reads, nothing skipped)."""
+    tr = bench.step_traffic("k_step")
+    assert tr is not None and "ctx" in tr
+    ratio = tr["bytes"] / bench.gpt2_step_bytes(tr["ctx"])
+    assert 1.0 <= ratio < 1.03, ratio
