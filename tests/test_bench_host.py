@@ -1,5 +1,8 @@
 """Host-side pieces of bench.py that need no GPU: the clock sampler against a
-stand-in NVML module (read-only queries; it sets nothing on any GPU)."""
+stand-in NVML module (read-only queries; it sets nothing on any GPU), the
+roofline's algorithmic byte counts and committed traffic, and the reference
+arm's JSON line."""
+import os
 import sys
 import time
 import types
@@ -56,3 +59,37 @@ def test_committed_step_traffic_is_one_read_of_the_algorithmic_bytes():
     assert tr is not None and "ctx" in tr
     ratio = tr["bytes"] / bench.gpt2_step_bytes(tr["ctx"])
     assert 1.0 <= ratio < 1.03, ratio
+
+
+def _run_bench(args, env_extra, tmp_path):
+    import json
+    import os
+    import subprocess
+    env = dict(os.environ, LMC_BENCH_CACHE=str(tmp_path), **env_extra)
+    r = subprocess.run([sys.executable, os.path.join(bench.ROOT, "bench.py")] + args, env=env, cwd=bench.ROOT,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    return [json.loads(ln) for ln in lines]
+
+
+def test_reference_arm_prints_the_contract_line(tmp_path):
+    """`bench.py --impl reference` times LMc's own model_forward (compiled
+    from its sources) on the host cores for the GPU arm's metric and
+    workload, and prints one JSON line with the reference arm's keys; under
+    torchrun the ranks other than 0 print nothing and exit 0."""
+    import pytest
+    from oracle import ref_library_path
+    if not os.path.exists(ref_library_path()):
+        pytest.skip("LMc reference build (oracle/_ref) not present")
+    (line,) = _run_bench(["--impl", "reference", "--steps", "8", "--warmup", "0"], {}, tmp_path)
+    assert line["impl"] == "reference"
+    assert line["metric"] == bench.METRIC and line["unit"] == bench.UNIT and line["higher_is_better"] is True
+    assert line["config"]["workload"] == bench.WORKLOAD
+    assert line["value"] > 0 and line["warmup"] >= 3 and line["n_gpus"] == 1
+    cb = line["cpu_baseline"]
+    assert cb["kind"] == "reference" and cb["cores"] >= 1 and cb["value"] == line["value"] and cb["sample"]
+    assert line["e2e"] == {"value": line["value"], "unit": bench.UNIT, "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+    assert _run_bench(["--impl", "reference", "--gpus", "2"], {"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"},
+                      tmp_path) == []
