@@ -1134,7 +1134,7 @@ extern "C" int lmc_step_prog_build(const lmc_step_op *ops, int n, lmc_step_prog 
                     ty != LMC_TYPE_F32)
                     s = 0;
                 d[i].e = EmbedArgs{(const uint8_t *)ops[i].wte, ops[i].wpe, ops[i].tok, ops[i].pos, ops[i].D,
-                                   ops[i].V, ops[i].S, (int)ty, ops[i].y};
+                                   ops[i].V, ops[i].S, (int)ty, ops[i].y, nullptr};
                 break;
             }
             case LMC_OP_SAMPLE:
