@@ -176,16 +176,17 @@ class Clocks:
 # ---------------------------------------------------------------------------
 # CPU side: LMc's own sources (oracle/_ref), timed on this host's cores
 # ---------------------------------------------------------------------------
-def cpu_reference(path, n_decode, reps=CPU_REPS):
+def cpu_reference(path, n_decode, reps=CPU_REPS, prompt=None):
     """Greedy decode with LMc's model_forward on all host threads: one
-    untimed warm-up run, then `reps` runs of the 8-token prompt and n_decode
-    decode tokens; returns the median decode and prompt-feed tokens/s."""
+    untimed warm-up run, then `reps` runs of the prompt (default: the
+    8-token GPT-2 prompt) and n_decode decode tokens; returns the median
+    decode and prompt-feed tokens/s."""
     from oracle import Ref
     ref = Ref()
     threads = os.cpu_count() or 1
     ref.set_threads(threads)
     ref.load(path)
-    p = prompt_ids()
+    p = prompt_ids() if prompt is None else np.ascontiguousarray(prompt, np.int32)
     ref.generate(p, 2)
     dec, feed = [], []
     for _ in range(reps):
@@ -193,7 +194,7 @@ def cpu_reference(path, n_decode, reps=CPU_REPS):
         dec.append(n_decode / td)
         feed.append(len(p) / tp)
     sample = (f"LMc model_forward (oracle/_ref, make-omp flags, {os.path.basename(ref.path)}), "
-              f"{N_PROMPT}-token prompt then {n_decode} greedy decode tokens, median of {reps} runs after a warm-up, "
+              f"{len(p)}-token prompt then {n_decode} greedy decode tokens, median of {reps} runs after a warm-up, "
               f"wall clock; prompt fed token by token (timed apart)")
     return float(np.median(dec)), float(np.median(feed)), threads, sample
 
@@ -505,6 +506,14 @@ def model_decode(args, rank, world, local_rank, dist):
             ps, npg, _ = m.kv_pages()
             res.update({"kv_page": ps, "kv_pages": npg})
     m.close()
+    if res is not None and world == 1 and (args.workload == "tinyllama" or os.environ.get("LMC_BENCH_CPU_8B") == "1"):
+        # LMc's model_forward on the same file, one sequence (it cannot
+        # batch), a bounded sample: the first 8 prompt ids of sequence 0,
+        # then 8 greedy tokens.  Its fp32 arena takes 4 bytes a weight of
+        # host memory (32 GB for the 8B shape: opt in with LMC_BENCH_CPU_8B=1).
+        rate, feed, threads, sample = cpu_reference(path, 8, reps=3, prompt=prompts[0][:N_PROMPT])
+        res["cpu_baseline"] = {"value": round(rate, 3), "unit": UNIT, "cores": threads, "kind": "reference",
+                               "sample": sample, "prompt_feed_tok_s": round(feed, 3)}
     return res if rank == 0 else None
 
 

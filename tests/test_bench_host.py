@@ -93,3 +93,17 @@ def test_reference_arm_prints_the_contract_line(tmp_path):
                            "d2h_bytes_per_step": 0}
     assert _run_bench(["--impl", "reference", "--gpus", "2"], {"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"},
                       tmp_path) == []
+
+
+def test_cpu_reference_times_a_llama_prompt(tmp_path):
+    """The model workloads' CPU baseline: LMc's model_forward on a LLaMA
+    file with the caller's prompt ids (not the GPT-2 prompt)."""
+    import pytest
+    from oracle import ref_library_path
+    from lmc_b200 import synth
+    if not os.path.exists(ref_library_path()):
+        pytest.skip("LMc reference build (oracle/_ref) not present")
+    path = synth.cached_model("llama", str(tmp_path), L=1, D=96, H=6, Hkv=3, F=192, S=16, V=64, seed=1)
+    rate, feed, threads, sample = bench.cpu_reference(path, 2, reps=1, prompt=[1, 2, 63])
+    assert rate > 0 and feed > 0 and threads >= 1
+    assert "3-token prompt then 2 greedy decode tokens" in sample
