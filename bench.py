@@ -199,20 +199,26 @@ def cpu_reference(path, n_decode, reps=CPU_REPS, prompt=None):
     return float(np.median(dec)), float(np.median(feed)), threads, sample
 
 
-def cpu_matmul_c1(reps=200):
-    """LMc's matmul_vec on the dequantized C1 weights (Q4_K 3072x768, the
-    same seeded blocks as the GPU measurement), all host threads: seconds per
+def cpu_matmul(t, M, K, reps=20, seed=0):
+    """LMc's matmul_vec on the dequantized weights of a `t` matrix M x K (the
+    same seeded blocks as the GPU measurement; LMc dequantizes at load, so
+    its per-token work is the fp32 product), all host threads: seconds per
     call (median of 5 timings of `reps` calls)."""
     from lmc_b200 import synth
     from oracle import Ref
     ref = Ref()
     ref.set_threads(os.cpu_count() or 1)
-    M, K = 3072, 768
-    blk = synth.random_blocks(synth.Q4_K, M * K, seed=0)
-    w = ref.dequant(synth.Q4_K, blk, M * K).reshape(M, K)
+    blk = synth.random_blocks(t, M * K, seed=seed)
+    w = ref.dequant(t, blk, M * K).reshape(M, K)
     x = np.random.default_rng(0).normal(0, 1, K).astype(np.float32)
-    ref.time_matmul(w, x, 20)
+    ref.time_matmul(w, x, max(reps // 10, 2))
     return float(np.median([ref.time_matmul(w, x, reps) / reps for _ in range(5)]))
+
+
+def cpu_matmul_c1(reps=200):
+    """cpu_matmul on the C1 weights (Q4_K 3072x768, seed 0)."""
+    from lmc_b200 import synth
+    return cpu_matmul(synth.Q4_K, 3072, 768, reps)
 
 
 def run_reference(args, rank, world):
@@ -399,17 +405,26 @@ def run_gemv(args):
                     cases.append((tn, shp, b))
     else:
         cases.append((args.type, f"{args.rows}x{args.cols}", args.batch))
+    from oracle import ref_library_path
+    have_ref = os.path.exists(ref_library_path())
+    ref_s = {}  # LMc's seconds per matmul_vec call, per (type, shape)
     for tn, shp, b in cases:
         t = names[tn]
         rows, cols = (int(v) for v in shp.split("x"))
         r = mb.run(torch, t, rows, cols, b, iters=max(args.steps, 20), seed=0)
         fl = 2.0 * rows * cols * b / (r["ms"] * 1e-3) / 1e12
-        print(json.dumps({"metric": "GEMV/GEMM throughput", "workload": "gemv", "type": tn, "rows": rows,
-                          "cols": cols, "batch": b, "kernel": r["kernel"],
-                          "us": round(r["ms"] * 1e3, 3), "gbs": round(r["gbs"], 1),
-                          "hbm_frac": round(r["gbs"] / peak, 4), "tflops": round(fl, 2),
-                          "algorithmic_bytes": r["bytes"], "peak_kind": kind,
-                          "l2": "rotated weight copies > 2x L2, graph of back-to-back launches"}), flush=True)
+        line = {"metric": "GEMV/GEMM throughput", "workload": "gemv", "type": tn, "rows": rows,
+                "cols": cols, "batch": b, "kernel": r["kernel"],
+                "us": round(r["ms"] * 1e3, 3), "gbs": round(r["gbs"], 1),
+                "hbm_frac": round(r["gbs"] / peak, 4), "tflops": round(fl, 2),
+                "algorithmic_bytes": r["bytes"], "peak_kind": kind,
+                "l2": "rotated weight copies > 2x L2, graph of back-to-back launches"}
+        if have_ref:  # LMc has no batched product: batch b is b matmul_vec calls
+            if (t, shp) not in ref_s:
+                ref_s[(t, shp)] = cpu_matmul(t, rows, cols)
+            line["reference_matmul_vec_us"] = round(ref_s[(t, shp)] * b * 1e6, 2)
+            line["reference"] = f"LMc matmul_vec (oracle/_ref), {os.cpu_count() or 1} host threads, b calls"
+        print(json.dumps(line), flush=True)
 
 
 def run_model(args, rank, world, local_rank, dist):

@@ -107,3 +107,17 @@ def test_cpu_reference_times_a_llama_prompt(tmp_path):
     rate, feed, threads, sample = bench.cpu_reference(path, 2, reps=1, prompt=[1, 2, 63])
     assert rate > 0 and feed > 0 and threads >= 1
     assert "3-token prompt then 2 greedy decode tokens" in sample
+
+
+def test_cpu_matmul_times_every_sweep_format():
+    """The gemv / sweep lines' LMc column: matmul_vec on the dequantized
+    weights of any format, including rows that start inside a block."""
+    import pytest
+    from oracle import ref_library_path
+    from lmc_b200 import synth
+    if not os.path.exists(ref_library_path()):
+        pytest.skip("LMc reference build (oracle/_ref) not present")
+    names = {v: k for k, v in synth.NAMES.items()}
+    for tn in bench.SWEEP_TYPES:
+        s = bench.cpu_matmul(names[tn], 64, 1600, reps=4)  # K = 1600: blocks straddle rows
+        assert 0 < s < 1.0, (tn, s)
