@@ -147,13 +147,18 @@ static void skip(Rd *r, uint32_t t) {
 
 typedef struct { char name[96]; uint32_t type; uint64_t dims[4]; uint32_t nd; uint64_t n, off; } TInfo;
 
+/* The tensor's bytes do not lie inside the fsz bytes of tensor data (the
+ * offset comes from the file: compared without forming off + bytes, which
+ * a crafted offset could wrap around). */
+static int past_end(const TInfo *t, size_t bytes, size_t fsz) { return t->off > fsz || bytes > fsz - t->off; }
+
 /* ------------------------------------------------------------------------ */
 static int upload_vec(const TInfo *t, const unsigned char *data, size_t fsz, int want, float **out) {
     size_t bytes;
     TRY(lmc_tensor_bytes(t->type, (size_t)t->n, &bytes));
     if ((int64_t)t->n != want) return lmc_set_error(LMC_ERR_IO, "tensor %s: %llu elements, expected %d", t->name,
                                                     (unsigned long long)t->n, want);
-    if (t->off + bytes > fsz) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
+    if (past_end(t, bytes, fsz)) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
     CUTRY(cudaMalloc((void **)out, sizeof(float) * (size_t)want + 16));
     if (t->type == LMC_TYPE_F32) {
         CUTRY(cudaMemcpy(*out, data + t->off, bytes, cudaMemcpyHostToDevice));
@@ -174,7 +179,7 @@ static int upload_mat(const TInfo *t, const unsigned char *data, size_t fsz, int
     TRY(lmc_tensor_bytes(t->type, (size_t)t->n, &bytes));
     if ((int64_t)t->n != (int64_t)rows * cols || (t->nd >= 2 && (t->dims[0] != (uint64_t)cols || t->dims[1] != (uint64_t)rows)))
         return lmc_set_error(LMC_ERR_IO, "tensor %s: shape mismatch (expected %d x %d)", t->name, rows, cols);
-    if (t->off + bytes > fsz) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
+    if (past_end(t, bytes, fsz)) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
     return lmc_qtensor_upload(t->type, rows, cols, data + t->off, bytes, out);
 }
 
@@ -185,7 +190,7 @@ static int upload_rows(const TInfo *t, const unsigned char *data, size_t fsz, in
     TRY(lmc_tensor_bytes(t->type, (size_t)t->n, &bytes));
     if ((int64_t)t->n != (int64_t)rows * cols || (t->nd >= 2 && (t->dims[0] != (uint64_t)cols || t->dims[1] != (uint64_t)rows)))
         return lmc_set_error(LMC_ERR_IO, "tensor %s: shape mismatch (expected %d x %d)", t->name, rows, cols);
-    if (t->off + bytes > fsz) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
+    if (past_end(t, bytes, fsz)) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
     if (lmc_tensor_bytes(t->type, (size_t)cols, &rb))
         return lmc_set_error(LMC_ERR_UNSUPPORTED, "tensor %s: rows share blocks, cannot shard by rows", t->name);
     return lmc_qtensor_upload(t->type, nr, cols, data + t->off + (size_t)r0 * rb, (size_t)nr * rb, out);
@@ -198,7 +203,7 @@ static int upload_cols(const TInfo *t, const unsigned char *data, size_t fsz, in
     TRY(lmc_tensor_bytes(t->type, (size_t)t->n, &bytes));
     if ((int64_t)t->n != (int64_t)rows * cols || (t->nd >= 2 && (t->dims[0] != (uint64_t)cols || t->dims[1] != (uint64_t)rows)))
         return lmc_set_error(LMC_ERR_IO, "tensor %s: shape mismatch (expected %d x %d)", t->name, rows, cols);
-    if (t->off + bytes > fsz) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
+    if (past_end(t, bytes, fsz)) return lmc_set_error(LMC_ERR_IO, "tensor %s: data past end of file", t->name);
     if (lmc_tensor_bytes(t->type, (size_t)cols, &rb) || lmc_tensor_bytes(t->type, (size_t)c0, &cb0) ||
         lmc_tensor_bytes(t->type, (size_t)nc, &cbn))
         return lmc_set_error(LMC_ERR_UNSUPPORTED, "tensor %s: column shard [%d, %d) is not block-aligned", t->name, c0,
@@ -448,6 +453,7 @@ static int load(lmc_model *m, const char *path) {
     if (r.err) { rc = lmc_set_error(LMC_ERR_IO, "%s: truncated tensor table", path); goto done; }
     {
         size_t data = ((size_t)(r.p - buf) + 31) / 32 * 32; /* src/gguf.c:285-287 */
+        if (data > (size_t)fsz) { rc = lmc_set_error(LMC_ERR_IO, "%s: no tensor data after the header", path); goto done; }
         for (uint64_t i = 0; i < nt && !rc; i++) rc = bind_tensor(m, &ti[i], buf + data, (size_t)fsz - data);
     }
     if (!rc) rc = check_complete(m);

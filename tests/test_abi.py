@@ -75,6 +75,27 @@ def _load_status(path, tp_rank=0, tp_size=1):
     return rc, rt.lib().lmc_last_error()
 
 
+def _table_end(raw):
+    """(end of the tensor table, position of the first tensor's offset field)
+    in a GGUF v3 file with u32 / f32 / string metadata (what synth writes)."""
+    import struct
+    n_t, n_kv = struct.unpack_from("<QQ", raw, 8)
+    p = 24
+    for _ in range(n_kv):
+        p += 8 + struct.unpack_from("<Q", raw, p)[0]  # key
+        typ = struct.unpack_from("<I", raw, p)[0]
+        p += 4
+        p += 8 + struct.unpack_from("<Q", raw, p)[0] if typ == 8 else 4
+    first_off = None
+    for _ in range(n_t):
+        p += 8 + struct.unpack_from("<Q", raw, p)[0]  # name
+        nd = struct.unpack_from("<I", raw, p)[0]
+        p += 4 + 8 * nd + 4
+        first_off = p if first_off is None else first_off
+        p += 8
+    return p, first_off
+
+
 def test_model_load_rejects_malformed_gguf(tmp_path):
     """Malformed GGUF headers are reported as status codes with a message
     (the header is parsed before anything is uploaded, so no GPU is needed):
@@ -100,6 +121,15 @@ def test_model_load_rejects_malformed_gguf(tmp_path):
     hdr_end = raw.index(b"token_embd.weight") + 8
     rc, msg = case("table.gguf", raw[:hdr_end])
     assert rc == -5 and b"truncated tensor table" in msg
+    # a crafted tensor offset (2^64 - 16: offset + size wraps around) and a
+    # file that ends at its tensor table (the aligned data start lies past
+    # the end): refused before anything is read or uploaded
+    end, first_off = _table_end(raw)
+    rc, msg = case("offset.gguf", raw[:first_off] + struct.pack("<Q", 2 ** 64 - 16) + raw[first_off + 8:])
+    assert rc == -5 and b"data past end of file" in msg
+    assert end % 32, "the header must not end on the data alignment for this case"
+    rc, msg = case("nodata.gguf", raw[:end])
+    assert rc == -5 and b"no tensor data after the header" in msg
     p = synth.write_gguf(str(tmp_path / "nokeys.gguf"), "llama", {"llama.block_count": 1}, {}, [])
     rc, msg = _load_status(p)
     assert rc == -5 and b"missing L/H/D metadata" in msg
