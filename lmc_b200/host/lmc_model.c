@@ -132,18 +132,24 @@ static const char *str(Rd *r, uint64_t *n) {
     return s;
 }
 static int is(const char *s, uint64_t n, const char *lit) { return strlen(lit) == n && !memcmp(s, lit, n); }
-static void skip(Rd *r, uint32_t t) {
+/* Skips one metadata value of type t.  Arrays may nest (arrays of arrays);
+ * a file nesting them deeper than any real one does is refused instead of
+ * recursing without bound. */
+#define GGUF_MAX_NESTING 16
+static void skip_at(Rd *r, uint32_t t, int depth) {
     static const int sz[13] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
     if (t == 8) { uint64_t n; str(r, &n); return; }
     if (t == 9) {
+        if (depth >= GGUF_MAX_NESTING) { r->err = 1; return; }
         uint32_t et = u32(r);
         uint64_t c = u64(r);
-        for (uint64_t i = 0; i < c && !r->err; i++) skip(r, et);
+        for (uint64_t i = 0; i < c && !r->err; i++) skip_at(r, et, depth + 1);
         return;
     }
     if (t > 12) { r->err = 1; return; }
     if (need(r, (size_t)sz[t])) r->p += sz[t];
 }
+static void skip(Rd *r, uint32_t t) { skip_at(r, t, 0); }
 
 typedef struct { char name[96]; uint32_t type; uint64_t dims[4]; uint32_t nd; uint64_t n, off; } TInfo;
 
@@ -414,6 +420,20 @@ static int load(lmc_model *m, const char *path) {
         if (c->arch == 2 && vn > 0 && vn < c->vocab_size) c->vocab_size = vn;
     }
     if (!c->n_layers || !c->n_heads || !c->embed_dim) { rc = lmc_set_error(LMC_ERR_IO, "%s: missing L/H/D metadata", path); goto done; }
+    {   /* the values are u32 in the file: none may be negative as an int or
+         * so large that products of them overflow before any allocation */
+        const int64_t lim = 1 << 24, f = c->ffn_dim ? c->ffn_dim : 4 * (int64_t)c->embed_dim;
+        const int64_t dims[7] = {c->n_layers, c->n_heads, c->n_kv_heads, c->embed_dim, f, c->seq_len,
+                                 c->vocab_size};
+        for (int i = 0; i < 7; i++)
+            if (dims[i] <= 0 || dims[i] > lim) {
+                rc = lmc_set_error(LMC_ERR_IO, "%s: model dimension %lld outside [1, %lld] (L, H, Hkv, D, F, S, V = "
+                                   "%d, %d, %d, %d, %lld, %d, %d)", path, (long long)dims[i], (long long)lim,
+                                   c->n_layers, c->n_heads, c->n_kv_heads, c->embed_dim, (long long)f, c->seq_len,
+                                   c->vocab_size);
+                goto done;
+            }
+    }
     if (!c->ffn_dim) c->ffn_dim = 4 * c->embed_dim;
     c->head_dim = c->embed_dim / c->n_heads;
     if (c->n_heads % c->n_kv_heads) { rc = lmc_set_error(LMC_ERR_IO, "%s: heads %d not a multiple of kv heads %d", path, c->n_heads, c->n_kv_heads); goto done; }

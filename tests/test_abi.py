@@ -96,6 +96,50 @@ def _table_end(raw):
     return p, first_off
 
 
+def _gguf_kv(key, typ, payload):
+    import struct
+    k = key.encode()
+    return struct.pack("<Q", len(k)) + k + struct.pack("<I", typ) + payload
+
+
+def _gguf(kvs):
+    """A GGUF v3 file with no tensors and the given encoded metadata pairs."""
+    import struct
+    return struct.pack("<IIQQ", 0x46554747, 3, 0, len(kvs)) + b"".join(kvs)
+
+
+def crafted_gguf_cases():
+    """(name, bytes, status, message) of metadata a crafted file can hold:
+    arrays nested 200000 deep (a reader that recurses per level runs out of
+    stack) and dimensions that are negative as ints (2^31 / -1 traps)."""
+    import struct
+    deep = struct.pack("<IQ", 9, 1) * 200000 + struct.pack("<IQ", 4, 0)
+    u32 = lambda v: struct.pack("<I", v)
+    arch = _gguf_kv("general.architecture", 8, struct.pack("<Q", 5) + b"llama")
+    return [
+        ("nested.gguf", _gguf([_gguf_kv("x.nested", 9, deep)]), -5, b"truncated metadata"),
+        ("negdim.gguf", _gguf([arch, _gguf_kv("llama.block_count", 4, u32(1)),
+                               _gguf_kv("llama.embedding_length", 4, u32(2 ** 31)),
+                               _gguf_kv("llama.attention.head_count", 4, u32(2 ** 32 - 1))]),
+         -5, b"model dimension"),
+        ("hugedim.gguf", _gguf([arch, _gguf_kv("llama.block_count", 4, u32(1)),
+                                _gguf_kv("llama.embedding_length", 4, u32(1 << 30)),
+                                _gguf_kv("llama.attention.head_count", 4, u32(4))]),
+         -5, b"model dimension"),
+    ]
+
+
+def test_model_load_rejects_crafted_metadata(tmp_path):
+    """Metadata no real file has is refused with a status code, not a
+    crash: arrays nested beyond any real file, dimensions that are negative
+    or absurdly large as the reader's ints."""
+    for name, data, code, word in crafted_gguf_cases():
+        p = tmp_path / name
+        p.write_bytes(data)
+        rc, msg = _load_status(p)
+        assert rc == code and word in msg, (name, rc, msg)
+
+
 def test_model_load_rejects_malformed_gguf(tmp_path):
     """Malformed GGUF headers are reported as status codes with a message
     (the header is parsed before anything is uploaded, so no GPU is needed):

@@ -4,7 +4,8 @@ tests/host_model_sanitize.c, linked with an instrumented build of
 lmc_model.c and the library's CUDA objects, loads well-formed GGUF files
 (the load stops at the first device allocation and must release
 everything it took) and malformed ones (bad magic, truncated metadata or
-tensor table, a wrapped tensor offset, no tensor data, a missing file),
+tensor table, a wrapped tensor offset, no tensor data, arrays nested past
+any real file, dimensions negative as ints, a missing file),
 contiguous and paged; every call must end in a status code with no
 out-of-bounds access, leak or undefined operation."""
 import os
@@ -32,7 +33,7 @@ def test_host_runtime_is_clean_under_asan_and_ubsan(tmp_path):
     objs = [o for o in objs if o.endswith(".o") and not os.path.basename(o).startswith("host_")]
     if not objs:
         pytest.skip("library objects not built (make -C lmc_b200)")
-    from tests.test_abi import _table_end
+    from tests.test_abi import _table_end, crafted_gguf_cases
     d = str(tmp_path)
     m_o, drv_o, exe = (os.path.join(d, n) for n in ("lmc_model.o", "drv.o", "drv"))
     cuda = "/usr/local/cuda"
@@ -49,6 +50,7 @@ def test_host_runtime_is_clean_under_asan_and_ubsan(tmp_path):
     bad = {"magic": b"GGUX" + raw[4:], "meta": raw[:60], "table": raw[:end - 3], "nodata": raw[:end],
            "offset": raw[:first_off] + struct.pack("<Q", 2 ** 64 - 16) + raw[first_off + 8:],
            "cut": raw[:len(raw) // 2]}
+    bad.update({name[:-5]: data for name, data, _, _ in crafted_gguf_cases()})
     paths = list(good)
     for k, v in bad.items():
         p = os.path.join(d, k + ".gguf")
@@ -64,5 +66,5 @@ def test_host_runtime_is_clean_under_asan_and_ubsan(tmp_path):
     assert all(c < 0 for c in codes[:-1]) and codes[-1] == 0  # no device here: every load fails, cleanly
     out = r.stdout
     for word in (b"not a GGUF", b"truncated metadata", b"truncated tensor table", b"no tensor data",
-                 b"data past end of file", b"cannot open"):
+                 b"data past end of file", b"cannot open", b"model dimension"):
         assert word.decode() in out, word
