@@ -7,6 +7,7 @@
  * and their init functions) and liblmc_b200.so.  Every op runs on the device;
  * a failing call ends the process through LMC_FATAL as LMc's errors do.
  */
+#include <limits.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -131,23 +132,33 @@ static uint64_t rd(Hdr *h, int bytes) {
     return v;
 }
 static uint64_t rd_len(Hdr *h) { return rd(h, h->v1 ? 4 : 8); }
+/* Forward only: a length from the file beyond what a long holds would turn
+ * into a backward seek (and the header would be read again, without end). */
 static void skip_bytes(Hdr *h, uint64_t n) {
-    if (fseek(h->f, (long)n, SEEK_CUR)) h->bad = 1;
+    if (n > (uint64_t)LONG_MAX || fseek(h->f, (long)n, SEEK_CUR)) h->bad = 1;
 }
-static void skip_value(Hdr *h, uint32_t type) {
+/* Arrays of arrays deeper than any real file are refused instead of
+ * recursing without bound. */
+#define GGUF_MAX_NESTING 16
+static void skip_value_at(Hdr *h, uint32_t type, int depth) {
     static const int size[13] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
     if (type == 8) {
         skip_bytes(h, rd_len(h));
     } else if (type == 9) {
+        if (depth >= GGUF_MAX_NESTING) {
+            h->bad = 1;
+            return;
+        }
         const uint32_t et = (uint32_t)rd(h, 4);
         const uint64_t n = rd_len(h);
-        for (uint64_t i = 0; i < n && !h->bad; i++) skip_value(h, et);
+        for (uint64_t i = 0; i < n && !h->bad; i++) skip_value_at(h, et, depth + 1);
     } else if (type < 13) {
         skip_bytes(h, (uint64_t)size[type]);
     } else {
         h->bad = 1;
     }
 }
+static void skip_value(Hdr *h, uint32_t type) { skip_value_at(h, type, 0); }
 static void read_llama_vocab(const char *path) {
     Hdr h = {fopen(path, "rb"), 0, 0};
     if (!h.f) return;
