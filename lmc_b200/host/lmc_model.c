@@ -1271,7 +1271,7 @@ static int prefill_chunks(lmc_model *m, int seq, const int *h_tokens, int n, int
 
 int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int start_pos, float *h_logits, int *h_next) {
     if (!m || !h_tokens || n <= 0 || seq < 0 || seq >= m->max_batch || start_pos < 0 ||
-        start_pos + n > m->cfg.seq_len)
+        start_pos > m->cfg.seq_len || n > m->cfg.seq_len - start_pos) /* (no int overflow) */
         return lmc_set_error(LMC_ERR_INVALID, "model_prefill: sequence %d (of %d), positions %d + %d (context %d)", seq,
                              m ? m->max_batch : 0, start_pos, n, m ? m->cfg.seq_len : 0);
     for (int i = 0; i < n; i++)
@@ -1354,7 +1354,7 @@ static int generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, int 
                     int *h_out_ids) {
     if (!m || !h_prompt || n_prompt <= 0 || n_new <= 0 || B <= 0 || B > m->max_batch || !h_out_ids)
         return lmc_set_error(LMC_ERR_INVALID, "model_generate: args");
-    if (n_prompt + n_new - 1 > m->cfg.seq_len)
+    if (n_prompt > m->cfg.seq_len || n_new - 1 > m->cfg.seq_len - n_prompt) /* (no int overflow) */
         return lmc_set_error(LMC_ERR_INVALID, "model_generate: %d + %d tokens exceed the context of %d", n_prompt,
                              n_new, m->cfg.seq_len);
     for (int i = 0; i < B * n_prompt; i++)
@@ -1452,7 +1452,7 @@ static int generate(lmc_model *m, const int *h_prompt, int n_prompt, int B, int 
 int lmc_model_replay(lmc_model *m, int n, void *stream_out) {
     if (!m || !m->g_batch) return lmc_set_error(LMC_ERR_INVALID, "model_replay: no generation to continue");
     if (m->page_size) { /* pages for the positions these steps write */
-        if (n < 0 || m->g_pos + n > m->cfg.seq_len)
+        if (n < 0 || n > m->cfg.seq_len - m->g_pos)
             return lmc_set_error(LMC_ERR_INVALID, "model_replay: positions %d + %d exceed the context of %d", m->g_pos,
                                  n, m->cfg.seq_len);
         TRY(pages_reserve_all(m, m->g_batch, m->g_pos + n));
