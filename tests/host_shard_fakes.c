@@ -36,6 +36,11 @@ int lmc_model_load(const char *path, int max_batch, int kv_dtype, lmc_model **ou
 int lmc_model_load_tp(const char *path, int max_batch, int kv_dtype, int tp_rank, int tp_size, const void *id,
                       lmc_model **out);
 int lmc_model_free(lmc_model *m);
+int lmc_model_load_paged(const char *path, int max_batch, int max_rows, int kv_dtype, int page_size, int n_pages,
+                         int tp_rank, int tp_size, const void *id, lmc_model **out);
+int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int batch, float *h_logits, int *h_next);
+int lmc_model_release_seq(lmc_model *m, int seq);
+int lmc_model_kv_pages(const lmc_model *m, int *page_size, int *n_pages, int *n_free);
 
 static char g_err[512];
 int lmc_set_error(int code, const char *fmt, ...) {
@@ -162,6 +167,41 @@ const char *ncclGetErrorString(int r) { (void)r; return "host stand-in"; }
 int ncclGetUniqueId(fake_nccl_id *id) { memset(id, 0, sizeof *id); return 0; }
 FAIL(ncclAllGather) FAIL(ncclAllReduce)
 
+/* The paged cache's page accounting (argv[3] == "paged"): a model with 2
+ * sequences and a pool of 6 pages of 16 positions; each forward takes its
+ * pages and then stops at its first kernel launch (there is no device
+ * here), so the pool's count shows what it took.  One line per step:
+ * "P <rc> <free pages>". */
+static void paged_step(lmc_model *m, int rc) {
+    int ps = 0, np = 0, nf = -1;
+    lmc_model_kv_pages(m, &ps, &np, &nf);
+    printf("P %d %d\n", rc, nf);
+}
+static int paged_scenario(const char *path) {
+    lmc_model *m = NULL;
+    int rc = lmc_model_load_paged(path, 2, 2, LMC_KV_F16, 16, 6, 0, 1, NULL, &m);
+    printf("rc %d %s\n", rc, rc ? lmc_last_error() : "");
+    if (rc) return 0;
+    const int tok[2] = {1, 2};
+    int pos[2] = {0, 0};
+    paged_step(m, lmc_model_forward(m, tok, pos, 2, NULL, NULL)); /* one page each: 4 free */
+    pos[0] = 39;
+    paged_step(m, lmc_model_forward(m, tok, pos, 1, NULL, NULL)); /* sequence 0 up to 3 pages: 2 free */
+    paged_step(m, lmc_model_release_seq(m, 0));                   /* 5 free */
+    pos[0] = 0;
+    pos[1] = 47;
+    paged_step(m, lmc_model_forward(m, tok, pos, 2, NULL, NULL)); /* 1 + 2 more: 2 free */
+    pos[0] = 40;
+    pos[1] = 63;
+    paged_step(m, lmc_model_forward(m, tok, pos, 2, NULL, NULL)); /* 2 + 1 wanted, 2 free: refused */
+    pos[0] = 31;
+    paged_step(m, lmc_model_forward(m, tok, pos, 1, NULL, NULL)); /* 1 more: 1 free */
+    paged_step(m, lmc_model_release_seq(m, 1));                   /* 4 free */
+    paged_step(m, lmc_model_release_seq(m, 2));                   /* no such sequence */
+    lmc_model_free(m);
+    return 0;
+}
+
 /* Loads argv[1] as shard r of argv[2] ranks for every r, one "R r rc" line
  * each before its uploads' lines. */
 int main(int argc, char **argv) {
@@ -172,6 +212,7 @@ int main(int argc, char **argv) {
         fprintf(stderr, "struct lmc_qtensor changed: update the copy in host_shard_fakes.c\n");
         return 3;
     }
+    if (argc > 3 && !strcmp(argv[3], "paged")) return paged_scenario(argv[1]);
     const int n = atoi(argv[2]);
     char id[128] = {0};
     for (int r = 0; r < n; r++) {

@@ -5,7 +5,9 @@ For 1, 2, 4 and 8 ranks, every rank's uploads must be exactly the bytes cut
 here from the GGUF file by the tensor-parallel layout: q/k/v rows by heads,
 gate/up rows and ffn_down columns by ffn rows, attn_output columns by heads,
 lm_head rows by ceil(V/N), the embedding whole; and the ranks' shards of each
-tensor must put the whole tensor back together."""
+tensor must put the whole tensor back together.  Built again under ASan and
+UBSan, whole loads and frees must be clean, and the paged cache's page pool
+must count as forward calls take pages and sequences give them back."""
 import os
 import struct
 import subprocess
@@ -95,11 +97,12 @@ def expected(raw, cfg, rank, n):
     return out
 
 
-@pytest.fixture(scope="module")
-def loader(tmp_path_factory):
+SAN = ["-fsanitize=address,undefined", "-fno-sanitize-recover=all", "-fno-omit-frame-pointer"]
+
+
+def build_loader(d, extra=()):
     if not os.path.isdir(CUDA_INC):
         pytest.skip("CUDA headers not present")
-    d = tmp_path_factory.mktemp("shards")
     layout = d / "layout.c"
     layout.write_text('#include <stddef.h>\n#include "%s"\n'
                       "const size_t qt_layout[5] = {offsetof(struct lmc_qtensor, rows), "
@@ -107,10 +110,29 @@ def loader(tmp_path_factory):
                       "offsetof(struct lmc_qtensor, gemm_wscale), sizeof(struct lmc_qtensor)};\n"
                       % os.path.join(ROOT, "lmc_b200", "csrc", "lmc_internal.h"))
     exe = str(d / "loader")
-    subprocess.check_call(["gcc", "-std=gnu99", "-O1", "-w", "-I" + CUDA_INC, "-o", exe,
+    subprocess.check_call(["gcc", "-std=gnu99", "-O1", "-g", "-w", "-I" + CUDA_INC] + list(extra) + ["-o", exe,
                            os.path.join(ROOT, "lmc_b200", "host", "lmc_model.c"),
                            os.path.join(HERE, "host_shard_fakes.c"), str(layout), "-lm"])
     return exe
+
+
+@pytest.fixture(scope="module")
+def loader(tmp_path_factory):
+    return build_loader(tmp_path_factory.mktemp("shards"))
+
+
+@pytest.fixture(scope="module")
+def loader_san(tmp_path_factory):
+    """The same loader under AddressSanitizer (leaks included) and
+    UndefinedBehaviorSanitizer."""
+    return build_loader(tmp_path_factory.mktemp("shards_san"), SAN)
+
+
+def run(exe, args, **env):
+    e = dict(os.environ, LMC_TP_PEER="0", ASAN_OPTIONS="detect_leaks=1", UBSAN_OPTIONS="print_stacktrace=1", **env)
+    r = subprocess.run([exe] + args, capture_output=True, text=True, env=e, timeout=300)
+    assert r.returncode == 0, (r.stdout[-1000:] + r.stderr[-3000:])
+    return r.stdout
 
 
 @pytest.mark.parametrize("n", [1, 2, 4, 8])
@@ -160,3 +182,26 @@ def test_shard_loader_uploads_the_tensor_parallel_layout(loader, tmp_path, n):
         else:  # column shards
             back = np.concatenate([np.frombuffer(p[2], np.uint8).reshape(rows, -1) for p in parts], axis=1)
             assert back.tobytes() == whole.tobytes(), name
+
+
+def test_whole_load_and_free_are_clean_under_asan(loader_san, tmp_path):
+    """Every host allocation of a load (tables, staging, the fused
+    q|k|v and gate|up tensors, the RoPE table, the tensor-parallel geometry)
+    released by lmc_model_free, nothing read or written out of bounds."""
+    gp = synth.make_gpt2(str(tmp_path / "g.gguf"), L=2, D=256, H=4, S=32, V=100, seed=1)
+    lp = synth.make_llama(str(tmp_path / "l.gguf"), L=2, D=512, H=8, Hkv=4, F=512, S=32, V=64, seed=1)
+    for path, n in ((gp, 1), (lp, 1), (lp, 2)):
+        out = run(loader_san, [path, str(n)])
+        assert out.count("rc 0") == n, out[-500:]
+
+
+def test_paged_cache_page_accounting(loader_san, tmp_path):
+    """The paged cache's pool as forward calls take pages and sequences give
+    them back (each forward stops at its first kernel launch, after taking its
+    pages): all-or-nothing refusal when the pool is short, release returns
+    every page, a bad sequence is refused; clean under the sanitizers."""
+    path = synth.make_llama(str(tmp_path / "p.gguf"), L=1, D=64, H=4, Hkv=2, F=128, S=64, V=64, seed=1)
+    out = run(loader_san, [path, "1", "paged"])
+    steps = [tuple(int(v) for v in ln.split()[1:]) for ln in out.splitlines() if ln.startswith("P ")]
+    launch, ok, oom, invalid = -2, 0, -4, -1
+    assert steps == [(launch, 4), (launch, 2), (ok, 5), (launch, 2), (oom, 2), (launch, 1), (ok, 4), (invalid, 4)]
