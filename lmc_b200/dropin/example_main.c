@@ -10,6 +10,8 @@
  *
  *   example_main MODEL.gguf gen N ID [ID ...]   prints "ids n id id ..."
  *   example_main MODEL.gguf ops                 prints "name n v v ..." lines
+ *   example_main format PATH [PATH ...]         prints "format f PATH" per path
+ *                                               (detect_format; no model)
  */
 #include <math.h>
 #include <stdio.h>
@@ -135,8 +137,12 @@ static int ops(void) {
 
 int main(int argc, char **argv) {
     if (argc < 3) {
-        fprintf(stderr, "usage: %s MODEL.gguf gen N ID... | ops\n", argv[0]);
+        fprintf(stderr, "usage: %s MODEL.gguf gen N ID... | ops, or %s format PATH...\n", argv[0], argv[0]);
         return 2;
+    }
+    if (!strcmp(argv[1], "format")) {
+        for (int i = 2; i < argc; i++) printf("format %d %s\n", (int)detect_format(argv[i]), argv[i]);
+        return 0;
     }
     load_model(argv[1]);
     init_kv_cache();

@@ -200,6 +200,23 @@ static void read_llama_vocab(const char *path) {
     fclose(h.f);
 }
 
+/* gguf.h's detect_format (src/gguf.c:394-403), kept alike because callers
+ * branch on it: a name ending in .gguf or .bin decides; otherwise the first
+ * four bytes of the file, GGUF's magic or that of LMc's .bin format; a file
+ * that cannot be read is FORMAT_UNKNOWN.  (This layer's load_model reads
+ * GGUF only; the .bin loader is not part of the device path.) */
+ModelFormat detect_format(const char *path) {
+    const size_t n = strlen(path);
+    if (n >= 5 && !strcmp(path + n - 5, ".gguf")) return FORMAT_GGUF;
+    if (n >= 4 && !strcmp(path + n - 4, ".bin")) return FORMAT_BIN;
+    FILE *f = fopen(path, "rb");
+    if (!f) return FORMAT_UNKNOWN;
+    uint32_t magic = 0;
+    if (fread(&magic, sizeof magic, 1, f) != 1) magic = 0;
+    fclose(f);
+    return magic == GGUF_MAGIC ? FORMAT_GGUF : magic == MODEL_MAGIC ? FORMAT_BIN : FORMAT_UNKNOWN;
+}
+
 /* LMc's CLI falls back to a model file at a default location when --model is
  * not given (src/gguf.c:414-420): the first of these that opens. */
 const char *find_default_model(void) {

@@ -22,7 +22,7 @@ DROPIN = os.path.join(ROOT, "lmc_b200", "dropin", "_build", "example_dropin")
 ARCHIVE = os.path.join(ROOT, "lmc_b200", "dropin", "_build", "liblmc_ops_dropin.a")
 OPS_H = ["load_model", "model_forward", "matmul_vec", "layer_norm", "rms_norm", "softmax", "gelu", "silu",
          "rope_apply", "attention_forward", "llama_attention_forward", "swiglu_ffn_forward",
-         "transformer_block_forward"]
+         "transformer_block_forward", "detect_format", "find_default_model"]
 
 MODELS = [
     ("gpt2", dict(L=2, D=256, H=4, S=128, V=1000, seed=21)),
@@ -77,6 +77,29 @@ def test_example_native_matches_lmc_generate(model_dir):
     ref.load(path)
     want, _, _ = ref.generate(np.array(prompt, np.int32), 12)
     assert ids == want.tolist()
+
+
+def test_detect_format_matches_lmc(tmp_path, model_dir):
+    """gguf.h's detect_format through the layer gives LMc's answer for
+    names that decide by suffix, files that decide by their magic (GGUF, LMc's
+    .bin header), unreadable and missing files.  No model is loaded."""
+    need(NATIVE)
+    need(DROPIN)
+    import struct
+    gguf = synth.cached_model(MODELS[0][0], model_dir, **MODELS[0][1])
+    plain = tmp_path / "model_without_suffix"
+    plain.write_bytes(open(gguf, "rb").read()[:64])
+    legacy = tmp_path / "legacy_weights"
+    legacy.write_bytes(struct.pack("<I", 0x47505432) + b"\0" * 60)
+    junk = tmp_path / "junk"
+    junk.write_bytes(b"abc")
+    paths = [str(p) for p in (plain, legacy, junk)] + [str(tmp_path / "x.gguf"), str(tmp_path / "y.bin"),
+                                                       str(tmp_path / "missing"), gguf]
+    rc_n, out_n, err_n = run(NATIVE, "format", *paths)
+    rc_d, out_d, err_d = run(DROPIN, "format", *paths)
+    assert rc_n == 0 and rc_d == 0, (err_n, err_d)
+    assert out_d == out_n
+    assert [int(l.split()[1]) for l in out_n.splitlines()] == [2, 1, 0, 2, 1, 0, 2]
 
 
 def test_dropin_fails_loudly_without_gpu(model_dir):
