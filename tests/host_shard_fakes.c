@@ -41,6 +41,10 @@ int lmc_model_load_paged(const char *path, int max_batch, int max_rows, int kv_d
 int lmc_model_forward(lmc_model *m, const int *h_tokens, const int *h_pos, int batch, float *h_logits, int *h_next);
 int lmc_model_release_seq(lmc_model *m, int seq);
 int lmc_model_kv_pages(const lmc_model *m, int *page_size, int *n_pages, int *n_free);
+int lmc_model_prefill(lmc_model *m, int seq, const int *h_tokens, int n, int start_pos, float *h_logits, int *h_next);
+int lmc_model_generate(lmc_model *m, const int *h_prompt, int n_prompt, int batch, int n_new, int use_graph,
+                       int *h_out_ids);
+int lmc_model_replay(lmc_model *m, int n, void *stream_out);
 
 static char g_err[512];
 int lmc_set_error(int code, const char *fmt, ...) {
@@ -204,6 +208,31 @@ static int paged_scenario(const char *path) {
     return 0;
 }
 
+/* Argument checks of the model entry points on a loaded model (argv[3] ==
+ * "args"): calls that must be refused before any work, sizes chosen so
+ * that a check written as a sum would overflow an int.  One "A <rc>" line
+ * per call. */
+static int args_scenario(const char *path) {
+    lmc_model *m = NULL;
+    int rc = lmc_model_load(path, 2, LMC_KV_F16, &m);
+    printf("rc %d %s\n", rc, rc ? lmc_last_error() : "");
+    if (rc) return 0;
+    const int big = 2147483600, tok[2] = {1, 2}, bad_tok[1] = {1 << 30}, pos_ok[2] = {0, 0};
+    int pos_bad[1] = {-1}, ids[4];
+    printf("A %d\n", lmc_model_forward(m, tok, pos_bad, 1, NULL, NULL));          /* negative position */
+    pos_bad[0] = 1 << 30;
+    printf("A %d\n", lmc_model_forward(m, tok, pos_bad, 1, NULL, NULL));          /* beyond the context */
+    printf("A %d\n", lmc_model_forward(m, bad_tok, pos_ok, 1, NULL, NULL));       /* token beyond V */
+    printf("A %d\n", lmc_model_forward(m, tok, pos_ok, 3, NULL, NULL));           /* more rows than sequences */
+    printf("A %d\n", lmc_model_prefill(m, 0, tok, 100, big, NULL, NULL));         /* start + n past INT_MAX */
+    printf("A %d\n", lmc_model_prefill(m, 2, tok, 2, 0, NULL, NULL));             /* no such sequence */
+    printf("A %d\n", lmc_model_generate(m, tok, 2, 1, 2147483647, 1, ids));       /* n_prompt + n_new past INT_MAX */
+    printf("A %d\n", lmc_model_generate(m, tok, big, 1, 4, 1, ids));              /* prompt beyond the context */
+    printf("A %d\n", lmc_model_replay(m, 1, NULL));                               /* no generation yet */
+    lmc_model_free(m);
+    return 0;
+}
+
 /* Loads argv[1] as shard r of argv[2] ranks for every r, one "R r rc" line
  * each before its uploads' lines. */
 int main(int argc, char **argv) {
@@ -215,6 +244,7 @@ int main(int argc, char **argv) {
         return 3;
     }
     if (argc > 3 && !strcmp(argv[3], "paged")) return paged_scenario(argv[1]);
+    if (argc > 3 && !strcmp(argv[3], "args")) return args_scenario(argv[1]);
     const int n = atoi(argv[2]);
     char id[128] = {0};
     for (int r = 0; r < n; r++) {

@@ -205,3 +205,14 @@ def test_paged_cache_page_accounting(loader_san, tmp_path):
     steps = [tuple(int(v) for v in ln.split()[1:]) for ln in out.splitlines() if ln.startswith("P ")]
     launch, ok, oom, invalid = -2, 0, -4, -1
     assert steps == [(launch, 4), (launch, 2), (ok, 5), (launch, 2), (oom, 2), (launch, 1), (ok, 4), (invalid, 4)]
+
+
+def test_model_entry_points_refuse_bad_arguments(loader_san, tmp_path):
+    """lmc_model_forward / _prefill / _generate / _replay on a loaded model
+    refuse negative or out-of-range positions, tokens and sequences, and
+    sizes whose sum would overflow an int (the checks are written without
+    the sum; UBSan would stop the run on a signed overflow)."""
+    path = synth.make_llama(str(tmp_path / "a.gguf"), L=1, D=64, H=4, Hkv=2, F=128, S=64, V=64, seed=1)
+    out = run(loader_san, [path, "1", "args"])
+    codes = [int(ln.split()[1]) for ln in out.splitlines() if ln.startswith("A ")]
+    assert codes == [-1] * 9, out[-800:]
